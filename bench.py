@@ -1,0 +1,451 @@
+"""Benchmark of the B200 sparse front end on the live-stream workload.
+
+Workload (per GPU, weak scaling): 32 independent 1024x1024 camera streams, each step a
+two-frame clip [3, 2, 1024, 1024] f16 -> patch-diff mask (~10% active tubelets by default)
+-> ViT-L/16 patch embed (D = 1024, K = 3*2*16*16 = 1536, f16 in, f32 accumulate) of the
+active tubelets -> in-place write into the stream's persistent f16 token cache [4096, 1024]
+(pre-filled N(0, 1)).  A "step" is one pass of that front end over every stream of the GPU.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--density D]
+                  [--sweep]
+
+For N > 1 it is launched by torch.distributed.run, one process per GPU; streams are
+sharded with no data-path collective (streams share nothing), and timings are the max
+over ranks.  Rank 0 prints one JSON line.
+
+value: active tubelets/s with the clips already resident in HBM (two input sets of 403 MB
+per GPU alternate, so every step reads its clips from HBM, not L2).
+e2e:   the same metric through the public API with host buffers: every step copies its
+clips from pinned host memory, runs the step and reads the per-stream active counts back.
+--impl reference: the reference's CPU algorithm (the C restatement in oracle/, f32 as on
+the reference's NdArray backend) on all host threads, over a bounded sample of streams.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+METRIC = "active tubelets/sec (1/2/4/8 B200) + % tensor-pipe/HBM roofline; ViT-L 1024² frames/s"
+UNIT = "active tubelets/s"
+
+STREAMS_PER_GPU = 32
+C, T, H, W, KT, P, D = 3, 2, 1024, 1024, 2, 16, 1024
+K = C * KT * P * P
+GRID = (T // KT, H // P, W // P)
+N_TOKENS = GRID[0] * GRID[1] * GRID[2]
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--density", type=float, default=0.10)
+    ap.add_argument("--streams", type=int, default=STREAMS_PER_GPU)
+    ap.add_argument("--sweep", action="store_true", help="also time densities 5/10/20/40%%")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--e2e-steps", type=int, default=5)
+    return ap.parse_args()
+
+
+def read_peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling during the timed region
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for name, val in zip(names, parts[5:9]):
+                if val.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing (timing only; no data-path collective)
+# ---------------------------------------------------------------------------
+def dist_setup():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
+    return world, rank, local
+
+
+def all_reduce(value: float, op: str, world: int, device):
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+# ---------------------------------------------------------------------------
+# CPU (oracle) leg
+# ---------------------------------------------------------------------------
+def cpu_front_end_rate(video_f32_streams, weight_f32, bias_f32, thr, budget_s=15.0):
+    """Times the oracle front end (f32, all OpenMP threads) stream by stream until `budget_s`
+    of CPU work.  Returns (tubelets/s, tubelets, streams, seconds, threads)."""
+    import numpy as np
+
+    import oracle
+
+    cfg = oracle.PatchifyConfig(C, D, T, H, W, KT, P, P)
+    mcfg = oracle.PatchDiffConfig.adaptive_threshold(thr, 1, N_TOKENS, 1)
+    cache = np.zeros((1, N_TOKENS, D), np.float32)
+    obs = np.zeros((1, N_TOKENS), np.float32)
+    age = np.zeros((1, N_TOKENS), np.float32)
+    total, elapsed, streams = 0, 0.0, 0
+    n = video_f32_streams.shape[0]
+    while True:  # cycle through the sample until `budget_s` of CPU work
+        s = streams % n
+        v = np.ascontiguousarray(video_f32_streams[s:s + 1])
+        t0 = time.perf_counter()
+        counts = oracle.front_end_streams(v, cfg, mcfg, weight_f32, bias_f32, cache, obs, age, age_observed=True)
+        elapsed += time.perf_counter() - t0
+        total += int(counts.sum())
+        streams += 1
+        if elapsed >= budget_s:
+            break
+    return total / elapsed, total, streams, elapsed, oracle.num_threads()
+
+
+# ---------------------------------------------------------------------------
+# GPU leg
+# ---------------------------------------------------------------------------
+def make_inputs(torch, dev, streams, density, seed_base):
+    from burn_jepa_b200 import workloads
+
+    sets = [workloads.rect_perturbation_clips_torch(seed_base + 1000 * i, streams, C, T, H, W, density, dev,
+                                                    torch.float16) for i in range(2)]
+    return sets
+
+
+def run_ours(args, world, rank, local):
+    import numpy as np
+    import torch
+
+    import burn_jepa_b200 as bj
+    from burn_jepa_b200 import workloads
+
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    S = args.streams
+    hbm_peak, tflops_peak, peak_kind = read_peaks()
+
+    weight = torch.from_numpy(workloads.normal(11, (D, C, KT, P, P), std=0.02)).to(dev, torch.float16)
+    bias = torch.from_numpy(workloads.normal(12, (D,), std=0.02)).to(dev)
+
+    def setup(density):
+        videos = make_inputs(torch, dev, S, density, seed_base=7 + 100003 * rank + int(density * 1e4))
+        # threshold: tubelets the rectangles do not touch score exactly 0, so any small positive
+        # threshold keeps exactly the changed tubelets; take it inside a score gap
+        sc = bj.patch_diff_token_scores(videos[0][:4].unsqueeze(1), KT, P).cpu().numpy().ravel()
+        thr = workloads.choose_threshold(sc, density, 1e-3)
+        mask = bj.PatchDiffConfig.adaptive_threshold(thr, 1, N_TOKENS, 1)
+        fe = bj.FrontEnd(S, C, T, H, W, KT, P, D, mask, torch.float16, torch.float16, dev)
+        caches = torch.randn((S, N_TOKENS, D), device=dev, dtype=torch.float32).to(torch.float16)
+        observed = torch.zeros((S, N_TOKENS), device=dev)
+        age = torch.zeros((S, N_TOKENS), device=dev)
+        counts_per_set = []
+        for v in videos:
+            c = fe.step(v, weight, bias, caches, observed, age)
+            counts_per_set.append(int(c.sum().item()))
+        return videos, thr, fe, caches, observed, age, counts_per_set
+
+    def time_steps(fe, videos, caches, observed, age, steps, warmup):
+        stream = torch.cuda.current_stream()
+        for i in range(warmup):
+            fe.step(videos[i % 2], weight, bias, caches, observed, age)
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        start.record(stream)
+        for i in range(steps):
+            fe.step(videos[i % 2], weight, bias, caches, observed, age)
+        end.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        return start.elapsed_time(end) / 1000.0
+
+    videos, thr, fe, caches, observed, age, counts_per_set = setup(args.density)
+    with ClockSampler(local) as clocks:
+        secs = time_steps(fe, videos, caches, observed, age, args.steps, args.warmup)
+    tubelets = sum(counts_per_set[i % 2] for i in range(args.steps))
+    max_secs = all_reduce(secs, "max", world, dev)
+    all_tubelets = all_reduce(float(tubelets), "sum", world, dev)
+    value = all_tubelets / max_secs
+    frames_per_s = all_reduce(float(S * args.steps), "sum", world, dev) / max_secs
+    assert not bj.device_error_check(), "a kernel reported a bounded-wait timeout"
+
+    # ---- per-kernel timings (CUDA events on the launching stream) ----
+    stream = torch.cuda.current_stream()
+    scores = torch.empty((S, N_TOKENS), device=dev)
+    nk = max(args.steps, 5)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(nk)]
+    for i in range(3):
+        bj.patch_diff_token_scores(videos[i % 2].unsqueeze(1), KT, P, out=scores)
+    torch.cuda.synchronize()
+    for i, (a, b) in enumerate(evs):
+        a.record(stream)
+        bj.patch_diff_token_scores(videos[i % 2].unsqueeze(1), KT, P, out=scores)
+        b.record(stream)
+    torch.cuda.synchronize()
+    mask_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    mask_bytes = S * C * T * H * W * 2 + S * N_TOKENS * 4  # clip read once + scores written
+    mask_gbs = mask_bytes / (mask_ms / 1e3) / 1e9
+
+    # gather-GEMM alone on the step's active rows (plain f16 output), same inputs
+    _, idx, cnt = bj.patch_diff_context_mask(videos[0].unsqueeze(1), KT, P, GRID, fe.desc.mask)
+    coords, total = bj.sparse_patchify_plan_coords(idx, GRID, batch=S, counts=cnt, capacity=S * N_TOKENS)
+    rows = int(total.item())
+    coords = coords[:rows].contiguous()
+    pcfg = bj.PatchifyConfig(C, D, T, H, W, KT, P, P)
+    vflat = videos[0]
+    feats = torch.empty((rows, D), device=dev, dtype=torch.float16)
+    for _ in range(3):
+        bj.sparse_patchify3d_forward(pcfg, vflat, coords, weight, bias, out=feats)
+    torch.cuda.synchronize()
+    for a, b in evs:
+        a.record(stream)
+        bj.sparse_patchify3d_forward(pcfg, vflat, coords, weight, bias, out=feats)
+        b.record(stream)
+    torch.cuda.synchronize()
+    gemm_ms = statistics.mean(a.elapsed_time(b) for a, b in evs)
+    gemm_tflops = 2.0 * rows * K * D / (gemm_ms / 1e3) / 1e12
+
+    step_ms = secs / args.steps * 1e3
+    dominant = "patch_diff_scores" if mask_ms >= gemm_ms else "gather_gemm"
+    if dominant == "patch_diff_scores":
+        roofline = {"kernel": "patch_diff_scores_vec_kernel<__half>", "bound": "hbm", "achieved": round(mask_gbs, 1),
+                    "peak": hbm_peak, "unit": "GB/s", "frac": round(mask_gbs / hbm_peak, 4),
+                    "traffic": None, "peak_source": peak_kind,
+                    "algorithmic_bytes_per_launch": mask_bytes, "avg_launch_ms": round(mask_ms, 4)}
+    else:
+        roofline = {"kernel": "gather_gemm_sm100_kernel<__half>", "bound": "tensor", "achieved": round(gemm_tflops, 1),
+                    "peak": tflops_peak, "unit": "TFLOP/s", "frac": round(gemm_tflops / tflops_peak, 4),
+                    "traffic": None, "peak_source": peak_kind,
+                    "algorithmic_flops_per_launch": 2 * rows * K * D, "avg_launch_ms": round(gemm_ms, 4)}
+    kernels = {
+        "patch_diff_scores": {"avg_ms": round(mask_ms, 4), "GB/s": round(mask_gbs, 1),
+                              "frac_hbm": round(mask_gbs / hbm_peak, 4)},
+        "gather_gemm": {"avg_ms": round(gemm_ms, 4), "rows": rows, "TFLOP/s": round(gemm_tflops, 1),
+                        "frac_tensor": round(gemm_tflops / tflops_peak, 4)},
+    }
+
+    # ---- e2e through the public API with host buffers ----
+    pinned = [v.cpu().pin_memory() for v in videos]
+    dev_video = torch.empty_like(videos[0])
+    counts_host = torch.empty((S,), dtype=torch.int32).pin_memory()
+    e2e_steps = max(1, args.e2e_steps)
+    for i in range(2):
+        dev_video.copy_(pinned[i % 2], non_blocking=True)
+        fe.step(dev_video, weight, bias, caches, observed, age)
+        counts_host.copy_(fe.counts, non_blocking=True)
+    torch.cuda.synchronize()
+    barrier(world)
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    e2e_tub = 0
+    for i in range(e2e_steps):
+        dev_video.copy_(pinned[i % 2], non_blocking=True)
+        fe.step(dev_video, weight, bias, caches, observed, age)
+        counts_host.copy_(fe.counts, non_blocking=True)
+        e2e_tub += counts_per_set[i % 2]
+    b.record(stream)
+    torch.cuda.synchronize()
+    e2e_secs = all_reduce(a.elapsed_time(b) / 1e3, "max", world, dev)
+    e2e_value = all_reduce(float(e2e_tub), "sum", world, dev) / e2e_secs
+    h2d = S * C * T * H * W * 2
+
+    sweep = None
+    if args.sweep:
+        sweep = {}
+        for dens in (0.05, 0.10, 0.20, 0.40):
+            del fe, caches, observed, age
+            torch.cuda.empty_cache()
+            videos2, thr2, fe, caches, observed, age, cps = setup(dens)
+            s2 = time_steps(fe, videos2, caches, observed, age, args.steps, args.warmup)
+            tub2 = sum(cps[i % 2] for i in range(args.steps))
+            s2m = all_reduce(s2, "max", world, dev)
+            sweep[f"{int(dens * 100)}%"] = {
+                "active_fraction": round(statistics.mean(cps) / (S * N_TOKENS), 4),
+                "value": round(all_reduce(float(tub2), "sum", world, dev) / s2m, 1),
+                "ms_per_step": round(s2m / args.steps * 1e3, 4)}
+            del videos2
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        import numpy as np
+
+        sample = videos[0][:8].float().cpu().numpy()
+        rate, tub, ns, el, threads = cpu_front_end_rate(sample, weight.float().cpu().numpy(), bias.cpu().numpy(), thr)
+        cpu = {"value": round(rate, 1), "unit": UNIT, "cores": threads, "kind": "port",
+               "sample": f"{ns} stream-steps cycling over 8 of the {S} streams (first input set), {tub} active "
+                          f"tubelets, {el:.1f} s of CPU work, f32"}
+
+    result = {
+        "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(max_secs / args.steps * 1e3, 4), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": "live camera streams: 32 x [3,2,1024,1024] f16 per GPU, ViT-L/16 patch embed "
+                               "(D=1024, K=1536), patch-diff mask, f16 token cache [4096,1024] per stream",
+                   "streams_per_gpu": S, "target_density": args.density,
+                   "active_fraction": round(statistics.mean(counts_per_set) / (S * N_TOKENS), 4),
+                   "active_tubelets_per_step_per_gpu": counts_per_set,
+                   "threshold": thr,
+                   "l2": "inputs larger than L2: two 403 MB clip sets per GPU alternate between steps",
+                   "parallelism": f"stream-sharded replicas x{world}, no collective"},
+        "frames_per_s": round(frames_per_s, 1),
+        "roofline": roofline, "kernels": kernels,
+        "cpu_baseline": cpu,
+        "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": S * 4,
+                "steps": e2e_steps},
+        "gpu_launches": 4 * args.steps,
+        "clocks": clocks.summary(),
+    }
+    if sweep:
+        result["density_sweep"] = sweep
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+def run_reference(args, world, rank, local):
+    """CPU reference arm: rank 0 times the oracle front end; other ranks exit."""
+    if rank != 0:
+        return
+    import numpy as np
+
+    import torch
+
+    from burn_jepa_b200 import workloads
+
+    # same recipe, generated on the host (no GPU in the reference arm)
+    S = min(args.streams, 8)
+    video = workloads.rect_perturbation_clips(7, S, C, T, H, W, args.density)
+    weight = workloads.normal(11, (D, C, KT, P, P), std=0.02)
+    bias = workloads.normal(12, (D,), std=0.02)
+    import oracle
+
+    sc = oracle.patch_diff_token_scores(video[0:1].astype(np.float16).astype(np.float32), KT, P)
+    thr = workloads.choose_threshold(sc, args.density, 1e-3)
+    vid = video.astype(np.float16).astype(np.float32)
+    for _ in range(max(0, min(args.warmup, 1))):
+        cpu_front_end_rate(vid[:1], weight, bias, thr, budget_s=0.0)
+    per_step = []
+    tubelets = 0
+    for _ in range(args.steps):
+        rate, tub, ns, el, threads = cpu_front_end_rate(vid, weight, bias, thr, budget_s=2.0)
+        per_step.append(el)
+        tubelets += tub
+    value = tubelets / sum(per_step)
+    print(json.dumps({
+        "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(statistics.mean(per_step) * 1e3, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "live camera streams: [3,2,1024,1024] per stream, ViT-L/16 patch embed (D=1024, "
+                               "K=1536), patch-diff mask, token cache [4096,1024] per stream",
+                   "target_density": args.density, "parallelism": "host threads (OpenMP)"},
+        "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"each step: stream-steps cycling over a {S}-stream sample until 2 s of CPU work"},
+        "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
+def main():
+    args = parse_args()
+    world, rank, local = dist_setup()
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank, local)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,257 @@
+"""B200 (sm_100a) sparse front end for burn_jepa.
+
+The three steps of burn_jepa's sparse video front end -- patch-diff mask, sparse
+patchify (gather-GEMM on tcgen05 tensor cores) and the in-place token-cache write --
+as hand-written CUDA kernels behind the C ABI of ``include/bjf.h`` (``libbjf.so``).
+
+This module is the Python face of that ABI for tests, the benchmark and scripting:
+each function takes torch CUDA tensors (torch only provides device memory and the
+current stream), checks shapes, and calls the C entry point that replaces the
+named burn_jepa function.  Nothing here computes on the host or falls back to a
+CPU implementation; the C library must be built (``build.build()``).
+"""
+from __future__ import annotations
+
+import ctypes
+
+from . import _abi
+from ._abi import (  # noqa: F401  (re-exported)
+    BjfError,
+    FrontEndDesc,
+    PatchDiffConfig,
+    PatchifyConfig,
+    check,
+    last_error,
+    load,
+)
+
+__all__ = [
+    "BjfError",
+    "FrontEnd",
+    "PatchDiffConfig",
+    "PatchifyConfig",
+    "TokenGridShape",
+    "device_error_check",
+    "feature_memory_assign_latest",
+    "load",
+    "patch_diff_context_mask",
+    "patch_diff_context_mask_from_scores",
+    "patch_diff_token_scores",
+    "sparse_patchify3d_forward",
+    "sparse_patchify_plan_coords",
+]
+
+
+class TokenGridShape(tuple):
+    """(depth, height, width) token grid (burn_jepa src/tokens.rs:5-32)."""
+
+    def __new__(cls, depth: int, height: int, width: int):
+        return super().__new__(cls, (int(depth), int(height), int(width)))
+
+    depth = property(lambda self: self[0])
+    height = property(lambda self: self[1])
+    width = property(lambda self: self[2])
+
+    def len(self) -> int:
+        return self[0] * self[1] * self[2]
+
+    def tokens_per_frame(self) -> int:
+        return self[1] * self[2]
+
+
+def _torch():
+    import torch
+
+    return torch
+
+
+def _dtype_code(t) -> int:
+    torch = _torch()
+    m = {torch.float32: _abi.DTYPE_F32, torch.float16: _abi.DTYPE_F16, torch.bfloat16: _abi.DTYPE_BF16,
+         torch.int32: _abi.DTYPE_I32}
+    if t.dtype not in m:
+        raise TypeError(f"unsupported dtype {t.dtype}")
+    return m[t.dtype]
+
+
+def _stream(stream=None) -> ctypes.c_void_p:
+    torch = _torch()
+    s = stream if stream is not None else torch.cuda.current_stream()
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+def _ptr(t) -> ctypes.c_void_p:
+    if t is None:
+        return ctypes.c_void_p(0)
+    if not t.is_cuda:
+        raise ValueError("tensor must be on a CUDA device")
+    if not t.is_contiguous():
+        raise ValueError("tensor must be contiguous")
+    return ctypes.c_void_p(t.data_ptr())
+
+
+def device_error_check(stream=None) -> bool:
+    """True when a kernel gave up on a bounded wait since the last check (then cleared)."""
+    flag = ctypes.c_int32(0)
+    check(load().bjf_device_error_check(_stream(stream), ctypes.byref(flag)))
+    return bool(flag.value)
+
+
+# ---------------------------------------------------------------------------
+# Step 1: patch-diff mask
+# ---------------------------------------------------------------------------
+def _video_dims(video, streams):
+    if video.dim() == 5:
+        return (1, tuple(video.shape)) if streams is None else (streams, tuple(video.shape))
+    if video.dim() == 6:
+        return video.shape[0], tuple(video.shape[1:])
+    raise ValueError("video must be [B,C,T,H,W] or [S,B,C,T,H,W]")
+
+
+def patch_diff_token_scores(video, tubelet_size: int, patch_size: int, out=None, stream=None):
+    """`patch_diff_token_scores` (src/nodes.rs:565-631) on the device.
+
+    video: [B,C,T,H,W] or [S,B,C,T,H,W] (S independent videos).  Returns [N] or [S,N] f32."""
+    torch = _torch()
+    S, vd = _video_dims(video, None)
+    B, C, T, H, W = vd
+    n = (T // tubelet_size) * (H // patch_size) * (W // patch_size)
+    if out is None:
+        out = torch.empty((S, n), dtype=torch.float32, device=video.device)
+    check(load().bjf_patch_diff_token_scores(_ptr(video), _dtype_code(video), _abi.dims(*vd), S, tubelet_size,
+                                             patch_size, _ptr(out), _stream(stream)))
+    return out[0] if video.dim() == 5 else out
+
+
+def patch_diff_context_mask_from_scores(scores, grid, config: PatchDiffConfig, indices=None, counts=None,
+                                        stream=None):
+    """`patch_diff_context_mask_from_scores` (src/nodes.rs:458-537) on the device.
+
+    scores: [N] or [S,N] f32.  Returns (indices [S,N] int32, counts [S] int32): row s holds
+    counts[s] ascending token indices."""
+    torch = _torch()
+    sc = scores if scores.dim() == 2 else scores.unsqueeze(0)
+    S, n = sc.shape
+    if indices is None:
+        indices = torch.empty((S, n), dtype=torch.int32, device=scores.device)
+    if counts is None:
+        counts = torch.empty((S,), dtype=torch.int32, device=scores.device)
+    check(load().bjf_patch_diff_context_mask_from_scores(_ptr(sc.contiguous()), S, _abi.dims(*grid),
+                                                         ctypes.byref(config), _ptr(indices), _ptr(counts),
+                                                         _stream(stream)))
+    return indices, counts
+
+
+def patch_diff_context_mask(video, tubelet_size: int, patch_size: int, grid, config: PatchDiffConfig,
+                            scores=None, indices=None, counts=None, stream=None):
+    """`patch_diff_context_mask_from_video` (src/nodes.rs:539-546) on the device.
+
+    Returns (scores [S,N] f32, indices [S,N] int32, counts [S] int32)."""
+    torch = _torch()
+    S, vd = _video_dims(video, None)
+    n = int(grid[0]) * int(grid[1]) * int(grid[2])
+    dev = video.device
+    scores = torch.empty((S, n), dtype=torch.float32, device=dev) if scores is None else scores
+    indices = torch.empty((S, n), dtype=torch.int32, device=dev) if indices is None else indices
+    counts = torch.empty((S,), dtype=torch.int32, device=dev) if counts is None else counts
+    check(load().bjf_patch_diff_context_mask(_ptr(video), _dtype_code(video), _abi.dims(*vd), S, tubelet_size,
+                                             patch_size, _abi.dims(*grid), ctypes.byref(config), _ptr(scores),
+                                             _ptr(indices), _ptr(counts), _stream(stream)))
+    return scores, indices, counts
+
+
+# ---------------------------------------------------------------------------
+# Plans
+# ---------------------------------------------------------------------------
+def sparse_patchify_plan_coords(indices, grid, batch: int, counts=None, capacity: int | None = None,
+                                coords=None, total_rows=None, stream=None):
+    """Device `SparsePatchifyPlan::new` / `SparsePatchifyBatchPlan::new` (src/sparse_patchify.rs:236-330).
+
+    indices: [mask_rows, stride] int32 (mask_rows 1 = uniform plan, or == batch).  Returns
+    (coords [capacity, 4] int32, total_rows [1] int32 on the device)."""
+    torch = _torch()
+    idx = indices if indices.dim() == 2 else indices.unsqueeze(0)
+    mask_rows, stride = idx.shape
+    if capacity is None:
+        capacity = batch * stride
+    dev = indices.device
+    coords = torch.empty((capacity, 4), dtype=torch.int32, device=dev) if coords is None else coords
+    total_rows = torch.empty((1,), dtype=torch.int32, device=dev) if total_rows is None else total_rows
+    check(load().bjf_sparse_patchify_plan_coords(_ptr(idx.contiguous()), stride, _ptr(counts), mask_rows, batch,
+                                                 _abi.dims(*grid), _ptr(coords), capacity, _ptr(total_rows),
+                                                 _stream(stream)))
+    return coords, total_rows
+
+
+# ---------------------------------------------------------------------------
+# Step 2: sparse patchify
+# ---------------------------------------------------------------------------
+def sparse_patchify3d_forward(config: PatchifyConfig, input, coords, weight, bias=None, out=None,
+                              out_dtype=None, stream=None):
+    """`burn_flex_gmm::cuda::sparse_patchify3d_forward_cuda` on the sm_100a gather-GEMM.
+
+    input [B,C,T,H,W]; coords [rows,4] int32; weight [D,C,kt,ph,pw]; bias [D] f32 or None.
+    Returns [rows, D] (f32 unless out_dtype/out say otherwise)."""
+    torch = _torch()
+    rows = coords.shape[0]
+    if out is None:
+        out = torch.empty((rows, config.out_channels), dtype=out_dtype or torch.float32, device=input.device)
+    check(load().bjf_sparse_patchify3d_forward(
+        ctypes.byref(config), _ptr(input), _dtype_code(input), _abi.dims(*input.shape), _ptr(coords), rows,
+        _ptr(weight), _dtype_code(weight), _abi.dims(*weight.shape), _ptr(bias), _ptr(out), _dtype_code(out),
+        _stream(stream)))
+    return out
+
+
+# ---------------------------------------------------------------------------
+# Step 3: token-cache write
+# ---------------------------------------------------------------------------
+def feature_memory_assign_latest(features, observed, age_frames, tokens, token_indices, age_observed: bool,
+                                 stream=None):
+    """`sparse_feature_memory_assign_latest_cuda_raw` (src/sparse_feature_memory.rs:296-313), in place.
+
+    features [B,N,D]; observed/age_frames [B,N] f32; tokens [B,S,D]; token_indices [B,S] int32."""
+    check(load().bjf_feature_memory_assign_latest(
+        _ptr(features), _dtype_code(features), _abi.dims(*features.shape), _ptr(observed),
+        _abi.dims(*observed.shape), _ptr(age_frames), _abi.dims(*age_frames.shape), _ptr(tokens),
+        _dtype_code(tokens), _abi.dims(*tokens.shape), _ptr(token_indices), _abi.dims(*token_indices.shape),
+        int(bool(age_observed)), _stream(stream)))
+
+
+# ---------------------------------------------------------------------------
+# Fused step over S independent streams
+# ---------------------------------------------------------------------------
+class FrontEnd:
+    """One frame step of the whole front end for S independent streams (``bjf_front_end_step``).
+
+    Each stream is a video [C, T, H, W] (batch 1) with its own persistent token cache
+    [N, D], observed [N] and age [N].  ``step`` runs patch-diff mask -> device plan ->
+    tcgen05 gather-GEMM -> in-place cache write for every stream and returns the device
+    tensor of per-stream active tubelet counts.  Owns its device workspace."""
+
+    def __init__(self, streams: int, channels: int, frames: int, height: int, width: int, tubelet_size: int,
+                 patch_size: int, embed_dim: int, mask: PatchDiffConfig, video_dtype, cache_dtype, device,
+                 weight_dtype=None):
+        torch = _torch()
+        dt = {torch.float32: _abi.DTYPE_F32, torch.float16: _abi.DTYPE_F16, torch.bfloat16: _abi.DTYPE_BF16}
+        self.desc = FrontEndDesc(streams, channels, frames, height, width, tubelet_size, patch_size, embed_dim,
+                                 dt[video_dtype], dt[weight_dtype or video_dtype], dt[cache_dtype], mask)
+        nbytes = load().bjf_front_end_workspace_bytes(ctypes.byref(self.desc))
+        if nbytes == 0:
+            raise BjfError(_abi.BJF_ERR_INVALID_ARGUMENT, last_error())
+        self.workspace = torch.empty(nbytes, dtype=torch.uint8, device=device)
+        self.counts = torch.zeros(streams, dtype=torch.int32, device=device)
+        self.grid = TokenGridShape(frames // tubelet_size, height // patch_size, width // patch_size)
+        self.steps = 0
+
+    def step(self, video, weight, bias, caches, observed, age_frames, age_observed=None, stream=None):
+        """video [S,C,T,H,W]; weight [D,C,kt,P,P]; bias [D] f32 or None; caches [S,N,D];
+        observed / age_frames [S,N] f32.  age_observed defaults to (this object has stepped)."""
+        if age_observed is None:
+            age_observed = self.steps > 0
+        check(load().bjf_front_end_step(
+            ctypes.byref(self.desc), _ptr(video), _ptr(weight), _ptr(bias), _ptr(caches), _ptr(observed),
+            _ptr(age_frames), int(bool(age_observed)), _ptr(self.workspace), self.workspace.numel(),
+            _ptr(self.counts), _stream(stream)))
+        self.steps += 1
+        return self.counts

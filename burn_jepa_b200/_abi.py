@@ -1,0 +1,167 @@
+"""ctypes binding of ``libbjf.so`` (the C ABI declared in ``include/bjf.h``).
+
+The library is built in-tree by ``burn_jepa_b200/build.py`` (nvcc, sm_100a).  Loading
+fails loudly when it is missing: there is no fallback implementation.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import re
+
+_PKG = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(_PKG, "libbjf.so")
+HEADER_PATH = os.path.join(os.path.dirname(_PKG), "include", "bjf.h")
+
+BJF_OK = 0
+BJF_ERR_INVALID_ARGUMENT = -1
+BJF_ERR_UNSUPPORTED = -2
+BJF_ERR_CUDA = 1
+
+DTYPE_F32, DTYPE_F16, DTYPE_BF16, DTYPE_I32 = 0, 1, 2, 3
+
+
+class BjfError(RuntimeError):
+    """A non-zero status from the C ABI, carrying the library's message."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(message)
+        self.status = status
+
+
+class PatchifyConfig(ctypes.Structure):
+    """bjf_patchify_config == burn_flex_gmm::SparsePatchify3dConfig (src/model.rs:1297-1306)."""
+
+    _fields_ = [
+        (n, ctypes.c_int64)
+        for n in ("in_channels", "out_channels", "frames", "height", "width", "tubelet_size", "patch_h", "patch_w")
+    ]
+
+
+class PatchDiffConfig(ctypes.Structure):
+    """bjf_patch_diff_config == SparseJepaPatchDiffSparsityConfig (src/nodes.rs:97-157)."""
+
+    _fields_ = [
+        ("threshold", ctypes.c_float),
+        ("context_tokens", ctypes.c_int64),
+        ("target_tokens", ctypes.c_int64),
+        ("dilation", ctypes.c_int64),
+        ("min_context_tokens", ctypes.c_int64),
+        ("fill_to_context_tokens", ctypes.c_int32),
+        ("allow_full_context", ctypes.c_int32),
+    ]
+
+    @classmethod
+    def new(cls, threshold: float, context_tokens: int, target_tokens: int) -> "PatchDiffConfig":
+        """SparseJepaPatchDiffSparsityConfig::new (src/nodes.rs:109-119)."""
+        return cls(threshold, context_tokens, target_tokens, 0, 1, 1, 0)
+
+    @classmethod
+    def adaptive_threshold(cls, threshold: float, min_context_tokens: int, max_context_tokens: int,
+                           target_tokens: int) -> "PatchDiffConfig":
+        """SparseJepaPatchDiffSparsityConfig::adaptive_threshold (src/nodes.rs:121-136)."""
+        return cls(threshold, max_context_tokens, target_tokens, 0, min_context_tokens, 0, 1)
+
+    def with_dilation(self, dilation: int) -> "PatchDiffConfig":
+        c = PatchDiffConfig.from_buffer_copy(self)
+        c.dilation = dilation
+        return c
+
+    def with_min_context_tokens(self, n: int) -> "PatchDiffConfig":
+        c = PatchDiffConfig.from_buffer_copy(self)
+        c.min_context_tokens = n
+        return c
+
+    def with_fill_to_context_tokens(self, v: bool) -> "PatchDiffConfig":
+        c = PatchDiffConfig.from_buffer_copy(self)
+        c.fill_to_context_tokens = int(bool(v))
+        return c
+
+    def with_allow_full_context(self, v: bool) -> "PatchDiffConfig":
+        c = PatchDiffConfig.from_buffer_copy(self)
+        c.allow_full_context = int(bool(v))
+        return c
+
+
+class FrontEndDesc(ctypes.Structure):
+    """bjf_front_end_desc: S independent streams, each video [C, T, H, W] with batch 1."""
+
+    _fields_ = [
+        ("streams", ctypes.c_int64),
+        ("channels", ctypes.c_int64),
+        ("frames", ctypes.c_int64),
+        ("height", ctypes.c_int64),
+        ("width", ctypes.c_int64),
+        ("tubelet_size", ctypes.c_int64),
+        ("patch_size", ctypes.c_int64),
+        ("embed_dim", ctypes.c_int64),
+        ("video_dtype", ctypes.c_int32),
+        ("weight_dtype", ctypes.c_int32),
+        ("cache_dtype", ctypes.c_int32),
+        ("mask", PatchDiffConfig),
+    ]
+
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+_I32 = ctypes.c_int32
+_DIMS = ctypes.POINTER(ctypes.c_int64)
+
+# name -> (restype, argtypes)
+SIGNATURES = {
+    "bjf_abi_version": (ctypes.c_int32, []),
+    "bjf_get_last_error_string": (ctypes.c_size_t, [ctypes.c_char_p, ctypes.c_size_t]),
+    "bjf_device_error_check": (_I32, [_P, ctypes.POINTER(_I32)]),
+    "bjf_patch_diff_token_scores": (_I32, [_P, _I32, _DIMS, _I64, _I64, _I64, _P, _P]),
+    "bjf_patch_diff_context_mask_from_scores": (_I32, [_P, _I64, _DIMS, ctypes.POINTER(PatchDiffConfig), _P, _P, _P]),
+    "bjf_patch_diff_context_mask": (_I32, [_P, _I32, _DIMS, _I64, _I64, _I64, _DIMS,
+                                           ctypes.POINTER(PatchDiffConfig), _P, _P, _P, _P]),
+    "bjf_sparse_patchify_plan_coords": (_I32, [_P, _I64, _P, _I64, _I64, _DIMS, _P, _I64, _P, _P]),
+    "bjf_sparse_patchify3d_forward": (_I32, [ctypes.POINTER(PatchifyConfig), _P, _I32, _DIMS, _P, _I64, _P, _I32,
+                                             _DIMS, _P, _P, _I32, _P]),
+    "bjf_front_end_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(FrontEndDesc)]),
+    "bjf_front_end_step": (_I32, [ctypes.POINTER(FrontEndDesc), _P, _P, _P, _P, _P, _P, _I32, _P, ctypes.c_size_t,
+                                  _P, _P]),
+    "bjf_feature_memory_assign_latest": (_I32, [_P, _I32, _DIMS, _P, _DIMS, _P, _DIMS, _P, _I32, _DIMS, _P, _DIMS,
+                                                _I32, _P]),
+}
+
+_lib = None
+
+
+def header_symbols() -> list[str]:
+    """Every function ``include/bjf.h`` declares."""
+    text = open(HEADER_PATH).read()
+    return sorted(set(re.findall(r"BJF_API\s+[\w\s\*]+?\b(bjf_\w+)\s*\(", text)))
+
+
+def load() -> ctypes.CDLL:
+    """Loads libbjf.so (raises if it has not been built)."""
+    global _lib
+    if _lib is None:
+        if not os.path.exists(LIB_PATH):
+            raise RuntimeError(
+                f"{LIB_PATH} is missing: build it with `python -c 'import __graft_entry__ as g; g.build()'`")
+        lib = ctypes.CDLL(LIB_PATH)
+        for name, (res, args) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = lib
+    return _lib
+
+
+def last_error() -> str:
+    buf = ctypes.create_string_buffer(1024)
+    load().bjf_get_last_error_string(buf, len(buf))
+    return buf.value.decode()
+
+
+def check(status: int) -> None:
+    if status != BJF_OK:
+        raise BjfError(status, last_error())
+
+
+def dims(*values) -> ctypes.Array:
+    arr = (ctypes.c_int64 * len(values))(*[int(v) for v in values])
+    return arr

@@ -1,0 +1,150 @@
+// front_end.cu -- one step of the sparse front end for S independent streams,
+// fully on the device:
+//
+//   1. patch-diff scores          [S, N] f32                  (memory-bound pass over the clips)
+//   2. selection + cache aging    indices [S, N], counts [S]  (one CTA per stream; the
+//                                 AssignLatest aging age += observed runs in the same launch)
+//   3. plan                       coords [S*N, 4], total rows (concatenated ragged streams)
+//   4. gather-GEMM                tcgen05 tiles over the concatenated active rows; the
+//                                 epilogue adds the bias and writes each row straight into
+//                                 its stream's token cache slot, setting observed = 1, age = 0
+//
+// This is the composition the reference pipeline performs per stream and per frame
+// (patch_diff_context_mask -> SparsePatchifyPlan::new -> sparse_patchify3d_forward_cuda ->
+// update_tokens_tiled_assign_cuda_raw, src/nodes.rs:411-456, src/sparse_patchify.rs:236-269,
+// src/model.rs:1273-1328, src/feature_memory.rs:616-645), with no host round trip: the
+// mask never leaves the device and the features never exist outside the cache.  Row
+// counts are only known on the device, so the GEMM grid is sized for the capacity and
+// surplus tiles exit at once.
+#include <algorithm>
+#include <string>
+
+#include "common.cuh"
+#include "gather_gemm.hpp"
+#include "patch_diff.hpp"
+#include "runtime.hpp"
+#include "status.hpp"
+
+namespace bjf {
+namespace {
+
+struct Workspace {
+  size_t scores, indices, counts, coords, total, bytes;
+};
+
+Workspace layout(int64_t S, int64_t N) {
+  auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+  Workspace w{};
+  size_t off = 0;
+  w.scores = off;
+  off = up(off + sizeof(float) * S * N);
+  w.indices = off;
+  off = up(off + sizeof(int32_t) * S * N);
+  w.counts = off;
+  off = up(off + sizeof(int32_t) * S);
+  w.coords = off;
+  off = up(off + sizeof(int32_t) * 4 * S * N);
+  w.total = off;
+  off = up(off + sizeof(int32_t));
+  w.bytes = off;
+  return w;
+}
+
+bjf_status validate(const bjf_front_end_desc* d, int64_t& N) {
+  if (!d) return fail(BJF_ERR_INVALID_ARGUMENT, "front-end descriptor must not be null");
+  const int64_t v[9] = {d->streams, d->channels, d->frames, d->height, d->width,
+                        d->tubelet_size, d->patch_size, d->embed_dim, 1};
+  for (int64_t x : v)
+    if (x <= 0 || x > (1 << 30)) return fail(BJF_ERR_INVALID_ARGUMENT, "front-end sizes must be positive");
+  if (d->frames % d->tubelet_size || d->height % d->patch_size || d->width % d->patch_size)
+    return fail(BJF_ERR_INVALID_ARGUMENT,
+                "patch-diff sparsity requires frames/height/width divisible by tubelet and patch sizes");
+  N = (d->frames / d->tubelet_size) * (d->height / d->patch_size) * (d->width / d->patch_size);
+  if (d->streams > 4096) return fail(BJF_ERR_UNSUPPORTED, "the front end supports up to 4096 streams per call");
+  if (d->streams * N > INT32_MAX) return fail(BJF_ERR_UNSUPPORTED, "streams x tokens exceeds 2^31-1");
+  if (dtype_size(d->cache_dtype) == 0 || d->cache_dtype == BJF_DTYPE_I32)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "cache dtype must be f32, f16 or bf16");
+  return BJF_OK;
+}
+
+}  // namespace
+}  // namespace bjf
+
+using namespace bjf;
+
+extern "C" size_t bjf_front_end_workspace_bytes(const bjf_front_end_desc* d) {
+  int64_t N = 0;
+  if (validate(d, N)) return 0;
+  return layout(d->streams, N).bytes;
+}
+
+extern "C" bjf_status bjf_front_end_step(const bjf_front_end_desc* d, const void* video, const void* weight,
+                                         const float* bias, void* caches, float* observed, float* age_frames,
+                                         int32_t age_observed, void* workspace, size_t workspace_bytes,
+                                         int32_t* counts_out, bjf_stream_t stream) {
+  int64_t N = 0;
+  bjf_status rc = validate(d, N);
+  if (rc) return rc;
+  const int64_t S = d->streams;
+  const Workspace w = layout(S, N);
+  if (!workspace || workspace_bytes < w.bytes)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "front-end workspace too small: need " + std::to_string(w.bytes) + " bytes");
+  if (reinterpret_cast<uintptr_t>(workspace) % 256)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "front-end workspace must be 256-byte aligned");
+  if (!video || !weight || !caches || !observed || !age_frames)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "front-end buffers must not be null");
+  const int64_t grid[3] = {d->frames / d->tubelet_size, d->height / d->patch_size, d->width / d->patch_size};
+  SelectParams sel;
+  rc = resolve_select(&d->mask, grid, sel);
+  if (rc) return rc;
+  const DeviceInfo* dev = nullptr;
+  rc = current_device(&dev);
+  if (rc) return rc;
+
+  char* ws = static_cast<char*>(workspace);
+  float* scores = reinterpret_cast<float*>(ws + w.scores);
+  int32_t* indices = reinterpret_cast<int32_t*>(ws + w.indices);
+  int32_t* counts = counts_out ? counts_out : reinterpret_cast<int32_t*>(ws + w.counts);
+  int32_t* coords = reinterpret_cast<int32_t*>(ws + w.coords);
+  int32_t* total = reinterpret_cast<int32_t*>(ws + w.total);
+  cudaStream_t st = as_cuda(stream);
+
+  const int64_t vd[5] = {1, d->channels, d->frames, d->height, d->width};
+  rc = launch_scores(video, d->video_dtype, vd, S, d->tubelet_size, d->patch_size, scores, st);
+  if (rc) return rc;
+  if (age_observed) {
+    sel.age = age_frames;
+    sel.observed = observed;
+  }
+  rc = launch_select(scores, S, sel, indices, counts, st);
+  if (rc) return rc;
+  rc = bjf_sparse_patchify_plan_coords(indices, N, counts, S, S, grid, coords, S * N, total, stream);
+  if (rc) return rc;
+
+  GatherGeometry g{};
+  g.C = (int)d->channels;
+  g.T = (int)d->frames;
+  g.H = (int)d->height;
+  g.W = (int)d->width;
+  g.kt = (int)d->tubelet_size;
+  g.ph = (int)d->patch_size;
+  g.pw = (int)d->patch_size;
+  g.batch = (int)S;
+  g.depth = (int)grid[0];
+  g.gh = (int)grid[1];
+  g.gw = (int)grid[2];
+  g.K = (int)(d->channels * d->tubelet_size * d->patch_size * d->patch_size);
+  g.D = (int)d->embed_dim;
+  EpilogueArgs ep{};
+  ep.mode = kEpilogueScatter;
+  ep.out = caches;
+  ep.out_dtype = d->cache_dtype;
+  ep.out_elem_bytes = (int)dtype_size(d->cache_dtype);
+  ep.ldo = d->embed_dim;
+  ep.dense_tokens = N;
+  ep.observed = observed;
+  ep.age = age_frames;
+  ep.bias = bias;
+  return launch_gather_gemm(*dev, video, d->video_dtype, weight, d->weight_dtype, g,
+                            reinterpret_cast<const int4*>(coords), total, S * N, ep, st);
+}

@@ -1,0 +1,562 @@
+// gather_gemm.cu -- step 2 of the sparse front end: sparse patchify as a
+// gather-GEMM, the operation burn_flex_gmm::cuda::sparse_patchify3d_forward_cuda
+// performs for burn_jepa (called at src/model.rs:1140, 1197, 1319):
+//
+//   out[m, d] = bias[d] + sum_k W[d, k] * A[m, k]
+//   A[m, k]   = x[b, c, t*kt + dt, r*ph + dy, col*pw + dx],  (b, t, r, col) = coords[m]
+//   k         = ((c*kt + dt)*ph + dy)*pw + dx            (Conv3d weight [D, C, kt, ph, pw])
+//
+// sm_100a path (f16 / bf16): one CTA per 128-row x BN-column output tile.
+//   warps 0-3  gather producers: thread m owns tile row m and, per 64-wide K block,
+//              copies its eight 16-byte runs (pw-contiguous image rows) with cp.async
+//              straight into the 128B-swizzled K-major A stage; after the copies land
+//              it fences them into the async proxy and arrives on the stage barrier.
+//              They turn into the epilogue once the accumulator is ready.
+//   warp 4     allocates TMEM and issues tcgen05.mma (M=128, N=BN, K=16) from one
+//              thread; tcgen05.commit releases each stage and finally the accumulator.
+//   warp 5     TMA producer for the weight tile (2-D tiled, 128B swizzle, no multicast).
+//   epilogue   tcgen05.ld 32x32b -> + bias -> convert -> store (or scatter into a
+//              token cache row, which fuses step 3).
+// Every mbarrier wait is bounded in time; on expiry the kernel records an error
+// flag, drains its own copies, frees TMEM and returns.
+//
+// Generic path (f32, or shapes the tensor-core path does not take): a tiled SIMT
+// FFMA GEMM over the same gather, f32 accumulation.
+#include <cuda.h>
+
+#include <algorithm>
+#include <mutex>
+#include <string>
+
+#include "common.cuh"
+#include "gather_gemm.hpp"
+#include "runtime.hpp"
+#include "sm100.cuh"
+#include "status.hpp"
+
+namespace bjf {
+namespace {
+
+using namespace sm100;
+
+constexpr int kBM = 128;
+constexpr int kBK = 64;
+constexpr int kStages = 4;
+constexpr int kMaxBN = 256;
+constexpr int kLag = 2;  // cp.async groups a producer keeps in flight before arriving
+constexpr int kThreads = 192;
+constexpr int kMaxKBlocks = 128;  // K <= 8192
+constexpr uint64_t kWaitLimitNs = 2000000000ull;
+
+constexpr int kAStageBytes = kBM * kBK * 2;      // 16 KB
+constexpr int kBStageBytes = kMaxBN * kBK * 2;   // 32 KB
+
+struct SmemLayout {
+  static constexpr int a_off = 0;
+  static constexpr int b_off = a_off + kStages * kAStageBytes;
+  static constexpr int bar_off = b_off + kStages * kBStageBytes;
+  // full_a[kStages], full_b[kStages], empty[kStages], acc_full
+  static constexpr int misc_off = bar_off + (3 * kStages + 1) * 8;
+  // tmem base (4 B), abort flag (4 B)
+  static constexpr int koff_off = misc_off + 16;
+  static constexpr int total = koff_off + kMaxKBlocks * 8 * 8;
+  static constexpr int alloc = total + 1024;  // room to align the base to 1024 B
+};
+
+__device__ __forceinline__ int64_t row_base_offset(const GatherGeometry& g, int4 c, bool& valid) {
+  valid = c.x >= 0 && c.x < g.batch && c.y >= 0 && c.y < g.depth && c.z >= 0 && c.z < g.gh &&
+          c.w >= 0 && c.w < g.gw;
+  if (!valid) return 0;
+  return (((int64_t)c.x * g.C * g.T + (int64_t)c.y * g.kt) * g.H + (int64_t)c.z * g.ph) * g.W +
+         (int64_t)c.w * g.pw;
+}
+
+// Offset of element k of a tubelet row relative to its (b, t*kt, r*ph, col*pw) corner.
+__host__ __device__ __forceinline__ int64_t k_offset(const GatherGeometry& g, int k) {
+  int q = k / g.pw;
+  int dx = k - q * g.pw;
+  int dy = q % g.ph;
+  int q2 = q / g.ph;
+  int dt = q2 % g.kt;
+  int ch = q2 / g.kt;
+  return (((int64_t)ch * g.T + dt) * g.H + dy) * g.W + dx;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 1)
+    gather_gemm_sm100_kernel(const __grid_constant__ CUtensorMap wmap, const T* __restrict__ video,
+                             const int4* __restrict__ coords, const int32_t* __restrict__ rows_dev,
+                             int rows_cap, GatherGeometry g, int bn, EpilogueArgs ep,
+                             int* __restrict__ error_flag) {
+  extern __shared__ uint8_t smem_dyn[];
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+
+  int M = rows_cap;
+  if (rows_dev) M = min(M, max(0, __ldg(rows_dev)));
+  const int m_tile = blockIdx.y;
+  if (m_tile * kBM >= M) return;  // uniform early exit before any allocation
+  const int n0 = blockIdx.x * bn;
+
+  uint8_t* smem = smem_dyn + ((1024 - (smem_u32(smem_dyn) & 1023)) & 1023);
+  uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + SmemLayout::bar_off);
+  uint64_t* full_b = full_a + kStages;
+  uint64_t* empty = full_b + kStages;
+  uint64_t* acc_full = empty + kStages;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SmemLayout::misc_off);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SmemLayout::misc_off + 4);
+  int64_t* koff = reinterpret_cast<int64_t*>(smem + SmemLayout::koff_off);
+
+  const int num_kb = g.num_kb;
+  if (tid == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(&full_a[s], kBM);
+      mbar_init(&full_b[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    mbar_init(acc_full, 1);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == 5 && lane == 0) tma_prefetch_desc(&wmap);
+  for (int i = tid; i < num_kb * 8; i += kThreads) koff[i] = k_offset(g, i * 8);
+  const uint32_t tmem_cols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
+  if (warp == 4) {
+    tmem_alloc(tmem_slot, tmem_cols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const uint32_t a_smem = smem_u32(smem + SmemLayout::a_off);
+  const uint32_t b_smem = smem_u32(smem + SmemLayout::b_off);
+  bool aborted = false;
+
+  if (warp < 4) {
+    // ---------------- gather producers ----------------
+    const int m = tid;  // tile row
+    const int gm = m_tile * kBM + m;
+    bool valid = false;
+    int64_t base = 0;
+    int4 c = make_int4(-1, -1, -1, -1);
+    if (gm < M) {
+      c = coords[gm];
+      base = row_base_offset(g, c, valid);
+    }
+    const T* src_row = video + base;
+    const uint32_t row_off = (uint32_t)((m >> 3) * 1024 + (m & 7) * 128);
+    const uint32_t sw = (uint32_t)(m & 7);
+    for (int kb = 0; kb < num_kb; ++kb) {
+      const int s = kb % kStages;
+      const uint32_t par = ((kb / kStages) & 1) ^ 1;
+      if (!mbar_wait_bounded(&empty[s], par, abort_flag, kWaitLimitNs)) {
+        aborted = true;
+        break;
+      }
+      if (valid) {
+        const uint32_t dst = a_smem + s * kAStageBytes + row_off;
+        const int64_t* ko = koff + kb * 8;
+#pragma unroll
+        for (int j = 0; j < 8; ++j) cp_async_16(dst + ((j ^ sw) << 4), src_row + ko[j]);
+      }
+      cp_async_commit();
+      if (kb >= kLag) {
+        cp_async_wait_group<kLag>();
+        fence_proxy_async_smem();
+        mbar_arrive(&full_a[(kb - kLag) % kStages]);
+      }
+    }
+    cp_async_wait_all();
+    if (!aborted) {
+      fence_proxy_async_smem();
+      for (int kb = max(0, num_kb - kLag); kb < num_kb; ++kb) mbar_arrive(&full_a[kb % kStages]);
+    }
+
+    // ---------------- epilogue ----------------
+    // tcgen05.ld is warp-collective: decide per warp.
+    aborted = __any_sync(0xffffffffu, aborted);
+    if (!aborted && !mbar_wait_bounded(acc_full, 0, abort_flag, kWaitLimitNs)) aborted = true;
+    aborted = __any_sync(0xffffffffu, aborted);
+    if (!aborted) {
+      tc_fence_after();
+      const uint32_t taddr = tmem_base + ((uint32_t)(warp * 32) << 16);
+      bool meta_valid = false;
+      char* dst_row = nullptr;
+      const int ce = ep.out_elem_bytes;
+      if (gm < M) {
+        if (ep.mode == kEpiloguePlain) {
+          dst_row = static_cast<char*>(ep.out) + (int64_t)gm * ep.ldo * ce;
+        } else if (valid) {
+          const int64_t idx = ((int64_t)c.y * g.gh + c.z) * g.gw + c.w;
+          const int64_t slot = (int64_t)c.x * ep.dense_tokens + idx;
+          dst_row = static_cast<char*>(ep.out) + slot * ep.ldo * ce;
+          meta_valid = blockIdx.x == 0;
+          if (meta_valid) {
+            if (ep.observed) ep.observed[slot] = 1.0f;
+            if (ep.age) ep.age[slot] = 0.0f;
+          }
+        }
+      }
+      for (int c0 = 0; c0 < bn; c0 += 32) {
+        uint32_t r[32];
+        tmem_ld_32x32b_x32(taddr + (uint32_t)c0, r);
+        tmem_ld_wait();
+        if (!dst_row) continue;
+        const int col0 = n0 + c0;
+        const int ncol = min(32, min(bn - c0, g.D - col0));
+        if (ncol <= 0) continue;
+        float v[32];
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          float b = (ep.bias && j < ncol) ? __ldg(ep.bias + col0 + j) : 0.0f;
+          v[j] = valid ? __uint_as_float(r[j]) + b : 0.0f;
+        }
+        char* dst = dst_row + (int64_t)col0 * ce;
+        const bool vec = ncol == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
+        if (ep.out_dtype == BJF_DTYPE_F32) {
+          float* o = reinterpret_cast<float*>(dst);
+          if (vec) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              float w8[8] = {v[j], v[j + 1], v[j + 2], v[j + 3], v[j + 4], v[j + 5], v[j + 6], v[j + 7]};
+              store8<float>(o + j, w8);
+            }
+          } else {
+            for (int j = 0; j < ncol; ++j) o[j] = v[j];
+          }
+        } else if (ep.out_dtype == BJF_DTYPE_F16) {
+          __half* o = reinterpret_cast<__half*>(dst);
+          if (vec) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              float w8[8] = {v[j], v[j + 1], v[j + 2], v[j + 3], v[j + 4], v[j + 5], v[j + 6], v[j + 7]};
+              store8<__half>(o + j, w8);
+            }
+          } else {
+            for (int j = 0; j < ncol; ++j) o[j] = __float2half_rn(v[j]);
+          }
+        } else {
+          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(dst);
+          if (vec) {
+#pragma unroll
+            for (int j = 0; j < 32; j += 8) {
+              float w8[8] = {v[j], v[j + 1], v[j + 2], v[j + 3], v[j + 4], v[j + 5], v[j + 6], v[j + 7]};
+              store8<__nv_bfloat16>(o + j, w8);
+            }
+          } else {
+            for (int j = 0; j < ncol; ++j) o[j] = __float2bfloat16_rn(v[j]);
+          }
+        }
+      }
+    }
+  } else if (warp == 4) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16_f32(g.is_bf16 ? 1u : 0u, kBM, (uint32_t)bn);
+      int issued = 0;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % kStages;
+        const uint32_t par = (kb / kStages) & 1;
+        if (!mbar_wait_bounded(&full_a[s], par, abort_flag, kWaitLimitNs) ||
+            !mbar_wait_bounded(&full_b[s], par, abort_flag, kWaitLimitNs)) {
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t a_base = a_smem + s * kAStageBytes;
+        const uint32_t b_base = b_smem + s * kBStageBytes;
+#pragma unroll
+        for (int kk = 0; kk < kBK / 16; ++kk) {
+          mma_f16_ss(tmem_base, smem_desc_sw128_kmajor(a_base + kk * 32),
+                     smem_desc_sw128_kmajor(b_base + kk * 32), idesc, (kb | kk) != 0);
+        }
+        ++issued;
+        mma_commit(&empty[s]);
+      }
+      mma_commit(acc_full);
+      if (aborted && issued > 0) {
+        // Let the issued MMAs retire before TMEM is freed (bounded, abort ignored).
+        int zero = 0;
+        mbar_wait_bounded(acc_full, 0, &zero, kWaitLimitNs);
+      }
+    }
+  } else {
+    // ---------------- TMA producer (weight) ----------------
+    if (lane == 0) {
+      int issued = 0;
+      for (int kb = 0; kb < num_kb; ++kb) {
+        const int s = kb % kStages;
+        const uint32_t par = ((kb / kStages) & 1) ^ 1;
+        if (!mbar_wait_bounded(&empty[s], par, abort_flag, kWaitLimitNs)) {
+          aborted = true;
+          break;
+        }
+        mbar_arrive_expect_tx(&full_b[s], (uint32_t)(bn * kBK * 2));
+        tma_load_2d(b_smem + s * kBStageBytes, &wmap, kb * kBK, n0, &full_b[s]);
+        ++issued;
+      }
+      if (aborted) {
+        // Wait for the weight tiles still in flight before the CTA's smem goes away.
+        int zero = 0;
+        for (int kb = max(0, issued - kStages); kb < issued; ++kb)
+          mbar_wait_bounded(&full_b[kb % kStages], (kb / kStages) & 1, &zero, kWaitLimitNs);
+      }
+    }
+  }
+
+  if (aborted) {
+    *abort_flag = 1;
+    atomicExch(error_flag, 1);
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 4) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, tmem_cols);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// SIMT path
+// ---------------------------------------------------------------------------
+constexpr int kSBM = 64, kSBN = 64, kSBK = 32, kSThreads = 256;
+
+template <typename TIn, typename TW>
+__global__ void __launch_bounds__(kSThreads)
+    gather_gemm_simt_kernel(const TIn* __restrict__ video, const int4* __restrict__ coords,
+                            const int32_t* __restrict__ rows_dev, int rows_cap, GatherGeometry g,
+                            const TW* __restrict__ weight, EpilogueArgs ep) {
+  __shared__ float As[kSBK][kSBM + 4];
+  __shared__ float Ws[kSBK][kSBN + 4];
+  __shared__ int64_t row_base[kSBM];
+  __shared__ int row_valid[kSBM];
+  __shared__ int64_t koffs[kSBK];
+
+  int M = rows_cap;
+  if (rows_dev) M = min(M, max(0, __ldg(rows_dev)));
+  const int m0 = blockIdx.y * kSBM;
+  if (m0 >= M) return;
+  const int n0 = blockIdx.x * kSBN;
+  const int tid = threadIdx.x;
+  const int tx = tid % 16, ty = tid / 16;
+
+  if (tid < kSBM) {
+    const int gm = m0 + tid;
+    bool valid = false;
+    int64_t base = 0;
+    if (gm < M) base = row_base_offset(g, coords[gm], valid);
+    row_base[tid] = base;
+    row_valid[tid] = valid;
+  }
+  float acc[4][4] = {};
+  for (int k0 = 0; k0 < g.K; k0 += kSBK) {
+    __syncthreads();
+    if (tid < kSBK) koffs[tid] = (k0 + tid < g.K) ? k_offset(g, k0 + tid) : 0;
+    __syncthreads();
+    for (int e = tid; e < kSBM * kSBK; e += kSThreads) {
+      const int m = e / kSBK, k = e % kSBK;
+      float v = 0.0f;
+      if (row_valid[m] && k0 + k < g.K) v = to_f32<TIn>(video[row_base[m] + koffs[k]]);
+      As[k][m] = v;
+    }
+    for (int e = tid; e < kSBN * kSBK; e += kSThreads) {
+      const int n = e / kSBK, k = e % kSBK;
+      float v = 0.0f;
+      if (n0 + n < g.D && k0 + k < g.K) v = to_f32<TW>(weight[(int64_t)(n0 + n) * g.K + k0 + k]);
+      Ws[k][n] = v;
+    }
+    __syncthreads();
+#pragma unroll 8
+    for (int k = 0; k < kSBK; ++k) {
+      float a[4], b[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) a[i] = As[k][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) b[j] = Ws[k][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(a[i], b[j], acc[i][j]);
+    }
+  }
+  const int ce = ep.out_elem_bytes;
+  for (int i = 0; i < 4; ++i) {
+    const int m = ty * 4 + i;
+    const int gm = m0 + m;
+    if (gm >= M) continue;
+    const bool valid = row_valid[m];
+    char* dst_row = nullptr;
+    if (ep.mode == kEpiloguePlain) {
+      dst_row = static_cast<char*>(ep.out) + (int64_t)gm * ep.ldo * ce;
+    } else if (valid) {
+      int4 c = coords[gm];
+      const int64_t slot = (int64_t)c.x * ep.dense_tokens + ((int64_t)c.y * g.gh + c.z) * g.gw + c.w;
+      dst_row = static_cast<char*>(ep.out) + slot * ep.ldo * ce;
+      if (blockIdx.x == 0 && tx == 0) {
+        if (ep.observed) ep.observed[slot] = 1.0f;
+        if (ep.age) ep.age[slot] = 0.0f;
+      }
+    }
+    if (!dst_row) continue;
+    for (int j = 0; j < 4; ++j) {
+      const int col = n0 + tx * 4 + j;
+      if (col >= g.D) continue;
+      float v = valid ? acc[i][j] + (ep.bias ? ep.bias[col] : 0.0f) : 0.0f;
+      if (ep.out_dtype == BJF_DTYPE_F32)
+        reinterpret_cast<float*>(dst_row)[col] = v;
+      else if (ep.out_dtype == BJF_DTYPE_F16)
+        reinterpret_cast<__half*>(dst_row)[col] = __float2half_rn(v);
+      else
+        reinterpret_cast<__nv_bfloat16*>(dst_row)[col] = __float2bfloat16_rn(v);
+    }
+  }
+}
+
+int choose_bn(int D) {
+  if (D <= kMaxBN) return (D + 15) / 16 * 16;
+  for (int bn = kMaxBN; bn >= 128; bn -= 16)
+    if (D % bn == 0) return bn;
+  return kMaxBN;
+}
+
+std::mutex g_attr_mu;
+bool g_attr_set[64][2] = {};
+
+}  // namespace
+
+bool sm100_path_supported(const DeviceInfo& dev, const GatherGeometry& g, int32_t in_dt, int32_t w_dt,
+                          const void* input, const void* weight) {
+  if (dev.cc_major != 10) return false;
+  if (in_dt != w_dt || (in_dt != BJF_DTYPE_F16 && in_dt != BJF_DTYPE_BF16)) return false;
+  if (g.pw % 8 != 0 || g.W % 8 != 0) return false;
+  if (g.K % kBK != 0 || g.K / kBK > kMaxKBlocks) return false;
+  if (reinterpret_cast<uintptr_t>(input) % 16 != 0 || reinterpret_cast<uintptr_t>(weight) % 16 != 0)
+    return false;
+  if (dev.max_smem_optin < (size_t)SmemLayout::alloc) return false;
+  return true;
+}
+
+bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t in_dt,
+                              const void* weight, int32_t w_dt, const GatherGeometry& g0,
+                              const int4* coords, const int32_t* rows_dev, int64_t rows_cap,
+                              const EpilogueArgs& ep, cudaStream_t st) {
+  if (rows_cap <= 0 || g0.D <= 0) return BJF_OK;
+  GatherGeometry g = g0;
+  g.num_kb = g.K / kBK;
+  g.is_bf16 = in_dt == BJF_DTYPE_BF16;
+  if (sm100_path_supported(dev, g, in_dt, w_dt, input, weight)) {
+    EncodeTiledFn encode = nullptr;
+    bjf_status rc = encode_tiled_fn(&encode);
+    if (rc) return rc;
+    const int bn = choose_bn(g.D);
+    CUtensorMap map;
+    cuuint64_t dims[2] = {(cuuint64_t)g.K, (cuuint64_t)g.D};
+    cuuint64_t strides[1] = {(cuuint64_t)g.K * 2};
+    cuuint32_t box[2] = {(cuuint32_t)kBK, (cuuint32_t)bn};
+    cuuint32_t estr[2] = {1, 1};
+    CUresult cr = encode(&map, g.is_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16,
+                         2, const_cast<void*>(weight), dims, strides, box, estr,
+                         CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                         CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (cr != CUDA_SUCCESS)
+      return fail(BJF_ERR_CUDA, "cuTensorMapEncodeTiled(weight) failed with code " + std::to_string((int)cr));
+    const int slot = g.is_bf16 ? 1 : 0;
+    {
+      std::lock_guard<std::mutex> lock(g_attr_mu);
+      if (!g_attr_set[dev.device][slot]) {
+        cudaError_t e = g.is_bf16
+                            ? cudaFuncSetAttribute(gather_gemm_sm100_kernel<__nv_bfloat16>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::alloc)
+                            : cudaFuncSetAttribute(gather_gemm_sm100_kernel<__half>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::alloc);
+        if (e != cudaSuccess) return cuda_status(e, "gather-GEMM smem attribute");
+        g_attr_set[dev.device][slot] = true;
+      }
+    }
+    dim3 grid((unsigned)ceil_div(g.D, bn), (unsigned)ceil_div(rows_cap, kBM));
+    if (g.is_bf16)
+      gather_gemm_sm100_kernel<__nv_bfloat16><<<grid, kThreads, SmemLayout::alloc, st>>>(
+          map, static_cast<const __nv_bfloat16*>(input), coords, rows_dev, (int)rows_cap, g, bn, ep,
+          dev.error_flag);
+    else
+      gather_gemm_sm100_kernel<__half><<<grid, kThreads, SmemLayout::alloc, st>>>(
+          map, static_cast<const __half*>(input), coords, rows_dev, (int)rows_cap, g, bn, ep, dev.error_flag);
+    return check_launch("gather-GEMM (tcgen05) launch");
+  }
+  dim3 grid((unsigned)ceil_div(g.D, kSBN), (unsigned)ceil_div(rows_cap, kSBM));
+  bool ok = dispatch_float(in_dt, [&](auto itag) {
+    dispatch_float(w_dt, [&](auto wtag) {
+      gather_gemm_simt_kernel<decltype(itag), decltype(wtag)><<<grid, kSThreads, 0, st>>>(
+          static_cast<const decltype(itag)*>(input), coords, rows_dev, (int)rows_cap, g,
+          static_cast<const decltype(wtag)*>(weight), ep);
+    });
+  });
+  if (!ok) return fail(BJF_ERR_INVALID_ARGUMENT, "input dtype must be f32, f16 or bf16");
+  return check_launch("gather-GEMM (SIMT) launch");
+}
+
+}  // namespace bjf
+
+using namespace bjf;
+
+extern "C" bjf_status bjf_sparse_patchify3d_forward(const bjf_patchify_config* cfg, const void* input,
+                                                    bjf_dtype input_dtype, const int64_t id[5],
+                                                    const int32_t* coords, int64_t rows,
+                                                    const void* weight, bjf_dtype weight_dtype,
+                                                    const int64_t wd[5], const float* bias, void* out,
+                                                    bjf_dtype out_dtype, bjf_stream_t stream) {
+  if (!cfg || !id || !wd) return fail(BJF_ERR_INVALID_ARGUMENT, "config and dims must not be null");
+  const int64_t vals[8] = {cfg->in_channels, cfg->out_channels, cfg->frames, cfg->height,
+                           cfg->width, cfg->tubelet_size, cfg->patch_h, cfg->patch_w};
+  for (int64_t v : vals)
+    if (v <= 0 || v > (1 << 30)) return fail(BJF_ERR_INVALID_ARGUMENT, "sparse patchify config fields must be positive");
+  if (id[0] <= 0) return fail(BJF_ERR_INVALID_ARGUMENT, "sparse patchify batch must be nonzero");
+  if (id[1] != cfg->in_channels || id[2] != cfg->frames || id[3] != cfg->height || id[4] != cfg->width)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "sparse patchify input dims " + dims_str(id, 5) +
+                                              " do not match the config");
+  if (wd[0] != cfg->out_channels || wd[1] != cfg->in_channels || wd[2] != cfg->tubelet_size ||
+      wd[3] != cfg->patch_h || wd[4] != cfg->patch_w)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "sparse patchify weight dims " + dims_str(wd, 5) +
+                                              " do not match the config");
+  if (cfg->frames % cfg->tubelet_size || cfg->height % cfg->patch_h || cfg->width % cfg->patch_w)
+    return fail(BJF_ERR_INVALID_ARGUMENT,
+                "sparse patchify input frames/height/width must be divisible by the tubelet and patch sizes");
+  if (rows < 0) return fail(BJF_ERR_INVALID_ARGUMENT, "sparse patchify rows must be non-negative");
+  if (rows > INT32_MAX) return fail(BJF_ERR_UNSUPPORTED, "sparse patchify supports up to 2^31-1 rows");
+  const int64_t K = cfg->in_channels * cfg->tubelet_size * cfg->patch_h * cfg->patch_w;
+  if (K > (1 << 24) || cfg->out_channels > (1 << 24)) return fail(BJF_ERR_UNSUPPORTED, "sparse patchify K or D too large");
+  if (dtype_size(out_dtype) == 0 || out_dtype == BJF_DTYPE_I32)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "output dtype must be f32, f16 or bf16");
+  if (rows == 0) return BJF_OK;
+  if (!input || !coords || !weight || !out) return fail(BJF_ERR_INVALID_ARGUMENT, "buffers must not be null");
+  if (reinterpret_cast<uintptr_t>(coords) % 16) return fail(BJF_ERR_INVALID_ARGUMENT, "coords must be 16-byte aligned");
+  const DeviceInfo* dev = nullptr;
+  bjf_status rc = current_device(&dev);
+  if (rc) return rc;
+  GatherGeometry g{};
+  g.C = (int)cfg->in_channels;
+  g.T = (int)cfg->frames;
+  g.H = (int)cfg->height;
+  g.W = (int)cfg->width;
+  g.kt = (int)cfg->tubelet_size;
+  g.ph = (int)cfg->patch_h;
+  g.pw = (int)cfg->patch_w;
+  g.batch = (int)std::min<int64_t>(id[0], INT32_MAX);
+  g.depth = g.T / g.kt;
+  g.gh = g.H / g.ph;
+  g.gw = g.W / g.pw;
+  g.K = (int)K;
+  g.D = (int)cfg->out_channels;
+  EpilogueArgs ep{};
+  ep.mode = kEpiloguePlain;
+  ep.out = out;
+  ep.out_dtype = out_dtype;
+  ep.out_elem_bytes = (int)dtype_size(out_dtype);
+  ep.ldo = g.D;
+  ep.bias = bias;
+  return launch_gather_gemm(*dev, input, input_dtype, weight, weight_dtype, g,
+                            reinterpret_cast<const int4*>(coords), nullptr, rows, ep, as_cuda(stream));
+}

@@ -1,0 +1,51 @@
+// gather_gemm.hpp -- internal interface of the sparse-patchify gather-GEMM.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/bjf.h"
+#include "runtime.hpp"
+
+namespace bjf {
+
+// Input video and token-grid geometry of one sparse patchify call.
+struct GatherGeometry {
+  int C, T, H, W;      // channels, frames, height, width of each batch element
+  int kt, ph, pw;      // tubelet and patch sizes
+  int batch;           // batch elements in the input
+  int depth, gh, gw;   // token grid
+  int K, D;            // C*kt*ph*pw and output channels
+  int num_kb;          // K / 64 (tensor-core path)
+  int is_bf16;
+};
+
+enum { kEpiloguePlain = 0, kEpilogueScatter = 1 };
+
+// Where the projected rows go.
+//  plain:   out[m, :] with row stride ldo elements
+//  scatter: out[(b * dense_tokens + token_index(t, r, col)), :] with row stride ldo, plus
+//           observed[slot] = 1, age[slot] = 0 (a fused token-cache write)
+struct EpilogueArgs {
+  void* out;
+  int32_t out_dtype;
+  int out_elem_bytes;
+  int64_t ldo;
+  int mode;
+  int64_t dense_tokens;
+  float* observed;
+  float* age;
+  const float* bias;
+};
+
+// Enqueues out = gather(input, coords) x weight^T + bias.  `rows_dev` (device,
+// nullable) caps the row count at run time; `rows_cap` bounds the grid.
+bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t in_dt,
+                              const void* weight, int32_t w_dt, const GatherGeometry& g,
+                              const int4* coords, const int32_t* rows_dev, int64_t rows_cap,
+                              const EpilogueArgs& ep, cudaStream_t st);
+
+bool sm100_path_supported(const DeviceInfo& dev, const GatherGeometry& g, int32_t in_dt,
+                          int32_t w_dt, const void* input, const void* weight);
+
+}  // namespace bjf

@@ -1,0 +1,35 @@
+// patch_diff.hpp -- internal interface of the patch-diff mask kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/bjf.h"
+
+namespace bjf {
+
+struct SelectParams {
+  float threshold;
+  int cap;          // threshold-phase cap (grid.len() with allow_full_context)
+  int fill_target;  // context_tokens (fill_to_context_tokens) or min_context_tokens
+  int dilation;
+  int depth, gh, gw, n;
+  // Optional token-cache aging fused into the selection launch (one CTA per stream):
+  // age[s, :] += observed[s, :] (the first half of the AssignLatest update,
+  // src/sparse_feature_memory.rs:46-52).  Null when not requested.
+  float* age;
+  const float* observed;
+};
+
+// Resolves the reference's context budget arithmetic (src/nodes.rs:463-498, 516-520).
+bjf_status resolve_select(const bjf_patch_diff_config* cfg, const int64_t* grid, SelectParams& p);
+
+// One CTA per stream: selection (and optional aging) -> indices [streams, n], counts [streams].
+bjf_status launch_select(const float* scores, int64_t streams, const SelectParams& p, int32_t* indices,
+                         int32_t* counts, cudaStream_t st);
+
+// Per-tubelet mean |delta| scores for `streams` videos [B, C, T, H, W] -> [streams, N].
+bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* video_dims, int64_t streams,
+                         int64_t tubelet_size, int64_t patch_size, float* scores, cudaStream_t st);
+
+}  // namespace bjf

@@ -1,0 +1,243 @@
+/*
+ * bjf.h -- C ABI of the B200 (sm_100a) sparse front end for burn_jepa.
+ *
+ * The three steps of burn_jepa's sparse video front end, as stateless C entry
+ * points over caller-owned device memory:
+ *
+ *   1. patch-diff mask   per-tubelet mean |frame delta| -> threshold policy ->
+ *                        ascending active token indices
+ *   2. sparse patchify   gather the active kt x ph x pw tubelets and project them
+ *                        through the Conv3d patch-embed weight (+ bias)
+ *   3. token-cache write scatter the new token features into the persistent
+ *                        [B, N, D] token cache and update observed / age metadata
+ *
+ * Each entry point names the reference (mosure/burn_jepa 0.21.0) interface it
+ * replaces.  Conventions shared by every function:
+ *   - All pointers are device pointers unless the parameter says "host".
+ *   - Work is enqueued on `stream` (NULL = legacy default stream); nothing
+ *     synchronises the host.  Inputs must stay valid until the work completes.
+ *   - Return value: 0 = success; negative = invalid argument (nothing was
+ *     launched; the message is available from bjf_get_last_error_string on the
+ *     calling thread); positive = CUDA launch/runtime error.
+ *   - Shapes are passed as the tensor dims the caller already holds (Rust:
+ *     `tensor.dims()`), so the library can return the reference's own shape
+ *     error messages.  Tensors are contiguous row-major.
+ *   - Token indices and coordinates are int32 (the reference's Int element on
+ *     the Cuda<f32, i32> backend).
+ *   - Functions are thread-safe; per-device state is created lazily.
+ */
+#ifndef BJF_H
+#define BJF_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define BJF_ABI_VERSION 1
+
+#if defined(__GNUC__)
+#define BJF_API __attribute__((visibility("default")))
+#else
+#define BJF_API
+#endif
+
+/* cudaStream_t without pulling in the CUDA headers. */
+typedef struct CUstream_st* bjf_stream_t;
+
+typedef int32_t bjf_status;
+enum {
+  BJF_OK = 0,
+  BJF_ERR_INVALID_ARGUMENT = -1, /* shape / value error (message set) */
+  BJF_ERR_UNSUPPORTED = -2,      /* valid request this build does not serve (message set) */
+  BJF_ERR_CUDA = 1               /* CUDA error (message set) */
+};
+
+typedef enum bjf_dtype {
+  BJF_DTYPE_F32 = 0,
+  BJF_DTYPE_F16 = 1,
+  BJF_DTYPE_BF16 = 2,
+  BJF_DTYPE_I32 = 3
+} bjf_dtype;
+
+/* burn_flex_gmm::SparsePatchify3dConfig (fields as the reference fills them,
+ * src/model.rs:1297-1306).  All fields must be positive. */
+typedef struct bjf_patchify_config {
+  int64_t in_channels;
+  int64_t out_channels;
+  int64_t frames;
+  int64_t height;
+  int64_t width;
+  int64_t tubelet_size;
+  int64_t patch_h;
+  int64_t patch_w;
+} bjf_patchify_config;
+
+/* SparseJepaPatchDiffSparsityConfig (src/nodes.rs:97-157). */
+typedef struct bjf_patch_diff_config {
+  float threshold;            /* finite, >= 0 */
+  int64_t context_tokens;     /* cap (or budget) on selected tokens */
+  int64_t target_tokens;      /* carried for parity; the mask does not use it */
+  int64_t dilation;           /* spatial dilation radius in tokens */
+  int64_t min_context_tokens; /* adaptive fill target */
+  int32_t fill_to_context_tokens;
+  int32_t allow_full_context;
+} bjf_patch_diff_config;
+
+/* ABI version of the loaded library (BJF_ABI_VERSION it was built with). */
+BJF_API int32_t bjf_abi_version(void);
+
+/* Copies the message of the last failing call made on this thread into `buf`
+ * (NUL-terminated, truncated to `len`).  Returns the length of the full message. */
+BJF_API size_t bjf_get_last_error_string(char* buf, size_t len);
+
+/* Synchronises `stream` and reports whether any kernel of this library on the
+ * current device gave up on a bounded wait since the last check (*flag_out = 1;
+ * the flag is then cleared).  Kernels never spin forever: a pipeline wait that
+ * exceeds its time limit records this flag, releases its resources and returns. */
+BJF_API bjf_status bjf_device_error_check(bjf_stream_t stream, int32_t* flag_out);
+
+/* ------------------------------------------------------------------------
+ * Step 1: patch-diff mask
+ * ---------------------------------------------------------------------- */
+
+/* Replaces `patch_diff_token_scores` (src/nodes.rs:565-619, frame pairs :621-631).
+ * video: `streams` independent videos, each [B, C, T, H, W] (dims in video_dims),
+ * stored back to back.  scores: [streams, N] f32, N = T/kt * H/P * W/P.  Within a
+ * video the batch is summed into one score map, as in the reference. */
+BJF_API bjf_status bjf_patch_diff_token_scores(const void* video, bjf_dtype video_dtype,
+                                       const int64_t video_dims[5], int64_t streams,
+                                       int64_t tubelet_size, int64_t patch_size, float* scores,
+                                       bjf_stream_t stream);
+
+/* Replaces `patch_diff_context_mask_from_scores` (src/nodes.rs:458-537) and the
+ * top-k fast path `patch_diff_topk_context_mask` (:548-563): the selection runs on
+ * the device, with no host sort.  scores: [streams, N] for grid (depth, height,
+ * width).  Writes each stream's mask as ascending unique int32 token indices into
+ * indices[s * N ...] and its length into counts[s] (device).  Grids up to 32768
+ * tokens (16384 with dilation > 0). */
+BJF_API bjf_status bjf_patch_diff_context_mask_from_scores(const float* scores, int64_t streams,
+                                                   const int64_t grid[3],
+                                                   const bjf_patch_diff_config* config,
+                                                   int32_t* indices, int32_t* counts,
+                                                   bjf_stream_t stream);
+
+/* Replaces `patch_diff_context_mask_from_video` (src/nodes.rs:539-546 -> 411-456):
+ * scores then selection.  `grid` must equal the grid of the video shape.  scores
+ * ([streams, N] f32) is required: it holds the per-tubelet scores on return. */
+BJF_API bjf_status bjf_patch_diff_context_mask(const void* video, bjf_dtype video_dtype,
+                                       const int64_t video_dims[5], int64_t streams,
+                                       int64_t tubelet_size, int64_t patch_size,
+                                       const int64_t grid[3], const bjf_patch_diff_config* config,
+                                       float* scores, int32_t* indices, int32_t* counts,
+                                       bjf_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Plans
+ * ---------------------------------------------------------------------- */
+
+/* Device-resident `SparsePatchifyPlan::new` / `SparsePatchifyBatchPlan::new`
+ * (src/sparse_patchify.rs:236-269, 290-330): token indices -> coords rows
+ * (batch, tubelet, row, col), batch-major then mask order.
+ * indices: [mask_rows, index_stride] int32; counts: [mask_rows] int32 device
+ * lengths, or NULL when every row holds exactly `index_stride` indices.
+ * mask_rows == 1: the one mask is repeated for every batch element (uniform plan);
+ * mask_rows == batch: row b uses mask row b (batch plan; rows may differ in length,
+ * they are concatenated).  coords: [coords_capacity, 4] int32.
+ * total_rows (device, nullable) receives the number of rows written. */
+BJF_API bjf_status bjf_sparse_patchify_plan_coords(const int32_t* indices, int64_t index_stride,
+                                           const int32_t* counts, int64_t mask_rows,
+                                           int64_t batch, const int64_t grid[3], int32_t* coords,
+                                           int64_t coords_capacity, int32_t* total_rows,
+                                           bjf_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Step 2: sparse patchify (gather-GEMM)
+ * ---------------------------------------------------------------------- */
+
+/* Replaces `burn_flex_gmm::cuda::sparse_patchify3d_forward_cuda` (burn_flex_gmm
+ * 0.21.2, called at src/model.rs:1140, 1197, 1319 and src/sparse_patchify.rs:184):
+ *   out[m, d] = bias[d] + sum_k W[d, k] * x[b, c, t*kt+dt, r*ph+dy, col*pw+dx]
+ * with (b, t, r, col) = coords[m], k = ((c*kt + dt)*ph + dy)*pw + dx: Conv3d with
+ * stride = kernel evaluated at the selected tubelets.
+ * input: [B, C, T, H, W] (dims in input_dims); weight: [D, C, kt, ph, pw];
+ * bias: [D] f32 or NULL (zeros, as the reference substitutes at src/model.rs:1307-1318);
+ * out: [rows, D].  f16/bf16 input and weight (same dtype) run on the tcgen05 tensor
+ * cores with f32 accumulation; f32 runs in f32.  Rows whose coords lie outside
+ * the input are written as zeros. */
+BJF_API bjf_status bjf_sparse_patchify3d_forward(const bjf_patchify_config* config, const void* input,
+                                         bjf_dtype input_dtype, const int64_t input_dims[5],
+                                         const int32_t* coords, int64_t rows, const void* weight,
+                                         bjf_dtype weight_dtype, const int64_t weight_dims[5],
+                                         const float* bias, void* out, bjf_dtype out_dtype,
+                                         bjf_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Step 3: token-cache write
+ * ---------------------------------------------------------------------- */
+
+/* Replaces `sparse_feature_memory_assign_latest_cuda_raw`
+ * (src/sparse_feature_memory.rs:296-313 -> 110-267), the kernels behind
+ * `InterframeJepaFeatureMemory::update_tokens_tiled_assign_cuda(_raw)`
+ * (src/feature_memory.rs:586-645).  In place:
+ *   if age_observed: age_frames += observed          (every slot)
+ *   features[b, idx[b,s], :] = tokens[b, s, :]; observed = 1; age_frames = 0
+ * Indices < 0 or >= N are skipped.  features: [B, N, D] (f32/f16/bf16);
+ * observed, age_frames: [B, N] f32; tokens: [B, S, D]; token_indices: [B, S] int32.
+ * Shape errors return the reference's messages (:127-178).  Duplicate indices in a
+ * row race (as in the reference's kernel); masks from SparseTokenMask are unique. */
+BJF_API bjf_status bjf_feature_memory_assign_latest(void* features, bjf_dtype features_dtype,
+                                            const int64_t features_dims[3], float* observed,
+                                            const int64_t observed_dims[2], float* age_frames,
+                                            const int64_t age_dims[2], const void* tokens,
+                                            bjf_dtype tokens_dtype, const int64_t tokens_dims[3],
+                                            const int32_t* token_indices,
+                                            const int64_t indices_dims[2], int32_t age_observed,
+                                            bjf_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Fused step: mask -> plan -> patchify -> cache write, for S independent streams
+ * ---------------------------------------------------------------------- */
+
+/* One video stream per index s: video [S, C, T, H, W] (batch 1 each), token caches
+ * [S, N, D], observed / age [S, N] f32, N = T/kt * H/P * W/P. */
+typedef struct bjf_front_end_desc {
+  int64_t streams;
+  int64_t channels;
+  int64_t frames;
+  int64_t height;
+  int64_t width;
+  int64_t tubelet_size;
+  int64_t patch_size;
+  int64_t embed_dim;
+  bjf_dtype video_dtype;  /* f16 / bf16 run the tcgen05 path; f32 runs SIMT */
+  bjf_dtype weight_dtype; /* same as video_dtype for the tensor-core path */
+  bjf_dtype cache_dtype;  /* f32 / f16 / bf16 */
+  bjf_patch_diff_config mask;
+} bjf_front_end_desc;
+
+/* Bytes of device workspace bjf_front_end_step needs (0 for an invalid descriptor). */
+BJF_API size_t bjf_front_end_workspace_bytes(const bjf_front_end_desc* desc);
+
+/* One frame step of the front end for every stream, the per-stream composition of
+ * patch_diff_context_mask (src/nodes.rs:411-456) -> SparsePatchifyPlan::new
+ * (src/sparse_patchify.rs:236-269) -> sparse_patchify3d_forward_cuda (src/model.rs:1273-1328)
+ * -> InterframeJepaFeatureMemory::update_tokens_tiled_assign_cuda_raw
+ * (src/feature_memory.rs:616-645), with the patch-embed features written straight into
+ * each stream's token cache.  age_observed: the memory has stepped before (step > 0).
+ * weight [D, C, kt, P, P]; bias [D] f32 or NULL.  workspace: 256-byte aligned device
+ * memory of bjf_front_end_workspace_bytes(desc) bytes.  counts_out (device, nullable):
+ * [S] int32 active tubelets per stream. */
+BJF_API bjf_status bjf_front_end_step(const bjf_front_end_desc* desc, const void* video,
+                                      const void* weight, const float* bias, void* caches,
+                                      float* observed, float* age_frames, int32_t age_observed,
+                                      void* workspace, size_t workspace_bytes, int32_t* counts_out,
+                                      bjf_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* BJF_H */

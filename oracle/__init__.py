@@ -1,0 +1,362 @@
+"""CPU oracle for the burn_jepa sparse front end -- TEST INFRASTRUCTURE ONLY.
+
+A numpy/ctypes face over ``oracle/bjf_oracle.c``, the plain-C restatement of the
+reference algorithm (mosure/burn_jepa 0.21.0).  Only ``tests/``,
+``__graft_entry__.smoke()`` and the CPU-baseline leg of ``bench.py`` may import it,
+and only as the checker or the timed CPU baseline; the product never calls it.
+
+Each wrapper names the reference file:line that the C function restates.  The
+restatement is pinned by the known-answer vectors of the reference's own tests
+(``tests/golden/reference_known_answers.json``) and, for the Conv3d arithmetic that
+lives in the un-vendored crate burn_flex_gmm 0.21.2, by torch ``F.conv3d`` fixtures
+(``tests/golden/conv3d_tiny.npz``).
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+import subprocess
+from dataclasses import dataclass
+
+import numpy as np
+
+_HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB_PATH = os.path.join(_HERE, "_build", "libbjf_oracle.so")
+
+_ERRORS = {
+    -1: "dense token count must be nonzero",
+    -2: "sparse token index outside dense token range",
+    -3: "patch-diff sparsity threshold must be finite and non-negative",
+    -4: "patch-diff sparsity received unexpected score length",
+    -5: "sparse JEPA mode requires at least two dense tokens",
+    -6: "patch-diff sparsity requires frames/height/width divisible by tubelet and patch sizes",
+    -7: "patch-diff sparsity grid must match the video shape",
+    -8: "sparse patchify batch must be nonzero",
+    -9: "feature memory sparse assignment requires at least one token",
+    -10: "invalid argument",
+}
+
+
+class OracleError(RuntimeError):
+    """Raised where the reference returns Err / fails an ensure!."""
+
+
+def build() -> str:
+    """Compile the oracle with its Makefile (gcc + OpenMP)."""
+    subprocess.run(["make", "-s", "-C", _HERE], check=True)
+    return _LIB_PATH
+
+
+_lib = None
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.exists(_LIB_PATH):
+            build()
+        _lib = ctypes.CDLL(_LIB_PATH)
+        _declare(_lib)
+    return _lib
+
+
+class PatchDiffConfig(ctypes.Structure):
+    """SparseJepaPatchDiffSparsityConfig (src/nodes.rs:97-157)."""
+
+    _fields_ = [
+        ("threshold", ctypes.c_float),
+        ("context_tokens", ctypes.c_int64),
+        ("target_tokens", ctypes.c_int64),
+        ("dilation", ctypes.c_int64),
+        ("min_context_tokens", ctypes.c_int64),
+        ("fill_to_context_tokens", ctypes.c_int32),
+        ("allow_full_context", ctypes.c_int32),
+    ]
+
+    @classmethod
+    def new(cls, threshold, context_tokens, target_tokens):
+        """SparseJepaPatchDiffSparsityConfig::new (nodes.rs:109-119)."""
+        return cls(threshold, context_tokens, target_tokens, 0, 1, 1, 0)
+
+    @classmethod
+    def adaptive_threshold(cls, threshold, min_context_tokens, max_context_tokens, target_tokens):
+        """SparseJepaPatchDiffSparsityConfig::adaptive_threshold (nodes.rs:121-136)."""
+        return cls(threshold, max_context_tokens, target_tokens, 0, min_context_tokens, 0, 1)
+
+
+class PatchifyConfig(ctypes.Structure):
+    """burn_flex_gmm::SparsePatchify3dConfig as built at src/model.rs:1297-1306."""
+
+    _fields_ = [
+        (n, ctypes.c_int64)
+        for n in (
+            "in_channels",
+            "out_channels",
+            "frames",
+            "height",
+            "width",
+            "tubelet_size",
+            "patch_h",
+            "patch_w",
+        )
+    ]
+
+
+_P = ctypes.c_void_p
+_I64 = ctypes.c_int64
+
+
+def _declare(L):
+    L.bjo_token_index_to_coords.argtypes = [_I64] * 4 + [ctypes.POINTER(_I64)] * 3
+    L.bjo_token_index_to_coords.restype = None
+    L.bjo_coords_to_token_index.argtypes = [_I64] * 6
+    L.bjo_coords_to_token_index.restype = _I64
+    L.bjo_sparse_token_mask_new.argtypes = [_P, _I64, _I64]
+    L.bjo_sparse_token_mask_new.restype = _I64
+    L.bjo_from_keep_ratio.argtypes = [_I64, ctypes.c_float, _P]
+    L.bjo_from_keep_ratio.restype = _I64
+    L.bjo_evenly_spaced_indices.argtypes = [_I64, _I64, _P]
+    L.bjo_evenly_spaced_indices.restype = _I64
+    L.bjo_complement.argtypes = [_P, _I64, _I64, _P]
+    L.bjo_complement.restype = _I64
+    L.bjo_padded_to_len.argtypes = [_P, _I64, _I64, _I64, _P]
+    L.bjo_padded_to_len.restype = _I64
+    L.bjo_target_mask_from_context.argtypes = [_P, _I64, _I64, _I64, _P]
+    L.bjo_target_mask_from_context.restype = _I64
+    L.bjo_patch_diff_token_scores.argtypes = [_P] + [_I64] * 7 + [_P]
+    L.bjo_patch_diff_token_scores.restype = ctypes.c_int
+    L.bjo_patch_diff_context_mask_from_scores.argtypes = [_P, _I64, _I64, _I64, _I64, _P, _P, _P]
+    L.bjo_patch_diff_context_mask_from_scores.restype = ctypes.c_int
+    L.bjo_patch_diff_context_mask.argtypes = [_P] + [_I64] * 10 + [_P, _P, _P]
+    L.bjo_patch_diff_context_mask.restype = ctypes.c_int
+    L.bjo_sparse_patchify_plan.argtypes = [_P, _I64, _I64, _I64, _I64, _I64, _P]
+    L.bjo_sparse_patchify_plan.restype = ctypes.c_int
+    L.bjo_sparse_patchify3d_forward.argtypes = [_P, _I64, _P, _P, _I64, _P, _P, _P]
+    L.bjo_sparse_patchify3d_forward.restype = ctypes.c_int
+    L.bjo_patch_embed3d_dense.argtypes = [_P, _I64, _P, _P, _P, _P]
+    L.bjo_patch_embed3d_dense.restype = ctypes.c_int
+    L.bjo_feature_memory_assign_latest.argtypes = [_P] * 5 + [_I64] * 4 + [ctypes.c_int32]
+    L.bjo_feature_memory_assign_latest.restype = ctypes.c_int
+    L.bjo_front_end_streams.argtypes = [_P, _I64, _P, _P, _P, _P, _P, _P, _P, ctypes.c_int32, _P]
+    L.bjo_front_end_streams.restype = ctypes.c_int
+    L.bjo_splitmix64.argtypes = [ctypes.c_uint64]
+    L.bjo_splitmix64.restype = ctypes.c_uint64
+    L.bjo_num_threads.argtypes = []
+    L.bjo_num_threads.restype = ctypes.c_int
+
+
+def _ptr(a: np.ndarray):
+    return a.ctypes.data_as(ctypes.c_void_p)
+
+
+def _check(rc: int):
+    if rc < 0:
+        raise OracleError(_ERRORS.get(int(rc), f"oracle error {rc}"))
+    return rc
+
+
+def num_threads() -> int:
+    return int(lib().bjo_num_threads())
+
+
+# --------------------------------------------------------------------------
+# Grid addressing and masks (src/positional.rs, src/tokens.rs)
+# --------------------------------------------------------------------------
+@dataclass(frozen=True)
+class TokenGridShape:
+    """src/tokens.rs:5-32."""
+
+    depth: int
+    height: int
+    width: int
+
+    def __len__(self):
+        return self.depth * self.height * self.width
+
+    def tokens_per_frame(self):
+        return self.height * self.width
+
+
+def token_index_to_coords(index: int, grid: TokenGridShape):
+    """src/positional.rs:10-17."""
+    f, r, c = _I64(), _I64(), _I64()
+    lib().bjo_token_index_to_coords(index, grid.depth, grid.height, grid.width,
+                                    ctypes.byref(f), ctypes.byref(r), ctypes.byref(c))
+    return (f.value, r.value, c.value)
+
+
+def coords_to_token_index(frame: int, row: int, col: int, grid: TokenGridShape) -> int:
+    """src/positional.rs:19-21."""
+    return int(lib().bjo_coords_to_token_index(frame, row, col, grid.depth, grid.height, grid.width))
+
+
+def sparse_token_mask_new(indices, dense_len: int) -> np.ndarray:
+    """SparseTokenMask::new (src/tokens.rs:41-50): sorted, deduplicated, range-checked."""
+    a = np.ascontiguousarray(np.asarray(indices, dtype=np.int64).copy())
+    n = _check(lib().bjo_sparse_token_mask_new(_ptr(a), a.size, dense_len))
+    return a[:n].copy()
+
+
+def from_keep_ratio(dense_len: int, keep_ratio: float) -> np.ndarray:
+    """SparseTokenMask::from_keep_ratio (src/tokens.rs:52-59)."""
+    out = np.zeros(max(dense_len, 1), dtype=np.int64)
+    n = lib().bjo_from_keep_ratio(dense_len, keep_ratio, _ptr(out))
+    return out[:n].copy()
+
+
+def evenly_spaced_indices(dense_len: int, keep: int) -> np.ndarray:
+    """SparseTokenMask::evenly_spaced_indices (src/tokens.rs:66-75)."""
+    out = np.zeros(max(dense_len, keep, 1), dtype=np.int64)
+    n = lib().bjo_evenly_spaced_indices(dense_len, keep, _ptr(out))
+    return out[:n].copy()
+
+
+def complement(indices, dense_len: int) -> np.ndarray:
+    """SparseTokenMask::complement (src/tokens.rs:143-157)."""
+    a = np.ascontiguousarray(np.asarray(indices, dtype=np.int64))
+    out = np.zeros(max(dense_len, 1), dtype=np.int64)
+    n = lib().bjo_complement(_ptr(a), a.size, dense_len, _ptr(out))
+    return out[:n].copy()
+
+
+def padded_to_len(indices, dense_len: int, target_len: int) -> np.ndarray:
+    """SparseTokenMask::padded_to_len (src/tokens.rs:94-128)."""
+    a = np.ascontiguousarray(np.asarray(indices, dtype=np.int64))
+    out = np.zeros(max(dense_len, a.size, 1), dtype=np.int64)
+    n = _check(lib().bjo_padded_to_len(_ptr(a), a.size, dense_len, target_len, _ptr(out)))
+    return out[:n].copy()
+
+
+def padded_to_multiple(indices, dense_len: int, multiple: int) -> np.ndarray:
+    """SparseTokenMask::padded_to_multiple (src/tokens.rs:130-141)."""
+    a = np.asarray(indices, dtype=np.int64)
+    if multiple <= 1 or a.size >= dense_len:
+        return a.copy()
+    target = min(-(-a.size // multiple) * multiple, dense_len)
+    return padded_to_len(a, dense_len, target)
+
+
+def target_mask_from_context(context, dense_len: int, target_tokens: int) -> np.ndarray:
+    """target_mask_from_context (src/tokens.rs:497-528)."""
+    a = np.ascontiguousarray(np.asarray(context, dtype=np.int64))
+    out = np.zeros(max(dense_len, 1), dtype=np.int64)
+    n = _check(lib().bjo_target_mask_from_context(_ptr(a), a.size, dense_len, target_tokens, _ptr(out)))
+    return out[:n].copy()
+
+
+def make_context_target_masks(grid: TokenGridShape, context_keep_ratio: float):
+    """make_context_target_masks (src/tokens.rs:488-495)."""
+    context = from_keep_ratio(len(grid), context_keep_ratio)
+    return context, complement(context, len(grid))
+
+
+# --------------------------------------------------------------------------
+# Patch-diff mask (src/nodes.rs)
+# --------------------------------------------------------------------------
+def patch_diff_token_scores(video: np.ndarray, tubelet_size: int, patch_size: int) -> np.ndarray:
+    """patch_diff_token_scores (src/nodes.rs:565-631). video [B,C,T,H,W] -> [N] f32."""
+    v = np.ascontiguousarray(video, dtype=np.float32)
+    B, C, T, H, W = v.shape
+    kt, P = max(tubelet_size, 1), max(patch_size, 1)
+    out = np.zeros(max((T // kt) * (H // P) * (W // P), 1), dtype=np.float32)
+    _check(lib().bjo_patch_diff_token_scores(_ptr(v), B, C, T, H, W, tubelet_size, patch_size, _ptr(out)))
+    return out[: (T // kt) * (H // P) * (W // P)].copy()
+
+
+def patch_diff_context_mask_from_scores(scores, grid: TokenGridShape, config: PatchDiffConfig) -> np.ndarray:
+    """patch_diff_context_mask_from_scores (src/nodes.rs:458-537)."""
+    s = np.ascontiguousarray(np.asarray(scores, dtype=np.float32))
+    out = np.zeros(max(len(grid), 1), dtype=np.int64)
+    cnt = _I64()
+    _check(lib().bjo_patch_diff_context_mask_from_scores(
+        _ptr(s), s.size, grid.depth, grid.height, grid.width, ctypes.byref(config), _ptr(out), ctypes.byref(cnt)))
+    return out[: cnt.value].copy()
+
+
+def patch_diff_context_mask_from_video(video: np.ndarray, tubelet_size: int, patch_size: int,
+                                       grid: TokenGridShape, config: PatchDiffConfig) -> np.ndarray:
+    """patch_diff_context_mask_from_video (src/nodes.rs:539-546 -> 411-456)."""
+    v = np.ascontiguousarray(video, dtype=np.float32)
+    B, C, T, H, W = v.shape
+    out = np.zeros(max(len(grid), 1), dtype=np.int64)
+    cnt = _I64()
+    _check(lib().bjo_patch_diff_context_mask(
+        _ptr(v), B, C, T, H, W, tubelet_size, patch_size, grid.depth, grid.height, grid.width,
+        ctypes.byref(config), _ptr(out), ctypes.byref(cnt)))
+    return out[: cnt.value].copy()
+
+
+# --------------------------------------------------------------------------
+# Sparse patchify (src/sparse_patchify.rs, flex-gmm semantics)
+# --------------------------------------------------------------------------
+def sparse_patchify_plan_coords(mask_indices, grid: TokenGridShape, batch: int) -> np.ndarray:
+    """SparsePatchifyPlan::new coords (src/sparse_patchify.rs:236-269) -> [batch*n, 4] int32."""
+    m = np.ascontiguousarray(np.asarray(mask_indices, dtype=np.int64))
+    out = np.zeros((max(batch, 1) * m.size, 4), dtype=np.int32)
+    _check(lib().bjo_sparse_patchify_plan(_ptr(m), m.size, grid.depth, grid.height, grid.width, batch, _ptr(out)))
+    return out
+
+
+def sparse_patchify3d_forward(config: PatchifyConfig, input: np.ndarray, coords: np.ndarray,
+                              weight: np.ndarray, bias) -> np.ndarray:
+    """flex-gmm sparse_patchify3d_forward semantics (Conv3d at selected tubelets) -> [rows, D]."""
+    x = np.ascontiguousarray(input, dtype=np.float32)
+    c = np.ascontiguousarray(coords, dtype=np.int32).reshape(-1, 4)
+    w = np.ascontiguousarray(weight, dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    out = np.zeros((c.shape[0], config.out_channels), dtype=np.float32)
+    _check(lib().bjo_sparse_patchify3d_forward(
+        ctypes.byref(config), x.shape[0], _ptr(x), _ptr(c), c.shape[0], _ptr(w),
+        None if b is None else _ptr(b), _ptr(out)))
+    return out
+
+
+def patch_embed3d_dense(config: PatchifyConfig, input: np.ndarray, weight: np.ndarray, bias) -> np.ndarray:
+    """PatchEmbed3d::forward (src/model.rs:88-93) -> [B, N, D]."""
+    x = np.ascontiguousarray(input, dtype=np.float32)
+    w = np.ascontiguousarray(weight, dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    B = x.shape[0]
+    n = (config.frames // config.tubelet_size) * (config.height // config.patch_h) * (config.width // config.patch_w)
+    out = np.zeros((B, n, config.out_channels), dtype=np.float32)
+    _check(lib().bjo_patch_embed3d_dense(ctypes.byref(config), B, _ptr(x), _ptr(w),
+                                         None if b is None else _ptr(b), _ptr(out)))
+    return out
+
+
+# --------------------------------------------------------------------------
+# Token cache (src/sparse_feature_memory.rs)
+# --------------------------------------------------------------------------
+def feature_memory_assign_latest(features, observed, age_frames, tokens, token_indices, age_observed: bool):
+    """sparse_feature_memory_assign_latest (src/sparse_feature_memory.rs:22-108), in place on
+    float32 numpy arrays features [B,N,D], observed/age [B,N]; tokens [B,S,D]; indices [B,S]."""
+    for a in (features, observed, age_frames):
+        assert a.dtype == np.float32 and a.flags.c_contiguous
+    t = np.ascontiguousarray(tokens, dtype=np.float32)
+    i = np.ascontiguousarray(token_indices, dtype=np.int32)
+    B, N, D = features.shape
+    S = i.shape[1]
+    _check(lib().bjo_feature_memory_assign_latest(
+        _ptr(features), _ptr(observed), _ptr(age_frames), _ptr(t), _ptr(i), B, N, D, S, int(bool(age_observed))))
+
+
+def front_end_streams(video, config: PatchifyConfig, mask_config: PatchDiffConfig, weight, bias,
+                      caches, observed, age_frames, age_observed: bool) -> np.ndarray:
+    """One front-end step over S independent streams (f32), in place on the caches."""
+    v = np.ascontiguousarray(video, dtype=np.float32)
+    w = np.ascontiguousarray(weight, dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    for a in (caches, observed, age_frames):
+        assert a.dtype == np.float32 and a.flags.c_contiguous
+    S = v.shape[0]
+    counts = np.zeros(S, dtype=np.int64)
+    _check(lib().bjo_front_end_streams(
+        _ptr(v), S, ctypes.byref(config), ctypes.byref(mask_config), _ptr(w),
+        None if b is None else _ptr(b), _ptr(caches), _ptr(observed), _ptr(age_frames),
+        int(bool(age_observed)), _ptr(counts)))
+    return counts
+
+
+def splitmix64(value: int) -> int:
+    """training/mask.rs:557-563."""
+    return int(lib().bjo_splitmix64(ctypes.c_uint64(value & 0xFFFFFFFFFFFFFFFF)))

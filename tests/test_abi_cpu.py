@@ -1,0 +1,108 @@
+"""C ABI checks that need no GPU: the library loads, exports every symbol include/bjf.h
+declares, and rejects invalid arguments on the host with the reference's messages
+before anything is launched."""
+import ctypes
+
+import pytest
+
+import burn_jepa_b200 as bj
+from burn_jepa_b200 import _abi
+
+FAKE = ctypes.c_void_p(0x1000)  # never dereferenced: every call below fails validation first
+
+
+def test_library_exports_every_header_symbol():
+    lib = bj.load()
+    declared = _abi.header_symbols()
+    assert declared, "no declarations parsed from include/bjf.h"
+    for name in declared:
+        assert hasattr(lib, name), f"libbjf.so does not export {name}"
+    assert set(declared) == set(_abi.SIGNATURES), "ctypes signatures out of sync with include/bjf.h"
+
+
+def test_abi_version():
+    assert bj.load().bjf_abi_version() == 1
+
+
+def _fm(features, observed, age, tokens, indices):
+    return bj.load().bjf_feature_memory_assign_latest(
+        FAKE, _abi.DTYPE_F32, _abi.dims(*features), FAKE, _abi.dims(*observed), FAKE, _abi.dims(*age), FAKE,
+        _abi.DTYPE_F32, _abi.dims(*tokens), FAKE, _abi.dims(*indices), 0, None)
+
+
+def test_feature_memory_shape_errors_mirror_reference_messages():
+    from helpers import known_answers
+
+    ka = known_answers()["feature_memory_shape_errors"]
+    c = ka["index_shape_mismatch"]
+    assert _fm(c["features"], c["features"][:2], c["features"][:2], c["tokens"], c["indices"]) == -1
+    assert c["message_contains"] in bj.last_error()
+    assert bj.last_error() == "feature memory index dims mismatch: indices=[1,2] expected=[1,1]"
+    c = ka["sparse_len_zero"]
+    assert _fm(c["features"], c["features"][:2], c["features"][:2], c["tokens"], c["indices"]) == -1
+    assert bj.last_error() == c["message"]
+    c = ka["metadata_mismatch"]
+    assert _fm(c["features"], c["observed"], c["age"], [1, 1, 2], [1, 1]) == -1
+    assert bj.last_error() == ("feature memory metadata dims mismatch: features=[1,4,2] observed=[1,3] "
+                               "age=[1,4]")
+    c = ka["token_dim_mismatch"]
+    assert _fm(c["features"], c["features"][:2], c["features"][:2], c["tokens"], c["indices"]) == -1
+    assert bj.last_error() == "feature memory token dims mismatch: tokens=[1,1,3] expected=[1,sparse,2]"
+
+
+@pytest.mark.parametrize("threshold", [float("nan"), -1.0, float("inf")])
+def test_patch_diff_threshold_rejected(threshold):
+    cfg = bj.PatchDiffConfig.new(threshold, 1, 2)
+    rc = bj.load().bjf_patch_diff_context_mask_from_scores(FAKE, 1, _abi.dims(2, 2, 2), ctypes.byref(cfg), FAKE,
+                                                           FAKE, None)
+    assert rc == -1 and bj.last_error() == "patch-diff sparsity threshold must be finite and non-negative"
+    rc = bj.load().bjf_patch_diff_context_mask(FAKE, _abi.DTYPE_F32, _abi.dims(1, 3, 4, 32, 32), 1, 2, 16,
+                                               _abi.dims(2, 2, 2), ctypes.byref(cfg), FAKE, FAKE, FAKE, None)
+    assert rc == -1 and bj.last_error() == "patch-diff sparsity threshold must be finite and non-negative"
+
+
+def test_patch_diff_video_shape_errors():
+    cfg = bj.PatchDiffConfig.new(0.1, 1, 2)
+    L = bj.load()
+    rc = L.bjf_patch_diff_context_mask(FAKE, _abi.DTYPE_F32, _abi.dims(1, 3, 4, 30, 32), 1, 2, 16,
+                                       _abi.dims(2, 2, 2), ctypes.byref(cfg), FAKE, FAKE, FAKE, None)
+    assert rc == -1
+    assert bj.last_error() == ("patch-diff sparsity requires frames/height/width divisible by tubelet and "
+                               "patch sizes")
+    rc = L.bjf_patch_diff_context_mask(FAKE, _abi.DTYPE_F32, _abi.dims(1, 3, 4, 32, 32), 1, 2, 16,
+                                       _abi.dims(2, 1, 2), ctypes.byref(cfg), FAKE, FAKE, FAKE, None)
+    assert rc == -1 and bj.last_error() == "patch-diff sparsity grid must match the video shape"
+    # a one-token grid has no context budget (nodes.rs:379-385)
+    rc = L.bjf_patch_diff_context_mask_from_scores(FAKE, 1, _abi.dims(1, 1, 1), ctypes.byref(cfg), FAKE, FAKE, None)
+    assert rc == -1 and bj.last_error() == "sparse JEPA mode requires at least two dense tokens"
+
+
+def test_patchify_config_errors():
+    L = bj.load()
+    cfg = bj.PatchifyConfig(3, 32, 4, 32, 32, 2, 16, 16)
+    rc = L.bjf_sparse_patchify3d_forward(ctypes.byref(cfg), FAKE, _abi.DTYPE_F32, _abi.dims(1, 3, 4, 32, 16), FAKE,
+                                         4, FAKE, _abi.DTYPE_F32, _abi.dims(32, 3, 2, 16, 16), None, FAKE,
+                                         _abi.DTYPE_F32, None)
+    assert rc == -1 and "input dims [1,3,4,32,16] do not match the config" in bj.last_error()
+    rc = L.bjf_sparse_patchify3d_forward(ctypes.byref(cfg), FAKE, _abi.DTYPE_F32, _abi.dims(1, 3, 4, 32, 32), FAKE,
+                                         4, FAKE, _abi.DTYPE_F32, _abi.dims(32, 3, 1, 16, 16), None, FAKE,
+                                         _abi.DTYPE_F32, None)
+    assert rc == -1 and "weight dims [32,3,1,16,16] do not match the config" in bj.last_error()
+    bad = bj.PatchifyConfig(3, 32, 4, 32, 32, 0, 16, 16)
+    rc = L.bjf_sparse_patchify3d_forward(ctypes.byref(bad), FAKE, _abi.DTYPE_F32, _abi.dims(1, 3, 4, 32, 32), FAKE,
+                                         4, FAKE, _abi.DTYPE_F32, _abi.dims(32, 3, 0, 16, 16), None, FAKE,
+                                         _abi.DTYPE_F32, None)
+    assert rc == -1 and "must be positive" in bj.last_error()
+    # zero rows is a valid no-op and launches nothing
+    rc = L.bjf_sparse_patchify3d_forward(ctypes.byref(cfg), FAKE, _abi.DTYPE_F32, _abi.dims(1, 3, 4, 32, 32), FAKE,
+                                         0, FAKE, _abi.DTYPE_F32, _abi.dims(32, 3, 2, 16, 16), None, FAKE,
+                                         _abi.DTYPE_F32, None)
+    assert rc == 0
+
+
+def test_plan_errors():
+    L = bj.load()
+    rc = L.bjf_sparse_patchify_plan_coords(FAKE, 3, None, 1, 0, _abi.dims(2, 3, 4), FAKE, 6, None, None)
+    assert rc == -1 and bj.last_error() == "sparse patchify batch must be nonzero"
+    rc = L.bjf_sparse_patchify_plan_coords(FAKE, 3, None, 3, 2, _abi.dims(2, 3, 4), FAKE, 6, None, None)
+    assert rc == -1 and "mask rows must be 1 or equal the batch" in bj.last_error()

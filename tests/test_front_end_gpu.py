@@ -1,0 +1,75 @@
+"""Fused front-end step (bjf_front_end_step) against the oracle's per-stream composition
+(patch_diff_context_mask -> plan -> sparse patchify -> AssignLatest cache write) over
+several steps: masks and cache slots bit-exact, written rows within the f16 tolerance,
+untouched rows unchanged, observed/age exact."""
+import numpy as np
+import pytest
+
+import burn_jepa_b200 as bj
+import oracle
+from burn_jepa_b200 import workloads
+from helpers import max_rel_err
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.fixture(autouse=True)
+def _no_device_timeouts(cuda_device):
+    yield
+    assert not bj.device_error_check(), "a kernel reported a bounded-wait timeout"
+
+
+@pytest.mark.parametrize("S,H,W,D,cache_dt,video_dt", [
+    (3, 128, 128, 256, "f16", "f16"),
+    (2, 64, 96, 1024, "f16", "bf16"),
+    (2, 64, 64, 1408, "bf16", "bf16"),
+    (2, 64, 64, 96, "f32", "f32"),
+])
+def test_front_end_steps_match_oracle(cuda_device, S, H, W, D, cache_dt, video_dt):
+    import torch
+
+    dt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}
+    C, T, KT, P = 3, 2, 2, 16
+    n = (T // KT) * (H // P) * (W // P)
+    weight = workloads.splitmix_normal(21, (D, C, KT, P, P), 0.02)
+    bias = workloads.splitmix_normal(22, (D,), 0.02)
+    wd = torch.from_numpy(weight).to(cuda_device, dt[video_dt])
+    bd = torch.from_numpy(bias).to(cuda_device)
+    cache0 = workloads.splitmix_normal(23, (S, n, D), 1.0)
+    caches = torch.from_numpy(cache0).to(cuda_device, dt[cache_dt])
+    observed = torch.zeros((S, n), device=cuda_device)
+    age = torch.zeros((S, n), device=cuda_device)
+
+    ref_cache = caches.float().cpu().numpy()
+    ref_obs = np.zeros((S, n), np.float32)
+    ref_age = np.zeros((S, n), np.float32)
+    w_exact = wd.float().cpu().numpy()
+    ocfg = oracle.PatchifyConfig(C, D, T, H, W, KT, P, P)
+    fe = None
+    for step in range(3):
+        video = workloads.rect_perturbation_clips(100 + step, S, C, T, H, W, area_fraction=0.2)
+        vd = torch.from_numpy(video).to(cuda_device, dt[video_dt])
+        xs = vd.float().cpu().numpy()
+        thr = workloads.choose_threshold(oracle.patch_diff_token_scores(xs[0:1], KT, P), 0.2)
+        mask = bj.PatchDiffConfig.adaptive_threshold(thr, 1, n, 1)
+        fe = bj.FrontEnd(S, C, T, H, W, KT, P, D, mask, dt[video_dt], dt[cache_dt], cuda_device)
+        counts = fe.step(vd, wd, bd, caches, observed, age, age_observed=step > 0).cpu().numpy()
+        omask = oracle.PatchDiffConfig.adaptive_threshold(thr, 1, n, 1)
+        for s in range(S):
+            idx = oracle.patch_diff_context_mask_from_video(xs[s:s + 1], KT, P, oracle.TokenGridShape(T // KT, H // P, W // P), omask)
+            assert counts[s] == len(idx), (step, s)
+            coords = oracle.sparse_patchify_plan_coords(idx, oracle.TokenGridShape(T // KT, H // P, W // P), 1)
+            feats = oracle.sparse_patchify3d_forward(ocfg, xs[s:s + 1], coords, w_exact, bias)
+            rc, ro, ra = ref_cache[s:s + 1], ref_obs[s:s + 1], ref_age[s:s + 1]
+            oracle.feature_memory_assign_latest(rc, ro, ra, feats[None], idx.astype(np.int32)[None],
+                                                age_observed=step > 0)
+        got = caches.float().cpu().numpy()
+        assert np.array_equal(observed.cpu().numpy(), ref_obs)
+        assert np.array_equal(age.cpu().numpy(), ref_age)
+        written = ref_obs.astype(bool) if step == 0 else None
+        tol = 1e-2 if cache_dt != "f32" or video_dt != "f32" else 1e-4
+        assert max_rel_err(got, ref_cache) <= tol
+        if written is not None:
+            # rows never written keep their exact pre-filled values
+            assert np.array_equal(got[~written], caches.new_tensor(cache0).to(dt[cache_dt]).float().cpu().numpy()[~written])
+        ref_cache = got.copy()  # carry the device's rounding forward; exactness is checked per step
