@@ -85,7 +85,8 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.PIPE, text=True)
+            time.sleep(0.5)  # let the sampler start before the load begins
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except Exception:
@@ -95,6 +96,12 @@ class ClockSampler:
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
+
+    def errors(self) -> str:
+        try:
+            return self.proc.stderr.read()[:300] if self.proc else "nvidia-smi not started"
+        except Exception:
+            return ""
 
     def __exit__(self, *exc):
         if self.proc:
@@ -120,7 +127,8 @@ class ClockSampler:
                 if val.lower().startswith("active"):
                     reasons.add(name)
         if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0,
+                    "raw": self.lines[:3], "stderr": self.errors()}
         return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
 
 
@@ -231,11 +239,17 @@ def run_ours(args, world, rank, local):
             counts_per_set.append(int(c.sum().item()))
         return videos, thr, fe, caches, observed, age, counts_per_set
 
-    def time_steps(fe, videos, caches, observed, age, steps, warmup):
+    def time_steps(fe, videos, caches, observed, age, steps, warmup, load_s=0.0):
         stream = torch.cuda.current_stream()
         for i in range(warmup):
             fe.step(videos[i % 2], weight, bias, caches, observed, age)
         torch.cuda.synchronize()
+        # sustained load right before the timed steps, long enough for the clock sampler
+        t_end = time.perf_counter() + load_s
+        while time.perf_counter() < t_end:
+            for i in range(64):
+                fe.step(videos[i % 2], weight, bias, caches, observed, age)
+            torch.cuda.synchronize()
         barrier(world)
         torch.cuda.synchronize()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -249,8 +263,12 @@ def run_ours(args, world, rank, local):
         return start.elapsed_time(end) / 1000.0
 
     videos, thr, fe, caches, observed, age, counts_per_set = setup(args.density)
-    with ClockSampler(local) as clocks:
-        secs = time_steps(fe, videos, caches, observed, age, args.steps, args.warmup)
+    try:  # nvidia-smi ignores CUDA_VISIBLE_DEVICES: address the GPU by its UUID
+        gpu_id = "GPU-" + str(torch.cuda.get_device_properties(dev).uuid)
+    except Exception:
+        gpu_id = str(local)
+    with ClockSampler(gpu_id) as clocks:
+        secs = time_steps(fe, videos, caches, observed, age, args.steps, args.warmup, load_s=2.0)
     tubelets = sum(counts_per_set[i % 2] for i in range(args.steps))
     max_secs = all_reduce(secs, "max", world, dev)
     all_tubelets = all_reduce(float(tubelets), "sum", world, dev)
@@ -375,6 +393,8 @@ def run_ours(args, world, rank, local):
                    "active_tubelets_per_step_per_gpu": counts_per_set,
                    "threshold": thr,
                    "l2": "inputs larger than L2: two 403 MB clip sets per GPU alternate between steps",
+                   "clocks_note": "nvidia-smi sampled every 100 ms over 2 s of back-to-back steps "
+                                  "immediately before and through the timed steps",
                    "parallelism": f"stream-sharded replicas x{world}, no collective"},
         "frames_per_s": round(frames_per_s, 1),
         "roofline": roofline, "kernels": kernels,
