@@ -122,6 +122,7 @@ SIGNATURES = {
     "bjf_front_end_workspace_bytes": (ctypes.c_size_t, [ctypes.POINTER(FrontEndDesc)]),
     "bjf_front_end_step": (_I32, [ctypes.POINTER(FrontEndDesc), _P, _P, _P, _P, _P, _P, _I32, _P, ctypes.c_size_t,
                                   _P, _P]),
+    "bjf_front_end_step_no_alloc": (_I32, [ctypes.POINTER(FrontEndDesc), _P, _P, _P, _P, _P, _P, _I32, _P, _P]),
     "bjf_feature_memory_assign_latest": (_I32, [_P, _I32, _DIMS, _P, _DIMS, _P, _DIMS, _P, _I32, _DIMS, _P, _DIMS,
                                                 _I32, _P]),
 }

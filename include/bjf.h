@@ -236,6 +236,23 @@ BJF_API bjf_status bjf_front_end_step(const bjf_front_end_desc* desc, const void
                                       void* workspace, size_t workspace_bytes, int32_t* counts_out,
                                       bjf_stream_t stream);
 
+/* No counterpart in the reference: bjf_front_end_step for callers that cannot
+ * allocate device memory (a host whose device memory belongs to its framework's caching
+ * allocator, or a real-time loop that forbids allocation after start-up because an
+ * allocation can stall the device).  Same arguments and results as bjf_front_end_step,
+ * minus the workspace: the step's scratch lives in a fixed 4 MiB __device__ array that
+ * every GPU loading the library holds until exit, so streams x tokens is limited to about
+ * 174k (the bench's 32 streams x 4096 tokens fit); larger steps return
+ * BJF_ERR_UNSUPPORTED.  All calls on a device share that array: calls that overlap on the
+ * GPU race, so issue them in order on one stream.  The first call on each device looks up
+ * the array's address; make it before any stream capture begins.  A call allocates
+ * nothing. */
+BJF_API bjf_status bjf_front_end_step_no_alloc(const bjf_front_end_desc* desc, const void* video,
+                                               const void* weight, const float* bias, void* caches,
+                                               float* observed, float* age_frames,
+                                               int32_t age_observed, int32_t* counts_out,
+                                               bjf_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
