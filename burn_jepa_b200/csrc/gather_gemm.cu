@@ -41,10 +41,15 @@ using namespace sm100;
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kStages = 4;
+constexpr int kStagesA = 7;  // gathered tubelet rows (from HBM): deep ring
+constexpr int kStagesB = 3;  // weight tiles (L2-resident): shallow ring
 constexpr int kMaxBN = 256;
-constexpr int kLag = 2;  // cp.async groups a producer keeps in flight before arriving
-constexpr int kThreads = 192;
+constexpr int kLag = 4;  // cp.async groups a producer keeps in flight before arriving
+constexpr int kEpilogueWarps = 4;   // warps 0-3: TMEM lane quarters 0-3
+constexpr int kProducerWarps = 4;   // warps 4-7: one gathered tile row per thread
+constexpr int kMmaWarp = 8;
+constexpr int kTmaWarp = 9;
+constexpr int kThreads = 32 * 10;
 constexpr int kMaxKBlocks = 128;  // K <= 8192
 constexpr uint64_t kWaitLimitNs = 2000000000ull;
 
@@ -53,13 +58,13 @@ constexpr int kBStageBytes = kMaxBN * kBK * 2;   // 32 KB
 
 struct SmemLayout {
   static constexpr int a_off = 0;
-  static constexpr int b_off = a_off + kStages * kAStageBytes;
-  static constexpr int bar_off = b_off + kStages * kBStageBytes;
-  // full_a[kStages], full_b[kStages], empty[kStages], acc_full
-  static constexpr int misc_off = bar_off + (3 * kStages + 1) * 8;
+  static constexpr int b_off = a_off + kStagesA * kAStageBytes;
+  static constexpr int bar_off = b_off + kStagesB * kBStageBytes;
+  // full_a[A], empty_a[A], full_b[B], empty_b[B], acc_full[2], acc_empty[2]
+  static constexpr int misc_off = bar_off + (2 * kStagesA + 2 * kStagesB + 4) * 8;
   // tmem base (4 B), abort flag (4 B)
   static constexpr int koff_off = misc_off + 16;
-  static constexpr int total = koff_off + kMaxKBlocks * 8 * 8;
+  static constexpr int total = koff_off + kMaxKBlocks * 8 * 4;
   static constexpr int alloc = total + 1024;  // room to align the base to 1024 B
 };
 
@@ -71,7 +76,8 @@ __device__ __forceinline__ int64_t row_base_offset(const GatherGeometry& g, int4
          (int64_t)c.w * g.pw;
 }
 
-// Offset of element k of a tubelet row relative to its (b, t*kt, r*ph, col*pw) corner.
+// Offset of element k of a tubelet row relative to its (b, t*kt, r*ph, col*pw) corner
+// (< C*T*H*W of one batch element, which the launch checks fits in int32).
 __host__ __device__ __forceinline__ int64_t k_offset(const GatherGeometry& g, int k) {
   int q = k / g.pw;
   int dx = k - q * g.pw;
@@ -82,6 +88,27 @@ __host__ __device__ __forceinline__ int64_t k_offset(const GatherGeometry& g, in
   return (((int64_t)ch * g.T + dt) * g.H + dy) * g.W + dx;
 }
 
+// Stores 32 consecutive output columns of one row (ncol of them valid).
+template <typename O>
+__device__ __forceinline__ void store_chunk(char* dst, const float (&v)[32], int ncol) {
+  O* o = reinterpret_cast<O*>(dst);
+  if (ncol == 32 && (reinterpret_cast<uintptr_t>(dst) & 15) == 0) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      float w8[8] = {v[j], v[j + 1], v[j + 2], v[j + 3], v[j + 4], v[j + 5], v[j + 6], v[j + 7]};
+      store8<O>(o + j, w8);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < ncol) o[j] = from_f32<O>(v[j]);
+  }
+}
+
+// Persistent, warp-specialised gather-GEMM.  grid = min(#SMs, tiles); CTA b takes tiles
+// b, b + grid, ... in (m-tile major, n-tile minor) order so concurrently running CTAs share
+// their gathered A rows through L2.  Two TMEM accumulators let the epilogue of one tile
+// overlap the main loop of the next.
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     gather_gemm_sm100_kernel(const __grid_constant__ CUtensorMap wmap, const T* __restrict__ video,
@@ -95,34 +122,43 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   int M = rows_cap;
   if (rows_dev) M = min(M, max(0, __ldg(rows_dev)));
-  const int m_tile = blockIdx.y;
-  if (m_tile * kBM >= M) return;  // uniform early exit before any allocation
-  const int n0 = blockIdx.x * bn;
+  const int n_tiles = (g.D + bn - 1) / bn;
+  const int num_tiles = ((M + kBM - 1) / kBM) * n_tiles;
+  if ((int)blockIdx.x >= num_tiles) return;  // uniform early exit before any allocation
 
   uint8_t* smem = smem_dyn + ((1024 - (smem_u32(smem_dyn) & 1023)) & 1023);
   uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + SmemLayout::bar_off);
-  uint64_t* full_b = full_a + kStages;
-  uint64_t* empty = full_b + kStages;
-  uint64_t* acc_full = empty + kStages;
+  uint64_t* empty_a = full_a + kStagesA;
+  uint64_t* full_b = empty_a + kStagesA;
+  uint64_t* empty_b = full_b + kStagesB;
+  uint64_t* acc_full = empty_b + kStagesB;
+  uint64_t* acc_empty = acc_full + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SmemLayout::misc_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SmemLayout::misc_off + 4);
-  int64_t* koff = reinterpret_cast<int64_t*>(smem + SmemLayout::koff_off);
+  int32_t* koff = reinterpret_cast<int32_t*>(smem + SmemLayout::koff_off);
 
   const int num_kb = g.num_kb;
   if (tid == 0) {
-    for (int s = 0; s < kStages; ++s) {
-      mbar_init(&full_a[s], kBM);
-      mbar_init(&full_b[s], 1);
-      mbar_init(&empty[s], 1);
+    for (int s = 0; s < kStagesA; ++s) {
+      mbar_init(&full_a[s], kProducerWarps * 32);
+      mbar_init(&empty_a[s], 1);
     }
-    mbar_init(acc_full, 1);
+    for (int s = 0; s < kStagesB; ++s) {
+      mbar_init(&full_b[s], 1);
+      mbar_init(&empty_b[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], kEpilogueWarps);
+    }
     *abort_flag = 0;
     fence_mbarrier_init();
   }
-  if (warp == 5 && lane == 0) tma_prefetch_desc(&wmap);
-  for (int i = tid; i < num_kb * 8; i += kThreads) koff[i] = k_offset(g, i * 8);
-  const uint32_t tmem_cols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
-  if (warp == 4) {
+  if (warp == kTmaWarp && lane == 0) tma_prefetch_desc(&wmap);
+  for (int i = tid; i < num_kb * 8; i += kThreads) koff[i] = (int32_t)k_offset(g, i * 8);
+  const uint32_t acc_cols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
+  const uint32_t tmem_cols = 2 * acc_cols;
+  if (warp == kMmaWarp) {
     tmem_alloc(tmem_slot, tmem_cols);
     tmem_relinquish();
   }
@@ -135,175 +171,179 @@ __global__ void __launch_bounds__(kThreads, 1)
   const uint32_t b_smem = smem_u32(smem + SmemLayout::b_off);
   bool aborted = false;
 
-  if (warp < 4) {
+  if (warp >= kEpilogueWarps && warp < kEpilogueWarps + kProducerWarps) {
     // ---------------- gather producers ----------------
-    const int m = tid;  // tile row
-    const int gm = m_tile * kBM + m;
-    bool valid = false;
-    int64_t base = 0;
-    int4 c = make_int4(-1, -1, -1, -1);
-    if (gm < M) {
-      c = coords[gm];
-      base = row_base_offset(g, c, valid);
-    }
-    const T* src_row = video + base;
+    const int m = tid - kEpilogueWarps * 32;  // tile row
     const uint32_t row_off = (uint32_t)((m >> 3) * 1024 + (m & 7) * 128);
     const uint32_t sw = (uint32_t)(m & 7);
-    for (int kb = 0; kb < num_kb; ++kb) {
-      const int s = kb % kStages;
-      const uint32_t par = ((kb / kStages) & 1) ^ 1;
-      if (!mbar_wait_bounded(&empty[s], par, abort_flag, kWaitLimitNs)) {
-        aborted = true;
-        break;
-      }
-      if (valid) {
-        const uint32_t dst = a_smem + s * kAStageBytes + row_off;
-        const int64_t* ko = koff + kb * 8;
+    int kbg = 0;  // k blocks issued by this CTA so far (all tiles)
+    for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x) {
+      const int gm = (tile / n_tiles) * kBM + m;
+      bool valid = false;
+      int64_t base = 0;
+      if (gm < M) base = row_base_offset(g, __ldg(coords + gm), valid);
+      const T* src_row = video + base;
+      for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
+        const int s = kbg % kStagesA;
+        const uint32_t par = ((kbg / kStagesA) & 1) ^ 1;
+        if (!mbar_wait_bounded(&empty_a[s], par, abort_flag, kWaitLimitNs)) {
+          aborted = true;
+          break;
+        }
+        if (valid) {
+          const uint32_t dst = a_smem + s * kAStageBytes + row_off;
+          const int32_t* ko = koff + kb * 8;
 #pragma unroll
-        for (int j = 0; j < 8; ++j) cp_async_16(dst + ((j ^ sw) << 4), src_row + ko[j]);
-      }
-      cp_async_commit();
-      if (kb >= kLag) {
-        cp_async_wait_group<kLag>();
-        fence_proxy_async_smem();
-        mbar_arrive(&full_a[(kb - kLag) % kStages]);
+          for (int j = 0; j < 8; ++j) cp_async_16(dst + ((j ^ sw) << 4), src_row + ko[j]);
+        }
+        cp_async_commit();
+        if (kbg >= kLag) {
+          cp_async_wait_group<kLag>();
+          fence_proxy_async_smem();
+          mbar_arrive(&full_a[(kbg - kLag) % kStagesA]);
+        }
       }
     }
     cp_async_wait_all();
     if (!aborted) {
       fence_proxy_async_smem();
-      for (int kb = max(0, num_kb - kLag); kb < num_kb; ++kb) mbar_arrive(&full_a[kb % kStages]);
+      for (int k = max(0, kbg - kLag); k < kbg; ++k) mbar_arrive(&full_a[k % kStagesA]);
     }
-
-    // ---------------- epilogue ----------------
-    // tcgen05.ld is warp-collective: decide per warp.
-    aborted = __any_sync(0xffffffffu, aborted);
-    if (!aborted && !mbar_wait_bounded(acc_full, 0, abort_flag, kWaitLimitNs)) aborted = true;
-    aborted = __any_sync(0xffffffffu, aborted);
-    if (!aborted) {
+  } else if (warp == kMmaWarp) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      const uint32_t idesc = idesc_f16_f32(g.is_bf16 ? 1u : 0u, kBM, (uint32_t)bn);
+      int kbg = 0, it = 0;
+      int commits0 = 0;  // tcgen05.commit arrivals on acc_full[0] so far
+      bool issued_any = false;
+      for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x, ++it) {
+        const int buf = it & 1;
+        const uint32_t use_par = ((it >> 1) & 1) ^ 1;
+        if (!mbar_wait_bounded(&acc_empty[buf], use_par, abort_flag, kWaitLimitNs)) {
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)buf * acc_cols;
+        for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
+          const int sa = kbg % kStagesA, sb = kbg % kStagesB;
+          if (!mbar_wait_bounded(&full_a[sa], (kbg / kStagesA) & 1, abort_flag, kWaitLimitNs) ||
+              !mbar_wait_bounded(&full_b[sb], (kbg / kStagesB) & 1, abort_flag, kWaitLimitNs)) {
+            aborted = true;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_base = a_smem + sa * kAStageBytes;
+          const uint32_t b_base = b_smem + sb * kBStageBytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            mma_f16_ss(d_tmem, smem_desc_sw128_kmajor(a_base + kk * 32),
+                       smem_desc_sw128_kmajor(b_base + kk * 32), idesc, (kb | kk) != 0);
+          }
+          issued_any = true;
+          mma_commit(&empty_a[sa]);
+          mma_commit(&empty_b[sb]);
+        }
+        if (aborted) break;
+        mma_commit(&acc_full[buf]);
+        commits0 += buf == 0;
+      }
+      if (aborted && issued_any) {
+        // Let the issued MMAs retire before TMEM is freed: one more commit on acc_full[0]
+        // completes phase `commits0` once every earlier MMA is done (bounded, abort ignored).
+        mma_commit(&acc_full[0]);
+        int zero = 0;
+        mbar_wait_bounded(&acc_full[0], (uint32_t)(commits0 & 1), &zero, kWaitLimitNs);
+      }
+    }
+  } else if (warp == kTmaWarp) {
+    // ---------------- TMA producer (weight) ----------------
+    if (lane == 0) {
+      int kbg = 0;
+      for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x) {
+        const int n0 = (tile % n_tiles) * bn;
+        for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
+          const int s = kbg % kStagesB;
+          const uint32_t par = ((kbg / kStagesB) & 1) ^ 1;
+          if (!mbar_wait_bounded(&empty_b[s], par, abort_flag, kWaitLimitNs)) {
+            aborted = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_b[s], (uint32_t)(bn * kBK * 2));
+          tma_load_2d(b_smem + s * kBStageBytes, &wmap, kb * kBK, n0, &full_b[s]);
+        }
+      }
+      if (aborted) {
+        // Wait for the weight tiles still in flight before the CTA's smem goes away.
+        int zero = 0;
+        for (int k = max(0, kbg - kStagesB); k < kbg; ++k)
+          mbar_wait_bounded(&full_b[k % kStagesB], (k / kStagesB) & 1, &zero, kWaitLimitNs);
+      }
+    }
+  } else {
+    // ---------------- epilogue (warps 0-3) ----------------
+    const int m = tid;  // TMEM lane = tile row
+    const int ce = ep.out_elem_bytes;
+    int it = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
+      const int buf = it & 1;
+      const uint32_t par = (it >> 1) & 1;
+      bool ok = mbar_wait_bounded(&acc_full[buf], par, abort_flag, kWaitLimitNs);
+      if (__any_sync(0xffffffffu, !ok)) {  // tcgen05.ld is warp-collective: decide per warp
+        aborted = true;
+        break;
+      }
       tc_fence_after();
-      const uint32_t taddr = tmem_base + ((uint32_t)(warp * 32) << 16);
-      bool meta_valid = false;
+      const int m_tile = tile / n_tiles;
+      const int n0 = (tile % n_tiles) * bn;
+      const int gm = m_tile * kBM + m;
+      bool valid = false;
+      int4 c = make_int4(-1, -1, -1, -1);
       char* dst_row = nullptr;
-      const int ce = ep.out_elem_bytes;
       if (gm < M) {
+        c = __ldg(coords + gm);
+        row_base_offset(g, c, valid);
         if (ep.mode == kEpiloguePlain) {
           dst_row = static_cast<char*>(ep.out) + (int64_t)gm * ep.ldo * ce;
         } else if (valid) {
           const int64_t idx = ((int64_t)c.y * g.gh + c.z) * g.gw + c.w;
           const int64_t slot = (int64_t)c.x * ep.dense_tokens + idx;
           dst_row = static_cast<char*>(ep.out) + slot * ep.ldo * ce;
-          meta_valid = blockIdx.x == 0;
-          if (meta_valid) {
+          if (n0 == 0) {
             if (ep.observed) ep.observed[slot] = 1.0f;
             if (ep.age) ep.age[slot] = 0.0f;
           }
         }
       }
+      const uint32_t taddr = tmem_base + (uint32_t)buf * acc_cols + ((uint32_t)(warp * 32) << 16);
       for (int c0 = 0; c0 < bn; c0 += 32) {
         uint32_t r[32];
         tmem_ld_32x32b_x32(taddr + (uint32_t)c0, r);
         tmem_ld_wait();
-        if (!dst_row) continue;
         const int col0 = n0 + c0;
-        const int ncol = min(32, min(bn - c0, g.D - col0));
+        const int ncol = min(32, min(bn - c0, g.D - col0));  // the same for the whole warp
         if (ncol <= 0) continue;
+        // lane j holds bias[col0 + j]; broadcast it to every row of the warp
+        const float bl = (ep.bias && lane < ncol) ? __ldg(ep.bias + col0 + lane) : 0.0f;
         float v[32];
 #pragma unroll
         for (int j = 0; j < 32; ++j) {
-          float b = (ep.bias && j < ncol) ? __ldg(ep.bias + col0 + j) : 0.0f;
+          const float b = __shfl_sync(0xffffffffu, bl, j);
           v[j] = valid ? __uint_as_float(r[j]) + b : 0.0f;
         }
+        if (!dst_row) continue;
         char* dst = dst_row + (int64_t)col0 * ce;
-        const bool vec = ncol == 32 && ((reinterpret_cast<uintptr_t>(dst) & 15) == 0);
-        if (ep.out_dtype == BJF_DTYPE_F32) {
-          float* o = reinterpret_cast<float*>(dst);
-          if (vec) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              float w8[8] = {v[j], v[j + 1], v[j + 2], v[j + 3], v[j + 4], v[j + 5], v[j + 6], v[j + 7]};
-              store8<float>(o + j, w8);
-            }
-          } else {
-            for (int j = 0; j < ncol; ++j) o[j] = v[j];
-          }
-        } else if (ep.out_dtype == BJF_DTYPE_F16) {
-          __half* o = reinterpret_cast<__half*>(dst);
-          if (vec) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              float w8[8] = {v[j], v[j + 1], v[j + 2], v[j + 3], v[j + 4], v[j + 5], v[j + 6], v[j + 7]};
-              store8<__half>(o + j, w8);
-            }
-          } else {
-            for (int j = 0; j < ncol; ++j) o[j] = __float2half_rn(v[j]);
-          }
-        } else {
-          __nv_bfloat16* o = reinterpret_cast<__nv_bfloat16*>(dst);
-          if (vec) {
-#pragma unroll
-            for (int j = 0; j < 32; j += 8) {
-              float w8[8] = {v[j], v[j + 1], v[j + 2], v[j + 3], v[j + 4], v[j + 5], v[j + 6], v[j + 7]};
-              store8<__nv_bfloat16>(o + j, w8);
-            }
-          } else {
-            for (int j = 0; j < ncol; ++j) o[j] = __float2bfloat16_rn(v[j]);
-          }
-        }
+        if (ep.out_dtype == BJF_DTYPE_F32)
+          store_chunk<float>(dst, v, ncol);
+        else if (ep.out_dtype == BJF_DTYPE_F16)
+          store_chunk<__half>(dst, v, ncol);
+        else
+          store_chunk<__nv_bfloat16>(dst, v, ncol);
       }
-    }
-  } else if (warp == 4) {
-    // ---------------- MMA issuer ----------------
-    if (lane == 0) {
-      const uint32_t idesc = idesc_f16_f32(g.is_bf16 ? 1u : 0u, kBM, (uint32_t)bn);
-      int issued = 0;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % kStages;
-        const uint32_t par = (kb / kStages) & 1;
-        if (!mbar_wait_bounded(&full_a[s], par, abort_flag, kWaitLimitNs) ||
-            !mbar_wait_bounded(&full_b[s], par, abort_flag, kWaitLimitNs)) {
-          aborted = true;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t a_base = a_smem + s * kAStageBytes;
-        const uint32_t b_base = b_smem + s * kBStageBytes;
-#pragma unroll
-        for (int kk = 0; kk < kBK / 16; ++kk) {
-          mma_f16_ss(tmem_base, smem_desc_sw128_kmajor(a_base + kk * 32),
-                     smem_desc_sw128_kmajor(b_base + kk * 32), idesc, (kb | kk) != 0);
-        }
-        ++issued;
-        mma_commit(&empty[s]);
-      }
-      mma_commit(acc_full);
-      if (aborted && issued > 0) {
-        // Let the issued MMAs retire before TMEM is freed (bounded, abort ignored).
-        int zero = 0;
-        mbar_wait_bounded(acc_full, 0, &zero, kWaitLimitNs);
-      }
-    }
-  } else {
-    // ---------------- TMA producer (weight) ----------------
-    if (lane == 0) {
-      int issued = 0;
-      for (int kb = 0; kb < num_kb; ++kb) {
-        const int s = kb % kStages;
-        const uint32_t par = ((kb / kStages) & 1) ^ 1;
-        if (!mbar_wait_bounded(&empty[s], par, abort_flag, kWaitLimitNs)) {
-          aborted = true;
-          break;
-        }
-        mbar_arrive_expect_tx(&full_b[s], (uint32_t)(bn * kBK * 2));
-        tma_load_2d(b_smem + s * kBStageBytes, &wmap, kb * kBK, n0, &full_b[s]);
-        ++issued;
-      }
-      if (aborted) {
-        // Wait for the weight tiles still in flight before the CTA's smem goes away.
-        int zero = 0;
-        for (int kb = max(0, issued - kStages); kb < issued; ++kb)
-          mbar_wait_bounded(&full_b[kb % kStages], (kb / kStages) & 1, &zero, kWaitLimitNs);
-      }
+      // This warp has finished reading accumulator `buf`: hand it back to the MMA warp.
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&acc_empty[buf]);
     }
   }
 
@@ -313,7 +353,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     tmem_dealloc(tmem_base, tmem_cols);
   }
@@ -447,7 +487,8 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
   GatherGeometry g = g0;
   g.num_kb = g.K / kBK;
   g.is_bf16 = in_dt == BJF_DTYPE_BF16;
-  if (sm100_path_supported(dev, g, in_dt, w_dt, input, weight)) {
+  if (sm100_path_supported(dev, g, in_dt, w_dt, input, weight) &&
+      (int64_t)g.C * g.T * g.H * g.W < (int64_t(1) << 31)) {
     EncodeTiledFn encode = nullptr;
     bjf_status rc = encode_tiled_fn(&encode);
     if (rc) return rc;
@@ -476,7 +517,8 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
         g_attr_set[dev.device][slot] = true;
       }
     }
-    dim3 grid((unsigned)ceil_div(g.D, bn), (unsigned)ceil_div(rows_cap, kBM));
+    const int64_t tiles_cap = ceil_div(g.D, bn) * ceil_div(rows_cap, kBM);
+    dim3 grid((unsigned)std::min<int64_t>(tiles_cap, dev.sm_count > 0 ? dev.sm_count : 148));
     if (g.is_bf16)
       gather_gemm_sm100_kernel<__nv_bfloat16><<<grid, kThreads, SmemLayout::alloc, st>>>(
           map, static_cast<const __nv_bfloat16*>(input), coords, rows_dev, (int)rows_cap, g, bn, ep,

@@ -22,6 +22,8 @@
 #include <algorithm>
 #include <cmath>
 
+#include <mutex>
+
 #include "common.cuh"
 #include "patch_diff.hpp"
 #include "status.hpp"
@@ -48,19 +50,22 @@ __device__ __forceinline__ void tubelet_pairs(int t, int kt, int frames, int& fi
   }
 }
 
-// Vectorised scores: one warp per (stream, tubelet, token row, chunk of token
-// columns).  Lane l covers VEC elements of token column (chunk*TPW + l/LPT).
+// Vectorised scores: a work unit is one (stream, tubelet, token row, chunk of token
+// columns); warps stride over the units (persistent grid, 4 blocks of 8 warps per SM at
+// <= 64 registers, so ~128 KB of loads are in flight per SM and the last units leave no
+// idle tail).  Consecutive warps of a block take adjacent column chunks of the same rows.
+// Lane l covers VEC elements of token column (chunk*TPW + l/LPT).
 template <typename T>
-__global__ void __launch_bounds__(kScoreThreads)
+__global__ void __launch_bounds__(kScoreThreads, 4)
     patch_diff_scores_vec_kernel(const T* __restrict__ video, float* __restrict__ scores, int batch,
                                  int channels, int frames, int height, int width, int kt, int P,
                                  int depth, int gh, int gw, int chunks_per_row, long long total_warps) {
   constexpr int VEC = 16 / sizeof(T);
   const int LPT = P / VEC;      // lanes per token column
   const int TPW = 32 / LPT;     // token columns per warp
-  long long wid = (long long)blockIdx.x * (kScoreThreads / 32) + (threadIdx.x >> 5);
-  if (wid >= total_warps) return;
   const int lane = threadIdx.x & 31;
+  for (long long wid = (long long)blockIdx.x * (kScoreThreads / 32) + (threadIdx.x >> 5); wid < total_warps;
+       wid += (long long)gridDim.x * (kScoreThreads / 32)) {
   const int chunk = (int)(wid % chunks_per_row);
   long long rest = wid / chunks_per_row;
   const int r = (int)(rest % gh);
@@ -79,7 +84,7 @@ __global__ void __launch_bounds__(kScoreThreads)
   float* out = scores + s * n_tokens + ((long long)t * gh + r) * gw;
   if (npairs == 0) {
     if (valid && part == 0) out[col] = 0.0f;
-    return;
+    continue;
   }
 
   const long long plane = (long long)height * width;
@@ -109,6 +114,7 @@ __global__ void __launch_bounds__(kScoreThreads)
   if (valid && part == 0) {
     const double denom = (double)npairs * batch * channels * P * P;
     out[col] = acc * (float)(1.0 / denom);
+  }
   }
 }
 
@@ -476,6 +482,22 @@ bjf_status launch_select(const float* scores, int64_t streams, const SelectParam
   return check_launch("dilated patch-diff select launch");
 }
 
+namespace {
+constexpr int kMaxDev = 64;
+std::mutex g_scores_mu;
+int g_sms[kMaxDev] = {};
+
+// SM count of the current device by attribute query (nothing here allocates).
+int sm_count() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return 148;
+  std::lock_guard<std::mutex> lock(g_scores_mu);
+  if (!g_sms[dev] && cudaDeviceGetAttribute(&g_sms[dev], cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    return 148;
+  return g_sms[dev];
+}
+}  // namespace
+
 bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* vd, int64_t streams,
                          int64_t kt, int64_t P, float* scores, cudaStream_t st) {
   const int64_t B = vd[0], C = vd[1], T = vd[2], H = vd[3], W = vd[4];
@@ -493,7 +515,8 @@ bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* vd, in
       const int TPW = 32 / LPT;
       const int chunks = (int)ceil_div(gw, TPW);
       long long warps = (long long)streams * depth * gh * chunks;
-      long long blocks = ceil_div(warps, kScoreThreads / 32);
+      // persistent: a few resident blocks per SM stride over the work units
+      long long blocks = std::min<long long>(ceil_div(warps, kScoreThreads / 32), (long long)sm_count() * 4);
       patch_diff_scores_vec_kernel<T_><<<(unsigned)blocks, kScoreThreads, 0, st>>>(
           static_cast<const T_*>(video), scores, (int)B, (int)C, (int)T, (int)H, (int)W, (int)kt,
           (int)P, (int)depth, (int)gh, (int)gw, chunks, warps);
