@@ -109,6 +109,12 @@ __device__ __forceinline__ void store_chunk(char* dst, const float (&v)[32], int
 // b, b + grid, ... in (m-tile major, n-tile minor) order so concurrently running CTAs share
 // their gathered A rows through L2.  Two TMEM accumulators let the epilogue of one tile
 // overlap the main loop of the next.
+//
+// A producers: a 64-wide K block of a tile row is eight 16-byte runs of image rows.  In
+// one cp.async instruction a warp copies 4 rows x 8 runs (lane = 8 x row + run), lane pairs
+// sharing each 32-byte sector, so an instruction touches 16 sectors rather than 32.  A
+// thread owns one run index j (0..7) of eight rows; after its copies land it fences them
+// into the async proxy and arrives on the stage barrier (wait_group -> fence -> arrive).
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     gather_gemm_sm100_kernel(const __grid_constant__ CUtensorMap wmap, const T* __restrict__ video,
@@ -172,17 +178,26 @@ __global__ void __launch_bounds__(kThreads, 1)
   bool aborted = false;
 
   if (warp >= kEpilogueWarps && warp < kEpilogueWarps + kProducerWarps) {
-    // ---------------- gather producers ----------------
-    const int m = tid - kEpilogueWarps * 32;  // tile row
-    const uint32_t row_off = (uint32_t)((m >> 3) * 1024 + (m & 7) * 128);
-    const uint32_t sw = (uint32_t)(m & 7);
+    // ---------------- gather producers (cp.async) ----------------
+    const int pw_ = warp - kEpilogueWarps;  // producer warp 0..3: tile rows [32 pw_, 32 pw_ + 32)
+    const int j = lane & 7;                 // 16-byte run index within the 128-byte K line
+    const int sub = lane >> 3;              // row within a group of 4
     int kbg = 0;  // k blocks issued by this CTA so far (all tiles)
     for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x) {
-      const int gm = (tile / n_tiles) * kBM + m;
-      bool valid = false;
-      int64_t base = 0;
-      if (gm < M) base = row_base_offset(g, __ldg(coords + gm), valid);
-      const T* src_row = video + base;
+      // this thread's eight rows: m_i = 32 pw_ + 4 i + sub
+      int64_t base[8];
+      uint32_t dst_off[8];
+      uint32_t valid_mask = 0;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int m = 32 * pw_ + 4 * i + sub;
+        const int gm = (tile / n_tiles) * kBM + m;
+        bool valid = false;
+        base[i] = 0;
+        if (gm < M) base[i] = row_base_offset(g, __ldg(coords + gm), valid);
+        valid_mask |= (uint32_t)valid << i;
+        dst_off[i] = (uint32_t)((m >> 3) * 1024 + (m & 7) * 128 + ((j ^ (m & 7)) << 4));
+      }
       for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
         const int s = kbg % kStagesA;
         const uint32_t par = ((kbg / kStagesA) & 1) ^ 1;
@@ -190,12 +205,11 @@ __global__ void __launch_bounds__(kThreads, 1)
           aborted = true;
           break;
         }
-        if (valid) {
-          const uint32_t dst = a_smem + s * kAStageBytes + row_off;
-          const int32_t* ko = koff + kb * 8;
+        const uint32_t dst = a_smem + s * kAStageBytes;
+        const int64_t ko = koff[kb * 8 + j];
 #pragma unroll
-          for (int j = 0; j < 8; ++j) cp_async_16(dst + ((j ^ sw) << 4), src_row + ko[j]);
-        }
+        for (int i = 0; i < 8; ++i)
+          if (valid_mask & (1u << i)) cp_async_16(dst + dst_off[i], video + base[i] + ko);
         cp_async_commit();
         if (kbg >= kLag) {
           cp_async_wait_group<kLag>();
@@ -508,11 +522,9 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
     {
       std::lock_guard<std::mutex> lock(g_attr_mu);
       if (!g_attr_set[dev.device][slot]) {
-        cudaError_t e = g.is_bf16
-                            ? cudaFuncSetAttribute(gather_gemm_sm100_kernel<__nv_bfloat16>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::alloc)
-                            : cudaFuncSetAttribute(gather_gemm_sm100_kernel<__half>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::alloc);
+        const void* fn = g.is_bf16 ? (const void*)gather_gemm_sm100_kernel<__nv_bfloat16>
+                                   : (const void*)gather_gemm_sm100_kernel<__half>;
+        cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, SmemLayout::alloc);
         if (e != cudaSuccess) return cuda_status(e, "gather-GEMM smem attribute");
         g_attr_set[dev.device][slot] = true;
       }
