@@ -44,7 +44,6 @@ constexpr int kBK = 64;
 constexpr int kStagesA = 7;  // gathered tubelet rows (from HBM): deep ring
 constexpr int kStagesB = 3;  // weight tiles (L2-resident): shallow ring
 constexpr int kMaxBN = 256;
-constexpr int kLag = 4;  // cp.async groups a producer keeps in flight before arriving
 constexpr int kEpilogueWarps = 4;   // warps 0-3: TMEM lane quarters 0-3
 constexpr int kProducerWarps = 4;   // warps 4-7: one gathered tile row per thread
 constexpr int kMmaWarp = 8;
@@ -113,8 +112,10 @@ __device__ __forceinline__ void store_chunk(char* dst, const float (&v)[32], int
 // A producers: a 64-wide K block of a tile row is eight 16-byte runs of image rows.  In
 // one cp.async instruction a warp copies 4 rows x 8 runs (lane = 8 x row + run), lane pairs
 // sharing each 32-byte sector, so an instruction touches 16 sectors rather than 32.  A
-// thread owns one run index j (0..7) of eight rows; after its copies land it fences them
-// into the async proxy and arrives on the stage barrier (wait_group -> fence -> arrive).
+// thread owns one run index j (0..7) of eight rows and signals the stage barrier with an
+// asynchronous cp.async arrive, so producers never block on their own copies and keep every
+// free stage in flight; the MMA thread fences the landed stage into the async proxy before
+// issuing on it.
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     gather_gemm_sm100_kernel(const __grid_constant__ CUtensorMap wmap, const T* __restrict__ video,
@@ -210,19 +211,10 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
         for (int i = 0; i < 8; ++i)
           if (valid_mask & (1u << i)) cp_async_16(dst + dst_off[i], video + base[i] + ko);
-        cp_async_commit();
-        if (kbg >= kLag) {
-          cp_async_wait_group<kLag>();
-          fence_proxy_async_smem();
-          mbar_arrive(&full_a[(kbg - kLag) % kStagesA]);
-        }
+        cp_async_arrive_noinc(&full_a[s]);
       }
     }
-    cp_async_wait_all();
-    if (!aborted) {
-      fence_proxy_async_smem();
-      for (int k = max(0, kbg - kLag); k < kbg; ++k) mbar_arrive(&full_a[k % kStagesA]);
-    }
+    cp_async_wait_all();  // nothing of this thread may still be landing when the CTA exits
   } else if (warp == kMmaWarp) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
@@ -246,6 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             aborted = true;
             break;
           }
+          fence_proxy_async_smem();  // the stage's cp.async writes, acquired above, feed the MMA
           tc_fence_after();
           const uint32_t a_base = a_smem + sa * kAStageBytes;
           const uint32_t b_base = b_smem + sb * kBStageBytes;

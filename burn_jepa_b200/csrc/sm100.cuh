@@ -85,6 +85,12 @@ __device__ __forceinline__ void cp_async_wait_group() {
 }
 __device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
 
+// Arrives on `bar` (counted against its expected arrivals) once every cp.async this thread
+// issued before has completed; the thread itself does not wait.
+__device__ __forceinline__ void cp_async_arrive_noinc(uint64_t* bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 // Makes this thread's completed generic-proxy shared-memory writes visible to
 // later async-proxy readers (tcgen05.mma operands).
 __device__ __forceinline__ void fence_proxy_async_smem() {
