@@ -6,6 +6,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 #include "../../include/bjf.h"
 
 namespace bjf {
@@ -102,6 +104,35 @@ __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
 }
 
 __host__ __device__ constexpr int64_t ceil_div(int64_t a, int64_t b) { return (a + b - 1) / b; }
+
+// Programmatic dependent launch.  A kernel launched with pdl = true may start while the
+// kernel before it in the stream is still running; pdl_wait() blocks until that kernel has
+// completed and its writes are visible (it returns at once for an ordinary launch).
+// pdl_trigger() lets the next kernel of the stream, if it was launched with pdl = true,
+// start before this one completes.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+// Launches `kernel`, optionally as a programmatic dependent of the previous kernel.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_kernel(bool pdl, void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                                 cudaStream_t st, Args&&... args) {
+  if (!pdl) {
+    kernel<<<grid, block, smem, st>>>(std::forward<Args>(args)...);
+    return cudaGetLastError();
+  }
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 inline size_t dtype_size(int32_t dt) {
   switch (dt) {

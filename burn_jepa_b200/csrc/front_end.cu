@@ -9,6 +9,10 @@
 //                                 epilogue adds the bias and writes each row straight into
 //                                 its stream's token cache slot, setting observed = 1, age = 0
 //
+// The four kernels are chained with programmatic dependent launch: each waits for its
+// predecessor only where it reads that predecessor's output, and the patch-diff pass of the
+// next frame may run alongside this frame's GEMM (HBM-bound next to tensor-bound work).
+//
 // This is the composition the reference pipeline performs per stream and per frame
 // (patch_diff_context_mask -> SparsePatchifyPlan::new -> sparse_patchify3d_forward_cuda ->
 // update_tokens_tiled_assign_cuda_raw, src/nodes.rs:411-456, src/sparse_patchify.rs:236-269,
@@ -110,15 +114,15 @@ extern "C" bjf_status bjf_front_end_step(const bjf_front_end_desc* d, const void
   cudaStream_t st = as_cuda(stream);
 
   const int64_t vd[5] = {1, d->channels, d->frames, d->height, d->width};
-  rc = launch_scores(video, d->video_dtype, vd, S, d->tubelet_size, d->patch_size, scores, st);
+  rc = launch_scores(video, d->video_dtype, vd, S, d->tubelet_size, d->patch_size, scores, st, true);
   if (rc) return rc;
   if (age_observed) {
     sel.age = age_frames;
     sel.observed = observed;
   }
-  rc = launch_select(scores, S, sel, indices, counts, st);
+  rc = launch_select(scores, S, sel, indices, counts, st, true);
   if (rc) return rc;
-  rc = bjf_sparse_patchify_plan_coords(indices, N, counts, S, S, grid, coords, S * N, total, stream);
+  rc = launch_plan(indices, N, counts, S, S, grid, coords, S * N, total, st, true);
   if (rc) return rc;
 
   GatherGeometry g{};
@@ -146,5 +150,5 @@ extern "C" bjf_status bjf_front_end_step(const bjf_front_end_desc* d, const void
   ep.age = age_frames;
   ep.bias = bias;
   return launch_gather_gemm(*dev, video, d->video_dtype, weight, d->weight_dtype, g,
-                            reinterpret_cast<const int4*>(coords), total, S * N, ep, st);
+                            reinterpret_cast<const int4*>(coords), total, S * N, ep, st, true);
 }

@@ -127,6 +127,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int warp = tid >> 5;
   const int lane = tid & 31;
 
+  pdl_wait();     // coords / row count come from the kernels before (plan, selection)
+  pdl_trigger();  // the next frame's patch-diff pass may start alongside this GEMM
   int M = rows_cap;
   if (rows_dev) M = min(M, max(0, __ldg(rows_dev)));
   const int n_tiles = (g.D + bn - 1) / bn;
@@ -382,6 +384,8 @@ __global__ void __launch_bounds__(kSThreads)
   __shared__ int row_valid[kSBM];
   __shared__ int64_t koffs[kSBK];
 
+  pdl_wait();
+  pdl_trigger();
   int M = rows_cap;
   if (rows_dev) M = min(M, max(0, __ldg(rows_dev)));
   const int m0 = blockIdx.y * kSBM;
@@ -489,7 +493,7 @@ bool sm100_path_supported(const DeviceInfo& dev, const GatherGeometry& g, int32_
 bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t in_dt,
                               const void* weight, int32_t w_dt, const GatherGeometry& g0,
                               const int4* coords, const int32_t* rows_dev, int64_t rows_cap,
-                              const EpilogueArgs& ep, cudaStream_t st) {
+                              const EpilogueArgs& ep, cudaStream_t st, bool pdl) {
   if (rows_cap <= 0 || g0.D <= 0) return BJF_OK;
   GatherGeometry g = g0;
   g.num_kb = g.K / kBK;
@@ -524,21 +528,24 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
     }
     const int64_t tiles_cap = ceil_div(g.D, bn) * ceil_div(rows_cap, kBM);
     dim3 grid((unsigned)std::min<int64_t>(tiles_cap, dev.sm_count > 0 ? dev.sm_count : 148));
+    cudaError_t e;
     if (g.is_bf16)
-      gather_gemm_sm100_kernel<__nv_bfloat16><<<grid, kThreads, SmemLayout::alloc, st>>>(
-          map, static_cast<const __nv_bfloat16*>(input), coords, rows_dev, (int)rows_cap, g, bn, ep,
-          dev.error_flag);
+      e = launch_kernel(pdl, gather_gemm_sm100_kernel<__nv_bfloat16>, grid, dim3(kThreads), SmemLayout::alloc, st,
+                        map, static_cast<const __nv_bfloat16*>(input), coords, rows_dev, (int)rows_cap, g, bn, ep,
+                        dev.error_flag);
     else
-      gather_gemm_sm100_kernel<__half><<<grid, kThreads, SmemLayout::alloc, st>>>(
-          map, static_cast<const __half*>(input), coords, rows_dev, (int)rows_cap, g, bn, ep, dev.error_flag);
-    return check_launch("gather-GEMM (tcgen05) launch");
+      e = launch_kernel(pdl, gather_gemm_sm100_kernel<__half>, grid, dim3(kThreads), SmemLayout::alloc, st, map,
+                        static_cast<const __half*>(input), coords, rows_dev, (int)rows_cap, g, bn, ep,
+                        dev.error_flag);
+    return e == cudaSuccess ? BJF_OK : cuda_status(e, "gather-GEMM (tcgen05) launch");
   }
   dim3 grid((unsigned)ceil_div(g.D, kSBN), (unsigned)ceil_div(rows_cap, kSBM));
   bool ok = dispatch_float(in_dt, [&](auto itag) {
     dispatch_float(w_dt, [&](auto wtag) {
-      gather_gemm_simt_kernel<decltype(itag), decltype(wtag)><<<grid, kSThreads, 0, st>>>(
-          static_cast<const decltype(itag)*>(input), coords, rows_dev, (int)rows_cap, g,
-          static_cast<const decltype(wtag)*>(weight), ep);
+      cudaError_t e = launch_kernel(pdl, gather_gemm_simt_kernel<decltype(itag), decltype(wtag)>, grid,
+                                    dim3(kSThreads), 0, st, static_cast<const decltype(itag)*>(input), coords,
+                                    rows_dev, (int)rows_cap, g, static_cast<const decltype(wtag)*>(weight), ep);
+      if (e != cudaSuccess) cuda_status(e, "gather-GEMM (SIMT) launch");
     });
   });
   if (!ok) return fail(BJF_ERR_INVALID_ARGUMENT, "input dtype must be f32, f16 or bf16");

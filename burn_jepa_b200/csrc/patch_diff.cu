@@ -116,6 +116,10 @@ __global__ void __launch_bounds__(kScoreThreads, 4)
     out[col] = acc * (float)(1.0 / denom);
   }
   }
+  // Launched as a programmatic dependent, this pass may overlap the kernel before it (the
+  // previous frame's gather-GEMM, which none of its inputs depend on); it still does not
+  // complete before that kernel, so everything after it in the stream sees both finished.
+  pdl_wait();
 }
 
 // Generic scores (any patch size / alignment): one thread per token.
@@ -124,6 +128,7 @@ __global__ void __launch_bounds__(kScoreThreads)
     patch_diff_scores_scalar_kernel(const T* __restrict__ video, float* __restrict__ scores,
                                     int batch, int channels, int frames, int height, int width,
                                     int kt, int P, int depth, int gh, int gw, long long total) {
+  pdl_wait();
   long long i = (long long)blockIdx.x * kScoreThreads + threadIdx.x;
   if (i >= total) return;
   const long long n_tokens = (long long)depth * gh * gw;
@@ -227,6 +232,7 @@ __global__ void __launch_bounds__(kSelectThreads)
   __shared__ uint32_t sel_prefix;
   __shared__ int sel_remaining;
 
+  pdl_wait();
   const int n = p.n;
   const long long s = blockIdx.x;
   const float* sc = scores + s * n;
@@ -345,6 +351,7 @@ __global__ void __launch_bounds__(kSelectThreads)
   __shared__ int warp_sums[33];
   __shared__ int use_sequential;
 
+  pdl_wait();
   const int n = p.n;
   const long long s = blockIdx.x;
   const float* sc = scores + s * n;
@@ -457,7 +464,7 @@ bjf_status resolve_select(const bjf_patch_diff_config* cfg, const int64_t* grid,
 }
 
 bjf_status launch_select(const float* scores, int64_t streams, const SelectParams& p,
-                         int32_t* indices, int32_t* counts, cudaStream_t st) {
+                         int32_t* indices, int32_t* counts, cudaStream_t st, bool pdl) {
   if (p.dilation == 0) {
     if (p.n > kMaxSelectTokens)
       return fail(BJF_ERR_UNSUPPORTED, "patch-diff selection supports grids up to 32768 tokens");
@@ -465,8 +472,9 @@ bjf_status launch_select(const float* scores, int64_t streams, const SelectParam
     cudaError_t e = cudaFuncSetAttribute(patch_diff_select_kernel,
                                          cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
     if (e != cudaSuccess) return cuda_status(e, "patch-diff select attribute");
-    patch_diff_select_kernel<<<(unsigned)streams, kSelectThreads, smem, st>>>(scores, p, indices, counts);
-    return check_launch("patch-diff select launch");
+    e = launch_kernel(pdl, patch_diff_select_kernel, dim3((unsigned)streams), dim3(kSelectThreads), smem, st,
+                      scores, p, indices, counts);
+    return e == cudaSuccess ? BJF_OK : cuda_status(e, "patch-diff select launch");
   }
   if (p.n > kMaxDilatedTokens)
     return fail(BJF_ERR_UNSUPPORTED, "dilated patch-diff selection supports grids up to 16384 tokens");
@@ -477,9 +485,9 @@ bjf_status launch_select(const float* scores, int64_t streams, const SelectParam
   cudaError_t e = cudaFuncSetAttribute(patch_diff_select_dilated_kernel,
                                        cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return cuda_status(e, "dilated select attribute");
-  patch_diff_select_dilated_kernel<<<(unsigned)streams, kSelectThreads, smem, st>>>(scores, p, npow2,
-                                                                                   indices, counts);
-  return check_launch("dilated patch-diff select launch");
+  e = launch_kernel(pdl, patch_diff_select_dilated_kernel, dim3((unsigned)streams), dim3(kSelectThreads), smem,
+                    st, scores, p, npow2, indices, counts);
+  return e == cudaSuccess ? BJF_OK : cuda_status(e, "dilated patch-diff select launch");
 }
 
 namespace {
@@ -499,7 +507,7 @@ int sm_count() {
 }  // namespace
 
 bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* vd, int64_t streams,
-                         int64_t kt, int64_t P, float* scores, cudaStream_t st) {
+                         int64_t kt, int64_t P, float* scores, cudaStream_t st, bool pdl) {
   const int64_t B = vd[0], C = vd[1], T = vd[2], H = vd[3], W = vd[4];
   const int64_t depth = T / kt, gh = H / P, gw = W / P;
   const int64_t n_tok = depth * gh * gw;
@@ -517,9 +525,12 @@ bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* vd, in
       long long warps = (long long)streams * depth * gh * chunks;
       // persistent: a few resident blocks per SM stride over the work units
       long long blocks = std::min<long long>(ceil_div(warps, kScoreThreads / 32), (long long)sm_count() * 4);
-      patch_diff_scores_vec_kernel<T_><<<(unsigned)blocks, kScoreThreads, 0, st>>>(
-          static_cast<const T_*>(video), scores, (int)B, (int)C, (int)T, (int)H, (int)W, (int)kt,
-          (int)P, (int)depth, (int)gh, (int)gw, chunks, warps);
+      cudaError_t e = launch_kernel(pdl, patch_diff_scores_vec_kernel<T_>, dim3((unsigned)blocks),
+                                    dim3(kScoreThreads), 0, st, static_cast<const T_*>(video), scores, (int)B,
+                                    (int)C, (int)T, (int)H, (int)W, (int)kt, (int)P, (int)depth, (int)gh,
+                                    (int)gw, chunks, warps);
+      rc = e == cudaSuccess ? BJF_OK : cuda_status(e, "patch-diff scores launch");
+      return;
     } else {
       long long total = (long long)streams * n_tok;
       patch_diff_scores_scalar_kernel<T_><<<(unsigned)ceil_div(total, kScoreThreads), kScoreThreads, 0, st>>>(

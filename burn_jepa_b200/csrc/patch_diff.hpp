@@ -26,10 +26,16 @@ bjf_status resolve_select(const bjf_patch_diff_config* cfg, const int64_t* grid,
 
 // One CTA per stream: selection (and optional aging) -> indices [streams, n], counts [streams].
 bjf_status launch_select(const float* scores, int64_t streams, const SelectParams& p, int32_t* indices,
-                         int32_t* counts, cudaStream_t st);
+                         int32_t* counts, cudaStream_t st, bool pdl = false);
 
 // Per-tubelet mean |delta| scores for `streams` videos [B, C, T, H, W] -> [streams, N].
 bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* video_dims, int64_t streams,
-                         int64_t tubelet_size, int64_t patch_size, float* scores, cudaStream_t st);
+                         int64_t tubelet_size, int64_t patch_size, float* scores, cudaStream_t st,
+                         bool pdl = false);
+
+// Device plan (coords rows) from per-stream mask indices; see bjf_sparse_patchify_plan_coords.
+bjf_status launch_plan(const int32_t* indices, int64_t index_stride, const int32_t* counts, int64_t mask_rows,
+                       int64_t batch, const int64_t grid[3], int32_t* coords, int64_t coords_capacity,
+                       int32_t* total_rows, cudaStream_t st, bool pdl = false);
 
 }  // namespace bjf

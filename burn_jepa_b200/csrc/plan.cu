@@ -7,6 +7,7 @@
 // new mask never crosses PCIe.  Token index -> (tubelet, row, col) follows
 // token_index_to_coords (src/positional.rs:10-17).
 #include "common.cuh"
+#include "patch_diff.hpp"
 #include "status.hpp"
 
 namespace bjf {
@@ -21,6 +22,7 @@ __global__ void __launch_bounds__(kPlanThreads)
                        int gh, int gw, int4* __restrict__ coords, long long capacity,
                        int32_t* __restrict__ total_rows) {
   __shared__ long long offsets[kMaxPlanBatch + 1];
+  pdl_wait();  // indices / counts come from the kernel before (the selection)
   // Row offsets: exclusive prefix of the per-batch-row lengths (computed by every CTA).
   if (threadIdx.x == 0) {
     long long acc = 0;
@@ -71,11 +73,11 @@ __global__ void __launch_bounds__(kPlanThreads)
 
 using namespace bjf;
 
-extern "C" bjf_status bjf_sparse_patchify_plan_coords(const int32_t* indices, int64_t index_stride,
-                                                      const int32_t* counts, int64_t mask_rows,
-                                                      int64_t batch, const int64_t grid[3],
-                                                      int32_t* coords, int64_t coords_capacity,
-                                                      int32_t* total_rows, bjf_stream_t stream) {
+namespace bjf {
+
+bjf_status launch_plan(const int32_t* indices, int64_t index_stride, const int32_t* counts, int64_t mask_rows,
+                       int64_t batch, const int64_t grid[3], int32_t* coords, int64_t coords_capacity,
+                       int32_t* total_rows, cudaStream_t st, bool pdl) {
   if (batch <= 0) return fail(BJF_ERR_INVALID_ARGUMENT, "sparse patchify batch must be nonzero");
   if (!grid || grid[0] <= 0 || grid[1] <= 0 || grid[2] <= 0)
     return fail(BJF_ERR_INVALID_ARGUMENT, "sparse patchify grid must be non-empty");
@@ -90,8 +92,20 @@ extern "C" bjf_status bjf_sparse_patchify_plan_coords(const int32_t* indices, in
   if (reinterpret_cast<uintptr_t>(coords) % 16 != 0)
     return fail(BJF_ERR_INVALID_ARGUMENT, "coords must be 16-byte aligned");
   int blocks = (int)(batch < 1184 ? batch : 1184);
-  plan_coords_kernel<<<blocks, kPlanThreads, 0, as_cuda(stream)>>>(
-      indices, (int)index_stride, counts, (int)mask_rows, (int)batch, (int)grid[0], (int)grid[1],
-      (int)grid[2], reinterpret_cast<int4*>(coords), coords_capacity, total_rows);
-  return check_launch("sparse patchify plan launch");
+  cudaError_t e = launch_kernel(pdl, plan_coords_kernel, dim3(blocks), dim3(kPlanThreads), 0, st, indices,
+                                (int)index_stride, counts, (int)mask_rows, (int)batch, (int)grid[0], (int)grid[1],
+                                (int)grid[2], reinterpret_cast<int4*>(coords), (long long)coords_capacity,
+                                total_rows);
+  return e == cudaSuccess ? BJF_OK : cuda_status(e, "sparse patchify plan launch");
+}
+
+}  // namespace bjf
+
+extern "C" bjf_status bjf_sparse_patchify_plan_coords(const int32_t* indices, int64_t index_stride,
+                                                      const int32_t* counts, int64_t mask_rows,
+                                                      int64_t batch, const int64_t grid[3],
+                                                      int32_t* coords, int64_t coords_capacity,
+                                                      int32_t* total_rows, bjf_stream_t stream) {
+  return launch_plan(indices, index_stride, counts, mask_rows, batch, grid, coords, coords_capacity, total_rows,
+                     as_cuda(stream), false);
 }

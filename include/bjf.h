@@ -229,7 +229,9 @@ BJF_API size_t bjf_front_end_workspace_bytes(const bjf_front_end_desc* desc);
  * each stream's token cache.  age_observed: the memory has stepped before (step > 0).
  * weight [D, C, kt, P, P]; bias [D] f32 or NULL.  workspace: 256-byte aligned device
  * memory of bjf_front_end_workspace_bytes(desc) bytes.  counts_out (device, nullable):
- * [S] int32 active tubelets per stream. */
+ * [S] int32 active tubelets per stream.  Consecutive steps on one stream may overlap on the
+ * device (a step's patch-diff pass starts beside the previous step's GEMM); results are as
+ * if they ran one after another. */
 BJF_API bjf_status bjf_front_end_step(const bjf_front_end_desc* desc, const void* video,
                                       const void* weight, const float* bias, void* caches,
                                       float* observed, float* age_frames, int32_t age_observed,
