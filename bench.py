@@ -142,28 +142,12 @@ def dist_setup():
     if world > 1:
         import datetime
 
+        import torch
         import torch.distributed as dist
 
+        torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300))
     return world, rank, local
-
-
-def all_reduce(value: float, op: str, world: int, device):
-    if world == 1:
-        return value
-    import torch
-    import torch.distributed as dist
-
-    t = torch.tensor([value], dtype=torch.float64, device=device)
-    dist.all_reduce(t, op=dist.ReduceOp.MAX if op == "max" else dist.ReduceOp.SUM)
-    return float(t.item())
-
-
-def barrier(world):
-    if world > 1:
-        import torch.distributed as dist
-
-        dist.barrier()
 
 
 # ---------------------------------------------------------------------------
@@ -200,10 +184,15 @@ def cpu_front_end_rate(video_f32_streams, weight_f32, bias_f32, thr, budget_s=15
 # GPU leg
 # ---------------------------------------------------------------------------
 def make_inputs(torch, dev, streams, density, seed_base):
-    from burn_jepa_b200 import workloads
+    """Two input sets of this rank's global streams; each stream's clip depends only on its
+    global id, so a stream's content is the same at every GPU count."""
+    from burn_jepa_b200 import sharding, workloads
 
-    sets = [workloads.rect_perturbation_clips_torch(seed_base + 1000 * i, streams, C, T, H, W, density, dev,
-                                                    torch.float16) for i in range(2)]
+    sets = []
+    for i in range(2):
+        clips = [workloads.rect_perturbation_clips_torch(sharding.stream_seed(seed_base + 1000 * i, gs), 1, C, T, H, W,
+                                                         density, dev, torch.float16) for gs in streams]
+        sets.append(torch.cat(clips))
     return sets
 
 
@@ -212,22 +201,25 @@ def run_ours(args, world, rank, local):
     import torch
 
     import burn_jepa_b200 as bj
-    from burn_jepa_b200 import workloads
+    from burn_jepa_b200 import sharding, workloads
 
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
+    group = sharding.RankGroup(device=dev)
     S = args.streams
+    mine = sharding.shard_streams(S * world, world, rank)  # weak scaling: S streams per GPU
     hbm_peak, tflops_peak, peak_kind = read_peaks()
 
     weight = torch.from_numpy(workloads.normal(11, (D, C, KT, P, P), std=0.02)).to(dev, torch.float16)
     bias = torch.from_numpy(workloads.normal(12, (D,), std=0.02)).to(dev)
 
     def setup(density):
-        videos = make_inputs(torch, dev, S, density, seed_base=7 + 100003 * rank + int(density * 1e4))
+        videos = make_inputs(torch, dev, mine, density, seed_base=7 + int(density * 1e4))
         # threshold: tubelets the rectangles do not touch score exactly 0, so any small positive
-        # threshold keeps exactly the changed tubelets; take it inside a score gap
+        # threshold keeps exactly the changed tubelets; take it inside a score gap of the first
+        # global streams (rank 0's) and use it on every rank
         sc = bj.patch_diff_token_scores(videos[0][:4].unsqueeze(1), KT, P).cpu().numpy().ravel()
-        thr = workloads.choose_threshold(sc, density, 1e-3)
+        thr = group.broadcast_object(workloads.choose_threshold(sc, density, 1e-3))
         mask = bj.PatchDiffConfig.adaptive_threshold(thr, 1, N_TOKENS, 1)
         fe = bj.FrontEnd(S, C, T, H, W, KT, P, D, mask, torch.float16, torch.float16, dev)
         caches = torch.randn((S, N_TOKENS, D), device=dev, dtype=torch.float32).to(torch.float16)
@@ -250,7 +242,7 @@ def run_ours(args, world, rank, local):
             for i in range(64):
                 fe.step(videos[i % 2], weight, bias, caches, observed, age)
             torch.cuda.synchronize()
-        barrier(world)
+        group.barrier()
         torch.cuda.synchronize()
         start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         start.record(stream)
@@ -258,7 +250,7 @@ def run_ours(args, world, rank, local):
             fe.step(videos[i % 2], weight, bias, caches, observed, age)
         end.record(stream)
         torch.cuda.synchronize()
-        barrier(world)
+        group.barrier()
         torch.cuda.synchronize()
         return start.elapsed_time(end) / 1000.0
 
@@ -270,10 +262,10 @@ def run_ours(args, world, rank, local):
     with ClockSampler(gpu_id) as clocks:
         secs = time_steps(fe, videos, caches, observed, age, args.steps, args.warmup, load_s=2.0)
     tubelets = sum(counts_per_set[i % 2] for i in range(args.steps))
-    max_secs = all_reduce(secs, "max", world, dev)
-    all_tubelets = all_reduce(float(tubelets), "sum", world, dev)
+    max_secs = group.max(secs)
+    all_tubelets = group.sum(float(tubelets))
     value = all_tubelets / max_secs
-    frames_per_s = all_reduce(float(S * args.steps), "sum", world, dev) / max_secs
+    frames_per_s = group.sum(float(S * args.steps)) / max_secs
     assert not bj.device_error_check(), "a kernel reported a bounded-wait timeout"
 
     # ---- per-kernel timings (CUDA events on the launching stream) ----
@@ -341,7 +333,7 @@ def run_ours(args, world, rank, local):
         fe.step(dev_video, weight, bias, caches, observed, age)
         counts_host.copy_(fe.counts, non_blocking=True)
     torch.cuda.synchronize()
-    barrier(world)
+    group.barrier()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record(stream)
     e2e_tub = 0
@@ -352,8 +344,8 @@ def run_ours(args, world, rank, local):
         e2e_tub += counts_per_set[i % 2]
     b.record(stream)
     torch.cuda.synchronize()
-    e2e_secs = all_reduce(a.elapsed_time(b) / 1e3, "max", world, dev)
-    e2e_value = all_reduce(float(e2e_tub), "sum", world, dev) / e2e_secs
+    e2e_secs = group.max(a.elapsed_time(b) / 1e3)
+    e2e_value = group.sum(float(e2e_tub)) / e2e_secs
     h2d = S * C * T * H * W * 2
 
     sweep = None
@@ -365,10 +357,10 @@ def run_ours(args, world, rank, local):
             videos2, thr2, fe, caches, observed, age, cps = setup(dens)
             s2 = time_steps(fe, videos2, caches, observed, age, args.steps, args.warmup)
             tub2 = sum(cps[i % 2] for i in range(args.steps))
-            s2m = all_reduce(s2, "max", world, dev)
+            s2m = group.max(s2)
             sweep[f"{int(dens * 100)}%"] = {
                 "active_fraction": round(statistics.mean(cps) / (S * N_TOKENS), 4),
-                "value": round(all_reduce(float(tub2), "sum", world, dev) / s2m, 1),
+                "value": round(group.sum(float(tub2)) / s2m, 1),
                 "ms_per_step": round(s2m / args.steps * 1e3, 4)}
             del videos2
 

@@ -1,0 +1,790 @@
+// bjf.hpp -- C++ host API of the B200 sparse front end, layered on the C ABI in bjf.h.
+//
+// It mirrors the Rust types and calls of burn_jepa 0.21.0 that a caller of the sparse
+// front end uses, with the same names, argument meaning and error texts, so that code
+// written against the reference reads the same here:
+//
+//   TokenGridShape, token_index_to_coords, coords_to_token_index   src/tokens.rs:5-32,
+//                                                                  src/positional.rs:10-21
+//   SparseTokenMask (+ make_context_target_masks, ...)             src/tokens.rs:34-179, 477-528
+//   SparseJepaPatchDiffSparsityConfig                              src/nodes.rs:97-157
+//   patch_diff_token_scores / patch_diff_context_mask_from_scores /
+//   patch_diff_context_mask_from_video                             src/nodes.rs:411-631
+//   SparsePatchifyPlan, SparsePatchifyBatchPlan                    src/sparse_patchify.rs:236-330
+//   SparsePatchify3dConfig, sparse_patchify3d_forward_cuda         burn_flex_gmm 0.21.2, called at
+//                                                                  src/model.rs:1297-1327
+//   InterframeJepaFeatureMemory (+ update_tokens_tiled_assign_cuda) src/feature_memory.rs:137-645
+//   FrontEnd (one frame step over S streams)                       src/highres_pipeline.rs:2021-2040
+//
+// Rust's Result<T> becomes a return value or a thrown bjf::Error carrying the status and
+// the message (the reference's wording where it has one).  Device tensors are bjf::Tensor:
+// an owning, contiguous device buffer with a dtype and a shape.  All work is enqueued on
+// the caller's CUDA stream; functions that return host data (masks, to_host) synchronise
+// that stream, as the reference's own readbacks do.
+//
+// Header-only C++17; link with libbjf.so and the CUDA runtime.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <array>
+#include <cmath>
+#include <cstdint>
+#include <cstring>
+#include <stdexcept>
+#include <string>
+#include <tuple>
+#include <utility>
+#include <vector>
+
+#include "bjf.h"
+
+namespace bjf {
+
+// ---------------------------------------------------------------------------------------
+// errors
+// ---------------------------------------------------------------------------------------
+class Error : public std::runtime_error {
+ public:
+  Error(bjf_status status, const std::string& message) : std::runtime_error(message), status_(status) {}
+  bjf_status status() const { return status_; }
+
+ private:
+  bjf_status status_;
+};
+
+inline std::string last_error_string() {
+  char buf[2048];
+  bjf_get_last_error_string(buf, sizeof(buf));
+  return std::string(buf);
+}
+
+// Throws the library's last error when `st` is not BJF_OK.
+inline void check(bjf_status st) {
+  if (st != BJF_OK) throw Error(st, last_error_string());
+}
+
+// The reference's `ensure!(cond, msg)`.
+inline void ensure(bool cond, const char* message) {
+  if (!cond) throw Error(BJF_ERR_INVALID_ARGUMENT, message);
+}
+
+inline void check_cuda(cudaError_t e, const char* what) {
+  if (e != cudaSuccess) throw Error(BJF_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+inline bjf_stream_t to_bjf(cudaStream_t s) { return reinterpret_cast<bjf_stream_t>(s); }
+
+// ---------------------------------------------------------------------------------------
+// token grid and index math (src/tokens.rs:5-32, src/positional.rs:10-21)
+// ---------------------------------------------------------------------------------------
+struct TokenGridShape {
+  size_t depth = 0, height = 0, width = 0;
+
+  constexpr TokenGridShape() = default;
+  constexpr TokenGridShape(size_t d, size_t h, size_t w) : depth(d), height(h), width(w) {}
+  static constexpr TokenGridShape new_(size_t d, size_t h, size_t w) { return TokenGridShape(d, h, w); }
+
+  constexpr size_t len() const { return depth * height * width; }
+  constexpr bool is_empty() const { return depth == 0 || height == 0 || width == 0; }
+  constexpr size_t tokens_per_frame() const { return height * width; }
+  constexpr bool operator==(const TokenGridShape& o) const {
+    return depth == o.depth && height == o.height && width == o.width;
+  }
+  constexpr bool operator!=(const TokenGridShape& o) const { return !(*this == o); }
+  std::array<int64_t, 3> dims() const { return {(int64_t)depth, (int64_t)height, (int64_t)width}; }
+};
+
+inline std::tuple<size_t, size_t, size_t> token_index_to_coords(size_t index, TokenGridShape grid) {
+  const size_t tpf = std::max<size_t>(grid.tokens_per_frame(), 1);
+  const size_t w = std::max<size_t>(grid.width, 1);
+  const size_t frame = index / tpf;
+  const size_t rem = index - frame * tpf;
+  const size_t row = rem / w;
+  return {frame, row, rem - row * w};
+}
+
+inline size_t coords_to_token_index(size_t frame, size_t row, size_t col, TokenGridShape grid) {
+  return frame * grid.tokens_per_frame() + row * grid.width + col;
+}
+
+// ---------------------------------------------------------------------------------------
+// SparseTokenMask (src/tokens.rs:34-179): sorted, unique token indices into a dense grid.
+// ---------------------------------------------------------------------------------------
+class SparseTokenMask {
+ public:
+  SparseTokenMask() = default;
+
+  // Sorts and dedups; errors as SparseTokenMask::new (src/tokens.rs:41-50).
+  static SparseTokenMask new_(std::vector<size_t> indices, size_t dense_len) {
+    std::sort(indices.begin(), indices.end());
+    indices.erase(std::unique(indices.begin(), indices.end()), indices.end());
+    ensure(dense_len > 0, "dense token count must be nonzero");
+    ensure(std::all_of(indices.begin(), indices.end(), [&](size_t i) { return i < dense_len; }),
+           "sparse token index outside dense token range");
+    return SparseTokenMask(std::move(indices), dense_len);
+  }
+
+  static SparseTokenMask from_keep_ratio(size_t dense_len, float keep_ratio) {
+    const float r = std::min(std::max(keep_ratio, 0.0f), 1.0f);
+    size_t keep = (size_t)std::ceil((float)dense_len * r);
+    keep = std::min(std::max<size_t>(keep, 1), std::max<size_t>(dense_len, 1));
+    std::vector<size_t> idx(keep);
+    for (size_t i = 0; i < keep; ++i) idx[i] = i;
+    return SparseTokenMask(std::move(idx), dense_len);
+  }
+
+  static std::vector<size_t> evenly_spaced_indices(size_t dense_len, size_t keep) {
+    keep = std::min(std::max<size_t>(keep, 1), std::max<size_t>(dense_len, 1));
+    std::vector<size_t> out;
+    if (keep == dense_len) {
+      for (size_t i = 0; i < dense_len; ++i) out.push_back(i);
+      return out;
+    }
+    const size_t last = dense_len ? dense_len - 1 : 0;
+    for (size_t i = 0; i < keep; ++i) out.push_back((i * last + keep / 2) / keep);
+    return out;
+  }
+
+  static SparseTokenMask evenly_spaced(size_t dense_len, size_t keep) {
+    return new_(evenly_spaced_indices(dense_len, keep), dense_len);
+  }
+
+  static SparseTokenMask all(size_t dense_len) {
+    std::vector<size_t> idx(dense_len);
+    for (size_t i = 0; i < dense_len; ++i) idx[i] = i;
+    return SparseTokenMask(std::move(idx), dense_len);
+  }
+
+  bool is_dense_ordered() const {
+    if (indices_.size() != dense_len_) return false;
+    for (size_t i = 0; i < indices_.size(); ++i)
+      if (indices_[i] != i) return false;
+    return true;
+  }
+
+  // Keeps every index and adds evenly spaced ones, then the lowest missing ones, up to
+  // target_len (src/tokens.rs:94-128).
+  SparseTokenMask padded_to_len(size_t target_len) const {
+    if (target_len <= indices_.size()) return *this;
+    if (target_len >= dense_len_) return all(dense_len_);
+    std::vector<bool> keep(dense_len_, false);
+    std::vector<size_t> idx = indices_;
+    for (size_t i : idx) keep[i] = true;
+    for (size_t i : evenly_spaced_indices(dense_len_, target_len)) {
+      if (!keep[i]) {
+        keep[i] = true;
+        idx.push_back(i);
+        if (idx.size() >= target_len) break;
+      }
+    }
+    for (size_t i = 0; idx.size() < target_len && i < dense_len_; ++i) {
+      if (!keep[i]) {
+        keep[i] = true;
+        idx.push_back(i);
+      }
+    }
+    return new_(std::move(idx), dense_len_);
+  }
+
+  SparseTokenMask padded_to_multiple(size_t multiple) const {
+    if (multiple <= 1 || indices_.size() >= dense_len_) return *this;
+    const size_t target = std::min((indices_.size() + multiple - 1) / multiple * multiple, dense_len_);
+    return padded_to_len(target);
+  }
+
+  SparseTokenMask complement() const {
+    std::vector<bool> keep(dense_len_, false);
+    for (size_t i : indices_) keep[i] = true;
+    std::vector<size_t> idx;
+    for (size_t i = 0; i < dense_len_; ++i)
+      if (!keep[i]) idx.push_back(i);
+    return SparseTokenMask(std::move(idx), dense_len_);
+  }
+
+  const std::vector<size_t>& indices() const { return indices_; }
+  size_t dense_len() const { return dense_len_; }
+  size_t len() const { return indices_.size(); }
+  bool is_empty() const { return indices_.empty(); }
+  bool operator==(const SparseTokenMask& o) const { return dense_len_ == o.dense_len_ && indices_ == o.indices_; }
+
+ private:
+  SparseTokenMask(std::vector<size_t> idx, size_t dense_len) : indices_(std::move(idx)), dense_len_(dense_len) {}
+  std::vector<size_t> indices_;
+  size_t dense_len_ = 0;
+};
+
+inline std::vector<size_t> dense_token_indices(TokenGridShape grid) {
+  return SparseTokenMask::all(grid.len()).indices();
+}
+
+inline std::vector<size_t> complement_indices(const std::vector<size_t>& indices, size_t dense_len) {
+  return SparseTokenMask::new_(indices, dense_len).complement().indices();
+}
+
+inline std::pair<SparseTokenMask, SparseTokenMask> make_context_target_masks(TokenGridShape grid,
+                                                                           float context_keep_ratio) {
+  SparseTokenMask context = SparseTokenMask::from_keep_ratio(grid.len(), context_keep_ratio);
+  SparseTokenMask target = context.complement();
+  return {context, target};
+}
+
+// src/tokens.rs:497-528
+inline SparseTokenMask target_mask_from_context(const SparseTokenMask& context, size_t target_tokens) {
+  const size_t dense_len = context.dense_len();
+  const size_t free = dense_len > context.len() ? dense_len - context.len() : 0;
+  target_tokens = std::min(std::max<size_t>(target_tokens, 1), std::max<size_t>(free, 1));
+  std::vector<bool> blocked(dense_len, false);
+  for (size_t i : context.indices()) blocked[i] = true;
+  std::vector<size_t> target;
+  for (size_t i : SparseTokenMask::evenly_spaced_indices(dense_len, target_tokens))
+    if (!blocked[i]) target.push_back(i);
+  for (size_t i : target) blocked[i] = true;
+  for (size_t i = 0; target.size() < target_tokens && i < dense_len; ++i) {
+    if (!blocked[i]) {
+      target.push_back(i);
+      blocked[i] = true;
+    }
+  }
+  return SparseTokenMask::new_(std::move(target), dense_len);
+}
+
+// ---------------------------------------------------------------------------------------
+// device tensors
+// ---------------------------------------------------------------------------------------
+inline size_t dtype_bytes(bjf_dtype dt) {
+  switch (dt) {
+    case BJF_DTYPE_F32: return 4;
+    case BJF_DTYPE_F16: return 2;
+    case BJF_DTYPE_BF16: return 2;
+    case BJF_DTYPE_I32: return 4;
+  }
+  return 0;
+}
+
+// Owning, contiguous device tensor.  Move-only.
+class Tensor {
+ public:
+  Tensor() = default;
+  Tensor(std::vector<int64_t> shape, bjf_dtype dtype) : shape_(std::move(shape)), dtype_(dtype) {
+    const size_t bytes = nbytes();
+    if (bytes) check_cuda(cudaMalloc(&ptr_, bytes), "cudaMalloc");
+  }
+  ~Tensor() { release(); }
+  Tensor(const Tensor&) = delete;
+  Tensor& operator=(const Tensor&) = delete;
+  Tensor(Tensor&& o) noexcept { *this = std::move(o); }
+  Tensor& operator=(Tensor&& o) noexcept {
+    if (this != &o) {
+      release();
+      ptr_ = o.ptr_;
+      shape_ = std::move(o.shape_);
+      dtype_ = o.dtype_;
+      o.ptr_ = nullptr;
+      o.shape_.clear();
+    }
+    return *this;
+  }
+
+  static Tensor empty(std::vector<int64_t> shape, bjf_dtype dtype) { return Tensor(std::move(shape), dtype); }
+  static Tensor zeros(std::vector<int64_t> shape, bjf_dtype dtype, cudaStream_t st = nullptr) {
+    Tensor t(std::move(shape), dtype);
+    if (t.nbytes()) check_cuda(cudaMemsetAsync(t.ptr_, 0, t.nbytes(), st), "cudaMemsetAsync");
+    return t;
+  }
+  // Copies host elements whose in-memory form is `dtype` (float for F32, int32_t for I32,
+  // uint16_t bit patterns for F16 / BF16).
+  template <typename H>
+  static Tensor from_host(const std::vector<H>& values, std::vector<int64_t> shape, bjf_dtype dtype,
+                          cudaStream_t st = nullptr) {
+    ensure(sizeof(H) == dtype_bytes(dtype), "host element size does not match the tensor dtype");
+    Tensor t(std::move(shape), dtype);
+    ensure(values.size() == t.numel(), "host data length does not match the tensor shape");
+    if (t.nbytes()) {
+      check_cuda(cudaMemcpyAsync(t.ptr_, values.data(), t.nbytes(), cudaMemcpyHostToDevice, st), "H2D copy");
+      check_cuda(cudaStreamSynchronize(st), "H2D copy");
+    }
+    return t;
+  }
+  template <typename H>
+  std::vector<H> to_host(cudaStream_t st = nullptr) const {
+    ensure(sizeof(H) == dtype_bytes(dtype_), "host element size does not match the tensor dtype");
+    std::vector<H> out(numel());
+    if (nbytes()) {
+      check_cuda(cudaMemcpyAsync(out.data(), ptr_, nbytes(), cudaMemcpyDeviceToHost, st), "D2H copy");
+      check_cuda(cudaStreamSynchronize(st), "D2H copy");
+    }
+    return out;
+  }
+  Tensor clone(cudaStream_t st = nullptr) const {
+    Tensor t(shape_, dtype_);
+    if (nbytes()) check_cuda(cudaMemcpyAsync(t.ptr_, ptr_, nbytes(), cudaMemcpyDeviceToDevice, st), "D2D copy");
+    return t;
+  }
+
+  void* data() { return ptr_; }
+  const void* data() const { return ptr_; }
+  bjf_dtype dtype() const { return dtype_; }
+  const std::vector<int64_t>& shape() const { return shape_; }
+  size_t rank() const { return shape_.size(); }
+  size_t numel() const {
+    size_t n = 1;
+    for (int64_t d : shape_) n *= (size_t)d;
+    return shape_.empty() ? 0 : n;
+  }
+  size_t nbytes() const { return numel() * dtype_bytes(dtype_); }
+
+ private:
+  void release() {
+    if (ptr_) cudaFree(ptr_);
+    ptr_ = nullptr;
+  }
+  void* ptr_ = nullptr;
+  std::vector<int64_t> shape_;
+  bjf_dtype dtype_ = BJF_DTYPE_F32;
+};
+
+// ---------------------------------------------------------------------------------------
+// patch-diff mask (src/nodes.rs:97-157, 411-631)
+// ---------------------------------------------------------------------------------------
+struct SparseJepaPatchDiffSparsityConfig {
+  float threshold = 0.0f;
+  size_t context_tokens = 0;
+  size_t target_tokens = 0;
+  size_t dilation = 0;
+  size_t min_context_tokens = 1;
+  bool fill_to_context_tokens = true;
+  bool allow_full_context = false;
+
+  static SparseJepaPatchDiffSparsityConfig new_(float threshold, size_t context_tokens, size_t target_tokens) {
+    SparseJepaPatchDiffSparsityConfig c;
+    c.threshold = threshold;
+    c.context_tokens = context_tokens;
+    c.target_tokens = target_tokens;
+    return c;
+  }
+  static SparseJepaPatchDiffSparsityConfig adaptive_threshold(float threshold, size_t min_context_tokens,
+                                                              size_t max_context_tokens, size_t target_tokens) {
+    SparseJepaPatchDiffSparsityConfig c;
+    c.threshold = threshold;
+    c.context_tokens = max_context_tokens;
+    c.target_tokens = target_tokens;
+    c.min_context_tokens = min_context_tokens;
+    c.fill_to_context_tokens = false;
+    c.allow_full_context = true;
+    return c;
+  }
+  SparseJepaPatchDiffSparsityConfig with_dilation(size_t v) const { auto c = *this; c.dilation = v; return c; }
+  SparseJepaPatchDiffSparsityConfig with_min_context_tokens(size_t v) const {
+    auto c = *this;
+    c.min_context_tokens = v;
+    return c;
+  }
+  SparseJepaPatchDiffSparsityConfig with_fill_to_context_tokens(bool v) const {
+    auto c = *this;
+    c.fill_to_context_tokens = v;
+    return c;
+  }
+  SparseJepaPatchDiffSparsityConfig with_allow_full_context(bool v) const {
+    auto c = *this;
+    c.allow_full_context = v;
+    return c;
+  }
+
+  bjf_patch_diff_config to_c() const {
+    bjf_patch_diff_config c{};
+    c.threshold = threshold;
+    c.context_tokens = (int64_t)context_tokens;
+    c.target_tokens = (int64_t)target_tokens;
+    c.dilation = (int64_t)dilation;
+    c.min_context_tokens = (int64_t)min_context_tokens;
+    c.fill_to_context_tokens = fill_to_context_tokens ? 1 : 0;
+    c.allow_full_context = allow_full_context ? 1 : 0;
+    return c;
+  }
+};
+
+namespace detail {
+inline std::array<int64_t, 5> video_dims(const Tensor& video) {
+  ensure(video.rank() == 5, "video must be a [B, C, T, H, W] tensor");
+  std::array<int64_t, 5> d{};
+  for (int i = 0; i < 5; ++i) d[i] = video.shape()[i];
+  return d;
+}
+inline SparseTokenMask mask_from_device(const Tensor& indices, const Tensor& counts, size_t dense_len,
+                                        cudaStream_t st) {
+  const std::vector<int32_t> c = counts.to_host<int32_t>(st);
+  const std::vector<int32_t> idx = indices.to_host<int32_t>(st);
+  std::vector<size_t> v(idx.begin(), idx.begin() + c[0]);
+  return SparseTokenMask::new_(std::move(v), dense_len);
+}
+}  // namespace detail
+
+// Per-tubelet mean |frame difference|, the batch summed into one map: f32 [N].
+// `tubelet_size` and `patch_size` are the model config's (VJepaConfig).
+inline Tensor patch_diff_token_scores(const Tensor& video, size_t tubelet_size, size_t patch_size,
+                                      TokenGridShape grid, cudaStream_t st = nullptr) {
+  const auto d = detail::video_dims(video);
+  const size_t kt = std::max<size_t>(tubelet_size, 1), p = std::max<size_t>(patch_size, 1);
+  ensure(TokenGridShape((size_t)d[2] / kt, (size_t)d[3] / p, (size_t)d[4] / p) == grid,
+         "patch-diff sparsity grid must match the video shape");
+  Tensor scores({(int64_t)grid.len()}, BJF_DTYPE_F32);
+  check(bjf_patch_diff_token_scores(video.data(), video.dtype(), d.data(), 1, (int64_t)kt, (int64_t)p,
+                                    static_cast<float*>(scores.data()), to_bjf(st)));
+  return scores;
+}
+
+// Host scores -> mask (the reference takes the scores as a Vec<f32>).
+inline SparseTokenMask patch_diff_context_mask_from_scores(const std::vector<float>& score_values,
+                                                          TokenGridShape grid,
+                                                          const SparseJepaPatchDiffSparsityConfig& config,
+                                                          cudaStream_t st = nullptr) {
+  ensure(score_values.size() == grid.len(), "patch-diff sparsity received unexpected score length");
+  const Tensor scores = Tensor::from_host(score_values, {(int64_t)grid.len()}, BJF_DTYPE_F32, st);
+  Tensor indices({(int64_t)grid.len()}, BJF_DTYPE_I32);
+  Tensor counts({1}, BJF_DTYPE_I32);
+  const bjf_patch_diff_config c = config.to_c();
+  const auto g = grid.dims();
+  check(bjf_patch_diff_context_mask_from_scores(static_cast<const float*>(scores.data()), 1, g.data(), &c,
+                                                static_cast<int32_t*>(indices.data()),
+                                                static_cast<int32_t*>(counts.data()), to_bjf(st)));
+  return detail::mask_from_device(indices, counts, grid.len(), st);
+}
+
+inline SparseTokenMask patch_diff_context_mask_from_video(const Tensor& video, size_t tubelet_size,
+                                                         size_t patch_size, TokenGridShape grid,
+                                                         const SparseJepaPatchDiffSparsityConfig& config,
+                                                         cudaStream_t st = nullptr) {
+  const auto d = detail::video_dims(video);
+  const int64_t n = (int64_t)std::max<size_t>(grid.len(), 1);
+  Tensor scores({n}, BJF_DTYPE_F32);
+  Tensor indices({n}, BJF_DTYPE_I32);
+  Tensor counts({1}, BJF_DTYPE_I32);
+  const bjf_patch_diff_config c = config.to_c();
+  const auto g = grid.dims();
+  check(bjf_patch_diff_context_mask(video.data(), video.dtype(), d.data(), 1,
+                                    (int64_t)std::max<size_t>(tubelet_size, 1),
+                                    (int64_t)std::max<size_t>(patch_size, 1), g.data(), &c,
+                                    static_cast<float*>(scores.data()), static_cast<int32_t*>(indices.data()),
+                                    static_cast<int32_t*>(counts.data()), to_bjf(st)));
+  return detail::mask_from_device(indices, counts, grid.len(), st);
+}
+
+// ---------------------------------------------------------------------------------------
+// plans (src/sparse_patchify.rs:236-330): coords rows (b, t, r, c), batch-major
+// ---------------------------------------------------------------------------------------
+class SparsePatchifyPlan {
+ public:
+  static SparsePatchifyPlan new_(SparseTokenMask mask, TokenGridShape grid, size_t batch,
+                                 cudaStream_t st = nullptr) {
+    ensure(batch > 0, "sparse patchify batch must be nonzero");
+    ensure(mask.dense_len() == grid.len(), "sparse patchify mask dense token count must match grid");
+    SparsePatchifyPlan p;
+    p.grid = grid;
+    p.batch = batch;
+    for (size_t b = 0; b < batch; ++b)
+      for (size_t index : mask.indices()) {
+        const auto [t, r, c] = token_index_to_coords(index, grid);
+        p.coords_host.push_back({(uint32_t)b, (uint32_t)t, (uint32_t)r, (uint32_t)c});
+      }
+    p.mask = std::move(mask);
+    p.upload(st);
+    return p;
+  }
+  static SparsePatchifyPlan from_indices(std::vector<size_t> indices, TokenGridShape grid, size_t batch,
+                                         cudaStream_t st = nullptr) {
+    return new_(SparseTokenMask::new_(std::move(indices), grid.len()), grid, batch, st);
+  }
+  // Host half only (no device coords): for callers that build coords on the device.
+  static std::vector<std::array<uint32_t, 4>> host_coords(const SparseTokenMask& mask, TokenGridShape grid,
+                                                          size_t batch) {
+    ensure(batch > 0, "sparse patchify batch must be nonzero");
+    ensure(mask.dense_len() == grid.len(), "sparse patchify mask dense token count must match grid");
+    std::vector<std::array<uint32_t, 4>> out;
+    for (size_t b = 0; b < batch; ++b)
+      for (size_t index : mask.indices()) {
+        const auto [t, r, c] = token_index_to_coords(index, grid);
+        out.push_back({(uint32_t)b, (uint32_t)t, (uint32_t)r, (uint32_t)c});
+      }
+    return out;
+  }
+
+  size_t token_count() const { return mask.len(); }
+  size_t output_rows() const { return batch * mask.len(); }
+
+  SparseTokenMask mask;
+  TokenGridShape grid;
+  size_t batch = 0;
+  Tensor coords;  // [batch * tokens, 4] int32, device
+  std::vector<std::array<uint32_t, 4>> coords_host;
+
+ private:
+  void upload(cudaStream_t st) {
+    std::vector<int32_t> flat;
+    for (const auto& c : coords_host)
+      for (uint32_t v : c) flat.push_back((int32_t)v);
+    coords = Tensor::from_host(flat, {(int64_t)coords_host.size(), 4}, BJF_DTYPE_I32, st);
+  }
+};
+
+// Per-row masks of equal width (uniform or fixed-width); ragged rows are refused as in
+// SparsePatchifyBatchPlan::new (src/sparse_patchify.rs:290-330).
+class SparsePatchifyBatchPlan {
+ public:
+  static SparsePatchifyBatchPlan from_rows(std::vector<std::vector<size_t>> rows, TokenGridShape grid,
+                                           cudaStream_t st = nullptr) {
+    ensure(!rows.empty(), "sparse patchify batch must be nonzero");
+    const size_t dense_len = grid.len();
+    for (auto& row : rows) {
+      std::sort(row.begin(), row.end());
+      row.erase(std::unique(row.begin(), row.end()), row.end());
+      ensure(std::all_of(row.begin(), row.end(), [&](size_t i) { return i < dense_len; }),
+             "sparse token index outside dense token range");
+    }
+    const size_t width = rows[0].size();
+    ensure(std::all_of(rows.begin(), rows.end(), [&](const std::vector<size_t>& r) { return r.size() == width; }),
+           "sparse patchify batch plans require uniform or fixed-width masks; use ragged rollout grouping");
+    ensure(width > 0, "fixed-width sparse mask rows must be non-empty");
+    SparsePatchifyBatchPlan p;
+    p.grid = grid;
+    p.batch = rows.size();
+    p.width = width;
+    std::vector<int32_t> flat;
+    for (size_t b = 0; b < rows.size(); ++b)
+      for (size_t index : rows[b]) {
+        const auto [t, r, c] = token_index_to_coords(index, grid);
+        p.coords_host.push_back({(uint32_t)b, (uint32_t)t, (uint32_t)r, (uint32_t)c});
+        flat.insert(flat.end(), {(int32_t)b, (int32_t)t, (int32_t)r, (int32_t)c});
+      }
+    p.rows = std::move(rows);
+    p.coords = Tensor::from_host(flat, {(int64_t)p.coords_host.size(), 4}, BJF_DTYPE_I32, st);
+    return p;
+  }
+  size_t token_count() const { return width; }
+  size_t output_rows() const { return batch * width; }
+
+  std::vector<std::vector<size_t>> rows;
+  TokenGridShape grid;
+  size_t batch = 0, width = 0;
+  Tensor coords;
+  std::vector<std::array<uint32_t, 4>> coords_host;
+};
+
+// ---------------------------------------------------------------------------------------
+// sparse patchify (burn_flex_gmm::cuda::sparse_patchify3d_forward_cuda)
+// ---------------------------------------------------------------------------------------
+struct SparsePatchify3dConfig {
+  size_t in_channels = 0, out_channels = 0, frames = 0, height = 0, width = 0;
+  size_t tubelet_size = 0, patch_h = 0, patch_w = 0;
+
+  bjf_patchify_config to_c() const {
+    return bjf_patchify_config{(int64_t)in_channels, (int64_t)out_channels, (int64_t)frames, (int64_t)height,
+                               (int64_t)width, (int64_t)tubelet_size, (int64_t)patch_h, (int64_t)patch_w};
+  }
+};
+
+// out[M, D] = Conv3d(input, weight, stride = kernel) + bias at the coords rows.  `bias` may be
+// null (zeros, as the reference's caller substitutes, src/model.rs:1307-1318).  The output
+// dtype defaults to the input's.
+inline Tensor sparse_patchify3d_forward_cuda(const SparsePatchify3dConfig& config, const Tensor& input,
+                                             const Tensor& coords, const Tensor& weight, const Tensor* bias,
+                                             cudaStream_t st = nullptr, int out_dtype = -1) {
+  const auto d = detail::video_dims(input);
+  ensure(weight.rank() == 5, "sparse patchify weight must be [D, C, kt, ph, pw]");
+  ensure(coords.rank() == 2 && coords.shape()[1] == 4 && coords.dtype() == BJF_DTYPE_I32,
+         "sparse patchify coords must be an int32 [M, 4] tensor");
+  std::array<int64_t, 5> wd{};
+  for (int i = 0; i < 5; ++i) wd[i] = weight.shape()[i];
+  const bjf_patchify_config c = config.to_c();
+  const bjf_dtype odt = out_dtype < 0 ? input.dtype() : (bjf_dtype)out_dtype;
+  const int64_t rows = coords.shape()[0];
+  Tensor out({rows, (int64_t)config.out_channels}, odt);
+  check(bjf_sparse_patchify3d_forward(&c, input.data(), input.dtype(), d.data(),
+                                      static_cast<const int32_t*>(coords.data()), rows, weight.data(),
+                                      weight.dtype(), wd.data(),
+                                      bias ? static_cast<const float*>(bias->data()) : nullptr, out.data(), odt,
+                                      to_bjf(st)));
+  return out;
+}
+
+// ---------------------------------------------------------------------------------------
+// InterframeJepaFeatureMemory, AssignLatest mode (src/feature_memory.rs:137-645)
+// ---------------------------------------------------------------------------------------
+struct InterframeJepaFeatureMemoryOutput {
+  const Tensor* features;  // [B, N, D]
+  const Tensor* observed;  // [B, N] f32
+  const Tensor* age_frames;  // [B, N] f32
+  TokenGridShape grid;
+  size_t step;
+  size_t updated_tokens;
+  size_t dense_tokens;
+};
+
+class InterframeJepaFeatureMemory {
+ public:
+  // `features_dtype` f32 as the reference, or f16 / bf16 for a half-size cache.
+  static InterframeJepaFeatureMemory new_(size_t batch, TokenGridShape grid, size_t embed_dim,
+                                          bjf_dtype features_dtype = BJF_DTYPE_F32, cudaStream_t st = nullptr) {
+    ensure(batch > 0, "feature memory batch must be nonzero");
+    ensure(!grid.is_empty(), "feature memory grid must be nonempty");
+    ensure(embed_dim > 0, "feature memory embed dim must be nonzero");
+    InterframeJepaFeatureMemory m;
+    m.batch_ = batch;
+    m.grid_ = grid;
+    m.embed_dim_ = embed_dim;
+    const int64_t B = (int64_t)batch, N = (int64_t)grid.len(), D = (int64_t)embed_dim;
+    m.features_ = Tensor::zeros({B, N, D}, features_dtype, st);
+    m.observed_ = Tensor::zeros({B, N}, BJF_DTYPE_F32, st);
+    m.age_frames_ = Tensor::zeros({B, N}, BJF_DTYPE_F32, st);
+    return m;
+  }
+
+  size_t batch() const { return batch_; }
+  TokenGridShape grid() const { return grid_; }
+  size_t dense_tokens() const { return grid_.len(); }
+  size_t embed_dim() const { return embed_dim_; }
+  size_t step() const { return step_; }
+  InterframeJepaFeatureMemoryOutput snapshot() const { return output(last_updated_tokens_); }
+  Tensor& features() { return features_; }
+  Tensor& observed() { return observed_; }
+  Tensor& age_frames() { return age_frames_; }
+
+  // tokens [B, S, D], token_indices [B, S] int32.  In place (the reference copies the cache
+  // first; a caller that keeps the previous snapshot clones it before this call).
+  InterframeJepaFeatureMemoryOutput update_tokens_tiled_assign_cuda(const Tensor& tokens,
+                                                                   const Tensor& token_indices,
+                                                                   TokenGridShape grid, cudaStream_t st = nullptr) {
+    ensure(grid == grid_, "encoder output grid does not match feature memory grid");
+    ensure(tokens.rank() == 3 && token_indices.rank() == 2, "tokens must be [B, S, D] and indices [B, S]");
+    const int64_t b = tokens.shape()[0], s = tokens.shape()[1], d = tokens.shape()[2];
+    ensure((size_t)b == batch_, "encoder output batch does not match feature memory batch");
+    ensure((size_t)d == embed_dim_, "encoder output dim does not match feature memory dim");
+    ensure(token_indices.shape()[0] == b && token_indices.shape()[1] == s,
+           "token index shape must match sparse encoder token shape");
+    ensure(s > 0, "sparse update must include at least one token");
+    ensure(token_indices.dtype() == BJF_DTYPE_I32, "token indices must be int32");
+    const int64_t fd[3] = {features_.shape()[0], features_.shape()[1], features_.shape()[2]};
+    const int64_t od[2] = {observed_.shape()[0], observed_.shape()[1]};
+    const int64_t ad[2] = {age_frames_.shape()[0], age_frames_.shape()[1]};
+    const int64_t td[3] = {b, s, d};
+    const int64_t id[2] = {b, s};
+    check(bjf_feature_memory_assign_latest(features_.data(), features_.dtype(), fd,
+                                           static_cast<float*>(observed_.data()), od,
+                                           static_cast<float*>(age_frames_.data()), ad, tokens.data(),
+                                           tokens.dtype(), td, static_cast<const int32_t*>(token_indices.data()),
+                                           id, step_ > 0 ? 1 : 0, to_bjf(st)));
+    step_ += 1;
+    last_updated_tokens_ = (size_t)(b * s);
+    return output(last_updated_tokens_);
+  }
+
+  // update_masked_tokens with the tiled assign: one mask shared by every batch row.
+  InterframeJepaFeatureMemoryOutput update_masked_tokens_tiled_assign_cuda(const Tensor& tokens,
+                                                                          const SparseTokenMask& mask,
+                                                                          TokenGridShape grid,
+                                                                          cudaStream_t st = nullptr) {
+    ensure(mask.dense_len() == dense_tokens(), "sparse mask dense length must match feature memory grid");
+    std::vector<int32_t> idx;
+    for (size_t b = 0; b < batch_; ++b)
+      for (size_t i : mask.indices()) idx.push_back((int32_t)i);
+    const Tensor ti = Tensor::from_host(idx, {(int64_t)batch_, (int64_t)mask.len()}, BJF_DTYPE_I32, st);
+    return update_tokens_tiled_assign_cuda(tokens, ti, grid, st);
+  }
+
+  void reset(cudaStream_t st = nullptr) {
+    check_cuda(cudaMemsetAsync(features_.data(), 0, features_.nbytes(), st), "cudaMemsetAsync");
+    check_cuda(cudaMemsetAsync(observed_.data(), 0, observed_.nbytes(), st), "cudaMemsetAsync");
+    check_cuda(cudaMemsetAsync(age_frames_.data(), 0, age_frames_.nbytes(), st), "cudaMemsetAsync");
+    step_ = 0;
+    last_updated_tokens_ = 0;
+  }
+
+  // Zeroes the features and metadata of the given batch rows (src/feature_memory.rs:377-385).
+  void reset_row_indices(const std::vector<size_t>& rows, cudaStream_t st = nullptr) {
+    if (rows.empty()) return;
+    ensure(std::all_of(rows.begin(), rows.end(), [&](size_t r) { return r < batch_; }),
+           "feature memory row reset index outside batch");
+    const size_t N = dense_tokens();
+    const size_t frow = N * embed_dim_ * dtype_bytes(features_.dtype());
+    for (size_t r : rows) {
+      check_cuda(cudaMemsetAsync(static_cast<char*>(features_.data()) + r * frow, 0, frow, st), "cudaMemsetAsync");
+      check_cuda(cudaMemsetAsync(static_cast<float*>(observed_.data()) + r * N, 0, N * 4, st), "cudaMemsetAsync");
+      check_cuda(cudaMemsetAsync(static_cast<float*>(age_frames_.data()) + r * N, 0, N * 4, st),
+                 "cudaMemsetAsync");
+    }
+  }
+
+ private:
+  InterframeJepaFeatureMemoryOutput output(size_t updated) const {
+    return {&features_, &observed_, &age_frames_, grid_, step_, updated, grid_.len()};
+  }
+  size_t batch_ = 0, embed_dim_ = 0, step_ = 0, last_updated_tokens_ = 0;
+  TokenGridShape grid_;
+  Tensor features_, observed_, age_frames_;
+};
+
+// ---------------------------------------------------------------------------------------
+// FrontEnd: one frame step over S independent streams, fully on the device
+// (patch-diff mask -> plan -> gather-GEMM with bias -> in-place token-cache write).
+// ---------------------------------------------------------------------------------------
+class FrontEnd {
+ public:
+  FrontEnd(size_t streams, size_t channels, size_t frames, size_t height, size_t width, size_t tubelet_size,
+           size_t patch_size, size_t embed_dim, const SparseJepaPatchDiffSparsityConfig& mask,
+           bjf_dtype video_dtype, bjf_dtype cache_dtype, cudaStream_t st = nullptr) {
+    desc_.streams = (int64_t)streams;
+    desc_.channels = (int64_t)channels;
+    desc_.frames = (int64_t)frames;
+    desc_.height = (int64_t)height;
+    desc_.width = (int64_t)width;
+    desc_.tubelet_size = (int64_t)tubelet_size;
+    desc_.patch_size = (int64_t)patch_size;
+    desc_.embed_dim = (int64_t)embed_dim;
+    desc_.video_dtype = video_dtype;
+    desc_.weight_dtype = video_dtype;
+    desc_.cache_dtype = cache_dtype;
+    desc_.mask = mask.to_c();
+    const size_t ws = bjf_front_end_workspace_bytes(&desc_);
+    if (ws == 0) throw Error(BJF_ERR_INVALID_ARGUMENT, last_error_string());
+    grid_ = TokenGridShape(frames / tubelet_size, height / patch_size, width / patch_size);
+    workspace_ = Tensor::empty({(int64_t)((ws + 3) / 4)}, BJF_DTYPE_F32);  // cudaMalloc: 256-byte aligned
+    counts_ = Tensor::zeros({(int64_t)streams}, BJF_DTYPE_I32, st);
+    caches_ = Tensor::zeros({(int64_t)streams, (int64_t)grid_.len(), (int64_t)embed_dim}, cache_dtype, st);
+    observed_ = Tensor::zeros({(int64_t)streams, (int64_t)grid_.len()}, BJF_DTYPE_F32, st);
+    age_ = Tensor::zeros({(int64_t)streams, (int64_t)grid_.len()}, BJF_DTYPE_F32, st);
+  }
+
+  // video [S, C, T, H, W] (one clip per stream), weight [D, C, kt, P, P] (video dtype),
+  // bias [D] f32 or null.  Returns the per-stream active counts (device [S] int32).
+  const Tensor& step(const Tensor& video, const Tensor& weight, const Tensor* bias, cudaStream_t st = nullptr) {
+    check(bjf_front_end_step(&desc_, video.data(), weight.data(), bias ? static_cast<const float*>(bias->data()) : nullptr,
+                             caches_.data(), static_cast<float*>(observed_.data()), static_cast<float*>(age_.data()),
+                             steps_ > 0 ? 1 : 0, workspace_.data(), workspace_.nbytes(),
+                             static_cast<int32_t*>(counts_.data()), to_bjf(st)));
+    ++steps_;
+    return counts_;
+  }
+
+  TokenGridShape grid() const { return grid_; }
+  size_t steps() const { return steps_; }
+  Tensor& caches() { return caches_; }
+  Tensor& observed() { return observed_; }
+  Tensor& age_frames() { return age_; }
+  const bjf_front_end_desc& desc() const { return desc_; }
+
+ private:
+  bjf_front_end_desc desc_{};
+  TokenGridShape grid_;
+  size_t steps_ = 0;
+  Tensor workspace_, counts_, caches_, observed_, age_;
+};
+
+// Reports (and clears) a bounded-wait timeout recorded by any kernel of the library.
+inline bool device_error_check(cudaStream_t st = nullptr) {
+  int32_t flag = 0;
+  check(bjf_device_error_check(to_bjf(st), &flag));
+  return flag != 0;
+}
+
+}  // namespace bjf

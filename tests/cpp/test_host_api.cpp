@@ -1,0 +1,135 @@
+// test_host_api.cpp -- host-side ports of the reference's own tests onto the C++ API of
+// include/bjf.hpp.  Needs no GPU: every case here is decided before any device work.
+#include <set>
+
+#include "../../include/bjf.hpp"
+#include "check.hpp"
+
+using namespace bjf;
+
+// src/positional.rs:97-103
+TEST(token_index_round_trip_uses_depth_height_width_order) {
+  const TokenGridShape grid(3, 4, 5);
+  const size_t index = coords_to_token_index(2, 3, 4, grid);
+  CHECK_EQ(index, (size_t)59);
+  CHECK(token_index_to_coords(index, grid) == std::make_tuple((size_t)2, (size_t)3, (size_t)4));
+}
+
+// src/tokens.rs:563-568
+TEST(complement_preserves_sorted_indices) {
+  const auto mask = SparseTokenMask::new_({3, 1, 1}, 5);
+  CHECK_EQ(mask.indices(), (std::vector<size_t>{1, 3}));
+  CHECK_EQ(mask.complement().indices(), (std::vector<size_t>{0, 2, 4}));
+}
+
+// src/tokens.rs:570-580
+TEST(padded_mask_keeps_existing_tokens_and_rounds_to_bucket) {
+  const auto mask = SparseTokenMask::new_({7, 1, 3}, 10);
+  const auto padded = mask.padded_to_multiple(4);
+  CHECK_EQ(padded.len(), (size_t)4);
+  for (size_t index : {1, 3, 7})
+    CHECK(std::find(padded.indices().begin(), padded.indices().end(), index) != padded.indices().end());
+  CHECK(!padded.is_dense_ordered());
+}
+
+// src/tokens.rs:582-589
+TEST(padded_mask_promotes_to_dense_when_bucket_reaches_dense_len) {
+  const auto mask = SparseTokenMask::new_({0, 2, 4, 6, 8}, 10);
+  const auto padded = mask.padded_to_multiple(16);
+  CHECK_EQ(padded.indices(), SparseTokenMask::all(10).indices());
+  CHECK(padded.is_dense_ordered());
+}
+
+// src/tokens.rs:591-603
+TEST(target_mask_from_context_is_disjoint_and_fills_budget) {
+  const auto context = SparseTokenMask::new_({0, 2, 4}, 6);
+  const auto target = target_mask_from_context(context, 2);
+  CHECK_EQ(target.len(), (size_t)2);
+  for (size_t i : target.indices())
+    CHECK(std::find(context.indices().begin(), context.indices().end(), i) == context.indices().end());
+}
+
+// src/config.rs:373-378 (tiny grid has 8 tokens) and src/tokens.rs:488-495
+TEST(tiny_grid_context_target_masks) {
+  const TokenGridShape grid(4 / 2, 32 / 16, 32 / 16);
+  CHECK_EQ(grid.len(), (size_t)8);
+  const auto [context, target] = make_context_target_masks(grid, 0.5f);
+  CHECK_EQ(context.indices(), (std::vector<size_t>{0, 1, 2, 3}));
+  CHECK_EQ(target.indices(), (std::vector<size_t>{4, 5, 6, 7}));
+}
+
+// src/tokens.rs:41-50
+TEST(sparse_token_mask_rejects_bad_input) {
+  CHECK_THROWS_WITH(SparseTokenMask::new_({0}, 0), "dense token count must be nonzero");
+  CHECK_THROWS_WITH(SparseTokenMask::new_({0, 5}, 5), "sparse token index outside dense token range");
+}
+
+TEST(evenly_spaced_and_keep_ratio) {
+  CHECK_EQ(SparseTokenMask::evenly_spaced_indices(10, 3), (std::vector<size_t>{0, 3, 6}));
+  CHECK_EQ(SparseTokenMask::evenly_spaced_indices(4, 9), (std::vector<size_t>{0, 1, 2, 3}));
+  CHECK_EQ(SparseTokenMask::from_keep_ratio(10, 0.25f).len(), (size_t)3);
+  CHECK_EQ(SparseTokenMask::from_keep_ratio(10, -1.0f).len(), (size_t)1);
+}
+
+// src/sparse_patchify.rs:676-693
+TEST(sparse_patchify_plan_coords_are_batch_major) {
+  const TokenGridShape grid(2, 3, 4);
+  const auto mask = SparseTokenMask::new_({0, 7, 23}, grid.len());
+  const auto coords = SparsePatchifyPlan::host_coords(mask, grid, 2);
+  const std::vector<std::array<uint32_t, 4>> want = {
+      {0, 0, 0, 0}, {0, 0, 1, 3}, {0, 1, 2, 3}, {1, 0, 0, 0}, {1, 0, 1, 3}, {1, 1, 2, 3}};
+  CHECK(coords == want);
+}
+
+// src/sparse_patchify.rs:243-247, 291-299
+TEST(sparse_patchify_plans_reject_bad_input) {
+  const TokenGridShape grid(1, 2, 2);
+  CHECK_THROWS_WITH(SparsePatchifyPlan::host_coords(SparseTokenMask::new_({0}, 4), grid, 0),
+                    "sparse patchify batch must be nonzero");
+  CHECK_THROWS_WITH(SparsePatchifyPlan::host_coords(SparseTokenMask::new_({0}, 5), grid, 1),
+                    "sparse patchify mask dense token count must match grid");
+  CHECK_THROWS_WITH(SparsePatchifyBatchPlan::from_rows({{0, 1}, {2}}, grid),
+                    "sparse patchify batch plans require uniform or fixed-width masks");
+}
+
+// src/nodes.rs:97-157
+TEST(patch_diff_config_builders) {
+  const auto a = SparseJepaPatchDiffSparsityConfig::adaptive_threshold(0.5f, 2, 64, 3);
+  CHECK_EQ(a.context_tokens, (size_t)64);
+  CHECK_EQ(a.min_context_tokens, (size_t)2);
+  CHECK(!a.fill_to_context_tokens);
+  CHECK(a.allow_full_context);
+  const auto n = SparseJepaPatchDiffSparsityConfig::new_(0.1f, 4, 2).with_dilation(1);
+  CHECK_EQ(n.min_context_tokens, (size_t)1);
+  CHECK(n.fill_to_context_tokens);
+  CHECK(!n.allow_full_context);
+  CHECK_EQ(n.to_c().dilation, (int64_t)1);
+}
+
+// src/nodes.rs:463-466
+TEST(mask_from_scores_rejects_wrong_length) {
+  const auto cfg = SparseJepaPatchDiffSparsityConfig::new_(0.1f, 1, 1);
+  CHECK_THROWS_WITH(patch_diff_context_mask_from_scores({0.1f, 0.2f}, TokenGridShape(1, 1, 3), cfg),
+                    "patch-diff sparsity received unexpected score length");
+}
+
+// src/feature_memory.rs:152-162
+TEST(feature_memory_rejects_empty_shapes) {
+  CHECK_THROWS_WITH(InterframeJepaFeatureMemory::new_(0, TokenGridShape(1, 2, 2), 4),
+                    "feature memory batch must be nonzero");
+  CHECK_THROWS_WITH(InterframeJepaFeatureMemory::new_(1, TokenGridShape(0, 2, 2), 4),
+                    "feature memory grid must be nonempty");
+  CHECK_THROWS_WITH(InterframeJepaFeatureMemory::new_(1, TokenGridShape(1, 2, 2), 0),
+                    "feature memory embed dim must be nonzero");
+}
+
+// src/nodes.rs:427-432, through the C ABI's host-side validation
+TEST(front_end_rejects_indivisible_geometry) {
+  const auto cfg = SparseJepaPatchDiffSparsityConfig::adaptive_threshold(0.1f, 1, 4, 1);
+  CHECK_THROWS_WITH(FrontEnd(1, 3, 3, 32, 32, 2, 16, 64, cfg, BJF_DTYPE_F16, BJF_DTYPE_F16),
+                    "patch-diff sparsity requires frames/height/width divisible by tubelet and patch sizes");
+}
+
+TEST(abi_version_matches_header) { CHECK_EQ(bjf_abi_version(), BJF_ABI_VERSION); }
+
+TEST_MAIN()
