@@ -181,5 +181,5 @@ extern "C" bjf_status bjf_front_end_step_no_alloc(const bjf_front_end_desc* d, c
   ep.age = age_frames;
   ep.bias = bias;
   return launch_gather_gemm(dev, video, d->video_dtype, weight, d->weight_dtype, g,
-                            reinterpret_cast<const int4*>(coords), total, S * N, ep, st);
+                            coords_rows(reinterpret_cast<const int4*>(coords)), total, S * N, ep, st);
 }

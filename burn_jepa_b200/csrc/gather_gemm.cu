@@ -41,7 +41,7 @@ using namespace sm100;
 
 constexpr int kBM = 128;
 constexpr int kBK = 64;
-constexpr int kStagesA = 7;  // gathered tubelet rows (from HBM): deep ring
+constexpr int kStagesA = 6;  // gathered tubelet rows (from HBM): deep ring
 constexpr int kStagesB = 3;  // weight tiles (L2-resident): shallow ring
 constexpr int kMaxBN = 256;
 constexpr int kEpilogueWarps = 4;   // warps 0-3: TMEM lane quarters 0-3
@@ -59,13 +59,16 @@ struct SmemLayout {
   static constexpr int a_off = 0;
   static constexpr int b_off = a_off + kStagesA * kAStageBytes;
   static constexpr int bar_off = b_off + kStagesB * kBStageBytes;
-  // full_a[A], empty_a[A], full_b[B], empty_b[B], acc_full[2], acc_empty[2]
-  static constexpr int misc_off = bar_off + (2 * kStagesA + 2 * kStagesB + 4) * 8;
+  // full_a[A], empty_a[A], full_b[B], empty_b[B], acc_full[2], acc_empty[2], producers
+  static constexpr int misc_off = bar_off + (2 * kStagesA + 2 * kStagesB + 5) * 8;
   // tmem base (4 B), abort flag (4 B)
   static constexpr int koff_off = misc_off + 16;
-  static constexpr int total = koff_off + kMaxKBlocks * 8 * 4;
+  static constexpr int soff_off = koff_off + kMaxKBlocks * 8 * 4;  // stream row offsets
+  static constexpr int rowbase_off = soff_off + ((kMaxRowStreams + 1) * 4 + 15) / 16 * 16;
+  static constexpr int total = rowbase_off + kBM * 8;
   static constexpr int alloc = total + 1024;  // room to align the base to 1024 B
 };
+static_assert(SmemLayout::alloc <= 227 * 1024, "single-CTA kernel shared memory");
 
 __device__ __forceinline__ int64_t row_base_offset(const GatherGeometry& g, int4 c, bool& valid) {
   valid = c.x >= 0 && c.x < g.batch && c.y >= 0 && c.y < g.depth && c.z >= 0 && c.z < g.gh &&
@@ -74,6 +77,43 @@ __device__ __forceinline__ int64_t row_base_offset(const GatherGeometry& g, int4
   return (((int64_t)c.x * g.C * g.T + (int64_t)c.y * g.kt) * g.H + (int64_t)c.z * g.ph) * g.W +
          (int64_t)c.w * g.pw;
 }
+
+// Loads the stream offsets of an index row source into shared memory (all threads of the
+// block) and returns the row count they describe; explicit coords rows return INT32_MAX.
+__device__ __forceinline__ int load_row_offsets(const RowSource& rs, int* soff) {
+  if (rs.coords) return 0x7fffffff;
+  for (int i = threadIdx.x; i <= rs.streams; i += blockDim.x) soff[i] = __ldg(rs.offsets + i);
+  __syncthreads();
+  return soff[rs.streams];
+}
+
+// Coordinates (b, t, r, col) of row m; a token index outside the grid gives t = r = col = -1
+// (a zero row, as out-of-range coords).
+__device__ __forceinline__ int4 fetch_row(const RowSource& rs, const int* soff, const GatherGeometry& g, int m) {
+  if (rs.coords) return __ldg(rs.coords + m);
+  int lo = 0, hi = rs.streams;  // soff[lo] <= m < soff[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (soff[mid] <= m) lo = mid; else hi = mid;
+  }
+  const int idx = __ldg(rs.indices + (int64_t)lo * rs.index_stride + (m - soff[lo]));
+  const int tpf = g.gh * g.gw;
+  if (idx < 0 || idx >= g.depth * tpf) return make_int4(lo, -1, -1, -1);
+  const int t = idx / tpf, rem = idx - t * tpf, r = rem / g.gw;
+  return make_int4(lo, t, r, rem - r * g.gw);
+}
+
+// The 128 producer threads resolve a tile's 128 rows together: producer thread p resolves
+// row row0 + p into rowbase[p] (its element offset in the input, -1 for a zero row), so
+// each row costs one dependent load chain per tile rather than eight per thread.  Each
+// thread then picks up the eight rows it copies: 32 pw + 4 i + sub.  The producers meet
+// on an mbarrier (`bar`, 128 arrivals per phase, `phase` counts this thread's uses) whose
+// waits are bounded like every other wait, so a producer that gave up cannot strand the
+// others.  Returns false when a wait gave up.
+__device__ __forceinline__ bool producer_rows(const RowSource& rs, const int* soff, const GatherGeometry& g, int M,
+                                              int row0, int p, int64_t* rowbase, int pw, int sub,
+                                              int64_t (&base)[8], uint32_t& valid_mask, uint64_t* bar,
+                                              int& phase, volatile int* abort_flag);
 
 // Offset of element k of a tubelet row relative to its (b, t*kt, r*ph, col*pw) corner
 // (< C*T*H*W of one batch element, which the launch checks fits in int32).
@@ -85,6 +125,35 @@ __host__ __device__ __forceinline__ int64_t k_offset(const GatherGeometry& g, in
   int dt = q2 % g.kt;
   int ch = q2 / g.kt;
   return (((int64_t)ch * g.T + dt) * g.H + dy) * g.W + dx;
+}
+
+__device__ __forceinline__ bool producer_rows(const RowSource& rs, const int* soff, const GatherGeometry& g, int M,
+                                              int row0, int p, int64_t* rowbase, int pw, int sub,
+                                              int64_t (&base)[8], uint32_t& valid_mask, uint64_t* bar,
+                                              int& phase, volatile int* abort_flag) {
+  // every producer has read the previous tile's rows
+  mbar_arrive(bar);
+  if (!mbar_wait_bounded(bar, (uint32_t)(phase++ & 1), abort_flag, kWaitLimitNs)) return false;
+  {
+    const int gm = row0 + p;
+    int64_t b = -1;
+    if (gm < M) {
+      bool valid = false;
+      const int64_t o = row_base_offset(g, fetch_row(rs, soff, g, gm), valid);
+      if (valid) b = o;
+    }
+    rowbase[p] = b;
+  }
+  mbar_arrive(bar);
+  if (!mbar_wait_bounded(bar, (uint32_t)(phase++ & 1), abort_flag, kWaitLimitNs)) return false;
+  valid_mask = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int64_t b = rowbase[32 * pw + 4 * i + sub];
+    valid_mask |= (uint32_t)(b >= 0) << i;
+    base[i] = b >= 0 ? b : 0;
+  }
+  return true;
 }
 
 // Stores 32 consecutive output columns of one row (ncol of them valid).
@@ -104,6 +173,56 @@ __device__ __forceinline__ void store_chunk(char* dst, const float (&v)[32], int
   }
 }
 
+// Epilogue of one accumulator: this warp's 32 TMEM lanes (tile rows, lane = thread) x bn
+// columns from `taddr` -> + bias -> the row's destination (plain [M, D] or its token-cache
+// slot, which also marks the slot observed with age 0).  Warp-collective.
+__device__ __forceinline__ void drain_accumulator(const GatherGeometry& g, const EpilogueArgs& ep,
+                                                  const RowSource& rs, const int* soff, int M, int gm, int n0,
+                                                  int bn, uint32_t taddr, int lane) {
+  const int ce = ep.out_elem_bytes;
+  bool valid = false;
+  char* dst_row = nullptr;
+  if (gm < M) {
+    const int4 c = fetch_row(rs, soff, g, gm);
+    row_base_offset(g, c, valid);
+    if (ep.mode == kEpiloguePlain) {
+      dst_row = static_cast<char*>(ep.out) + (int64_t)gm * ep.ldo * ce;
+    } else if (valid) {
+      const int64_t idx = ((int64_t)c.y * g.gh + c.z) * g.gw + c.w;
+      const int64_t slot = (int64_t)c.x * ep.dense_tokens + idx;
+      dst_row = static_cast<char*>(ep.out) + slot * ep.ldo * ce;
+      if (n0 == 0) {
+        if (ep.observed) ep.observed[slot] = 1.0f;
+        if (ep.age) ep.age[slot] = 0.0f;
+      }
+    }
+  }
+  for (int c0 = 0; c0 < bn; c0 += 32) {
+    uint32_t r[32];
+    tmem_ld_32x32b_x32(taddr + (uint32_t)c0, r);
+    tmem_ld_wait();
+    const int col0 = n0 + c0;
+    const int ncol = min(32, min(bn - c0, g.D - col0));  // the same for the whole warp
+    if (ncol <= 0) continue;
+    // lane j holds bias[col0 + j]; broadcast it to every row of the warp
+    const float bl = (ep.bias && lane < ncol) ? __ldg(ep.bias + col0 + lane) : 0.0f;
+    float v[32];
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float b = __shfl_sync(0xffffffffu, bl, j);
+      v[j] = valid ? __uint_as_float(r[j]) + b : 0.0f;
+    }
+    if (!dst_row) continue;
+    char* dst = dst_row + (int64_t)col0 * ce;
+    if (ep.out_dtype == BJF_DTYPE_F32)
+      store_chunk<float>(dst, v, ncol);
+    else if (ep.out_dtype == BJF_DTYPE_F16)
+      store_chunk<__half>(dst, v, ncol);
+    else
+      store_chunk<__nv_bfloat16>(dst, v, ncol);
+  }
+}
+
 // Persistent, warp-specialised gather-GEMM.  grid = min(#SMs, tiles); CTA b takes tiles
 // b, b + grid, ... in (m-tile major, n-tile minor) order so concurrently running CTAs share
 // their gathered A rows through L2.  Two TMEM accumulators let the epilogue of one tile
@@ -119,29 +238,33 @@ __device__ __forceinline__ void store_chunk(char* dst, const float (&v)[32], int
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 1)
     gather_gemm_sm100_kernel(const __grid_constant__ CUtensorMap wmap, const T* __restrict__ video,
-                             const int4* __restrict__ coords, const int32_t* __restrict__ rows_dev,
+                             const RowSource rs, const int32_t* __restrict__ rows_dev,
                              int rows_cap, GatherGeometry g, int bn, EpilogueArgs ep,
                              int* __restrict__ error_flag) {
   extern __shared__ uint8_t smem_dyn[];
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
+  uint8_t* smem = smem_dyn + ((1024 - (smem_u32(smem_dyn) & 1023)) & 1023);
+  int* soff = reinterpret_cast<int*>(smem + SmemLayout::soff_off);
+  int64_t* rowbase = reinterpret_cast<int64_t*>(smem + SmemLayout::rowbase_off);
 
-  pdl_wait();     // coords / row count come from the kernels before (plan, selection)
+  pdl_wait();     // the rows and their count come from the kernels before (plan, selection)
   pdl_trigger();  // the next frame's patch-diff pass may start alongside this GEMM
   int M = rows_cap;
   if (rows_dev) M = min(M, max(0, __ldg(rows_dev)));
+  M = min(M, load_row_offsets(rs, soff));
   const int n_tiles = (g.D + bn - 1) / bn;
   const int num_tiles = ((M + kBM - 1) / kBM) * n_tiles;
   if ((int)blockIdx.x >= num_tiles) return;  // uniform early exit before any allocation
 
-  uint8_t* smem = smem_dyn + ((1024 - (smem_u32(smem_dyn) & 1023)) & 1023);
   uint64_t* full_a = reinterpret_cast<uint64_t*>(smem + SmemLayout::bar_off);
   uint64_t* empty_a = full_a + kStagesA;
   uint64_t* full_b = empty_a + kStagesA;
   uint64_t* empty_b = full_b + kStagesB;
   uint64_t* acc_full = empty_b + kStagesB;
   uint64_t* acc_empty = acc_full + 2;
+  uint64_t* prod_bar = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SmemLayout::misc_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SmemLayout::misc_off + 4);
   int32_t* koff = reinterpret_cast<int32_t*>(smem + SmemLayout::koff_off);
@@ -160,6 +283,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_empty[b], kEpilogueWarps);
     }
+    mbar_init(prod_bar, kProducerWarps * 32);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -186,19 +310,20 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int j = lane & 7;                 // 16-byte run index within the 128-byte K line
     const int sub = lane >> 3;              // row within a group of 4
     int kbg = 0;  // k blocks issued by this CTA so far (all tiles)
+    int prod_phase = 0;
     for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x) {
       // this thread's eight rows: m_i = 32 pw_ + 4 i + sub
       int64_t base[8];
       uint32_t dst_off[8];
       uint32_t valid_mask = 0;
+      if (!producer_rows(rs, soff, g, M, (tile / n_tiles) * kBM, tid - kEpilogueWarps * 32, rowbase, pw_, sub,
+                         base, valid_mask, prod_bar, prod_phase, abort_flag)) {
+        aborted = true;
+        break;
+      }
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int m = 32 * pw_ + 4 * i + sub;
-        const int gm = (tile / n_tiles) * kBM + m;
-        bool valid = false;
-        base[i] = 0;
-        if (gm < M) base[i] = row_base_offset(g, __ldg(coords + gm), valid);
-        valid_mask |= (uint32_t)valid << i;
         dst_off[i] = (uint32_t)((m >> 3) * 1024 + (m & 7) * 128 + ((j ^ (m & 7)) << 4));
       }
       for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
@@ -292,7 +417,6 @@ __global__ void __launch_bounds__(kThreads, 1)
   } else {
     // ---------------- epilogue (warps 0-3) ----------------
     const int m = tid;  // TMEM lane = tile row
-    const int ce = ep.out_elem_bytes;
     int it = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int buf = it & 1;
@@ -303,52 +427,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         break;
       }
       tc_fence_after();
-      const int m_tile = tile / n_tiles;
       const int n0 = (tile % n_tiles) * bn;
-      const int gm = m_tile * kBM + m;
-      bool valid = false;
-      int4 c = make_int4(-1, -1, -1, -1);
-      char* dst_row = nullptr;
-      if (gm < M) {
-        c = __ldg(coords + gm);
-        row_base_offset(g, c, valid);
-        if (ep.mode == kEpiloguePlain) {
-          dst_row = static_cast<char*>(ep.out) + (int64_t)gm * ep.ldo * ce;
-        } else if (valid) {
-          const int64_t idx = ((int64_t)c.y * g.gh + c.z) * g.gw + c.w;
-          const int64_t slot = (int64_t)c.x * ep.dense_tokens + idx;
-          dst_row = static_cast<char*>(ep.out) + slot * ep.ldo * ce;
-          if (n0 == 0) {
-            if (ep.observed) ep.observed[slot] = 1.0f;
-            if (ep.age) ep.age[slot] = 0.0f;
-          }
-        }
-      }
-      const uint32_t taddr = tmem_base + (uint32_t)buf * acc_cols + ((uint32_t)(warp * 32) << 16);
-      for (int c0 = 0; c0 < bn; c0 += 32) {
-        uint32_t r[32];
-        tmem_ld_32x32b_x32(taddr + (uint32_t)c0, r);
-        tmem_ld_wait();
-        const int col0 = n0 + c0;
-        const int ncol = min(32, min(bn - c0, g.D - col0));  // the same for the whole warp
-        if (ncol <= 0) continue;
-        // lane j holds bias[col0 + j]; broadcast it to every row of the warp
-        const float bl = (ep.bias && lane < ncol) ? __ldg(ep.bias + col0 + lane) : 0.0f;
-        float v[32];
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          const float b = __shfl_sync(0xffffffffu, bl, j);
-          v[j] = valid ? __uint_as_float(r[j]) + b : 0.0f;
-        }
-        if (!dst_row) continue;
-        char* dst = dst_row + (int64_t)col0 * ce;
-        if (ep.out_dtype == BJF_DTYPE_F32)
-          store_chunk<float>(dst, v, ncol);
-        else if (ep.out_dtype == BJF_DTYPE_F16)
-          store_chunk<__half>(dst, v, ncol);
-        else
-          store_chunk<__nv_bfloat16>(dst, v, ncol);
-      }
+      const int gm = (tile / n_tiles) * kBM + m;
+      drain_accumulator(g, ep, rs, soff, M, gm, n0, bn,
+                        tmem_base + (uint32_t)buf * acc_cols + ((uint32_t)(warp * 32) << 16), lane);
       // This warp has finished reading accumulator `buf`: hand it back to the MMA warp.
       tc_fence_before();
       __syncwarp();
@@ -369,25 +451,414 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 // ---------------------------------------------------------------------------
+// CTA-pair path: 256 x BN tiles on two SMs (tcgen05 cta_group::2)
+// ---------------------------------------------------------------------------
+// A cluster of two CTAs computes a 256-row x BN-column tile: each CTA gathers its own 128
+// rows of A and loads half of the BN weight rows (B) by TMA into the same shared-memory
+// offsets, and the even CTA issues tcgen05.mma.cta_group::2 (M = 256) that reads both CTAs'
+// operands and writes 128 rows of D into each CTA's TMEM.  Per SM this halves the weight
+// traffic of the 128 x BN tile of the single-CTA kernel for the same tensor work, so the
+// shared memory goes to a deeper ring of gathered rows (the latency-bound operand).
+//
+// Stage handshake: a stage (16 KB of gathered rows + BN/2 x 64 of B per CTA) is full in a
+// CTA when its 128 producer threads' cp.async arrivals and its TMA bytes have landed.
+// cp.async and TMA can only signal barriers of their own CTA, so lanes of the odd CTA's MMA
+// warp relay, one lane per stage: a lane waits for its stage's local full barrier, fences
+// the stage into the async proxy and arrives (relaxed, cluster scope) on the even CTA's
+// peer_full barrier.  The MMA thread waits for both CTAs' stages, issues, and
+// tcgen05.commit multicasts the stage release (empty) and the accumulator-ready signal
+// (acc_full) to both CTAs.  Both CTAs' epilogue warps hand the accumulator back on the even
+// CTA's acc_empty barrier.
+//
+// Epilogue: each epilogue warp converts its 32 accumulator rows 128 bytes of output at a
+// time into a shared-memory staging tile (rows padded to 144 bytes, so the eight rows a
+// quarter-warp writes fall in distinct banks) and each lane sends its row's 128 bytes to
+// global memory with one bulk asynchronous copy.  The copies run on the TMA engine, not
+// the load/store pipe that also carries the gather, and two staging buffers per warp let
+// the next chunk be converted while the previous one is still being read.
+constexpr int kPairStages = 4;
+constexpr int kBHalfStageBytes = (kMaxBN / 2) * kBK * 2;  // 16 KB
+constexpr int kEpiChunkBytes = 128;                       // output bytes per row per bulk copy
+constexpr int kEpiRowPitch = kEpiChunkBytes + 16;
+constexpr int kEpiBufs = 2;
+constexpr int kEpiWarpBytes = kEpiBufs * 32 * kEpiRowPitch;
+static_assert(kPairStages <= 32, "one relay lane per stage");
+
+struct PairSmemLayout {
+  static constexpr int a_off = 0;
+  static constexpr int b_off = a_off + kPairStages * kAStageBytes;
+  static constexpr int epi_off = b_off + kPairStages * kBHalfStageBytes;
+  static constexpr int bar_off = epi_off + kEpilogueWarps * kEpiWarpBytes;
+  // full[S], peer_full[S], empty[S], acc_full[2], acc_empty[2], producers
+  static constexpr int misc_off = bar_off + (3 * kPairStages + 5) * 8;
+  // tmem base (4 B), abort flag (4 B)
+  static constexpr int koff_off = misc_off + 16;
+  static constexpr int soff_off = koff_off + kMaxKBlocks * 8 * 4;  // stream row offsets
+  static constexpr int rowbase_off = soff_off + ((kMaxRowStreams + 1) * 4 + 15) / 16 * 16;
+  static constexpr int total = rowbase_off + kBM * 8;
+  static constexpr int alloc = total + 1024;
+};
+static_assert(PairSmemLayout::alloc <= 227 * 1024, "pair kernel shared memory");
+
+// Converts 32 accumulator values + bias into `ncol` (<= 32) output elements at `dst`
+// (shared memory, 16-byte aligned; ncol * sizeof(O) bytes).
+template <typename O>
+__device__ __forceinline__ void pack_chunk32(uint8_t* dst, const float (&v)[32], int ncol) {
+  O* o = reinterpret_cast<O*>(dst);
+  if (ncol == 32) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      float w8[8] = {v[j], v[j + 1], v[j + 2], v[j + 3], v[j + 4], v[j + 5], v[j + 6], v[j + 7]};
+      store8<O>(o + j, w8);
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < ncol) o[j] = from_f32<O>(v[j]);
+  }
+}
+
+// Epilogue of one accumulator through shared-memory staging and bulk stores: this warp's
+// 32 TMEM lanes (tile rows, lane = thread) x bn columns from `taddr` -> + bias -> the row's
+// destination.  `stage` / `stage_smem` address this warp's staging buffers; `chunk` counts
+// this thread's staged chunks (selects the buffer).  Warp-collective.
+__device__ __forceinline__ void drain_accumulator_bulk(const GatherGeometry& g, const EpilogueArgs& ep,
+                                                       const RowSource& rs, const int* soff, int M, int gm,
+                                                       int n0, int bn, uint32_t taddr, int lane, uint8_t* stage,
+                                                       uint32_t stage_smem, int& chunk) {
+  const int ce = ep.out_elem_bytes;
+  bool valid = false;
+  char* dst_row = nullptr;
+  if (gm < M) {
+    const int4 c = fetch_row(rs, soff, g, gm);
+    row_base_offset(g, c, valid);
+    if (ep.mode == kEpiloguePlain) {
+      dst_row = static_cast<char*>(ep.out) + (int64_t)gm * ep.ldo * ce;
+    } else if (valid) {
+      const int64_t idx = ((int64_t)c.y * g.gh + c.z) * g.gw + c.w;
+      const int64_t slot = (int64_t)c.x * ep.dense_tokens + idx;
+      dst_row = static_cast<char*>(ep.out) + slot * ep.ldo * ce;
+      if (n0 == 0) {
+        if (ep.observed) ep.observed[slot] = 1.0f;
+        if (ep.age) ep.age[slot] = 0.0f;
+      }
+    }
+  }
+  const int cpc = kEpiChunkBytes / ce;  // columns per chunk: 64 (16-bit) or 32 (f32)
+  for (int c0 = 0; c0 < bn; c0 += cpc, ++chunk) {
+    const int col0 = n0 + c0;
+    const int ncol = min(cpc, min(bn - c0, g.D - col0));  // the same for the whole warp
+    if (ncol <= 0) break;
+    const int buf = chunk % kEpiBufs;
+    bulk_wait_read<kEpiBufs - 1>();  // this buffer's previous copy has read its source
+    __syncwarp();
+    uint8_t* srow = stage + buf * (32 * kEpiRowPitch) + lane * kEpiRowPitch;
+    for (int h = 0; h * 32 < ncol; ++h) {
+      uint32_t r[32];
+      tmem_ld_32x32b_x32(taddr + (uint32_t)(c0 + 32 * h), r);
+      tmem_ld_wait();
+      const int nh = min(32, ncol - 32 * h);
+      const float bl = (ep.bias && lane < nh) ? __ldg(ep.bias + col0 + 32 * h + lane) : 0.0f;
+      float v[32];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) {
+        const float b = __shfl_sync(0xffffffffu, bl, j);
+        v[j] = valid ? __uint_as_float(r[j]) + b : 0.0f;
+      }
+      uint8_t* d = srow + 32 * h * ce;
+      if (ep.out_dtype == BJF_DTYPE_F32)
+        pack_chunk32<float>(d, v, nh);
+      else if (ep.out_dtype == BJF_DTYPE_F16)
+        pack_chunk32<__half>(d, v, nh);
+      else
+        pack_chunk32<__nv_bfloat16>(d, v, nh);
+    }
+    if (dst_row) {
+      char* dst = dst_row + (int64_t)col0 * ce;
+      const uint32_t nbytes = (uint32_t)(ncol * ce);
+      if (((reinterpret_cast<uintptr_t>(dst) | nbytes) & 15) == 0) {
+        fence_proxy_async_smem();  // the staged bytes feed the bulk copy (async proxy)
+        bulk_store_s2g(dst, stage_smem + (uint32_t)(buf * (32 * kEpiRowPitch) + lane * kEpiRowPitch), nbytes);
+      } else {
+        for (uint32_t b = 0; b < nbytes; ++b) dst[b] = static_cast<char>(srow[b]);  // unaligned row: bytes
+      }
+    }
+    bulk_commit();
+  }
+}
+
+// Relaxed arrive on another CTA's mbarrier: the stage it announces has already landed in
+// shared memory and been fenced into the async proxy by the relaying thread.
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+// At most 80 registers per thread: with three of the ten warps on one SM sub-partition that
+// leaves room beside each CTA for two blocks of the next frame's patch-diff pass (which
+// programmatic dependent launch starts while this kernel runs).
+template <typename T>
+__global__ void __maxnreg__(80)
+    gather_gemm_sm100_pair_kernel(const __grid_constant__ CUtensorMap wmap, const T* __restrict__ video,
+                                  const RowSource rs, const int32_t* __restrict__ rows_dev,
+                                  int rows_cap, GatherGeometry g, int bn, EpilogueArgs ep,
+                                  int* __restrict__ error_flag) {
+  extern __shared__ uint8_t smem_dyn[];
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  // both CTAs use the same dynamic shared memory base, so offsets agree across the pair
+  uint8_t* smem = smem_dyn + ((1024 - (smem_u32(smem_dyn) & 1023)) & 1023);
+  int* soff = reinterpret_cast<int*>(smem + PairSmemLayout::soff_off);
+  int64_t* rowbase = reinterpret_cast<int64_t*>(smem + PairSmemLayout::rowbase_off);
+
+  pdl_wait();     // the rows and their count come from the kernels before (selection)
+  pdl_trigger();  // the next frame's patch-diff pass may start alongside this GEMM
+  int M = rows_cap;
+  if (rows_dev) M = min(M, max(0, __ldg(rows_dev)));
+  M = min(M, load_row_offsets(rs, soff));
+  const int n_tiles = (g.D + bn - 1) / bn;
+  const int num_tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * n_tiles;  // 256-row pair tiles
+  const uint32_t rank = cluster_ctarank();                           // 0: issues the MMAs
+  const int cluster = (int)(blockIdx.x >> 1);
+  const int nclusters = (int)(gridDim.x >> 1);
+  if (cluster >= num_tiles) return;  // the same for both CTAs of the pair, before any allocation
+  const int half = bn >> 1;
+  const int my_tiles = (num_tiles - cluster + nclusters - 1) / nclusters;
+
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PairSmemLayout::bar_off);
+  uint64_t* peer_full = full + kPairStages;
+  uint64_t* empty = peer_full + kPairStages;
+  uint64_t* acc_full = empty + kPairStages;
+  uint64_t* acc_empty = acc_full + 2;
+  uint64_t* prod_bar = acc_empty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PairSmemLayout::misc_off);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + PairSmemLayout::misc_off + 4);
+  int32_t* koff = reinterpret_cast<int32_t*>(smem + PairSmemLayout::koff_off);
+
+  const int num_kb = g.num_kb;
+  if (tid == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
+      mbar_init(&full[s], kProducerWarps * 32 + 1);  // 128 cp.async arrivals + the TMA thread
+      mbar_init(&peer_full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 2 * kEpilogueWarps);  // epilogue warps of both CTAs
+    }
+    mbar_init(prod_bar, kProducerWarps * 32);
+    *abort_flag = 0;
+    fence_mbarrier_init();
+  }
+  if (warp == kTmaWarp && lane == 0) tma_prefetch_desc(&wmap);
+  for (int i = tid; i < num_kb * 8; i += kThreads) koff[i] = (int32_t)k_offset(g, i * 8);
+  const uint32_t acc_cols = bn <= 32 ? 32 : (bn <= 64 ? 64 : (bn <= 128 ? 128 : 256));
+  const uint32_t tmem_cols = 2 * acc_cols;
+  if (warp == kMmaWarp) {
+    tmem_alloc_pair(tmem_slot, tmem_cols);
+    tmem_relinquish_pair();
+  }
+  tc_fence_before();
+  cluster_sync();  // barriers of both CTAs initialised and TMEM allocated before any remote arrive
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  const uint32_t a_smem = smem_u32(smem + PairSmemLayout::a_off);
+  const uint32_t b_smem = smem_u32(smem + PairSmemLayout::b_off);
+  bool aborted = false;
+
+  if (warp >= kEpilogueWarps && warp < kEpilogueWarps + kProducerWarps) {
+    // ---------------- gather producers (cp.async), both CTAs ----------------
+    const int pw_ = warp - kEpilogueWarps;
+    const int j = lane & 7;
+    const int sub = lane >> 3;
+    int kbg = 0;
+    int prod_phase = 0;
+    for (int tile = cluster; tile < num_tiles && !aborted; tile += nclusters) {
+      int64_t base[8];
+      uint32_t dst_off[8];
+      uint32_t valid_mask = 0;
+      if (!producer_rows(rs, soff, g, M, (tile / n_tiles) * (2 * kBM) + (int)rank * kBM,
+                         tid - kEpilogueWarps * 32, rowbase, pw_, sub, base, valid_mask, prod_bar, prod_phase,
+                         abort_flag)) {
+        aborted = true;
+        break;
+      }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int m = 32 * pw_ + 4 * i + sub;
+        dst_off[i] = (uint32_t)((m >> 3) * 1024 + (m & 7) * 128 + ((j ^ (m & 7)) << 4));
+      }
+      for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
+        const int s = kbg % kPairStages;
+        const uint32_t par = ((kbg / kPairStages) & 1) ^ 1;
+        if (!mbar_wait_bounded(&empty[s], par, abort_flag, kWaitLimitNs)) {
+          aborted = true;
+          break;
+        }
+        const uint32_t dst = a_smem + s * kAStageBytes;
+        const int64_t ko = koff[kb * 8 + j];
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+          if (valid_mask & (1u << i)) cp_async_16(dst + dst_off[i], video + base[i] + ko);
+        cp_async_arrive_noinc(&full[s]);
+      }
+    }
+    cp_async_wait_all();
+  } else if (warp == kMmaWarp) {
+    if (rank == 0 && lane == 0) {
+      // ---------------- MMA issuer (even CTA) ----------------
+      const uint32_t idesc = idesc_f16_f32(g.is_bf16 ? 1u : 0u, 2 * kBM, (uint32_t)bn);
+      int kbg = 0, it = 0;
+      int commits0 = 0;
+      bool issued_any = false;
+      for (int tile = cluster; tile < num_tiles && !aborted; tile += nclusters, ++it) {
+        const int buf = it & 1;
+        const uint32_t use_par = ((it >> 1) & 1) ^ 1;
+        if (!mbar_wait_bounded_cluster(&acc_empty[buf], use_par, abort_flag, kWaitLimitNs)) {
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + (uint32_t)buf * acc_cols;
+        for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
+          const int s = kbg % kPairStages;
+          const uint32_t par = (kbg / kPairStages) & 1;
+          if (!mbar_wait_bounded(&full[s], par, abort_flag, kWaitLimitNs) ||
+              !mbar_wait_bounded_cluster(&peer_full[s], par, abort_flag, kWaitLimitNs)) {
+            aborted = true;
+            break;
+          }
+          fence_proxy_async_smem();  // this CTA's landed cp.async writes feed the MMA
+          tc_fence_after();
+          const uint32_t a_base = a_smem + s * kAStageBytes;
+          const uint32_t b_base = b_smem + s * kBHalfStageBytes;
+#pragma unroll
+          for (int kk = 0; kk < kBK / 16; ++kk) {
+            mma_f16_ss_pair(d_tmem, smem_desc_sw128_kmajor(a_base + kk * 32),
+                            smem_desc_sw128_kmajor(b_base + kk * 32), idesc, (kb | kk) != 0);
+          }
+          issued_any = true;
+          mma_commit_pair(&empty[s], 0x3);
+        }
+        if (aborted) break;
+        mma_commit_pair(&acc_full[buf], 0x3);
+        commits0 += buf == 0;
+      }
+      if (aborted && issued_any) {
+        // the issued MMAs read both CTAs' shared memory and write both TMEMs: let them retire
+        // (a commit to this CTA only; bounded, abort ignored)
+        mma_commit_pair(&acc_full[0], 0x1);
+        int zero = 0;
+        mbar_wait_bounded(&acc_full[0], (uint32_t)(commits0 & 1), &zero, kWaitLimitNs);
+      }
+    } else if (rank == 1 && lane < kPairStages) {
+      // ---------------- stage relay (odd CTA): lane s relays stage s ----------------
+      const int s = lane;
+      const uint32_t remote = cluster_map(smem_u32(&peer_full[s]), 0);
+      const int total_kb = my_tiles * num_kb;
+      for (int kbg = s; kbg < total_kb; kbg += kPairStages) {
+        if (!mbar_wait_bounded(&full[s], (kbg / kPairStages) & 1, abort_flag, kWaitLimitNs)) {
+          aborted = true;
+          break;
+        }
+        fence_proxy_async_smem();  // this CTA's landed stage feeds the peer's MMA
+        mbar_arrive_remote_relaxed(remote);
+      }
+    }
+  } else if (warp == kTmaWarp) {
+    // ---------------- TMA producer (this CTA's half of the weight rows) ----------------
+    if (lane == 0) {
+      int kbg = 0;
+      for (int tile = cluster; tile < num_tiles && !aborted; tile += nclusters) {
+        const int n0 = (tile % n_tiles) * bn + (int)rank * half;
+        for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
+          const int s = kbg % kPairStages;
+          const uint32_t par = ((kbg / kPairStages) & 1) ^ 1;
+          if (!mbar_wait_bounded(&empty[s], par, abort_flag, kWaitLimitNs)) {
+            aborted = true;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[s], (uint32_t)(half * kBK * 2));
+          tma_load_2d(b_smem + s * kBHalfStageBytes, &wmap, kb * kBK, n0, &full[s]);
+        }
+      }
+      // Every stage release is a multicast from the even CTA's MMA thread: wait until the
+      // last one of each stage has landed here before this CTA's shared memory goes away.
+      int zero = 0;
+      const uint64_t limit = aborted ? 1000000ull : kWaitLimitNs;
+      for (int k = max(0, kbg - kPairStages); k < kbg; ++k)
+        mbar_wait_bounded(&empty[k % kPairStages], (k / kPairStages) & 1, &zero, limit);
+    }
+  } else {
+    // ---------------- epilogue (warps 0-3, both CTAs) ----------------
+    const int m = tid;
+    const uint32_t remote_acc_empty = cluster_map(smem_u32(&acc_empty[0]), 0);
+    uint8_t* stage = smem + PairSmemLayout::epi_off + warp * kEpiWarpBytes;
+    const uint32_t stage_smem = smem_u32(stage);
+    int chunk = 0;
+    int it = 0;
+    for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
+      const int buf = it & 1;
+      const uint32_t par = (it >> 1) & 1;
+      bool ok = mbar_wait_bounded(&acc_full[buf], par, abort_flag, kWaitLimitNs);
+      if (__any_sync(0xffffffffu, !ok)) {
+        aborted = true;
+        break;
+      }
+      tc_fence_after();
+      const int n0 = (tile % n_tiles) * bn;
+      const int gm = (tile / n_tiles) * (2 * kBM) + (int)rank * kBM + m;
+      drain_accumulator_bulk(g, ep, rs, soff, M, gm, n0, bn,
+                             tmem_base + (uint32_t)buf * acc_cols + ((uint32_t)(warp * 32) << 16), lane, stage,
+                             stage_smem, chunk);
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) {
+        if (rank == 0)
+          mbar_arrive(&acc_empty[buf]);
+        else
+          mbar_arrive_remote(remote_acc_empty + (uint32_t)buf * 8);
+      }
+    }
+    bulk_wait<0>();  // every bulk store of this thread has written global memory
+  }
+
+  if (aborted) {
+    *abort_flag = 1;
+    atomicExch(error_flag, 1);
+  }
+  tc_fence_before();
+  cluster_sync();  // no CTA leaves while its peer may still touch its barriers, smem or TMEM
+  if (warp == kMmaWarp) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem_base, tmem_cols);
+  }
+}
+
+// ---------------------------------------------------------------------------
 // SIMT path
 // ---------------------------------------------------------------------------
 constexpr int kSBM = 64, kSBN = 64, kSBK = 32, kSThreads = 256;
 
 template <typename TIn, typename TW>
 __global__ void __launch_bounds__(kSThreads)
-    gather_gemm_simt_kernel(const TIn* __restrict__ video, const int4* __restrict__ coords,
+    gather_gemm_simt_kernel(const TIn* __restrict__ video, const RowSource rs,
                             const int32_t* __restrict__ rows_dev, int rows_cap, GatherGeometry g,
                             const TW* __restrict__ weight, EpilogueArgs ep) {
+  __shared__ int soff[kMaxRowStreams + 1];
   __shared__ float As[kSBK][kSBM + 4];
   __shared__ float Ws[kSBK][kSBN + 4];
   __shared__ int64_t row_base[kSBM];
   __shared__ int row_valid[kSBM];
+  __shared__ int4 row_c[kSBM];
   __shared__ int64_t koffs[kSBK];
 
   pdl_wait();
   pdl_trigger();
   int M = rows_cap;
   if (rows_dev) M = min(M, max(0, __ldg(rows_dev)));
+  M = min(M, load_row_offsets(rs, soff));
   const int m0 = blockIdx.y * kSBM;
   if (m0 >= M) return;
   const int n0 = blockIdx.x * kSBN;
@@ -398,9 +869,14 @@ __global__ void __launch_bounds__(kSThreads)
     const int gm = m0 + tid;
     bool valid = false;
     int64_t base = 0;
-    if (gm < M) base = row_base_offset(g, coords[gm], valid);
+    int4 c = make_int4(-1, -1, -1, -1);
+    if (gm < M) {
+      c = fetch_row(rs, soff, g, gm);
+      base = row_base_offset(g, c, valid);
+    }
     row_base[tid] = base;
     row_valid[tid] = valid;
+    row_c[tid] = c;
   }
   float acc[4][4] = {};
   for (int k0 = 0; k0 < g.K; k0 += kSBK) {
@@ -443,7 +919,7 @@ __global__ void __launch_bounds__(kSThreads)
     if (ep.mode == kEpiloguePlain) {
       dst_row = static_cast<char*>(ep.out) + (int64_t)gm * ep.ldo * ce;
     } else if (valid) {
-      int4 c = coords[gm];
+      const int4 c = row_c[m];
       const int64_t slot = (int64_t)c.x * ep.dense_tokens + ((int64_t)c.y * g.gh + c.z) * g.gw + c.w;
       dst_row = static_cast<char*>(ep.out) + slot * ep.ldo * ce;
       if (blockIdx.x == 0 && tx == 0) {
@@ -475,6 +951,7 @@ int choose_bn(int D) {
 
 std::mutex g_attr_mu;
 bool g_attr_set[64][2] = {};
+int g_pair_clusters[64][2] = {};  // resident CTA-pair clusters per device and operand type
 
 }  // namespace
 
@@ -486,14 +963,16 @@ bool sm100_path_supported(const DeviceInfo& dev, const GatherGeometry& g, int32_
   if (g.K % kBK != 0 || g.K / kBK > kMaxKBlocks) return false;
   if (reinterpret_cast<uintptr_t>(input) % 16 != 0 || reinterpret_cast<uintptr_t>(weight) % 16 != 0)
     return false;
-  if (dev.max_smem_optin < (size_t)SmemLayout::alloc) return false;
+  if (dev.max_smem_optin < (size_t)SmemLayout::alloc || dev.max_smem_optin < (size_t)PairSmemLayout::alloc) return false;
   return true;
 }
 
 bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t in_dt,
                               const void* weight, int32_t w_dt, const GatherGeometry& g0,
-                              const int4* coords, const int32_t* rows_dev, int64_t rows_cap,
+                              const RowSource& rows, const int32_t* rows_dev, int64_t rows_cap,
                               const EpilogueArgs& ep, cudaStream_t st, bool pdl) {
+  if (!rows.coords && (rows.streams <= 0 || rows.streams > kMaxRowStreams || !rows.indices || !rows.offsets))
+    return fail(BJF_ERR_INVALID_ARGUMENT, "gather-GEMM index rows need 1..4096 streams, indices and offsets");
   if (rows_cap <= 0 || g0.D <= 0) return BJF_OK;
   GatherGeometry g = g0;
   g.num_kb = g.K / kBK;
@@ -516,6 +995,67 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
     if (cr != CUDA_SUCCESS)
       return fail(BJF_ERR_CUDA, "cuTensorMapEncodeTiled(weight) failed with code " + std::to_string((int)cr));
     const int slot = g.is_bf16 ? 1 : 0;
+    // CTA pairs whenever there is more than one 128-row tile of rows
+    const bool pair = rows_cap > kBM && (bn / 2) % 8 == 0;
+    if (pair) {
+      cuuint32_t pbox[2] = {(cuuint32_t)kBK, (cuuint32_t)(bn / 2)};
+      cr = encode(&map, g.is_bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                  const_cast<void*>(weight), dims, strides, pbox, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      if (cr != CUDA_SUCCESS)
+        return fail(BJF_ERR_CUDA, "cuTensorMapEncodeTiled(weight) failed with code " + std::to_string((int)cr));
+      const void* fn = g.is_bf16 ? (const void*)gather_gemm_sm100_pair_kernel<__nv_bfloat16>
+                                 : (const void*)gather_gemm_sm100_pair_kernel<__half>;
+      int max_clusters = 0;
+      {
+        std::lock_guard<std::mutex> lock(g_attr_mu);
+        if (!g_pair_clusters[dev.device][slot]) {
+          cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, PairSmemLayout::alloc);
+          if (e != cudaSuccess) return cuda_status(e, "gather-GEMM pair smem attribute");
+          cudaLaunchConfig_t cfg = {};
+          cudaLaunchAttribute attr[1];
+          attr[0].id = cudaLaunchAttributeClusterDimension;
+          attr[0].val.clusterDim.x = 2;
+          attr[0].val.clusterDim.y = 1;
+          attr[0].val.clusterDim.z = 1;
+          cfg.gridDim = dim3(2 * (unsigned)std::max(1, dev.sm_count / 2));
+          cfg.blockDim = dim3(kThreads);
+          cfg.dynamicSmemBytes = PairSmemLayout::alloc;
+          cfg.attrs = attr;
+          cfg.numAttrs = 1;
+          e = cudaOccupancyMaxActiveClusters(&max_clusters, fn, &cfg);
+          if (e != cudaSuccess) return cuda_status(e, "gather-GEMM pair occupancy");
+          if (max_clusters <= 0) return fail(BJF_ERR_CUDA, "gather-GEMM pair kernel cannot be resident");
+          g_pair_clusters[dev.device][slot] = max_clusters;
+        }
+        max_clusters = g_pair_clusters[dev.device][slot];
+      }
+      const int64_t pair_tiles_cap = ceil_div(g.D, bn) * ceil_div(rows_cap, 2 * kBM);
+      const unsigned clusters = (unsigned)std::min<int64_t>(pair_tiles_cap, max_clusters);
+      cudaLaunchConfig_t cfg = {};
+      cudaLaunchAttribute attr[2];
+      attr[0].id = cudaLaunchAttributeClusterDimension;
+      attr[0].val.clusterDim.x = 2;
+      attr[0].val.clusterDim.y = 1;
+      attr[0].val.clusterDim.z = 1;
+      attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+      attr[1].val.programmaticStreamSerializationAllowed = 1;
+      cfg.gridDim = dim3(2 * clusters);
+      cfg.blockDim = dim3(kThreads);
+      cfg.dynamicSmemBytes = PairSmemLayout::alloc;
+      cfg.stream = st;
+      cfg.attrs = attr;
+      cfg.numAttrs = pdl ? 2 : 1;
+      cudaError_t e;
+      if (g.is_bf16)
+        e = cudaLaunchKernelEx(&cfg, gather_gemm_sm100_pair_kernel<__nv_bfloat16>, map,
+                               static_cast<const __nv_bfloat16*>(input), rows, rows_dev, (int)rows_cap, g, bn, ep,
+                               dev.error_flag);
+      else
+        e = cudaLaunchKernelEx(&cfg, gather_gemm_sm100_pair_kernel<__half>, map, static_cast<const __half*>(input),
+                               rows, rows_dev, (int)rows_cap, g, bn, ep, dev.error_flag);
+      return e == cudaSuccess ? BJF_OK : cuda_status(e, "gather-GEMM (tcgen05 pair) launch");
+    }
     {
       std::lock_guard<std::mutex> lock(g_attr_mu);
       if (!g_attr_set[dev.device][slot]) {
@@ -531,11 +1071,11 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
     cudaError_t e;
     if (g.is_bf16)
       e = launch_kernel(pdl, gather_gemm_sm100_kernel<__nv_bfloat16>, grid, dim3(kThreads), SmemLayout::alloc, st,
-                        map, static_cast<const __nv_bfloat16*>(input), coords, rows_dev, (int)rows_cap, g, bn, ep,
+                        map, static_cast<const __nv_bfloat16*>(input), rows, rows_dev, (int)rows_cap, g, bn, ep,
                         dev.error_flag);
     else
       e = launch_kernel(pdl, gather_gemm_sm100_kernel<__half>, grid, dim3(kThreads), SmemLayout::alloc, st, map,
-                        static_cast<const __half*>(input), coords, rows_dev, (int)rows_cap, g, bn, ep,
+                        static_cast<const __half*>(input), rows, rows_dev, (int)rows_cap, g, bn, ep,
                         dev.error_flag);
     return e == cudaSuccess ? BJF_OK : cuda_status(e, "gather-GEMM (tcgen05) launch");
   }
@@ -543,7 +1083,7 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
   bool ok = dispatch_float(in_dt, [&](auto itag) {
     dispatch_float(w_dt, [&](auto wtag) {
       cudaError_t e = launch_kernel(pdl, gather_gemm_simt_kernel<decltype(itag), decltype(wtag)>, grid,
-                                    dim3(kSThreads), 0, st, static_cast<const decltype(itag)*>(input), coords,
+                                    dim3(kSThreads), 0, st, static_cast<const decltype(itag)*>(input), rows,
                                     rows_dev, (int)rows_cap, g, static_cast<const decltype(wtag)*>(weight), ep);
       if (e != cudaSuccess) cuda_status(e, "gather-GEMM (SIMT) launch");
     });
@@ -612,5 +1152,5 @@ extern "C" bjf_status bjf_sparse_patchify3d_forward(const bjf_patchify_config* c
   ep.ldo = g.D;
   ep.bias = bias;
   return launch_gather_gemm(*dev, input, input_dtype, weight, weight_dtype, g,
-                            reinterpret_cast<const int4*>(coords), nullptr, rows, ep, as_cuda(stream));
+                            coords_rows(reinterpret_cast<const int4*>(coords)), nullptr, rows, ep, as_cuda(stream));
 }

@@ -38,11 +38,26 @@ struct EpilogueArgs {
   const float* bias;
 };
 
-// Enqueues out = gather(input, coords) x weight^T + bias.  `rows_dev` (device,
-// nullable) caps the row count at run time; `rows_cap` bounds the grid.
+// Where the gathered rows come from: either explicit coords rows (b, t, r, col), or the
+// per-stream token indices of a selection with the first row of each stream (the plan the
+// coords form describes, without materialising it): row m belongs to the stream s with
+// offsets[s] <= m < offsets[s + 1] and is its token indices[s, m - offsets[s]].
+constexpr int kMaxRowStreams = 4096;
+struct RowSource {
+  const int4* coords;      // [rows] or null
+  const int32_t* indices;  // [streams, index_stride] when coords is null
+  const int32_t* offsets;  // [streams + 1]; offsets[streams] = row count
+  int index_stride;
+  int streams;             // <= kMaxRowStreams
+};
+
+inline RowSource coords_rows(const int4* coords) { return RowSource{coords, nullptr, nullptr, 0, 0}; }
+
+// Enqueues out = gather(input, rows) x weight^T + bias.  `rows_dev` (device, nullable)
+// caps the row count at run time; `rows_cap` bounds the grid.
 bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t in_dt,
                               const void* weight, int32_t w_dt, const GatherGeometry& g,
-                              const int4* coords, const int32_t* rows_dev, int64_t rows_cap,
+                              const RowSource& rows, const int32_t* rows_dev, int64_t rows_cap,
                               const EpilogueArgs& ep, cudaStream_t st, bool pdl = false);
 
 bool sm100_path_supported(const DeviceInfo& dev, const GatherGeometry& g, int32_t in_dt,
