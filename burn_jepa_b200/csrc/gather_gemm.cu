@@ -104,14 +104,16 @@ __device__ __forceinline__ int4 fetch_row(const RowSource& rs, const int* soff, 
 }
 
 // The 128 producer threads resolve a tile's 128 rows together: producer thread p resolves
-// row row0 + p into rowbase[p] (its element offset in the input, -1 for a zero row), so
-// each row costs one dependent load chain per tile rather than eight per thread.  Each
-// thread then picks up the eight rows it copies: 32 pw + 4 i + sub.  The producers meet
-// on an mbarrier (`bar`, 128 arrivals per phase, `phase` counts this thread's uses) whose
-// waits are bounded like every other wait, so a producer that gave up cannot strand the
-// others.  Returns false when a wait gave up.
-__device__ __forceinline__ bool producer_rows(const RowSource& rs, const int* soff, const GatherGeometry& g, int M,
-                                              int row0, int p, int64_t* rowbase, int pw, int sub,
+// row p of the tile (resolve_row, issued a tile ahead so its load latency hides behind the
+// copies of the current tile) and shares it through rowbase[p], so each row costs one
+// dependent load chain per tile rather than eight per thread.  Each thread then picks up
+// the eight rows it copies: 32 pw + 4 i + sub.  The producers meet on an mbarrier (`bar`,
+// 128 arrivals per phase, `phase` counts this thread's uses) whose waits are bounded like
+// every other wait, so a producer that gave up cannot strand the others.  Returns false
+// when a wait gave up.
+__device__ __forceinline__ int64_t resolve_row(const RowSource& rs, const int* soff, const GatherGeometry& g, int M,
+                                               int gm);
+__device__ __forceinline__ bool producer_rows(int64_t my_row, int p, int64_t* rowbase, int pw, int sub,
                                               int64_t (&base)[8], uint32_t& valid_mask, uint64_t* bar,
                                               int& phase, volatile int* abort_flag);
 
@@ -127,23 +129,22 @@ __host__ __device__ __forceinline__ int64_t k_offset(const GatherGeometry& g, in
   return (((int64_t)ch * g.T + dt) * g.H + dy) * g.W + dx;
 }
 
-__device__ __forceinline__ bool producer_rows(const RowSource& rs, const int* soff, const GatherGeometry& g, int M,
-                                              int row0, int p, int64_t* rowbase, int pw, int sub,
+// Element offset of row gm in the input, or -1 for a zero row (beyond M or outside the grid).
+__device__ __forceinline__ int64_t resolve_row(const RowSource& rs, const int* soff, const GatherGeometry& g, int M,
+                                               int gm) {
+  if (gm >= M) return -1;
+  bool valid = false;
+  const int64_t o = row_base_offset(g, fetch_row(rs, soff, g, gm), valid);
+  return valid ? o : -1;
+}
+
+__device__ __forceinline__ bool producer_rows(int64_t my_row, int p, int64_t* rowbase, int pw, int sub,
                                               int64_t (&base)[8], uint32_t& valid_mask, uint64_t* bar,
                                               int& phase, volatile int* abort_flag) {
   // every producer has read the previous tile's rows
   mbar_arrive(bar);
   if (!mbar_wait_bounded(bar, (uint32_t)(phase++ & 1), abort_flag, kWaitLimitNs)) return false;
-  {
-    const int gm = row0 + p;
-    int64_t b = -1;
-    if (gm < M) {
-      bool valid = false;
-      const int64_t o = row_base_offset(g, fetch_row(rs, soff, g, gm), valid);
-      if (valid) b = o;
-    }
-    rowbase[p] = b;
-  }
+  rowbase[p] = my_row;
   mbar_arrive(bar);
   if (!mbar_wait_bounded(bar, (uint32_t)(phase++ & 1), abort_flag, kWaitLimitNs)) return false;
   valid_mask = 0;
@@ -176,14 +177,18 @@ __device__ __forceinline__ void store_chunk(char* dst, const float (&v)[32], int
 // Epilogue of one accumulator: this warp's 32 TMEM lanes (tile rows, lane = thread) x bn
 // columns from `taddr` -> + bias -> the row's destination (plain [M, D] or its token-cache
 // slot, which also marks the slot observed with age 0).  Warp-collective.
-__device__ __forceinline__ void drain_accumulator(const GatherGeometry& g, const EpilogueArgs& ep,
-                                                  const RowSource& rs, const int* soff, int M, int gm, int n0,
-                                                  int bn, uint32_t taddr, int lane) {
+// The row's coordinates `c` come from next_row() (fetched before the accumulator wait).
+__device__ __forceinline__ int4 next_row(const RowSource& rs, const int* soff, const GatherGeometry& g, int M,
+                                         int gm) {
+  return gm < M ? fetch_row(rs, soff, g, gm) : make_int4(-1, -1, -1, -1);
+}
+
+__device__ __forceinline__ void drain_accumulator(const GatherGeometry& g, const EpilogueArgs& ep, int4 c, int M,
+                                                  int gm, int n0, int bn, uint32_t taddr, int lane) {
   const int ce = ep.out_elem_bytes;
   bool valid = false;
   char* dst_row = nullptr;
   if (gm < M) {
-    const int4 c = fetch_row(rs, soff, g, gm);
     row_base_offset(g, c, valid);
     if (ep.mode == kEpiloguePlain) {
       dst_row = static_cast<char*>(ep.out) + (int64_t)gm * ep.ldo * ce;
@@ -311,16 +316,19 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int sub = lane >> 3;              // row within a group of 4
     int kbg = 0;  // k blocks issued by this CTA so far (all tiles)
     int prod_phase = 0;
+    const int p = tid - kEpilogueWarps * 32;
+    int64_t my_row = resolve_row(rs, soff, g, M, ((int)blockIdx.x / n_tiles) * kBM + p);
     for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x) {
       // this thread's eight rows: m_i = 32 pw_ + 4 i + sub
       int64_t base[8];
       uint32_t dst_off[8];
       uint32_t valid_mask = 0;
-      if (!producer_rows(rs, soff, g, M, (tile / n_tiles) * kBM, tid - kEpilogueWarps * 32, rowbase, pw_, sub,
-                         base, valid_mask, prod_bar, prod_phase, abort_flag)) {
+      if (!producer_rows(my_row, p, rowbase, pw_, sub, base, valid_mask, prod_bar, prod_phase, abort_flag)) {
         aborted = true;
         break;
       }
+      const int next = tile + (int)gridDim.x;  // resolved now, used at the next tile
+      my_row = next < num_tiles ? resolve_row(rs, soff, g, M, (next / n_tiles) * kBM + p) : -1;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int m = 32 * pw_ + 4 * i + sub;
@@ -418,6 +426,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     // ---------------- epilogue (warps 0-3) ----------------
     const int m = tid;  // TMEM lane = tile row
     int it = 0;
+    int4 c = next_row(rs, soff, g, M, ((int)blockIdx.x / n_tiles) * kBM + m);
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int buf = it & 1;
       const uint32_t par = (it >> 1) & 1;
@@ -429,12 +438,14 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_after();
       const int n0 = (tile % n_tiles) * bn;
       const int gm = (tile / n_tiles) * kBM + m;
-      drain_accumulator(g, ep, rs, soff, M, gm, n0, bn,
-                        tmem_base + (uint32_t)buf * acc_cols + ((uint32_t)(warp * 32) << 16), lane);
+      drain_accumulator(g, ep, c, M, gm, n0, bn, tmem_base + (uint32_t)buf * acc_cols + ((uint32_t)(warp * 32) << 16),
+                        lane);
       // This warp has finished reading accumulator `buf`: hand it back to the MMA warp.
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&acc_empty[buf]);
+      const int next = tile + (int)gridDim.x;
+      if (next < num_tiles) c = next_row(rs, soff, g, M, (next / n_tiles) * kBM + m);
     }
   }
 
@@ -522,15 +533,13 @@ __device__ __forceinline__ void pack_chunk32(uint8_t* dst, const float (&v)[32],
 // 32 TMEM lanes (tile rows, lane = thread) x bn columns from `taddr` -> + bias -> the row's
 // destination.  `stage` / `stage_smem` address this warp's staging buffers; `chunk` counts
 // this thread's staged chunks (selects the buffer).  Warp-collective.
-__device__ __forceinline__ void drain_accumulator_bulk(const GatherGeometry& g, const EpilogueArgs& ep,
-                                                       const RowSource& rs, const int* soff, int M, int gm,
-                                                       int n0, int bn, uint32_t taddr, int lane, uint8_t* stage,
-                                                       uint32_t stage_smem, int& chunk) {
+__device__ __forceinline__ void drain_accumulator_bulk(const GatherGeometry& g, const EpilogueArgs& ep, int4 c,
+                                                       int M, int gm, int n0, int bn, uint32_t taddr, int lane,
+                                                       uint8_t* stage, uint32_t stage_smem, int& chunk) {
   const int ce = ep.out_elem_bytes;
   bool valid = false;
   char* dst_row = nullptr;
   if (gm < M) {
-    const int4 c = fetch_row(rs, soff, g, gm);
     row_base_offset(g, c, valid);
     if (ep.mode == kEpiloguePlain) {
       dst_row = static_cast<char*>(ep.out) + (int64_t)gm * ep.ldo * ce;
@@ -674,16 +683,19 @@ __global__ void __maxnreg__(80)
     const int sub = lane >> 3;
     int kbg = 0;
     int prod_phase = 0;
+    const int p = tid - kEpilogueWarps * 32;
+    const int row_in_pair = (int)rank * kBM + p;
+    int64_t my_row = resolve_row(rs, soff, g, M, (cluster / n_tiles) * (2 * kBM) + row_in_pair);
     for (int tile = cluster; tile < num_tiles && !aborted; tile += nclusters) {
       int64_t base[8];
       uint32_t dst_off[8];
       uint32_t valid_mask = 0;
-      if (!producer_rows(rs, soff, g, M, (tile / n_tiles) * (2 * kBM) + (int)rank * kBM,
-                         tid - kEpilogueWarps * 32, rowbase, pw_, sub, base, valid_mask, prod_bar, prod_phase,
-                         abort_flag)) {
+      if (!producer_rows(my_row, p, rowbase, pw_, sub, base, valid_mask, prod_bar, prod_phase, abort_flag)) {
         aborted = true;
         break;
       }
+      const int next = tile + nclusters;  // resolved now, used at the next tile
+      my_row = next < num_tiles ? resolve_row(rs, soff, g, M, (next / n_tiles) * (2 * kBM) + row_in_pair) : -1;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int m = 32 * pw_ + 4 * i + sub;
@@ -798,6 +810,7 @@ __global__ void __maxnreg__(80)
     const uint32_t stage_smem = smem_u32(stage);
     int chunk = 0;
     int it = 0;
+    int4 c = next_row(rs, soff, g, M, (cluster / n_tiles) * (2 * kBM) + (int)rank * kBM + m);
     for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
       const int buf = it & 1;
       const uint32_t par = (it >> 1) & 1;
@@ -809,7 +822,7 @@ __global__ void __maxnreg__(80)
       tc_fence_after();
       const int n0 = (tile % n_tiles) * bn;
       const int gm = (tile / n_tiles) * (2 * kBM) + (int)rank * kBM + m;
-      drain_accumulator_bulk(g, ep, rs, soff, M, gm, n0, bn,
+      drain_accumulator_bulk(g, ep, c, M, gm, n0, bn,
                              tmem_base + (uint32_t)buf * acc_cols + ((uint32_t)(warp * 32) << 16), lane, stage,
                              stage_smem, chunk);
       tc_fence_before();
@@ -820,6 +833,8 @@ __global__ void __maxnreg__(80)
         else
           mbar_arrive_remote(remote_acc_empty + (uint32_t)buf * 8);
       }
+      const int next = tile + nclusters;
+      if (next < num_tiles) c = next_row(rs, soff, g, M, (next / n_tiles) * (2 * kBM) + (int)rank * kBM + m);
     }
     bulk_wait<0>();  // every bulk store of this thread has written global memory
   }

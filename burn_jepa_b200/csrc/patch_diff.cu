@@ -265,6 +265,9 @@ __global__ void __launch_bounds__(kSelectThreads)
   __shared__ uint32_t sel_prefix;
   __shared__ int sel_remaining;
 
+  // The kernel after the selection (the GEMM of the fused step) may launch now and wait
+  // for this one to complete; everything before the selection has completed by now.
+  pdl_trigger();
   pdl_wait();
   const int n = p.n;
   const long long s = blockIdx.x;
@@ -387,6 +390,7 @@ __global__ void __launch_bounds__(kSelectThreads)
   __shared__ int warp_sums[33];
   __shared__ int use_sequential;
 
+  pdl_trigger();
   pdl_wait();
   const int n = p.n;
   const long long s = blockIdx.x;
