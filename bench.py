@@ -39,6 +39,14 @@ METRIC = "active tubelets/sec (1/2/4/8 B200) + % tensor-pipe/HBM roofline; ViT-L
 UNIT = "active tubelets/s"
 
 STREAMS_PER_GPU = 32
+KERNELS_PER_STEP = 3  # patch-diff scores, selection (+ row plan), gather-GEMM (+ cache write)
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one scores launch per stream of
+# this workload, from one ncu --set full capture of the scores kernel at 16 streams
+# (208 346 368 bytes / 16), scaled by the stream count for the roofline's `traffic`.
+SCORES_DRAM_BYTES_PER_STREAM = 13021648
+# The same for the CTA-pair gather-GEMM per active row (34.9 MB read + 0.6 MB written at 6 687
+# rows in the same run; cold L2, so an upper bound for a warm step).
+GEMM_DRAM_BYTES_PER_ROW = 5314
 C, T, H, W, KT, P, D = 3, 2, 1024, 1024, 2, 16, 1024
 K = C * KT * P * P
 GRID = (T // KT, H // P, W // P)
@@ -56,6 +64,8 @@ def parse_args():
     ap.add_argument("--sweep", action="store_true", help="also time densities 5/10/20/40%%")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
+    ap.add_argument("--load-seconds", type=float, default=2.0,
+                    help="back-to-back steps before the timed ones, for the clock sampler (0 under a profiler)")
     return ap.parse_args()
 
 
@@ -260,7 +270,7 @@ def run_ours(args, world, rank, local):
     except Exception:
         gpu_id = str(local)
     with ClockSampler(gpu_id) as clocks:
-        secs = time_steps(fe, videos, caches, observed, age, args.steps, args.warmup, load_s=2.0)
+        secs = time_steps(fe, videos, caches, observed, age, args.steps, args.warmup, load_s=args.load_seconds)
     tubelets = sum(counts_per_set[i % 2] for i in range(args.steps))
     max_secs = group.max(secs)
     all_tubelets = group.sum(float(tubelets))
@@ -309,12 +319,15 @@ def run_ours(args, world, rank, local):
     if dominant == "patch_diff_scores":
         roofline = {"kernel": "patch_diff_scores_vec_kernel<__half>", "bound": "hbm", "achieved": round(mask_gbs, 1),
                     "peak": hbm_peak, "unit": "GB/s", "frac": round(mask_gbs / hbm_peak, 4),
-                    "traffic": None, "peak_source": peak_kind,
+                    "traffic": SCORES_DRAM_BYTES_PER_STREAM * S, "traffic_source": "ncu capture at 16 streams, "
+                    "scaled by the stream count", "peak_source": peak_kind,
                     "algorithmic_bytes_per_launch": mask_bytes, "avg_launch_ms": round(mask_ms, 4)}
     else:
-        roofline = {"kernel": "gather_gemm_sm100_kernel<__half>", "bound": "tensor", "achieved": round(gemm_tflops, 1),
+        roofline = {"kernel": "gather_gemm_sm100_pair_kernel<__half>", "bound": "tensor",
+                    "achieved": round(gemm_tflops, 1),
                     "peak": tflops_peak, "unit": "TFLOP/s", "frac": round(gemm_tflops / tflops_peak, 4),
-                    "traffic": None, "peak_source": peak_kind,
+                    "traffic": GEMM_DRAM_BYTES_PER_ROW * rows, "traffic_source": "ncu capture at 16 streams, "
+                    "scaled by the active rows", "peak_source": peak_kind,
                     "algorithmic_flops_per_launch": 2 * rows * K * D, "avg_launch_ms": round(gemm_ms, 4)}
     kernels = {
         "patch_diff_scores": {"avg_ms": round(mask_ms, 4), "GB/s": round(mask_gbs, 1),
@@ -393,7 +406,7 @@ def run_ours(args, world, rank, local):
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": S * 4,
                 "steps": e2e_steps},
-        "gpu_launches": 4 * args.steps,
+        "gpu_launches": KERNELS_PER_STEP * args.steps,
         "clocks": clocks.summary(),
     }
     if sweep:
