@@ -52,8 +52,9 @@ __device__ __forceinline__ void tubelet_pairs(int t, int kt, int frames, int& fi
 
 // Vectorised scores: a work unit is one (stream, tubelet, token row, chunk of token
 // columns); warps stride over the units (persistent grid, 4 blocks of 8 warps per SM at
-// <= 64 registers, so ~128 KB of loads are in flight per SM and the last units leave no
-// idle tail).  Consecutive warps of a block take adjacent column chunks of the same rows.
+// <= 64 registers, the row loop unrolled eight deep so each lane keeps up to 16 loads in
+// flight; the last units leave no idle tail).  Consecutive warps of a block take adjacent
+// column chunks of the same rows.
 // Lane l covers VEC elements of token column (chunk*TPW + l/LPT).
 template <typename T>
 __global__ void __launch_bounds__(kScoreThreads, 4)
@@ -99,7 +100,7 @@ __global__ void __launch_bounds__(kScoreThreads, 4)
         for (int p = 0; p < npairs; ++p) {
           const T* nxt = vbase + (long long)(first_next + p) * plane;
           const T* prv = nxt - plane;
-#pragma unroll 4
+#pragma unroll 8
           for (int py = 0; py < P; ++py) {
             uint4 un = ld_nc_v4(nxt + (long long)py * width);
             uint4 up = ld_nc_v4(prv + (long long)py * width);
@@ -274,7 +275,6 @@ __global__ void __launch_bounds__(kSelectThreads)
   const float* sc = scores + s * n;
   int seg_b, seg_e;
   thread_segment(n, seg_b, seg_e);
-  age_stream(p, s);
 
   // a thread's segment is at most 32 tokens (n <= 32768, 1024 threads): one pass bit each
   int pass_local = 0;
@@ -286,6 +286,7 @@ __global__ void __launch_bounds__(kSelectThreads)
     pass_local += pass;
     pass_bits |= (uint32_t)pass << (i - seg_b);
   }
+  age_stream(p, s);  // independent of the scores: its loads overlap the scan below
   int n_pass;
   const int pass_pos = block_exclusive_scan(pass_local, warp_sums, &n_pass);
   const int n_sel = max(min(n_pass, p.cap), p.fill_target);
