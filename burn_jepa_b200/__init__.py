@@ -218,6 +218,59 @@ def feature_memory_assign_latest(features, observed, age_frames, tokens, token_i
         int(bool(age_observed)), _stream(stream)))
 
 
+def feature_memory_update_ema(features, observed, age_frames, tokens, token_indices, alpha: float,
+                              age_observed: bool, stream=None):
+    """EMA mode of `InterframeJepaFeatureMemory::update_tokens` (src/feature_memory.rs:227-290), in place.
+
+    Same shapes as feature_memory_assign_latest; alpha is clamped to [0, 1]."""
+    check(load().bjf_feature_memory_update_ema(
+        _ptr(features), _dtype_code(features), _abi.dims(*features.shape), _ptr(observed),
+        _abi.dims(*observed.shape), _ptr(age_frames), _abi.dims(*age_frames.shape), _ptr(tokens),
+        _dtype_code(tokens), _abi.dims(*tokens.shape), _ptr(token_indices), _abi.dims(*token_indices.shape),
+        float(alpha), int(bool(age_observed)), _stream(stream)))
+
+
+def feature_memory_reset_rows(features, observed, age_frames, rows, stream=None):
+    """`InterframeJepaFeatureMemory::reset_rows` (src/feature_memory.rs:348-375): zero the listed batch rows.
+
+    rows: device int32 [R]; rows outside [0, B) are skipped."""
+    check(load().bjf_feature_memory_reset_rows(
+        _ptr(features), _dtype_code(features), _abi.dims(*features.shape), _ptr(observed), _ptr(age_frames),
+        _ptr(rows), int(rows.numel()), _stream(stream)))
+
+
+# ---------------------------------------------------------------------------
+# Live viewer scorer (RGBA u8 frames)
+# ---------------------------------------------------------------------------
+RgbaFrameStats = _abi.RgbaFrameStats
+
+
+def patch_diff_scores_from_rgba(prev, current, patch_size: int, grid, stats: bool = False, stream=None):
+    """`patch_diff_scores_from_rgba` (src/viewer.rs:1126-1157) for S frame pairs at once.
+
+    prev / current: uint8 [S, H, W, 4] (or [H, W, 4]) RGBA on the device; grid = (1, gh, gw).
+    Returns scores [S, gh * gw] f32 (and the per-stream RgbaFrameStats list when `stats`)."""
+    torch = _torch()
+    single = prev.dim() == 3
+    if single:
+        prev, current = prev.unsqueeze(0), current.unsqueeze(0)
+    S, H, W, _ = prev.shape
+    g = tuple(int(v) for v in (grid.depth, grid.height, grid.width)) if hasattr(grid, "depth") else tuple(grid)
+    scores = torch.empty((S, g[1] * g[2]), dtype=torch.float32, device=prev.device)
+    nbytes = load().bjf_rgba_patch_diff_workspace_bytes(S)
+    ws = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=prev.device)
+    st = torch.empty((S, ctypes.sizeof(RgbaFrameStats)), dtype=torch.uint8, device=prev.device) if stats else None
+    check(load().bjf_rgba_patch_diff_scores(
+        _ptr(prev), _ptr(current), S, W, H, int(patch_size), _abi.dims(*g), _ptr(scores),
+        _ptr(st) if st is not None else None, _ptr(ws), ws.numel(), _stream(stream)))
+    out = scores[0] if single else scores
+    if not stats:
+        return out
+    raw = st.cpu().numpy().tobytes()
+    sz = ctypes.sizeof(RgbaFrameStats)
+    return out, [RgbaFrameStats.from_buffer_copy(raw[i * sz:(i + 1) * sz]) for i in range(S)]
+
+
 # ---------------------------------------------------------------------------
 # Fused step over S independent streams
 # ---------------------------------------------------------------------------

@@ -102,6 +102,18 @@ class FrontEndDesc(ctypes.Structure):
     ]
 
 
+class RgbaFrameStats(ctypes.Structure):
+    """bjf_rgba_frame_stats: RgbaPatchDiffFrameStats (src/viewer.rs:1067-1076) plus the two means."""
+
+    _fields_ = [
+        ("channel_delta", ctypes.c_float * 3),
+        ("luma_delta", ctypes.c_float),
+        ("compensate_global_lighting", ctypes.c_int32),
+        ("raw_abs", ctypes.c_float),
+        ("residual_abs", ctypes.c_float),
+    ]
+
+
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I32 = ctypes.c_int32
@@ -123,8 +135,13 @@ SIGNATURES = {
     "bjf_front_end_step": (_I32, [ctypes.POINTER(FrontEndDesc), _P, _P, _P, _P, _P, _P, _I32, _P, ctypes.c_size_t,
                                   _P, _P]),
     "bjf_front_end_step_no_alloc": (_I32, [ctypes.POINTER(FrontEndDesc), _P, _P, _P, _P, _P, _P, _I32, _P, _P]),
+    "bjf_rgba_patch_diff_workspace_bytes": (ctypes.c_size_t, [_I64]),
+    "bjf_rgba_patch_diff_scores": (_I32, [_P, _P, _I64, _I64, _I64, _I64, _DIMS, _P, _P, _P, ctypes.c_size_t, _P]),
     "bjf_feature_memory_assign_latest": (_I32, [_P, _I32, _DIMS, _P, _DIMS, _P, _DIMS, _P, _I32, _DIMS, _P, _DIMS,
                                                 _I32, _P]),
+    "bjf_feature_memory_update_ema": (_I32, [_P, _I32, _DIMS, _P, _DIMS, _P, _DIMS, _P, _I32, _DIMS, _P, _DIMS,
+                                             ctypes.c_float, _I32, _P]),
+    "bjf_feature_memory_reset_rows": (_I32, [_P, _I32, _DIMS, _P, _P, _P, _I64, _P]),
 }
 
 _lib = None

@@ -197,6 +197,63 @@ BJF_API bjf_status bjf_feature_memory_assign_latest(void* features, bjf_dtype fe
                                             const int64_t indices_dims[2], int32_t age_observed,
                                             bjf_stream_t stream);
 
+/* Replaces the EMA mode of `InterframeJepaFeatureMemory::update_tokens`
+ * (InterframeJepaFeatureUpdateMode::Ema, src/feature_memory.rs:227-290), which the
+ * reference runs on its portable tensor path (update_tokens_tiled_assign_cuda falls back to
+ * it, :624-626).  In place, same shapes and errors as bjf_feature_memory_assign_latest:
+ *   if age_observed: age_frames += observed
+ *   features[b, idx, :] += (prev (1 - alpha) + tok alpha) observed[b, idx] + tok (1 - observed[b, idx]) - prev
+ *   observed = 1; age_frames = 0
+ * in the reference's f32 operation order; alpha is clamped to [0, 1] as the config's
+ * normalisation does.  Duplicate indices in a row race (the reference adds their deltas). */
+BJF_API bjf_status bjf_feature_memory_update_ema(void* features, bjf_dtype features_dtype,
+                                                 const int64_t features_dims[3], float* observed,
+                                                 const int64_t observed_dims[2], float* age_frames,
+                                                 const int64_t age_dims[2], const void* tokens,
+                                                 bjf_dtype tokens_dtype, const int64_t tokens_dims[3],
+                                                 const int32_t* token_indices, const int64_t indices_dims[2],
+                                                 float alpha, int32_t age_observed, bjf_stream_t stream);
+
+/* Replaces `InterframeJepaFeatureMemory::reset_rows` (src/feature_memory.rs:348-375): zeroes
+ * features[r], observed[r] and age_frames[r] for each of the `row_count` batch rows listed in
+ * `rows` (device int32).  Rows outside [0, B) are skipped (the host-list form,
+ * reset_row_indices :377-386, rejects them first in the C++ layer).  row_count 0 is a
+ * no-op; at most 65535 rows per call. */
+BJF_API bjf_status bjf_feature_memory_reset_rows(void* features, bjf_dtype features_dtype,
+                                                 const int64_t features_dims[3], float* observed,
+                                                 float* age_frames, const int32_t* rows, int64_t row_count,
+                                                 bjf_stream_t stream);
+
+/* ------------------------------------------------------------------------
+ * Live viewer scorer (RGBA u8 camera frames)
+ * ---------------------------------------------------------------------- */
+
+/* RgbaPatchDiffFrameStats (src/viewer.rs:1067-1076) plus the two means the compensation
+ * decision compares. */
+typedef struct bjf_rgba_frame_stats {
+  float channel_delta[3]; /* mean RGB delta in [0, 1] units */
+  float luma_delta;       /* mean luma delta */
+  int32_t compensate_global_lighting;
+  float raw_abs;          /* mean per-pixel |delta| */
+  float residual_abs;     /* mean per-pixel |delta - channel_delta| */
+} bjf_rgba_frame_stats;
+
+/* Bytes of device workspace bjf_rgba_patch_diff_scores needs for `streams` frame pairs
+ * (0 for a stream count outside 1..65535). */
+BJF_API size_t bjf_rgba_patch_diff_workspace_bytes(int64_t streams);
+
+/* Replaces `patch_diff_scores_from_rgba` (src/viewer.rs:1126-1157) with its frame statistics
+ * `rgba_patch_diff_frame_stats` (:1079-1124), for S frame pairs at once.  prev / current:
+ * [S, height, width, 4] u8 RGBA (4-byte aligned); grid = {1, height / P, width / P};
+ * scores: [S, grid[1] * grid[2]] f32 (device); stats_out: [S] (device, nullable).  The
+ * lighting statistics cover all height x width pixels of each frame, as the reference's cover
+ * its whole buffers.  Errors use the reference's messages (:1133-1146). */
+BJF_API bjf_status bjf_rgba_patch_diff_scores(const uint8_t* prev, const uint8_t* current, int64_t streams,
+                                              int64_t width, int64_t height, int64_t patch_size,
+                                              const int64_t grid[3], float* scores,
+                                              bjf_rgba_frame_stats* stats_out, void* workspace,
+                                              size_t workspace_bytes, bjf_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Fused step: mask -> plan -> patchify -> cache write, for S independent streams
  * ---------------------------------------------------------------------- */

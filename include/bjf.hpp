@@ -13,8 +13,10 @@
 //   SparsePatchifyPlan, SparsePatchifyBatchPlan                    src/sparse_patchify.rs:236-330
 //   SparsePatchify3dConfig, sparse_patchify3d_forward_cuda         burn_flex_gmm 0.21.2, called at
 //                                                                  src/model.rs:1297-1327
-//   InterframeJepaFeatureMemory (+ update_tokens_tiled_assign_cuda) src/feature_memory.rs:137-645
+//   InterframeJepaFeatureMemory(Config) (+ update_tokens, reset_rows) src/feature_memory.rs:7-645
 //   FrontEnd (one frame step over S streams)                       src/highres_pipeline.rs:2021-2040
+//   patch_diff_scores_from_rgba, patch_diff_dense_fallback,
+//   dilate_sparse_patch_mask, bucket_sparse_mask                   src/viewer.rs:780-885, 1067-1270
 //
 // Rust's Result<T> becomes a return value or a thrown bjf::Error carrying the status and
 // the message (the reference's wording where it has one).  Device tensors are bjf::Tensor:
@@ -472,6 +474,90 @@ inline SparseTokenMask patch_diff_context_mask_from_video(const Tensor& video, s
 }
 
 // ---------------------------------------------------------------------------------------
+// live viewer policy (src/viewer.rs): RGBA scorer and mask post-processing
+// ---------------------------------------------------------------------------------------
+constexpr float DEFAULT_PATCH_DIFF_QUALITY = 0.97f;                               // :19
+constexpr float DEFAULT_PATCH_DIFF_THRESHOLD = 1.0f - DEFAULT_PATCH_DIFF_QUALITY;  // :25
+constexpr float DEFAULT_PATCH_DIFF_DENSE_FALLBACK_DENSITY = 0.75f;                // :27
+constexpr size_t DEFAULT_PATCH_DIFF_DILATION_TILES = 1;                           // :29
+constexpr size_t DEFAULT_SPARSE_MASK_BUCKET_TOKENS = 256;                         // :31
+
+using RgbaPatchDiffFrameStats = bjf_rgba_frame_stats;
+
+// patch_diff_scores_from_rgba (src/viewer.rs:1126-1157) for `streams` frame pairs:
+// prev / current are device RGBA u8 [streams, height, width, 4].  Returns scores
+// [streams, grid.height * grid.width]; fills `stats` (host) when given.
+inline Tensor patch_diff_scores_from_rgba(const uint8_t* prev, const uint8_t* current, size_t width, size_t height,
+                                          size_t patch_size, TokenGridShape grid, size_t streams = 1,
+                                          std::vector<RgbaPatchDiffFrameStats>* stats = nullptr,
+                                          cudaStream_t st = nullptr) {
+  const size_t ws_bytes = bjf_rgba_patch_diff_workspace_bytes((int64_t)streams);
+  ensure(ws_bytes > 0, "RGBA patch-diff supports 1..65535 streams");
+  Tensor ws({(int64_t)((ws_bytes + 3) / 4)}, BJF_DTYPE_F32);
+  Tensor scores({(int64_t)streams, (int64_t)(grid.height * grid.width)}, BJF_DTYPE_F32);
+  void* dstats = nullptr;
+  if (stats) check_cuda(cudaMalloc(&dstats, sizeof(RgbaPatchDiffFrameStats) * streams), "cudaMalloc");
+  const auto g = grid.dims();
+  const bjf_status rc = bjf_rgba_patch_diff_scores(prev, current, (int64_t)streams, (int64_t)width, (int64_t)height,
+                                                   (int64_t)patch_size, g.data(), static_cast<float*>(scores.data()),
+                                                   static_cast<bjf_rgba_frame_stats*>(dstats), ws.data(), ws.nbytes(),
+                                                   to_bjf(st));
+  if (rc != BJF_OK) {
+    if (dstats) cudaFree(dstats);
+    throw Error(rc, last_error_string());
+  }
+  if (stats) {
+    stats->resize(streams);
+    cudaError_t e = cudaMemcpyAsync(stats->data(), dstats, sizeof(RgbaPatchDiffFrameStats) * streams,
+                                    cudaMemcpyDeviceToHost, st);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+    cudaFree(dstats);
+    check_cuda(e, "RGBA stats readback");
+  }
+  return scores;
+}
+
+// patch_diff_dense_fallback (src/viewer.rs:780-793): every token once the mask reaches
+// ceil(len * density) tokens (below the whole grid).
+inline SparseTokenMask patch_diff_dense_fallback(SparseTokenMask mask, TokenGridShape grid, float fallback_density) {
+  const float d = std::min(std::max(fallback_density, 0.0f), 1.0f);
+  const size_t fallback = (size_t)std::ceil((float)grid.len() * d);
+  if (mask.len() == grid.len() || (fallback < grid.len() && mask.len() >= std::max<size_t>(fallback, 1)))
+    return SparseTokenMask::all(grid.len());
+  return mask;
+}
+
+// dilate_sparse_patch_mask (src/viewer.rs:796-816, 844-869): every token within `dilation`
+// tiles of a mask token in the same tubelet; no cap.
+inline SparseTokenMask dilate_sparse_patch_mask(SparseTokenMask mask, TokenGridShape grid, size_t dilation) {
+  ensure(mask.dense_len() == grid.len(), "patch-diff dilation mask must match the token grid");
+  if (dilation == 0 || mask.is_dense_ordered()) return mask;
+  std::vector<bool> keep(grid.len(), false);
+  std::vector<size_t> selected;
+  for (size_t index : mask.indices()) {
+    if (index >= grid.len()) continue;
+    const auto [t, row, col] = token_index_to_coords(index, grid);
+    const size_t r0 = row > dilation ? row - dilation : 0, c0 = col > dilation ? col - dilation : 0;
+    const size_t r1 = std::min(row + dilation, grid.height - 1), c1 = std::min(col + dilation, grid.width - 1);
+    for (size_t r = r0; r <= r1; ++r)
+      for (size_t c = c0; c <= c1; ++c) {
+        const size_t i = coords_to_token_index(t, r, c, grid);
+        if (!keep[i]) {
+          keep[i] = true;
+          selected.push_back(i);
+        }
+      }
+  }
+  return SparseTokenMask::new_(std::move(selected), grid.len());
+}
+
+// bucket_sparse_mask (src/viewer.rs:873-885): pad to a multiple of min(bucket, len / 4).
+inline SparseTokenMask bucket_sparse_mask(SparseTokenMask mask, TokenGridShape grid, size_t bucket_tokens) {
+  if (bucket_tokens <= 1 || grid.len() < 256 || mask.is_dense_ordered()) return mask;
+  return mask.padded_to_multiple(std::min(bucket_tokens, std::max<size_t>(grid.len() / 4, 1)));
+}
+
+// ---------------------------------------------------------------------------------------
 // plans (src/sparse_patchify.rs:236-330): coords rows (b, t, r, c), batch-major
 // ---------------------------------------------------------------------------------------
 class SparsePatchifyPlan {
@@ -621,15 +707,44 @@ struct InterframeJepaFeatureMemoryOutput {
   size_t dense_tokens;
 };
 
+// InterframeJepaFeatureMemoryConfig (src/feature_memory.rs:7-49): AssignLatest or Ema { alpha }.
+struct InterframeJepaFeatureMemoryConfig {
+  enum class UpdateMode { AssignLatest, Ema };
+  UpdateMode update_mode = UpdateMode::AssignLatest;
+  float alpha = 0.0f;  // Ema only
+
+  static InterframeJepaFeatureMemoryConfig assign_latest() { return {}; }
+  static InterframeJepaFeatureMemoryConfig ema(float alpha) {
+    InterframeJepaFeatureMemoryConfig c;
+    c.update_mode = UpdateMode::Ema;
+    c.alpha = alpha;
+    return c;
+  }
+  // alpha clamped to [0, 1] (a NaN stays NaN), as the reference normalises it
+  InterframeJepaFeatureMemoryConfig normalized() const {
+    InterframeJepaFeatureMemoryConfig c = *this;
+    if (c.alpha < 0.0f) c.alpha = 0.0f;
+    if (c.alpha > 1.0f) c.alpha = 1.0f;
+    return c;
+  }
+};
+
 class InterframeJepaFeatureMemory {
  public:
   // `features_dtype` f32 as the reference, or f16 / bf16 for a half-size cache.
   static InterframeJepaFeatureMemory new_(size_t batch, TokenGridShape grid, size_t embed_dim,
                                           bjf_dtype features_dtype = BJF_DTYPE_F32, cudaStream_t st = nullptr) {
+    return with_config(InterframeJepaFeatureMemoryConfig::assign_latest(), batch, grid, embed_dim, features_dtype,
+                       st);
+  }
+  static InterframeJepaFeatureMemory with_config(const InterframeJepaFeatureMemoryConfig& config, size_t batch,
+                                                 TokenGridShape grid, size_t embed_dim,
+                                                 bjf_dtype features_dtype = BJF_DTYPE_F32, cudaStream_t st = nullptr) {
     ensure(batch > 0, "feature memory batch must be nonzero");
     ensure(!grid.is_empty(), "feature memory grid must be nonempty");
     ensure(embed_dim > 0, "feature memory embed dim must be nonzero");
     InterframeJepaFeatureMemory m;
+    m.config_ = config.normalized();
     m.batch_ = batch;
     m.grid_ = grid;
     m.embed_dim_ = embed_dim;
@@ -645,13 +760,22 @@ class InterframeJepaFeatureMemory {
   size_t dense_tokens() const { return grid_.len(); }
   size_t embed_dim() const { return embed_dim_; }
   size_t step() const { return step_; }
+  InterframeJepaFeatureMemoryConfig config() const { return config_; }
   InterframeJepaFeatureMemoryOutput snapshot() const { return output(last_updated_tokens_); }
   Tensor& features() { return features_; }
   Tensor& observed() { return observed_; }
   Tensor& age_frames() { return age_frames_; }
 
+  // update_tokens (src/feature_memory.rs:227-290) in the configured mode, on the device.
+  InterframeJepaFeatureMemoryOutput update_tokens(const Tensor& tokens, const Tensor& token_indices,
+                                                  TokenGridShape grid, cudaStream_t st = nullptr) {
+    return update_tokens_tiled_assign_cuda(tokens, token_indices, grid, st);
+  }
+
   // tokens [B, S, D], token_indices [B, S] int32.  In place (the reference copies the cache
-  // first; a caller that keeps the previous snapshot clones it before this call).
+  // first; a caller that keeps the previous snapshot clones it before this call).  In EMA
+  // mode the reference falls back to its portable update (src/feature_memory.rs:624-626);
+  // here the EMA update runs on the device too.
   InterframeJepaFeatureMemoryOutput update_tokens_tiled_assign_cuda(const Tensor& tokens,
                                                                    const Tensor& token_indices,
                                                                    TokenGridShape grid, cudaStream_t st = nullptr) {
@@ -669,11 +793,18 @@ class InterframeJepaFeatureMemory {
     const int64_t ad[2] = {age_frames_.shape()[0], age_frames_.shape()[1]};
     const int64_t td[3] = {b, s, d};
     const int64_t id[2] = {b, s};
-    check(bjf_feature_memory_assign_latest(features_.data(), features_.dtype(), fd,
-                                           static_cast<float*>(observed_.data()), od,
-                                           static_cast<float*>(age_frames_.data()), ad, tokens.data(),
-                                           tokens.dtype(), td, static_cast<const int32_t*>(token_indices.data()),
-                                           id, step_ > 0 ? 1 : 0, to_bjf(st)));
+    if (config_.update_mode == InterframeJepaFeatureMemoryConfig::UpdateMode::Ema)
+      check(bjf_feature_memory_update_ema(features_.data(), features_.dtype(), fd,
+                                          static_cast<float*>(observed_.data()), od,
+                                          static_cast<float*>(age_frames_.data()), ad, tokens.data(), tokens.dtype(),
+                                          td, static_cast<const int32_t*>(token_indices.data()), id, config_.alpha,
+                                          step_ > 0 ? 1 : 0, to_bjf(st)));
+    else
+      check(bjf_feature_memory_assign_latest(features_.data(), features_.dtype(), fd,
+                                             static_cast<float*>(observed_.data()), od,
+                                             static_cast<float*>(age_frames_.data()), ad, tokens.data(),
+                                             tokens.dtype(), td, static_cast<const int32_t*>(token_indices.data()),
+                                             id, step_ > 0 ? 1 : 0, to_bjf(st)));
     step_ += 1;
     last_updated_tokens_ = (size_t)(b * s);
     return output(last_updated_tokens_);
@@ -700,6 +831,17 @@ class InterframeJepaFeatureMemory {
     last_updated_tokens_ = 0;
   }
 
+  // reset_rows (src/feature_memory.rs:348-375): rows is a device int32 tensor [R]; rows outside
+  // the batch are skipped.
+  void reset_rows(const Tensor& rows, cudaStream_t st = nullptr) {
+    ensure(rows.rank() == 1 && rows.dtype() == BJF_DTYPE_I32, "feature memory reset rows must be an int32 [R] tensor");
+    if (rows.numel() == 0) return;
+    const int64_t fd[3] = {features_.shape()[0], features_.shape()[1], features_.shape()[2]};
+    check(bjf_feature_memory_reset_rows(features_.data(), features_.dtype(), fd, static_cast<float*>(observed_.data()),
+                                        static_cast<float*>(age_frames_.data()),
+                                        static_cast<const int32_t*>(rows.data()), (int64_t)rows.numel(), to_bjf(st)));
+  }
+
   // Zeroes the features and metadata of the given batch rows (src/feature_memory.rs:377-385).
   void reset_row_indices(const std::vector<size_t>& rows, cudaStream_t st = nullptr) {
     if (rows.empty()) return;
@@ -719,6 +861,7 @@ class InterframeJepaFeatureMemory {
   InterframeJepaFeatureMemoryOutput output(size_t updated) const {
     return {&features_, &observed_, &age_frames_, grid_, step_, updated, grid_.len()};
   }
+  InterframeJepaFeatureMemoryConfig config_;
   size_t batch_ = 0, embed_dim_ = 0, step_ = 0, last_updated_tokens_ = 0;
   TokenGridShape grid_;
   Tensor features_, observed_, age_frames_;

@@ -83,6 +83,12 @@ class PatchDiffConfig(ctypes.Structure):
         """SparseJepaPatchDiffSparsityConfig::adaptive_threshold (nodes.rs:121-136)."""
         return cls(threshold, max_context_tokens, target_tokens, 0, min_context_tokens, 0, 1)
 
+    def with_dilation(self, dilation):
+        """SparseJepaPatchDiffSparsityConfig::with_dilation (nodes.rs:138-141)."""
+        c = PatchDiffConfig.from_buffer_copy(self)
+        c.dilation = dilation
+        return c
+
 
 class PatchifyConfig(ctypes.Structure):
     """burn_flex_gmm::SparsePatchify3dConfig as built at src/model.rs:1297-1306."""
@@ -137,6 +143,20 @@ def _declare(L):
     L.bjo_patch_embed3d_dense.restype = ctypes.c_int
     L.bjo_feature_memory_assign_latest.argtypes = [_P] * 5 + [_I64] * 4 + [ctypes.c_int32]
     L.bjo_feature_memory_assign_latest.restype = ctypes.c_int
+    L.bjo_feature_memory_update_ema.argtypes = [_P] * 5 + [_I64] * 4 + [ctypes.c_float, ctypes.c_int32]
+    L.bjo_feature_memory_update_ema.restype = ctypes.c_int
+    L.bjo_feature_memory_reset_rows.argtypes = [_P] * 3 + [_I64] * 3 + [_P, _I64]
+    L.bjo_feature_memory_reset_rows.restype = ctypes.c_int
+    L.bjo_rgba_patch_diff_frame_stats.argtypes = [_P, _I64, _P, _I64, _P]
+    L.bjo_rgba_patch_diff_frame_stats.restype = None
+    L.bjo_patch_diff_scores_from_rgba.argtypes = [_P, _I64, _P, _I64] + [_I64] * 5 + [_P, _P]
+    L.bjo_patch_diff_scores_from_rgba.restype = ctypes.c_int
+    L.bjo_patch_diff_dense_fallback.argtypes = [_P, _I64, _I64, ctypes.c_float, _P]
+    L.bjo_patch_diff_dense_fallback.restype = _I64
+    L.bjo_dilate_sparse_patch_mask.argtypes = [_P] + [_I64] * 5 + [_P]
+    L.bjo_dilate_sparse_patch_mask.restype = _I64
+    L.bjo_bucket_sparse_mask.argtypes = [_P, _I64, _I64, _I64, _P]
+    L.bjo_bucket_sparse_mask.restype = _I64
     L.bjo_front_end_streams.argtypes = [_P, _I64, _P, _P, _P, _P, _P, _P, _P, ctypes.c_int32, _P]
     L.bjo_front_end_streams.restype = ctypes.c_int
     L.bjo_splitmix64.argtypes = [ctypes.c_uint64]
@@ -338,6 +358,84 @@ def feature_memory_assign_latest(features, observed, age_frames, tokens, token_i
     S = i.shape[1]
     _check(lib().bjo_feature_memory_assign_latest(
         _ptr(features), _ptr(observed), _ptr(age_frames), _ptr(t), _ptr(i), B, N, D, S, int(bool(age_observed))))
+
+
+def feature_memory_update_ema(features, observed, age_frames, tokens, token_indices, alpha: float,
+                              age_observed: bool):
+    """EMA update mode (src/feature_memory.rs:227-290), in place on float32 numpy arrays."""
+    for a in (features, observed, age_frames):
+        assert a.dtype == np.float32 and a.flags.c_contiguous
+    t = np.ascontiguousarray(tokens, dtype=np.float32)
+    i = np.ascontiguousarray(token_indices, dtype=np.int32)
+    B, N, D = features.shape
+    S = i.shape[1]
+    _check(lib().bjo_feature_memory_update_ema(
+        _ptr(features), _ptr(observed), _ptr(age_frames), _ptr(t), _ptr(i), B, N, D, S, float(alpha),
+        int(bool(age_observed))))
+
+
+def feature_memory_reset_rows(features, observed, age_frames, rows):
+    """reset_rows (src/feature_memory.rs:348-375), in place."""
+    for a in (features, observed, age_frames):
+        assert a.dtype == np.float32 and a.flags.c_contiguous
+    r = np.ascontiguousarray(rows, dtype=np.int32)
+    B, N, D = features.shape
+    _check(lib().bjo_feature_memory_reset_rows(_ptr(features), _ptr(observed), _ptr(age_frames), B, N, D, _ptr(r),
+                                              r.size))
+
+
+# ---- live viewer policy (src/viewer.rs) ----
+class RgbaFrameStats(ctypes.Structure):
+    """RgbaPatchDiffFrameStats (src/viewer.rs:1067-1076) plus the means the decision compares."""
+
+    _fields_ = [("channel_delta", ctypes.c_float * 3), ("luma_delta", ctypes.c_float),
+                ("compensate_global_lighting", ctypes.c_int32), ("raw_abs", ctypes.c_float),
+                ("residual_abs", ctypes.c_float)]
+
+
+def rgba_patch_diff_frame_stats(prev, current) -> RgbaFrameStats:
+    """rgba_patch_diff_frame_stats (src/viewer.rs:1079-1124) over two RGBA u8 buffers."""
+    p = np.ascontiguousarray(prev, dtype=np.uint8).ravel()
+    c = np.ascontiguousarray(current, dtype=np.uint8).ravel()
+    st = RgbaFrameStats()
+    lib().bjo_rgba_patch_diff_frame_stats(_ptr(p), p.size, _ptr(c), c.size, ctypes.byref(st))
+    return st
+
+
+def patch_diff_scores_from_rgba(prev, current, width: int, patch_size: int, grid: "TokenGridShape"):
+    """patch_diff_scores_from_rgba (src/viewer.rs:1126-1157): scores [grid.len()] f32 and the stats."""
+    p = np.ascontiguousarray(prev, dtype=np.uint8).ravel()
+    c = np.ascontiguousarray(current, dtype=np.uint8).ravel()
+    out = np.zeros(grid.height * grid.width, dtype=np.float32)
+    st = RgbaFrameStats()
+    _check(lib().bjo_patch_diff_scores_from_rgba(_ptr(p), p.size, _ptr(c), c.size, width, patch_size, grid.depth,
+                                                 grid.height, grid.width, _ptr(out), ctypes.byref(st)))
+    return out, st
+
+
+def patch_diff_dense_fallback(indices, dense_len: int, fallback_density: float) -> np.ndarray:
+    """patch_diff_dense_fallback (src/viewer.rs:780-793)."""
+    a = np.ascontiguousarray(np.asarray(indices, dtype=np.int64))
+    out = np.zeros(max(dense_len, a.size, 1), dtype=np.int64)
+    n = lib().bjo_patch_diff_dense_fallback(_ptr(a), a.size, dense_len, float(fallback_density), _ptr(out))
+    return out[:n].copy()
+
+
+def dilate_sparse_patch_mask(indices, grid: "TokenGridShape", dilation: int) -> np.ndarray:
+    """dilate_sparse_patch_mask (src/viewer.rs:796-816)."""
+    a = np.ascontiguousarray(np.asarray(indices, dtype=np.int64))
+    out = np.zeros(max(len(grid), a.size, 1), dtype=np.int64)
+    n = _check(lib().bjo_dilate_sparse_patch_mask(_ptr(a), a.size, grid.depth, grid.height, grid.width, dilation,
+                                                  _ptr(out)))
+    return out[:n].copy()
+
+
+def bucket_sparse_mask(indices, dense_len: int, bucket_tokens: int) -> np.ndarray:
+    """bucket_sparse_mask (src/viewer.rs:873-885)."""
+    a = np.ascontiguousarray(np.asarray(indices, dtype=np.int64))
+    out = np.zeros(max(dense_len, a.size, 1), dtype=np.int64)
+    n = lib().bjo_bucket_sparse_mask(_ptr(a), a.size, dense_len, bucket_tokens, _ptr(out))
+    return out[:n].copy()
 
 
 def front_end_streams(video, config: PatchifyConfig, mask_config: PatchDiffConfig, weight, bias,

@@ -471,6 +471,75 @@ int bjo_feature_memory_assign_latest(float* features, float* observed, float* ag
   return BJO_OK;
 }
 
+/* src/feature_memory.rs:227-290, InterframeJepaFeatureUpdateMode::Ema { alpha } (the
+ * portable update_tokens path, with the config's clamp of alpha, :40-48):
+ *   if age_observed: age += observed
+ *   previous = features[b, idx]; obs = observed[b, idx]            (gathered before any write)
+ *   blended = previous * (1 - alpha) + tokens * alpha
+ *   delta = (blended * obs + tokens * (-obs + 1)) - previous
+ *   features = features.scatter(idx, delta, Add)                   (duplicates add their deltas)
+ *   observed += 1 - observed[b, idx];  age += 0 - age[b, idx]      (scatter-add likewise)
+ * f32 arithmetic, one operation at a time (the build does not contract). */
+int bjo_feature_memory_update_ema(float* features, float* observed, float* age_frames, const float* tokens,
+                                  const int32_t* token_indices, int64_t batch, int64_t dense_tokens,
+                                  int64_t embed_dim, int64_t sparse_len, float alpha, int32_t age_observed) {
+  if (sparse_len == 0) return BJO_E_SPARSE_LEN_ZERO;
+  if (alpha < 0.0f) alpha = 0.0f;
+  if (alpha > 1.0f) alpha = 1.0f;
+  const float one_minus_alpha = 1.0f - alpha;
+  if (age_observed) {
+    for (int64_t i = 0; i < batch * dense_tokens; ++i) age_frames[i] += observed[i];
+  }
+  const int64_t rows = batch * sparse_len;
+  float* delta = (float*)malloc(sizeof(float) * (size_t)(rows * embed_dim + 2 * rows));
+  if (!delta) return BJO_E_BAD_ARG;
+  float* dobs = delta + rows * embed_dim;
+  float* dage = dobs + rows;
+  for (int64_t b = 0; b < batch; ++b)
+    for (int64_t s = 0; s < sparse_len; ++s) {
+      const int64_t r = b * sparse_len + s;
+      const int32_t idx = token_indices[r];
+      if (idx < 0 || idx >= dense_tokens) continue;
+      const int64_t slot = b * dense_tokens + idx;
+      const float obs = observed[slot];
+      const float first = -obs + 1.0f;
+      for (int64_t d = 0; d < embed_dim; ++d) {
+        const float prev = features[slot * embed_dim + d];
+        const float tok = tokens[r * embed_dim + d];
+        const float blended = prev * one_minus_alpha + tok * alpha;
+        delta[r * embed_dim + d] = (blended * obs + tok * first) - prev;
+      }
+      dobs[r] = 1.0f - obs;
+      dage[r] = 0.0f - age_frames[slot];
+    }
+  for (int64_t b = 0; b < batch; ++b)
+    for (int64_t s = 0; s < sparse_len; ++s) {
+      const int64_t r = b * sparse_len + s;
+      const int32_t idx = token_indices[r];
+      if (idx < 0 || idx >= dense_tokens) continue;
+      const int64_t slot = b * dense_tokens + idx;
+      for (int64_t d = 0; d < embed_dim; ++d) features[slot * embed_dim + d] += delta[r * embed_dim + d];
+      observed[slot] += dobs[r];
+      age_frames[slot] += dage[r];
+    }
+  free(delta);
+  return BJO_OK;
+}
+
+/* src/feature_memory.rs:348-375 reset_rows: zero features / observed / age of the listed rows
+ * (rows outside [0, batch) are skipped here; the reference's host form rejects them). */
+int bjo_feature_memory_reset_rows(float* features, float* observed, float* age_frames, int64_t batch,
+                                  int64_t dense_tokens, int64_t embed_dim, const int32_t* rows, int64_t row_count) {
+  for (int64_t i = 0; i < row_count; ++i) {
+    const int32_t r = rows[i];
+    if (r < 0 || r >= batch) continue;
+    memset(features + (int64_t)r * dense_tokens * embed_dim, 0, sizeof(float) * (size_t)(dense_tokens * embed_dim));
+    memset(observed + (int64_t)r * dense_tokens, 0, sizeof(float) * (size_t)dense_tokens);
+    memset(age_frames + (int64_t)r * dense_tokens, 0, sizeof(float) * (size_t)dense_tokens);
+  }
+  return BJO_OK;
+}
+
 int bjo_front_end_streams(const float* video, int64_t streams, const bjo_patchify_config* cfg,
                           const bjo_patch_diff_config* mask_cfg, const float* weight,
                           const float* bias, float* caches, float* observed, float* age_frames,
@@ -503,6 +572,187 @@ int bjo_front_end_streams(const float* video, int64_t streams, const bjo_patchif
   free(coords);
   free(idx);
   return rc;
+}
+
+/* ---- live viewer policy (src/viewer.rs) ---- */
+
+static void rgba_rgb(const uint8_t* rgba, int64_t offset, float out[3]) {
+  /* :1246-1252 */
+  out[0] = (float)rgba[offset] / 255.0f;
+  out[1] = (float)rgba[offset + 1] / 255.0f;
+  out[2] = (float)rgba[offset + 2] / 255.0f;
+}
+
+static float rgb_luma(const float rgb[3]) { return rgb[0] * 0.2126f + rgb[1] * 0.7152f + rgb[2] * 0.0722f; }
+
+static void rgb_chroma(const float rgb[3], float out[3]) {
+  /* :1267-1270 */
+  float denom = rgb[0] + rgb[1] + rgb[2];
+  if (denom < 0.10f) denom = 0.10f;
+  out[0] = rgb[0] / denom;
+  out[1] = rgb[1] / denom;
+  out[2] = rgb[2] / denom;
+}
+
+static float rgb_chroma_diff(const float prev[3], const float cur[3]) {
+  /* :1258-1265 */
+  float p[3], c[3];
+  rgb_chroma(prev, p);
+  rgb_chroma(cur, c);
+  return (fabsf(c[0] - p[0]) + fabsf(c[1] - p[1]) + fabsf(c[2] - p[2])) / 3.0f;
+}
+
+static float fmax_rust(float a, float b) { return a > b ? a : b; } /* finite inputs */
+
+/* :1079-1124  rgba_patch_diff_frame_stats: sequential f32 sums over min(len) / 4 pixels. */
+void bjo_rgba_patch_diff_frame_stats(const uint8_t* prev, int64_t prev_len, const uint8_t* cur, int64_t cur_len,
+                                     bjo_rgba_frame_stats* out) {
+  int64_t pixels = (prev_len < cur_len ? prev_len : cur_len) / 4;
+  if (pixels < 1) pixels = 1;
+  float channel_delta[3] = {0.0f, 0.0f, 0.0f};
+  float luma_delta = 0.0f, raw_abs = 0.0f;
+  for (int64_t i = 0; i < pixels; ++i) {
+    float p[3], c[3];
+    rgba_rgb(prev, i * 4, p);
+    rgba_rgb(cur, i * 4, c);
+    float pixel_abs = 0.0f;
+    for (int ch = 0; ch < 3; ++ch) {
+      const float d = c[ch] - p[ch];
+      channel_delta[ch] += d;
+      pixel_abs += fabsf(d);
+    }
+    raw_abs += pixel_abs / 3.0f;
+    luma_delta += rgb_luma(c) - rgb_luma(p);
+  }
+  for (int ch = 0; ch < 3; ++ch) channel_delta[ch] /= (float)pixels;
+  luma_delta /= (float)pixels;
+  float residual_abs = 0.0f;
+  for (int64_t i = 0; i < pixels; ++i) {
+    float p[3], c[3];
+    rgba_rgb(prev, i * 4, p);
+    rgba_rgb(cur, i * 4, c);
+    float pixel_abs = 0.0f;
+    for (int ch = 0; ch < 3; ++ch) pixel_abs += fabsf(c[ch] - p[ch] - channel_delta[ch]);
+    residual_abs += pixel_abs / 3.0f;
+  }
+  raw_abs = raw_abs / (float)pixels;
+  residual_abs = residual_abs / (float)pixels;
+  out->channel_delta[0] = channel_delta[0];
+  out->channel_delta[1] = channel_delta[1];
+  out->channel_delta[2] = channel_delta[2];
+  out->luma_delta = luma_delta;
+  out->compensate_global_lighting = raw_abs > 1.0e-4f && residual_abs <= raw_abs * 0.35f;
+  out->raw_abs = raw_abs;
+  out->residual_abs = residual_abs;
+}
+
+/* :1216-1244  rgba_patch_diff_pixel_score */
+static float rgba_pixel_score(const uint8_t* prev, const uint8_t* cur, int64_t offset, const bjo_rgba_frame_stats* st) {
+  float p[3], c[3];
+  rgba_rgb(prev, offset, p);
+  rgba_rgb(cur, offset, c);
+  float rgb_abs = 0.0f;
+  for (int ch = 0; ch < 3; ++ch) {
+    float d = c[ch] - p[ch];
+    if (st->compensate_global_lighting) d -= st->channel_delta[ch];
+    rgb_abs += fabsf(d);
+  }
+  rgb_abs = rgb_abs / 3.0f;
+  const float pl = rgb_luma(p), cl = rgb_luma(c);
+  float ld = cl - pl;
+  if (st->compensate_global_lighting) ld -= st->luma_delta;
+  const float luma_abs = fabsf(ld);
+  float rel = luma_abs / fmax_rust(fmax_rust(pl, cl), 0.10f);
+  if (rel > 1.0f) rel = 1.0f;
+  rel = rel * 0.25f;
+  const float chroma = rgb_chroma_diff(p, c) * 0.5f;
+  return fmax_rust(fmax_rust(fmax_rust(rgb_abs, luma_abs), rel), chroma);
+}
+
+/* :1126-1157 and :1199-1214  patch_diff_scores_from_rgba */
+int bjo_patch_diff_scores_from_rgba(const uint8_t* prev, int64_t prev_len, const uint8_t* cur, int64_t cur_len,
+                                    int64_t width, int64_t patch_size, int64_t depth, int64_t gh, int64_t gw,
+                                    float* scores, bjo_rgba_frame_stats* stats_out) {
+  if (depth != 1) return BJO_E_BAD_ARG;
+  if (patch_size <= 0) return BJO_E_BAD_ARG;
+  if (width != gw * patch_size) return BJO_E_BAD_ARG;
+  const int64_t expected = width * gh * patch_size * 4;
+  if (prev_len < expected || cur_len < expected) return BJO_E_BAD_ARG;
+  bjo_rgba_frame_stats st;
+  bjo_rgba_patch_diff_frame_stats(prev, prev_len, cur, cur_len, &st);
+  if (stats_out) *stats_out = st;
+  for (int64_t row = 0; row < gh; ++row)
+    for (int64_t col = 0; col < gw; ++col) {
+      float sum = 0.0f;
+      for (int64_t y = row * patch_size; y < (row + 1) * patch_size; ++y)
+        for (int64_t x = col * patch_size; x < (col + 1) * patch_size; ++x)
+          sum += rgba_pixel_score(prev, cur, (y * width + x) * 4, &st);
+      scores[row * gw + col] = sum / (float)(patch_size * patch_size);
+    }
+  return BJO_OK;
+}
+
+/* :780-793  patch_diff_dense_fallback: the mask, or every token when it is already at least
+ * ceil(len * density) long (and that is below the grid). Returns the new length. */
+int64_t bjo_patch_diff_dense_fallback(const int64_t* idx, int64_t n, int64_t dense_len, float density, int64_t* out) {
+  if (density < 0.0f) density = 0.0f;
+  if (density > 1.0f) density = 1.0f;
+  const int64_t fallback = (int64_t)ceilf((float)dense_len * density);
+  const int64_t at_least = fallback > 1 ? fallback : 1;
+  if (n == dense_len || (fallback < dense_len && n >= at_least)) {
+    for (int64_t i = 0; i < dense_len; ++i) out[i] = i;
+    return dense_len;
+  }
+  for (int64_t i = 0; i < n; ++i) out[i] = idx[i];
+  return n;
+}
+
+/* :796-816 and :844-869  dilate_sparse_patch_mask: every token within `dilation` tiles of a
+ * mask token (same tubelet), sorted and unique; no cap. Returns the new length. */
+int64_t bjo_dilate_sparse_patch_mask(const int64_t* idx, int64_t n, int64_t depth, int64_t gh, int64_t gw,
+                                     int64_t dilation, int64_t* out) {
+  const int64_t len = depth * gh * gw;
+  int dense_ordered = n == len;
+  for (int64_t i = 0; dense_ordered && i < n; ++i) dense_ordered = idx[i] == i;
+  if (dilation == 0 || dense_ordered) {
+    for (int64_t i = 0; i < n; ++i) out[i] = idx[i];
+    return n;
+  }
+  unsigned char* keep = (unsigned char*)calloc((size_t)(len > 0 ? len : 1), 1);
+  if (!keep) return -1;
+  const int64_t tpf = gh * gw > 0 ? gh * gw : 1;
+  for (int64_t k = 0; k < n; ++k) {
+    const int64_t index = idx[k];
+    if (index < 0 || index >= len) continue;
+    const int64_t t = index / tpf, local = index % tpf;
+    const int64_t row = local / (gw > 0 ? gw : 1), col = local % (gw > 0 ? gw : 1);
+    const int64_t r0 = row > dilation ? row - dilation : 0, c0 = col > dilation ? col - dilation : 0;
+    const int64_t r1 = row + dilation < gh - 1 ? row + dilation : gh - 1;
+    const int64_t c1 = col + dilation < gw - 1 ? col + dilation : gw - 1;
+    for (int64_t r = r0; r <= r1; ++r)
+      for (int64_t c = c0; c <= c1; ++c) keep[t * tpf + r * gw + c] = 1;
+  }
+  int64_t m = 0;
+  for (int64_t i = 0; i < len; ++i)
+    if (keep[i]) out[m++] = i;
+  free(keep);
+  return m;
+}
+
+/* :873-885  bucket_sparse_mask: padded_to_multiple(min(bucket, max(len / 4, 1))) for grids of at
+ * least 256 tokens that are not dense-ordered. Returns the new length. */
+int64_t bjo_bucket_sparse_mask(const int64_t* idx, int64_t n, int64_t dense_len, int64_t bucket_tokens, int64_t* out) {
+  int dense_ordered = n == dense_len;
+  for (int64_t i = 0; dense_ordered && i < n; ++i) dense_ordered = idx[i] == i;
+  if (bucket_tokens <= 1 || dense_len < 256 || dense_ordered || n >= dense_len) {
+    for (int64_t i = 0; i < n; ++i) out[i] = idx[i];
+    return n;
+  }
+  int64_t quarter = dense_len / 4 > 1 ? dense_len / 4 : 1;
+  const int64_t bucket = bucket_tokens < quarter ? bucket_tokens : quarter;
+  int64_t target = (n + bucket - 1) / bucket * bucket;
+  if (target > dense_len) target = dense_len;
+  return bjo_padded_to_len(idx, n, dense_len, target, out);
 }
 
 /* training/mask.rs:557-563 */

@@ -145,6 +145,16 @@ int bjo_feature_memory_assign_latest(float* features, float* observed, float* ag
                                      int64_t batch, int64_t dense_tokens, int64_t embed_dim,
                                      int64_t sparse_len, int32_t age_observed);
 
+/* src/feature_memory.rs:227-290, EMA update mode (portable path, in place, f32; duplicates
+ * add their deltas as the reference's scatter-add does). */
+int bjo_feature_memory_update_ema(float* features, float* observed, float* age_frames, const float* tokens,
+                                  const int32_t* token_indices, int64_t batch, int64_t dense_tokens,
+                                  int64_t embed_dim, int64_t sparse_len, float alpha, int32_t age_observed);
+
+/* src/feature_memory.rs:348-375 reset_rows (rows outside [0, batch) skipped). */
+int bjo_feature_memory_reset_rows(float* features, float* observed, float* age_frames, int64_t batch,
+                                  int64_t dense_tokens, int64_t embed_dim, const int32_t* rows, int64_t row_count);
+
 /* One front-end step over S independent streams, the per-stream composition the
  * reference pipeline runs (src/highres_pipeline.rs:2021-2040 with the patch-diff
  * driver of src/nodes.rs:411-456): patch_diff_context_mask -> SparsePatchifyPlan
@@ -155,6 +165,30 @@ int bjo_front_end_streams(const float* video, int64_t streams, const bjo_patchif
                           const bjo_patch_diff_config* mask_config, const float* weight,
                           const float* bias, float* caches, float* observed, float* age_frames,
                           int32_t age_observed, int64_t* counts);
+
+/* ---- live viewer policy (src/viewer.rs) ---- */
+typedef struct bjo_rgba_frame_stats {
+  float channel_delta[3];
+  float luma_delta;
+  int32_t compensate_global_lighting;
+  float raw_abs;
+  float residual_abs;
+} bjo_rgba_frame_stats;
+
+/* src/viewer.rs:1079-1124 rgba_patch_diff_frame_stats (sequential f32, as the reference). */
+void bjo_rgba_patch_diff_frame_stats(const uint8_t* prev, int64_t prev_len, const uint8_t* cur, int64_t cur_len,
+                                     bjo_rgba_frame_stats* out);
+/* src/viewer.rs:1126-1244 patch_diff_scores_from_rgba (scores [gh * gw]). */
+int bjo_patch_diff_scores_from_rgba(const uint8_t* prev, int64_t prev_len, const uint8_t* cur, int64_t cur_len,
+                                    int64_t width, int64_t patch_size, int64_t depth, int64_t gh, int64_t gw,
+                                    float* scores, bjo_rgba_frame_stats* stats_out);
+/* src/viewer.rs:780-793 patch_diff_dense_fallback (returns the new length). */
+int64_t bjo_patch_diff_dense_fallback(const int64_t* idx, int64_t n, int64_t dense_len, float density, int64_t* out);
+/* src/viewer.rs:796-816, 844-869 dilate_sparse_patch_mask (returns the new length, -1 on error). */
+int64_t bjo_dilate_sparse_patch_mask(const int64_t* idx, int64_t n, int64_t depth, int64_t gh, int64_t gw,
+                                     int64_t dilation, int64_t* out);
+/* src/viewer.rs:873-885 bucket_sparse_mask (returns the new length). */
+int64_t bjo_bucket_sparse_mask(const int64_t* idx, int64_t n, int64_t dense_len, int64_t bucket_tokens, int64_t* out);
 
 /* training/mask.rs:557-563 splitmix64 (the reference's own mixer; used for seeded inputs) */
 uint64_t bjo_splitmix64(uint64_t value);

@@ -298,6 +298,30 @@ TEST(reset_rows_and_reset_clear_memory) {
   CHECK_EQ(host_f32(*memory.snapshot().age_frames), std::vector<float>(6, 0.0f));
 }
 
+// tests/feature_memory.rs:145-177 (EMA on the device; the reference runs it on its portable path)
+TEST(ema_updates_assign_first_observation_then_blend_repeated_tokens) {
+  const TokenGridShape grid(1, 1, 2);
+  auto memory = InterframeJepaFeatureMemory::with_config(InterframeJepaFeatureMemoryConfig::ema(0.25f), 1, grid, 1);
+  memory.update_tokens(Tensor::from_host(std::vector<float>{8}, {1, 1, 1}, BJF_DTYPE_F32),
+                       Tensor::from_host(std::vector<int32_t>{0}, {1, 1}, BJF_DTYPE_I32), grid);
+  const auto out = memory.update_tokens(Tensor::from_host(std::vector<float>{12}, {1, 1, 1}, BJF_DTYPE_F32),
+                                        Tensor::from_host(std::vector<int32_t>{0}, {1, 1}, BJF_DTYPE_I32), grid);
+  CHECK_EQ(host_f32(*out.features), (std::vector<float>{9, 0}));
+  CHECK(InterframeJepaFeatureMemoryConfig::ema(3.0f).normalized().alpha == 1.0f);
+}
+
+// tests/feature_memory.rs:300-339 with the device-tensor form of reset_rows
+TEST(reset_rows_device_tensor_clears_rows) {
+  const TokenGridShape grid(1, 1, 3);
+  auto memory = InterframeJepaFeatureMemory::new_(2, grid, 1);
+  memory.update_tokens(Tensor::from_host(std::vector<float>{1, 2, 3, 4}, {2, 2, 1}, BJF_DTYPE_F32),
+                       Tensor::from_host(std::vector<int32_t>{0, 1, 1, 2}, {2, 2}, BJF_DTYPE_I32), grid);
+  memory.reset_rows(Tensor::from_host(std::vector<int32_t>{1}, {1}, BJF_DTYPE_I32));
+  auto snap = memory.snapshot();
+  CHECK_EQ(host_f32(*snap.features), (std::vector<float>{1, 2, 0, 0, 0, 0}));
+  CHECK_EQ(host_f32(*snap.observed), (std::vector<float>{1, 1, 0, 0, 0, 0}));
+}
+
 // tests/feature_memory.rs:341-377
 TEST(update_rejects_incompatible_shapes) {
   const TokenGridShape grid(1, 2, 2);
@@ -353,6 +377,21 @@ TEST(adaptive_patch_diff_threshold_cases) {
                                                SparseJepaPatchDiffSparsityConfig::adaptive_threshold(0.0f, 1, 1, 1))
                .indices(),
            (std::vector<size_t>{0, 1, 2, 3}));
+}
+
+// src/viewer.rs:1391-1403 on the device scorer
+TEST(rgba_patch_diff_ignores_uniform_lighting_shift) {
+  const std::vector<int32_t> prev_words(64 * 64, 0x50505050), cur_words(64 * 64, 0x6e6e6e6e);  // 80 / 110 per byte
+  const Tensor prev = Tensor::from_host(prev_words, {64 * 64}, BJF_DTYPE_I32);
+  const Tensor cur = Tensor::from_host(cur_words, {64 * 64}, BJF_DTYPE_I32);
+  std::vector<RgbaPatchDiffFrameStats> stats;
+  const auto scores = patch_diff_scores_from_rgba(static_cast<const uint8_t*>(prev.data()),
+                                                  static_cast<const uint8_t*>(cur.data()), 64, 64, 16,
+                                                  TokenGridShape(1, 4, 4), 1, &stats)
+                          .to_host<float>();
+  for (float v : scores) CHECK(v < DEFAULT_PATCH_DIFF_THRESHOLD);
+  CHECK_EQ(stats.size(), (size_t)1);
+  CHECK_EQ(stats[0].compensate_global_lighting, 1);
 }
 
 // The fused step over S streams against the oracle's per-stream composition.  Unchanged

@@ -130,6 +130,31 @@ TEST(front_end_rejects_indivisible_geometry) {
                     "patch-diff sparsity requires frames/height/width divisible by tubelet and patch sizes");
 }
 
+// src/viewer.rs:1455-1481: direct mask -> dense fallback -> dilation
+TEST(dense_cutoff_runs_before_dilation) {
+  const TokenGridShape grid(1, 5, 5);
+  const size_t center = coords_to_token_index(0, 2, 2, grid);
+  const auto direct = SparseTokenMask::new_({center}, grid.len());
+  const auto write = dilate_sparse_patch_mask(patch_diff_dense_fallback(direct, grid, 0.25f), grid, 1);
+  CHECK_EQ(write.len(), (size_t)9);
+  CHECK(!write.is_dense_ordered());
+  CHECK(std::find(write.indices().begin(), write.indices().end(), center) != write.indices().end());
+  CHECK(patch_diff_dense_fallback(SparseTokenMask::new_({0, 1, 2, 3, 4, 5, 6}, 25), grid, 0.25f).is_dense_ordered());
+}
+
+// crates/bevy_jepa/src/tests.rs:1917-1928
+TEST(sparse_mask_bucket_preserves_changed_tokens) {
+  const TokenGridShape grid(1, 32, 32);
+  std::vector<size_t> idx(103);
+  for (size_t i = 0; i < idx.size(); ++i) idx[i] = i;
+  const auto changed = SparseTokenMask::new_(idx, grid.len());
+  const auto bucketed = bucket_sparse_mask(changed, grid, DEFAULT_SPARSE_MASK_BUCKET_TOKENS);
+  CHECK_EQ(bucketed.len(), (size_t)256);
+  for (size_t i : changed.indices())
+    CHECK(std::find(bucketed.indices().begin(), bucketed.indices().end(), i) != bucketed.indices().end());
+  CHECK(!bucketed.is_dense_ordered());
+}
+
 TEST(abi_version_matches_header) { CHECK_EQ(bjf_abi_version(), BJF_ABI_VERSION); }
 
 TEST_MAIN()

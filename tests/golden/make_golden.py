@@ -160,6 +160,19 @@ KNOWN_ANSWERS = {
         "token_dim_mismatch": {"features": [1, 4, 2], "tokens": [1, 1, 3], "indices": [1, 1],
                                "message_contains": "feature memory token dims mismatch"},
     },
+    "feature_memory_ema": {
+        "source": "tests/feature_memory.rs:145-177 (Ema { alpha: 0.25 }: first observation assigned, then blended)",
+        "batch": 1, "grid": [1, 1, 2], "embed_dim": 1, "alpha": 0.25,
+        "steps": [{"tokens": [8.0], "tokens_shape": [1, 1, 1], "indices": [0]},
+                  {"tokens": [12.0], "tokens_shape": [1, 1, 1], "indices": [0], "features": [9.0, 0.0]}],
+    },
+    "feature_memory_reset_rows": {
+        "source": "tests/feature_memory.rs:300-339",
+        "batch": 2, "grid": [1, 1, 3], "embed_dim": 1,
+        "update": {"tokens": [1.0, 2.0, 3.0, 4.0], "tokens_shape": [2, 2, 1], "indices": [0, 1, 1, 2]},
+        "reset": [{"rows": [1], "features": [1.0, 2.0, 0.0, 0.0, 0.0, 0.0], "observed": [1.0, 1.0, 0.0, 0.0, 0.0, 0.0]},
+                  {"rows": [0], "features": [0.0] * 6, "observed": [0.0] * 6}],
+    },
 }
 
 CONV3D_CASES = [

@@ -28,10 +28,10 @@ def _run(binary: str) -> str:
 
 def test_cpp_host_api():
     out = _run("test_host_api")
-    assert out.count("PASS ") >= 15
+    assert out.count("PASS ") >= 17
 
 
 @pytest.mark.gpu
 def test_cpp_device_api(cuda_device):
     out = _run("test_device_api")
-    assert out.count("PASS ") >= 14
+    assert out.count("PASS ") >= 17
