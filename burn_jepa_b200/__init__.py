@@ -203,6 +203,23 @@ def sparse_patchify3d_forward(config: PatchifyConfig, input, coords, weight, bia
     return out
 
 
+def sparse_patchify3d_forward_encoder_input(config: PatchifyConfig, input, coords, weight, bias=None,
+                                            position_table=None, modality_embed=None, out=None, out_dtype=None,
+                                            stream=None):
+    """Sparse patchify producing the encoder's input tokens (src/model.rs:690-703): after the bias
+    each row adds position_table[its token index] ([grid tokens, D] f32 or None) and then
+    modality_embed ([D] f32 or None)."""
+    torch = _torch()
+    rows = coords.shape[0]
+    if out is None:
+        out = torch.empty((rows, config.out_channels), dtype=out_dtype or torch.float32, device=input.device)
+    check(load().bjf_sparse_patchify3d_forward_encoder_input(
+        ctypes.byref(config), _ptr(input), _dtype_code(input), _abi.dims(*input.shape), _ptr(coords), rows,
+        _ptr(weight), _dtype_code(weight), _abi.dims(*weight.shape), _ptr(bias), _ptr(position_table),
+        _ptr(modality_embed), _ptr(out), _dtype_code(out), _stream(stream)))
+    return out
+
+
 # ---------------------------------------------------------------------------
 # Step 3: token-cache write
 # ---------------------------------------------------------------------------

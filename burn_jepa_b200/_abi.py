@@ -136,6 +136,8 @@ SIGNATURES = {
                                   _P, _P]),
     "bjf_front_end_step_no_alloc": (_I32, [ctypes.POINTER(FrontEndDesc), _P, _P, _P, _P, _P, _P, _I32, _P, _P]),
     "bjf_rgba_patch_diff_workspace_bytes": (ctypes.c_size_t, [_I64]),
+    "bjf_sparse_patchify3d_forward_encoder_input": (_I32, [ctypes.POINTER(PatchifyConfig), _P, _I32, _DIMS, _P, _I64,
+                                                           _P, _I32, _DIMS, _P, _P, _P, _P, _I32, _P]),
     "bjf_rgba_patch_diff_scores": (_I32, [_P, _P, _I64, _I64, _I64, _I64, _DIMS, _P, _P, _P, ctypes.c_size_t, _P]),
     "bjf_feature_memory_assign_latest": (_I32, [_P, _I32, _DIMS, _P, _DIMS, _P, _DIMS, _P, _I32, _DIMS, _P, _DIMS,
                                                 _I32, _P]),

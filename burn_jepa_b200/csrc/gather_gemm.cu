@@ -183,13 +183,36 @@ __device__ __forceinline__ int4 next_row(const RowSource& rs, const int* soff, c
   return gm < M ? fetch_row(rs, soff, g, gm) : make_int4(-1, -1, -1, -1);
 }
 
+// Encoder-input epilogue terms for 32 columns starting at col0 (ncol valid): + the row's
+// position embedding, then + the modality embedding (src/model.rs:690-703).  Rows without a
+// table row (zero rows) stay zero.  Warp-collective (the modality vector is broadcast).
+__device__ __forceinline__ void add_encoder_embeddings(const EpilogueArgs& ep, bool valid, const float* pos_row,
+                                                       int col0, int ncol, int lane, float (&v)[32]) {
+  if (pos_row) {
+#pragma unroll
+    for (int j = 0; j < 32; ++j)
+      if (j < ncol) v[j] = v[j] + __ldg(pos_row + col0 + j);
+  }
+  if (ep.modality_embed) {
+    const float ml = lane < ncol ? __ldg(ep.modality_embed + col0 + lane) : 0.0f;
+#pragma unroll
+    for (int j = 0; j < 32; ++j) {
+      const float m = __shfl_sync(0xffffffffu, ml, j);
+      if (valid) v[j] = v[j] + m;
+    }
+  }
+}
+
 __device__ __forceinline__ void drain_accumulator(const GatherGeometry& g, const EpilogueArgs& ep, int4 c, int M,
                                                   int gm, int n0, int bn, uint32_t taddr, int lane) {
   const int ce = ep.out_elem_bytes;
   bool valid = false;
   char* dst_row = nullptr;
+  const float* pos_row = nullptr;
   if (gm < M) {
     row_base_offset(g, c, valid);
+    if (valid && ep.position_table)
+      pos_row = ep.position_table + (((int64_t)c.y * g.gh + c.z) * g.gw + c.w) * ep.pos_ld;
     if (ep.mode == kEpiloguePlain) {
       dst_row = static_cast<char*>(ep.out) + (int64_t)gm * ep.ldo * ce;
     } else if (valid) {
@@ -217,6 +240,7 @@ __device__ __forceinline__ void drain_accumulator(const GatherGeometry& g, const
       const float b = __shfl_sync(0xffffffffu, bl, j);
       v[j] = valid ? __uint_as_float(r[j]) + b : 0.0f;
     }
+    add_encoder_embeddings(ep, valid, pos_row, col0, ncol, lane, v);
     if (!dst_row) continue;
     char* dst = dst_row + (int64_t)col0 * ce;
     if (ep.out_dtype == BJF_DTYPE_F32)
@@ -539,8 +563,11 @@ __device__ __forceinline__ void drain_accumulator_bulk(const GatherGeometry& g, 
   const int ce = ep.out_elem_bytes;
   bool valid = false;
   char* dst_row = nullptr;
+  const float* pos_row = nullptr;
   if (gm < M) {
     row_base_offset(g, c, valid);
+    if (valid && ep.position_table)
+      pos_row = ep.position_table + (((int64_t)c.y * g.gh + c.z) * g.gw + c.w) * ep.pos_ld;
     if (ep.mode == kEpiloguePlain) {
       dst_row = static_cast<char*>(ep.out) + (int64_t)gm * ep.ldo * ce;
     } else if (valid) {
@@ -574,6 +601,7 @@ __device__ __forceinline__ void drain_accumulator_bulk(const GatherGeometry& g, 
         const float b = __shfl_sync(0xffffffffu, bl, j);
         v[j] = valid ? __uint_as_float(r[j]) + b : 0.0f;
       }
+      add_encoder_embeddings(ep, valid, pos_row, col0 + 32 * h, nh, lane, v);
       uint8_t* d = srow + 32 * h * ce;
       if (ep.out_dtype == BJF_DTYPE_F32)
         pack_chunk32<float>(d, v, nh);
@@ -947,6 +975,11 @@ __global__ void __launch_bounds__(kSThreads)
       const int col = n0 + tx * 4 + j;
       if (col >= g.D) continue;
       float v = valid ? acc[i][j] + (ep.bias ? ep.bias[col] : 0.0f) : 0.0f;
+      if (valid && ep.position_table) {
+        const int4 c = row_c[m];
+        v = v + ep.position_table[(((int64_t)c.y * g.gh + c.z) * g.gw + c.w) * ep.pos_ld + col];
+      }
+      if (valid && ep.modality_embed) v = v + ep.modality_embed[col];
       if (ep.out_dtype == BJF_DTYPE_F32)
         reinterpret_cast<float*>(dst_row)[col] = v;
       else if (ep.out_dtype == BJF_DTYPE_F16)
@@ -1111,12 +1144,13 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
 
 using namespace bjf;
 
-extern "C" bjf_status bjf_sparse_patchify3d_forward(const bjf_patchify_config* cfg, const void* input,
-                                                    bjf_dtype input_dtype, const int64_t id[5],
-                                                    const int32_t* coords, int64_t rows,
-                                                    const void* weight, bjf_dtype weight_dtype,
-                                                    const int64_t wd[5], const float* bias, void* out,
-                                                    bjf_dtype out_dtype, bjf_stream_t stream) {
+namespace {
+
+bjf_status patchify_forward(const bjf_patchify_config* cfg, const void* input, bjf_dtype input_dtype,
+                            const int64_t id[5], const int32_t* coords, int64_t rows, const void* weight,
+                            bjf_dtype weight_dtype, const int64_t wd[5], const float* bias,
+                            const float* position_table, const float* modality_embed, void* out,
+                            bjf_dtype out_dtype, bjf_stream_t stream) {
   if (!cfg || !id || !wd) return fail(BJF_ERR_INVALID_ARGUMENT, "config and dims must not be null");
   const int64_t vals[8] = {cfg->in_channels, cfg->out_channels, cfg->frames, cfg->height,
                            cfg->width, cfg->tubelet_size, cfg->patch_h, cfg->patch_w};
@@ -1166,6 +1200,30 @@ extern "C" bjf_status bjf_sparse_patchify3d_forward(const bjf_patchify_config* c
   ep.out_elem_bytes = (int)dtype_size(out_dtype);
   ep.ldo = g.D;
   ep.bias = bias;
+  ep.position_table = position_table;
+  ep.pos_ld = g.D;
+  ep.modality_embed = modality_embed;
   return launch_gather_gemm(*dev, input, input_dtype, weight, weight_dtype, g,
                             coords_rows(reinterpret_cast<const int4*>(coords)), nullptr, rows, ep, as_cuda(stream));
+}
+
+}  // namespace
+
+extern "C" bjf_status bjf_sparse_patchify3d_forward(const bjf_patchify_config* cfg, const void* input,
+                                                    bjf_dtype input_dtype, const int64_t id[5],
+                                                    const int32_t* coords, int64_t rows,
+                                                    const void* weight, bjf_dtype weight_dtype,
+                                                    const int64_t wd[5], const float* bias, void* out,
+                                                    bjf_dtype out_dtype, bjf_stream_t stream) {
+  return patchify_forward(cfg, input, input_dtype, id, coords, rows, weight, weight_dtype, wd, bias, nullptr, nullptr,
+                          out, out_dtype, stream);
+}
+
+extern "C" bjf_status bjf_sparse_patchify3d_forward_encoder_input(
+    const bjf_patchify_config* cfg, const void* input, bjf_dtype input_dtype, const int64_t id[5],
+    const int32_t* coords, int64_t rows, const void* weight, bjf_dtype weight_dtype, const int64_t wd[5],
+    const float* bias, const float* position_table, const float* modality_embed, void* out, bjf_dtype out_dtype,
+    bjf_stream_t stream) {
+  return patchify_forward(cfg, input, input_dtype, id, coords, rows, weight, weight_dtype, wd, bias, position_table,
+                          modality_embed, out, out_dtype, stream);
 }

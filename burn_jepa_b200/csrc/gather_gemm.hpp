@@ -36,6 +36,11 @@ struct EpilogueArgs {
   float* observed;
   float* age;
   const float* bias;
+  // Encoder input (plain mode): out += position_table[token index of the row, :] (row stride
+  // pos_ld), then += modality_embed[:], after the bias and in that order.  Null when unused.
+  const float* position_table;
+  int64_t pos_ld;
+  const float* modality_embed;
 };
 
 // Where the gathered rows come from: either explicit coords rows (b, t, r, col), or the

@@ -174,6 +174,19 @@ BJF_API bjf_status bjf_sparse_patchify3d_forward(const bjf_patchify_config* conf
                                          const float* bias, void* out, bjf_dtype out_dtype,
                                          bjf_stream_t stream);
 
+/* bjf_sparse_patchify3d_forward producing the encoder's input tokens: after the bias each row
+ * adds its token's position embedding, then the modality embedding, in that order
+ * (VJepaEncoder::forward_sparse_plan, src/model.rs:690-703, with SparseEncoderPlan's
+ * position_embed, :296-319).  position_table: [T/kt * H/ph * W/pw, D] f32 indexed by the row's
+ * token index (t * gh * gw + r * gw + col), e.g. get_3d_sincos_pos_embed (src/positional.rs:42-85),
+ * or NULL (RoPE models); modality_embed: [D] f32 or NULL.  Rows with out-of-range coords stay
+ * zero. */
+BJF_API bjf_status bjf_sparse_patchify3d_forward_encoder_input(
+    const bjf_patchify_config* config, const void* input, bjf_dtype input_dtype, const int64_t input_dims[5],
+    const int32_t* coords, int64_t rows, const void* weight, bjf_dtype weight_dtype, const int64_t weight_dims[5],
+    const float* bias, const float* position_table, const float* modality_embed, void* out, bjf_dtype out_dtype,
+    bjf_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Step 3: token-cache write
  * ---------------------------------------------------------------------- */

@@ -13,6 +13,8 @@
 //   SparsePatchifyPlan, SparsePatchifyBatchPlan                    src/sparse_patchify.rs:236-330
 //   SparsePatchify3dConfig, sparse_patchify3d_forward_cuda         burn_flex_gmm 0.21.2, called at
 //                                                                  src/model.rs:1297-1327
+//   sparse_3d_sincos_pos_embed, sparse_patchify3d_encoder_input_cuda src/positional.rs:42-87,
+//                                                                  src/model.rs:690-703
 //   InterframeJepaFeatureMemory(Config) (+ update_tokens, reset_rows) src/feature_memory.rs:7-645
 //   FrontEnd (one frame step over S streams)                       src/highres_pipeline.rs:2021-2040
 //   patch_diff_scores_from_rgba, patch_diff_dense_fallback,
@@ -691,6 +693,63 @@ inline Tensor sparse_patchify3d_forward_cuda(const SparsePatchify3dConfig& confi
                                       weight.dtype(), wd.data(),
                                       bias ? static_cast<const float*>(bias->data()) : nullptr, out.data(), odt,
                                       to_bjf(st)));
+  return out;
+}
+
+// sparse_3d_sincos_pos_embed (src/positional.rs:46-87): [indices.size(), embed_dim] f32 on the
+// host, the frame / row / column sin-cos blocks of even(D/2), even(D/4), even(rest) dims.
+inline std::vector<float> sparse_3d_sincos_pos_embed(size_t embed_dim, TokenGridShape grid,
+                                                     const std::vector<size_t>& indices) {
+  auto even = [](size_t d) { return d - (d % 2); };
+  const size_t d_dim = even(embed_dim / 2), h_dim = even(embed_dim / 4);
+  const size_t w_dim = even(embed_dim > d_dim + h_dim ? embed_dim - (d_dim + h_dim) : 0);
+  const size_t rem = embed_dim > d_dim + h_dim + w_dim ? embed_dim - (d_dim + h_dim + w_dim) : 0;
+  auto block = [](std::vector<float>& out, size_t dim, float pos) {
+    if (dim == 0) return;
+    const size_t half = dim / 2;
+    const float h = (float)std::max<size_t>(half, 1);
+    for (size_t i = 0; i < half; ++i) out.push_back(std::sin(pos * (1.0f / std::pow(10000.0f, (float)i / h))));
+    for (size_t i = 0; i < half; ++i) out.push_back(std::cos(pos * (1.0f / std::pow(10000.0f, (float)i / h))));
+    if (dim % 2 == 1) out.push_back(0.0f);
+  };
+  std::vector<float> out;
+  out.reserve(indices.size() * embed_dim);
+  for (size_t index : indices) {
+    const auto [frame, row, col] = token_index_to_coords(index, grid);
+    block(out, d_dim, (float)frame);
+    block(out, h_dim, (float)row);
+    block(out, w_dim, (float)col);
+    out.insert(out.end(), rem, 0.0f);
+  }
+  return out;
+}
+
+inline std::vector<float> get_3d_sincos_pos_embed(size_t embed_dim, TokenGridShape grid) {
+  return sparse_3d_sincos_pos_embed(embed_dim, grid, dense_token_indices(grid));
+}
+
+// The encoder's input tokens (src/model.rs:690-703): sparse_patchify3d_forward_cuda, then the
+// row's position embedding (position_table [grid tokens, D] f32, nullable) and the modality
+// embedding ([D] f32, nullable), in the reference's order, fused into the GEMM epilogue.
+inline Tensor sparse_patchify3d_encoder_input_cuda(const SparsePatchify3dConfig& config, const Tensor& input,
+                                                   const Tensor& coords, const Tensor& weight, const Tensor* bias,
+                                                   const Tensor* position_table, const Tensor* modality_embed,
+                                                   cudaStream_t st = nullptr, int out_dtype = -1) {
+  const auto d = detail::video_dims(input);
+  ensure(weight.rank() == 5, "sparse patchify weight must be [D, C, kt, ph, pw]");
+  ensure(coords.rank() == 2 && coords.shape()[1] == 4 && coords.dtype() == BJF_DTYPE_I32,
+         "sparse patchify coords must be an int32 [M, 4] tensor");
+  std::array<int64_t, 5> wd{};
+  for (int i = 0; i < 5; ++i) wd[i] = weight.shape()[i];
+  const bjf_patchify_config c = config.to_c();
+  const bjf_dtype odt = out_dtype < 0 ? input.dtype() : (bjf_dtype)out_dtype;
+  const int64_t rows = coords.shape()[0];
+  Tensor out({rows, (int64_t)config.out_channels}, odt);
+  auto fptr = [](const Tensor* t) { return t ? static_cast<const float*>(t->data()) : nullptr; };
+  check(bjf_sparse_patchify3d_forward_encoder_input(&c, input.data(), input.dtype(), d.data(),
+                                                    static_cast<const int32_t*>(coords.data()), rows, weight.data(),
+                                                    weight.dtype(), wd.data(), fptr(bias), fptr(position_table),
+                                                    fptr(modality_embed), out.data(), odt, to_bjf(st)));
   return out;
 }
 

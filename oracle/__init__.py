@@ -147,6 +147,10 @@ def _declare(L):
     L.bjo_feature_memory_update_ema.restype = ctypes.c_int
     L.bjo_feature_memory_reset_rows.argtypes = [_P] * 3 + [_I64] * 3 + [_P, _I64]
     L.bjo_feature_memory_reset_rows.restype = ctypes.c_int
+    L.bjo_sparse_3d_sincos_pos_embed.argtypes = [_I64] * 4 + [_P, _I64, _P]
+    L.bjo_sparse_3d_sincos_pos_embed.restype = None
+    L.bjo_patchify_encoder_input.argtypes = [_P, _I64, _P, _P, _I64, _P, _P, _P, _P, _P]
+    L.bjo_patchify_encoder_input.restype = ctypes.c_int
     L.bjo_rgba_patch_diff_frame_stats.argtypes = [_P, _I64, _P, _I64, _P]
     L.bjo_rgba_patch_diff_frame_stats.restype = None
     L.bjo_patch_diff_scores_from_rgba.argtypes = [_P, _I64, _P, _I64] + [_I64] * 5 + [_P, _P]
@@ -382,6 +386,36 @@ def feature_memory_reset_rows(features, observed, age_frames, rows):
     B, N, D = features.shape
     _check(lib().bjo_feature_memory_reset_rows(_ptr(features), _ptr(observed), _ptr(age_frames), B, N, D, _ptr(r),
                                               r.size))
+
+
+# ---- encoder input (src/positional.rs, src/model.rs) ----
+def sparse_3d_sincos_pos_embed(embed_dim: int, grid: "TokenGridShape", indices) -> np.ndarray:
+    """sparse_3d_sincos_pos_embed (src/positional.rs:46-67): [len(indices), embed_dim] f32."""
+    a = np.ascontiguousarray(np.asarray(indices, dtype=np.int64))
+    out = np.zeros((a.size, embed_dim), dtype=np.float32)
+    lib().bjo_sparse_3d_sincos_pos_embed(embed_dim, grid.depth, grid.height, grid.width, _ptr(a), a.size, _ptr(out))
+    return out
+
+
+def get_3d_sincos_pos_embed(embed_dim: int, grid: "TokenGridShape") -> np.ndarray:
+    """get_3d_sincos_pos_embed (src/positional.rs:42-44): every token of the grid."""
+    return sparse_3d_sincos_pos_embed(embed_dim, grid, np.arange(len(grid)))
+
+
+def patchify_encoder_input(config: PatchifyConfig, input, coords, weight, bias, position_table, modality_embed):
+    """Patch embed + position table + modality embedding per row (src/model.rs:690-703), f32."""
+    x = np.ascontiguousarray(input, dtype=np.float32)
+    c = np.ascontiguousarray(coords, dtype=np.int32)
+    w = np.ascontiguousarray(weight, dtype=np.float32)
+    rows = c.shape[0]
+    out = np.zeros((rows, config.out_channels), dtype=np.float32)
+    b = None if bias is None else np.ascontiguousarray(bias, dtype=np.float32)
+    pt = None if position_table is None else np.ascontiguousarray(position_table, dtype=np.float32)
+    me = None if modality_embed is None else np.ascontiguousarray(modality_embed, dtype=np.float32)
+    _check(lib().bjo_patchify_encoder_input(ctypes.byref(config), x.shape[0], _ptr(x), _ptr(c), rows, _ptr(w),
+                                            None if b is None else _ptr(b), None if pt is None else _ptr(pt),
+                                            None if me is None else _ptr(me), _ptr(out)))
+    return out
 
 
 # ---- live viewer policy (src/viewer.rs) ----

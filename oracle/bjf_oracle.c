@@ -574,6 +574,70 @@ int bjo_front_end_streams(const float* video, int64_t streams, const bjo_patchif
   return rc;
 }
 
+/* ---- encoder input (src/positional.rs, src/model.rs) ---- */
+
+static int64_t even_dim(int64_t d) { return d - (d % 2); }
+
+/* src/positional.rs:69-87 one_position_sincos: sin(pos * omega_i) then cos(pos * omega_i),
+ * omega_i = 1 / 10000^(i / half) in f32; a trailing 0 for an odd dim. */
+static float* one_position_sincos(int64_t dim, float pos, float* out) {
+  if (dim == 0) return out;
+  const int64_t half = dim / 2;
+  const float h = (float)(half > 1 ? half : 1);
+  for (int64_t i = 0; i < half; ++i) *out++ = sinf(pos * (1.0f / powf(10000.0f, (float)i / h)));
+  for (int64_t i = 0; i < half; ++i) *out++ = cosf(pos * (1.0f / powf(10000.0f, (float)i / h)));
+  if (dim % 2 == 1) *out++ = 0.0f;
+  return out;
+}
+
+/* src/positional.rs:46-67 sparse_3d_sincos_pos_embed: per token index, the frame, row and
+ * column sin-cos blocks of dims even(D/2), even(D/4), even(D - both), zero-padded to D. */
+void bjo_sparse_3d_sincos_pos_embed(int64_t embed_dim, int64_t depth, int64_t gh, int64_t gw,
+                                    const int64_t* indices, int64_t n, float* out) {
+  const int64_t d_dim = even_dim(embed_dim / 2), h_dim = even_dim(embed_dim / 4);
+  int64_t w_dim = embed_dim - (d_dim + h_dim);
+  if (w_dim < 0) w_dim = 0;
+  w_dim = even_dim(w_dim);
+  int64_t rem = embed_dim - (d_dim + h_dim + w_dim);
+  if (rem < 0) rem = 0;
+  const int64_t tpf = gh * gw > 0 ? gh * gw : 1, w = gw > 0 ? gw : 1;
+  (void)depth;
+  for (int64_t k = 0; k < n; ++k) {
+    const int64_t index = indices[k];
+    const int64_t frame = index / tpf, local = index - frame * tpf, row = local / w, col = local - row * w;
+    float* o = out + k * embed_dim;
+    o = one_position_sincos(d_dim, (float)frame, o);
+    o = one_position_sincos(h_dim, (float)row, o);
+    o = one_position_sincos(w_dim, (float)col, o);
+    for (int64_t i = 0; i < rem; ++i) *o++ = 0.0f;
+  }
+}
+
+/* Encoder input tokens (src/model.rs:690-703 after the patch embed): ((conv + bias) + pos) +
+ * modality per row, pos = table[token index of the row]; f32, in that order.  Rows whose
+ * coords fall outside the input stay zero, as in bjo_sparse_patchify3d_forward. */
+int bjo_patchify_encoder_input(const bjo_patchify_config* config, int64_t batch, const float* input,
+                               const int32_t* coords, int64_t rows, const float* weight, const float* bias,
+                               const float* position_table, const float* modality_embed, float* out) {
+  int rc = bjo_sparse_patchify3d_forward(config, batch, input, coords, rows, weight, bias, out);
+  if (rc) return rc;
+  const int64_t D = config->out_channels, gh = config->height / config->patch_h, gw = config->width / config->patch_w;
+  const int64_t depth = config->frames / config->tubelet_size;
+  for (int64_t r = 0; r < rows; ++r) {
+    const int32_t* c = coords + r * 4;
+    if (c[0] < 0 || c[0] >= batch || c[1] < 0 || c[1] >= depth || c[2] < 0 || c[2] >= gh || c[3] < 0 || c[3] >= gw)
+      continue;
+    const int64_t token = ((int64_t)c[1] * gh + c[2]) * gw + c[3];
+    for (int64_t d = 0; d < D; ++d) {
+      float v = out[r * D + d];
+      if (position_table) v = v + position_table[token * D + d];
+      if (modality_embed) v = v + modality_embed[d];
+      out[r * D + d] = v;
+    }
+  }
+  return BJO_OK;
+}
+
 /* ---- live viewer policy (src/viewer.rs) ---- */
 
 static void rgba_rgb(const uint8_t* rgba, int64_t offset, float out[3]) {

@@ -166,6 +166,14 @@ int bjo_front_end_streams(const float* video, int64_t streams, const bjo_patchif
                           const float* bias, float* caches, float* observed, float* age_frames,
                           int32_t age_observed, int64_t* counts);
 
+/* src/positional.rs:46-87 sparse_3d_sincos_pos_embed -> out [n, embed_dim]. */
+void bjo_sparse_3d_sincos_pos_embed(int64_t embed_dim, int64_t depth, int64_t gh, int64_t gw,
+                                    const int64_t* indices, int64_t n, float* out);
+/* Patch embed + position table + modality embedding (src/model.rs:690-703), f32. */
+int bjo_patchify_encoder_input(const bjo_patchify_config* config, int64_t batch, const float* input,
+                               const int32_t* coords, int64_t rows, const float* weight, const float* bias,
+                               const float* position_table, const float* modality_embed, float* out);
+
 /* ---- live viewer policy (src/viewer.rs) ---- */
 typedef struct bjo_rgba_frame_stats {
   float channel_delta[3];

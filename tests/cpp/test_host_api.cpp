@@ -155,6 +155,14 @@ TEST(sparse_mask_bucket_preserves_changed_tokens) {
   CHECK(!bucketed.is_dense_ordered());
 }
 
+// src/positional.rs:104-111
+TEST(sparse_positional_encoding_has_expected_shape) {
+  const auto values = sparse_3d_sincos_pos_embed(10, TokenGridShape(2, 2, 2), {0, 7});
+  CHECK_EQ(values.size(), (size_t)20);
+  CHECK_EQ(values[0], 0.0f);
+  CHECK_EQ(values[3], 1.0f);
+}
+
 TEST(abi_version_matches_header) { CHECK_EQ(bjf_abi_version(), BJF_ABI_VERSION); }
 
 TEST_MAIN()

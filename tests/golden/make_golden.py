@@ -160,6 +160,11 @@ KNOWN_ANSWERS = {
         "token_dim_mismatch": {"features": [1, 4, 2], "tokens": [1, 1, 3], "indices": [1, 1],
                                "message_contains": "feature memory token dims mismatch"},
     },
+    "sparse_positional_encoding": {
+        "source": "src/positional.rs:104-111",
+        "embed_dim": 10, "grid": [2, 2, 2], "indices": [0, 7], "len": 20,
+        "values_at": {"0": 0.0, "3": 1.0},
+    },
     "feature_memory_ema": {
         "source": "tests/feature_memory.rs:145-177 (Ema { alpha: 0.25 }: first observation assigned, then blended)",
         "batch": 1, "grid": [1, 1, 2], "embed_dim": 1, "alpha": 0.25,

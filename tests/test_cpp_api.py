@@ -28,7 +28,7 @@ def _run(binary: str) -> str:
 
 def test_cpp_host_api():
     out = _run("test_host_api")
-    assert out.count("PASS ") >= 17
+    assert out.count("PASS ") >= 18
 
 
 @pytest.mark.gpu
