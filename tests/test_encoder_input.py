@@ -47,7 +47,7 @@ def test_device_encoder_input_matches_oracle(cuda_device, dtype, rows_kind, use_
     import burn_jepa_b200 as bj
 
     dt = {"f32": torch.float32, "f16": torch.float16, "bf16": torch.bfloat16}[dtype]
-    B, C, T, H, W, kt, P, D = 2, 3, 4, 128, 128, 2, 16, 256
+    B, C, T, H, W, kt, P, D = 2, 3, 4, 256, 256, 2, 16, 256
     grid = oracle.TokenGridShape(T // kt, H // P, W // P)
     n = len(grid)
     rng = np.random.default_rng(5)
