@@ -557,9 +557,11 @@ __device__ __forceinline__ void pack_chunk32(uint8_t* dst, const float (&v)[32],
 // 32 TMEM lanes (tile rows, lane = thread) x bn columns from `taddr` -> + bias -> the row's
 // destination.  `stage` / `stage_smem` address this warp's staging buffers; `chunk` counts
 // this thread's staged chunks (selects the buffer).  Warp-collective.
+// Columns [c_begin, c_end) of the accumulator (c_begin a multiple of the chunk width).
 __device__ __forceinline__ void drain_accumulator_bulk(const GatherGeometry& g, const EpilogueArgs& ep, int4 c,
-                                                       int M, int gm, int n0, int bn, uint32_t taddr, int lane,
-                                                       uint8_t* stage, uint32_t stage_smem, int& chunk) {
+                                                       int M, int gm, int n0, int c_begin, int c_end, uint32_t taddr,
+                                                       int lane, uint8_t* stage, uint32_t stage_smem, int& chunk) {
+  const int bn = c_end;
   const int ce = ep.out_elem_bytes;
   bool valid = false;
   char* dst_row = nullptr;
@@ -581,7 +583,7 @@ __device__ __forceinline__ void drain_accumulator_bulk(const GatherGeometry& g, 
     }
   }
   const int cpc = kEpiChunkBytes / ce;  // columns per chunk: 64 (16-bit) or 32 (f32)
-  for (int c0 = 0; c0 < bn; c0 += cpc, ++chunk) {
+  for (int c0 = c_begin; c0 < bn; c0 += cpc, ++chunk) {
     const int col0 = n0 + c0;
     const int ncol = min(cpc, min(bn - c0, g.D - col0));  // the same for the whole warp
     if (ncol <= 0) break;
@@ -661,6 +663,10 @@ __global__ void __maxnreg__(80)
   if (cluster >= num_tiles) return;  // the same for both CTAs of the pair, before any allocation
   const int half = bn >> 1;
   const int my_tiles = (num_tiles - cluster + nclusters - 1) / nclusters;
+  // On the CTA's last tile the producer warps, idle by then, drain accumulator columns
+  // [split, bn) while the epilogue warps drain [0, split): a chunk-aligned half.
+  const int epi_chunk_cols = kEpiChunkBytes / ep.out_elem_bytes;
+  const int split = (bn / 2) / epi_chunk_cols * epi_chunk_cols;
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + PairSmemLayout::bar_off);
   uint64_t* peer_full = full + kPairStages;
@@ -711,6 +717,7 @@ __global__ void __maxnreg__(80)
     const int sub = lane >> 3;
     int kbg = 0;
     int prod_phase = 0;
+    int4 last_c = make_int4(-1, -1, -1, -1);  // this lane's row of the last tile (for the drain below)
     const int p = tid - kEpilogueWarps * 32;
     const int row_in_pair = (int)rank * kBM + p;
     int64_t my_row = resolve_row(rs, soff, g, M, (cluster / n_tiles) * (2 * kBM) + row_in_pair);
@@ -724,6 +731,8 @@ __global__ void __maxnreg__(80)
       }
       const int next = tile + nclusters;  // resolved now, used at the next tile
       my_row = next < num_tiles ? resolve_row(rs, soff, g, M, (next / n_tiles) * (2 * kBM) + row_in_pair) : -1;
+      if (next >= num_tiles) last_c = next_row(rs, soff, g, M, (tile / n_tiles) * (2 * kBM) + (int)rank * kBM +
+                                                                32 * (warp - kEpilogueWarps) + lane);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int m = 32 * pw_ + 4 * i + sub;
@@ -745,6 +754,29 @@ __global__ void __maxnreg__(80)
       }
     }
     cp_async_wait_all();
+    // warp-uniform: the drain below is warp-collective (tcgen05.ld)
+    if (__all_sync(0xffffffffu, !aborted) && split > 0 && my_tiles > 0) {
+      // Help drain the last accumulator: once it is complete every MMA has finished reading
+      // this CTA's A stages, so they serve as this warp's staging buffers.
+      const int it_last = my_tiles - 1;
+      const int tile = cluster + it_last * nclusters;
+      const int buf = it_last & 1;
+      bool ok = mbar_wait_bounded(&acc_full[buf], (uint32_t)((it_last >> 1) & 1), abort_flag, kWaitLimitNs);
+      if (__any_sync(0xffffffffu, !ok)) {
+        aborted = true;
+      } else {
+        tc_fence_after();
+        const int qw = warp - kEpilogueWarps;  // TMEM lane quarter of this warp (warp % 4)
+        uint8_t* pstage = smem + PairSmemLayout::a_off + qw * kEpiWarpBytes;
+        int pchunk = 0;
+        drain_accumulator_bulk(g, ep, last_c, M, (tile / n_tiles) * (2 * kBM) + (int)rank * kBM + 32 * qw + lane,
+                               (tile % n_tiles) * bn, split, bn,
+                               tmem_base + (uint32_t)buf * acc_cols + ((uint32_t)(qw * 32) << 16), lane, pstage,
+                               smem_u32(pstage), pchunk);
+        tc_fence_before();
+        bulk_wait<0>();
+      }
+    }
   } else if (warp == kMmaWarp) {
     if (rank == 0 && lane == 0) {
       // ---------------- MMA issuer (even CTA) ----------------
@@ -850,7 +882,8 @@ __global__ void __maxnreg__(80)
       tc_fence_after();
       const int n0 = (tile % n_tiles) * bn;
       const int gm = (tile / n_tiles) * (2 * kBM) + (int)rank * kBM + m;
-      drain_accumulator_bulk(g, ep, c, M, gm, n0, bn,
+      const bool last = tile + nclusters >= num_tiles;
+      drain_accumulator_bulk(g, ep, c, M, gm, n0, 0, last && split > 0 ? split : bn,
                              tmem_base + (uint32_t)buf * acc_cols + ((uint32_t)(warp * 32) << 16), lane, stage,
                              stage_smem, chunk);
       tc_fence_before();

@@ -73,3 +73,68 @@ def test_front_end_steps_match_oracle(cuda_device, S, H, W, D, cache_dt, video_d
             # rows never written keep their exact pre-filled values
             assert np.array_equal(got[~written], caches.new_tensor(cache0).to(dt[cache_dt]).float().cpu().numpy()[~written])
         ref_cache = got.copy()  # carry the device's rounding forward; exactness is checked per step
+
+
+def _oracle_front_end(xs, weight, bias, ocfg, grid, omask, ref_cache, ref_obs, ref_age, age_observed):
+    counts = []
+    for s in range(xs.shape[0]):
+        idx = oracle.patch_diff_context_mask_from_video(xs[s:s + 1], ocfg.tubelet_size, ocfg.patch_h, grid, omask)
+        counts.append(len(idx))
+        coords = oracle.sparse_patchify_plan_coords(idx, grid, 1)
+        feats = oracle.sparse_patchify3d_forward(ocfg, xs[s:s + 1], coords, weight, bias)
+        oracle.feature_memory_assign_latest(ref_cache[s:s + 1], ref_obs[s:s + 1], ref_age[s:s + 1], feats[None],
+                                            idx.astype(np.int32)[None], age_observed=age_observed)
+    return np.array(counts)
+
+
+@pytest.mark.parametrize("name,S,T,H,W,D,mask_kind", [
+    ("dilated_cap", 3, 2, 128, 128, 256, "dilated"),      # dilated selection kernel + its row plan
+    ("topk_fill", 3, 2, 128, 128, 256, "topk"),           # threshold 0, fill to the budget: radix select
+    ("many_streams", 70, 2, 32, 48, 128, "adaptive"),     # 70 streams, some static: binary search of offsets
+    ("depth_two", 2, 4, 64, 64, 256, "adaptive"),         # two tubelets per clip
+    ("one_stream", 1, 2, 256, 256, 512, "adaptive"),
+])
+def test_front_end_mask_policies_match_oracle(cuda_device, name, S, T, H, W, D, mask_kind):
+    import torch
+
+    C, KT, P = 3, 2, 16
+    grid_t = (T // KT, H // P, W // P)
+    n = grid_t[0] * grid_t[1] * grid_t[2]
+    grid = oracle.TokenGridShape(*grid_t)
+    weight = workloads.splitmix_normal(31, (D, C, KT, P, P), 0.02)
+    bias = workloads.splitmix_normal(32, (D,), 0.02)
+    wd = torch.from_numpy(weight).to(cuda_device, torch.float16)
+    bd = torch.from_numpy(bias).to(cuda_device)
+    caches = torch.zeros((S, n, D), device=cuda_device, dtype=torch.float16)
+    observed = torch.zeros((S, n), device=cuda_device)
+    age = torch.zeros((S, n), device=cuda_device)
+    ref_cache = np.zeros((S, n, D), np.float32)
+    ref_obs = np.zeros((S, n), np.float32)
+    ref_age = np.zeros((S, n), np.float32)
+    ocfg = oracle.PatchifyConfig(C, D, T, H, W, KT, P, P)
+    for step in range(2):
+        video = workloads.rect_perturbation_clips(300 + step, S, C, T, H, W, area_fraction=0.15)
+        if name == "many_streams":
+            video[::7, :, 1:] = video[::7, :, :1]  # every 7th stream static: no change, fill to 1 token
+        vd = torch.from_numpy(video).to(cuda_device, torch.float16)
+        xs = vd.float().cpu().numpy()
+        thr = workloads.choose_threshold(oracle.patch_diff_token_scores(xs[1:2], KT, P), 0.15)
+        if mask_kind == "dilated":
+            args = (thr, max(2, n // 6), 1)
+            mask, omask = bj.PatchDiffConfig.new(*args).with_dilation(1), oracle.PatchDiffConfig.new(*args).with_dilation(1)
+        elif mask_kind == "topk":
+            args = (0.0, max(2, n // 5), 1)
+            mask, omask = bj.PatchDiffConfig.new(*args), oracle.PatchDiffConfig.new(*args)
+        else:
+            args = (thr, 1, n, 1)
+            mask, omask = bj.PatchDiffConfig.adaptive_threshold(*args), oracle.PatchDiffConfig.adaptive_threshold(*args)
+        fe = bj.FrontEnd(S, C, T, H, W, KT, P, D, mask, torch.float16, torch.float16, cuda_device)
+        counts = fe.step(vd, wd, bd, caches, observed, age, age_observed=step > 0).cpu().numpy()
+        want = _oracle_front_end(xs, wd.float().cpu().numpy(), bias, ocfg, grid, omask, ref_cache, ref_obs, ref_age,
+                                 step > 0)
+        assert np.array_equal(counts, want), name
+        assert np.array_equal(observed.cpu().numpy(), ref_obs)
+        assert np.array_equal(age.cpu().numpy(), ref_age)
+        got = caches.float().cpu().numpy()
+        assert max_rel_err(got, ref_cache) <= 1e-2
+        ref_cache = got.copy()
