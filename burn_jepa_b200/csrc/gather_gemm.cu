@@ -659,11 +659,8 @@ __global__ void __maxnreg__(80)
   const int num_tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * n_tiles;  // 256-row pair tiles
   const uint32_t rank = cluster_ctarank();                           // 0: issues the MMAs
   const int cluster = (int)(blockIdx.x >> 1);
-  // Only as many pairs as the number of tile rounds needs: the same rounds finish in the
-  // same time, and the SMs of the pairs that leave now run the next frame's patch-diff pass.
-  const int rounds = num_tiles > 0 ? (num_tiles + (int)(gridDim.x >> 1) - 1) / (int)(gridDim.x >> 1) : 1;
-  const int nclusters = num_tiles > 0 ? (num_tiles + rounds - 1) / rounds : 1;
-  if (cluster >= num_tiles || cluster >= nclusters) return;  // the same for both CTAs of the pair
+  const int nclusters = (int)(gridDim.x >> 1);
+  if (cluster >= num_tiles) return;  // the same for both CTAs of the pair, before any allocation
   const int half = bn >> 1;
   const int my_tiles = (num_tiles - cluster + nclusters - 1) / nclusters;
   // On the CTA's last tile the producer warps, idle by then, drain accumulator columns
