@@ -928,7 +928,8 @@ class InterframeJepaFeatureMemory {
 
 // ---------------------------------------------------------------------------------------
 // FrontEnd: one frame step over S independent streams, fully on the device
-// (patch-diff mask -> plan -> gather-GEMM with bias -> in-place token-cache write).
+// (patch-diff scores -> selection and row plan -> gather-GEMM with bias -> in-place
+// token-cache write; three kernels chained with programmatic dependent launch).
 // ---------------------------------------------------------------------------------------
 class FrontEnd {
  public:
