@@ -288,6 +288,50 @@ def patch_diff_scores_from_rgba(prev, current, patch_size: int, grid, stats: boo
     return out, [RgbaFrameStats.from_buffer_copy(raw[i * sz:(i + 1) * sz]) for i in range(S)]
 
 
+ViewerMaskPolicy = _abi.ViewerMaskPolicy
+
+
+def viewer_patch_diff_masks(direct_indices, direct_counts, grid, policy: "ViewerMaskPolicy", out=None,
+                            stream=None):
+    """The live viewer's policy after the selection (src/viewer.rs:780-816, 946-961) on the device.
+
+    direct_indices [S, N] / direct_counts [S] int32 (a selection without dilation) ->
+    (write_indices [S, N], write_counts [S], encode_indices [S, N], encode_counts [S]).
+    `out` may name the direct buffers as the write buffers."""
+    torch = _torch()
+    S, N = direct_indices.shape
+    if out is None:
+        dev = direct_indices.device
+        out = (torch.empty((S, N), dtype=torch.int32, device=dev), torch.empty((S,), dtype=torch.int32, device=dev),
+               torch.empty((S, N), dtype=torch.int32, device=dev), torch.empty((S,), dtype=torch.int32, device=dev))
+    wi, wc, ei, ec = out
+    check(load().bjf_viewer_patch_diff_masks(_ptr(direct_indices), _ptr(direct_counts), S, _abi.dims(*grid),
+                                             ctypes.byref(policy), _ptr(wi), _ptr(wc), _ptr(ei), _ptr(ec),
+                                             _stream(stream)))
+    return out
+
+
+def viewer_patch_diff_masks_from_scores(scores, grid, config: PatchDiffConfig, policy: "ViewerMaskPolicy",
+                                        stream=None):
+    """patch_diff_masks_from_scores (src/viewer.rs:831-841) on the device for S streams: the
+    selection of `config` without dilation, then the policy dilating by config.dilation.
+
+    scores [S, N] f32 -> (write_indices [S, N], write_counts [S], encode_indices [S, N],
+    encode_counts [S]), each row ascending up to its count."""
+    torch = _torch()
+    sc = scores if scores.dim() == 2 else scores.unsqueeze(0)
+    S, N = sc.shape
+    dev = scores.device
+    wi = torch.empty((S, N), dtype=torch.int32, device=dev)
+    wc = torch.empty((S,), dtype=torch.int32, device=dev)
+    ei = torch.empty((S, N), dtype=torch.int32, device=dev)
+    ec = torch.empty((S,), dtype=torch.int32, device=dev)
+    check(load().bjf_viewer_patch_diff_masks_from_scores(_ptr(sc.contiguous()), S, _abi.dims(*grid),
+                                                         ctypes.byref(config), ctypes.byref(policy), _ptr(wi),
+                                                         _ptr(wc), _ptr(ei), _ptr(ec), _stream(stream)))
+    return wi, wc, ei, ec
+
+
 # ---------------------------------------------------------------------------
 # Fused step over S independent streams
 # ---------------------------------------------------------------------------

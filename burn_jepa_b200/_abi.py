@@ -114,6 +114,31 @@ class RgbaFrameStats(ctypes.Structure):
     ]
 
 
+class ViewerMaskPolicy(ctypes.Structure):
+    """bjf_viewer_mask_policy: the mask fields of FeatureFrameViewerConfig (src/viewer.rs:566-579)."""
+
+    _fields_ = [
+        ("dense_fallback_density", ctypes.c_float),
+        ("dilation", ctypes.c_int64),
+        ("bucketed_encode", ctypes.c_int32),
+        ("bucket_tokens", ctypes.c_int64),
+        ("bucket_density_count", ctypes.c_int32),
+        ("bucket_densities", ctypes.c_float * 32),
+    ]
+
+    @classmethod
+    def new(cls, dense_fallback_density: float = 0.75, dilation: int = 1, bucketed_encode: bool = True,
+            bucket_tokens: int = 256, bucket_densities=(0.10, 0.25, 0.50)) -> "ViewerMaskPolicy":
+        """Defaults are FeatureFrameViewerConfig::default()'s (src/viewer.rs:27-33, 604-616)."""
+        d = list(bucket_densities)
+        if len(d) > 32:
+            raise ValueError("at most 32 bucket densities")
+        p = cls(float(dense_fallback_density), int(dilation), int(bool(bucketed_encode)), int(bucket_tokens), len(d))
+        for i, v in enumerate(d):
+            p.bucket_densities[i] = float(v)
+        return p
+
+
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I32 = ctypes.c_int32
@@ -136,6 +161,9 @@ SIGNATURES = {
                                   _P, _P]),
     "bjf_front_end_step_no_alloc": (_I32, [ctypes.POINTER(FrontEndDesc), _P, _P, _P, _P, _P, _P, _I32, _P, _P]),
     "bjf_rgba_patch_diff_workspace_bytes": (ctypes.c_size_t, [_I64]),
+    "bjf_viewer_patch_diff_masks": (_I32, [_P, _P, _I64, _DIMS, ctypes.POINTER(ViewerMaskPolicy), _P, _P, _P, _P, _P]),
+    "bjf_viewer_patch_diff_masks_from_scores": (_I32, [_P, _I64, _DIMS, ctypes.POINTER(PatchDiffConfig),
+                                                        ctypes.POINTER(ViewerMaskPolicy), _P, _P, _P, _P, _P]),
     "bjf_sparse_patchify3d_forward_encoder_input": (_I32, [ctypes.POINTER(PatchifyConfig), _P, _I32, _DIMS, _P, _I64,
                                                            _P, _I32, _DIMS, _P, _P, _P, _P, _I32, _P]),
     "bjf_rgba_patch_diff_scores": (_I32, [_P, _P, _I64, _I64, _I64, _I64, _DIMS, _P, _P, _P, ctypes.c_size_t, _P]),

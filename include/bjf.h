@@ -267,6 +267,40 @@ BJF_API bjf_status bjf_rgba_patch_diff_scores(const uint8_t* prev, const uint8_t
                                               bjf_rgba_frame_stats* stats_out, void* workspace,
                                               size_t workspace_bytes, bjf_stream_t stream);
 
+/* The live viewer's mask policy after the threshold selection: the mask fields of
+ * FeatureFrameViewerConfig (src/viewer.rs:566-579).  The encode bucket widths are derived on
+ * the device as sparse_mask_bucket_widths (:887-925) derives them. */
+typedef struct bjf_viewer_mask_policy {
+  float dense_fallback_density; /* patch_diff_dense_fallback_density */
+  int64_t dilation;             /* patch_diff_dilation_tiles (bjf_viewer_patch_diff_masks) */
+  int32_t bucketed_encode;      /* sparse_encode_mode: 0 Exact, 1 BucketedContext */
+  int64_t bucket_tokens;        /* sparse_mask_bucket_tokens (used with no densities) */
+  int32_t bucket_density_count; /* entries of bucket_densities in use, 0..32 */
+  float bucket_densities[32];   /* sparse_mask_bucket_densities */
+} bjf_viewer_mask_policy;
+
+/* Replaces patch_diff_dense_fallback -> dilate_sparse_patch_mask -> finalize_patch_diff_encode_masks
+ * (src/viewer.rs:780-816, 946-961) for S streams: direct_indices [S, N] / direct_counts [S]
+ * (a selection without dilation) -> write mask and encode mask, [S, N] / [S] each, ascending.
+ * The direct buffers may be the write buffers.  Grids up to 32768 tokens.  Errors: a null
+ * buffer or policy, an empty grid, more than 32 bucket densities. */
+BJF_API bjf_status bjf_viewer_patch_diff_masks(const int32_t* direct_indices, const int32_t* direct_counts,
+                                               int64_t streams, const int64_t grid[3],
+                                               const bjf_viewer_mask_policy* policy, int32_t* write_indices,
+                                               int32_t* write_counts, int32_t* encode_indices,
+                                               int32_t* encode_counts, bjf_stream_t stream);
+
+/* patch_diff_masks_from_scores (src/viewer.rs:831-841): the selection of `config` without its
+ * dilation (patch_diff_base_mask_from_scores, :819-829), then bjf_viewer_patch_diff_masks with
+ * config->dilation in place of the policy's (the reference dilates by the sparsity config).
+ * scores [S, N] f32 (device). */
+BJF_API bjf_status bjf_viewer_patch_diff_masks_from_scores(const float* scores, int64_t streams,
+                                                           const int64_t grid[3], const bjf_patch_diff_config* config,
+                                                           const bjf_viewer_mask_policy* policy,
+                                                           int32_t* write_indices, int32_t* write_counts,
+                                                           int32_t* encode_indices, int32_t* encode_counts,
+                                                           bjf_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Fused step: mask -> plan -> patchify -> cache write, for S independent streams
  * ---------------------------------------------------------------------- */

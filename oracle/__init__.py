@@ -472,6 +472,63 @@ def bucket_sparse_mask(indices, dense_len: int, bucket_tokens: int) -> np.ndarra
     return out[:n].copy()
 
 
+def sparse_mask_bucket_widths(dense_len: int, bucket_tokens: int, bucket_densities=()) -> list:
+    """sparse_mask_bucket_widths (src/viewer.rs:887-925) with density_tokens(.., Ceil, 0.0)
+    (:739-752): ascending unique encode widths, the grid length last; none below 256 tokens."""
+    if dense_len < 256:
+        return []
+    widths = []
+    if len(bucket_densities) == 0:
+        if bucket_tokens > 1:
+            bucket = min(bucket_tokens, max(dense_len // 4, 1))
+            w = bucket
+            while w < dense_len:
+                widths.append(w)
+                w += bucket
+    else:
+        for d in bucket_densities:
+            d = np.float32(d)
+            if np.isfinite(d) and d > 0:
+                t = int(np.ceil(np.float32(dense_len) * np.float32(min(d, np.float32(1.0)))))
+                widths.append(min(max(t, 1), max(dense_len, 1)))
+    widths.append(dense_len)
+    return sorted(set(widths))
+
+
+def finalize_patch_diff_encode_masks(write, dense_len: int, bucketed: bool, bucket_tokens: int,
+                                     bucket_densities=()) -> np.ndarray:
+    """The encode mask of finalize_patch_diff_encode_masks (src/viewer.rs:946-961):
+    Exact -> the write mask; BucketedContext -> bucket_sparse_mask_with_config (:927-944)."""
+    write = np.asarray(write, dtype=np.int64)
+    if not bucketed or dense_len < 256 or write.size == dense_len:
+        return write.copy()
+    for w in sparse_mask_bucket_widths(dense_len, bucket_tokens, bucket_densities):
+        if w >= write.size:
+            return padded_to_len(write, dense_len, w)
+    return write.copy()
+
+
+def viewer_patch_diff_masks(direct, grid: "TokenGridShape", dense_fallback_density: float, dilation: int,
+                            bucketed: bool = True, bucket_tokens: int = 256,
+                            bucket_densities=(0.10, 0.25, 0.50)):
+    """patch_diff_base_mask_from_scores after its selection (src/viewer.rs:826-828) and
+    finalize_patch_diff_encode_masks (:946-961): direct mask -> (write mask, encode mask)."""
+    n = len(grid)
+    m = patch_diff_dense_fallback(direct, n, dense_fallback_density)
+    write = dilate_sparse_patch_mask(m, grid, dilation)
+    return write, finalize_patch_diff_encode_masks(write, n, bucketed, bucket_tokens, bucket_densities)
+
+
+def viewer_patch_diff_masks_from_scores(scores, grid: "TokenGridShape", config: "PatchDiffConfig",
+                                        dense_fallback_density: float, bucketed: bool = True,
+                                        bucket_tokens: int = 256, bucket_densities=(0.10, 0.25, 0.50)):
+    """patch_diff_masks_from_scores (src/viewer.rs:831-841): the selection without dilation
+    (:819-825), then the viewer policy dilating by the config's dilation."""
+    direct = patch_diff_context_mask_from_scores(scores, grid, config.with_dilation(0))
+    return viewer_patch_diff_masks(direct, grid, dense_fallback_density, config.dilation, bucketed, bucket_tokens,
+                                   bucket_densities)
+
+
 def front_end_streams(video, config: PatchifyConfig, mask_config: PatchDiffConfig, weight, bias,
                       caches, observed, age_frames, age_observed: bool) -> np.ndarray:
     """One front-end step over S independent streams (f32), in place on the caches."""

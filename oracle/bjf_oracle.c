@@ -761,7 +761,8 @@ int bjo_patch_diff_scores_from_rgba(const uint8_t* prev, int64_t prev_len, const
 int64_t bjo_patch_diff_dense_fallback(const int64_t* idx, int64_t n, int64_t dense_len, float density, int64_t* out) {
   if (density < 0.0f) density = 0.0f;
   if (density > 1.0f) density = 1.0f;
-  const int64_t fallback = (int64_t)ceilf((float)dense_len * density);
+  /* `as usize` saturates: a NaN density gives 0 tokens */
+  const int64_t fallback = density != density ? 0 : (int64_t)ceilf((float)dense_len * density);
   const int64_t at_least = fallback > 1 ? fallback : 1;
   if (n == dense_len || (fallback < dense_len && n >= at_least)) {
     for (int64_t i = 0; i < dense_len; ++i) out[i] = i;

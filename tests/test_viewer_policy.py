@@ -118,3 +118,141 @@ def test_device_rgba_uniform_lighting_and_errors(cuda_device):
         bj.patch_diff_scores_from_rgba(prev, cur, 16, bj.TokenGridShape(1, 4, 3))
     with pytest.raises(bj.BjfError, match="smaller than the token grid"):
         bj.patch_diff_scores_from_rgba(prev, cur, 16, bj.TokenGridShape(1, 5, 4))
+
+
+# ---------------------------------------------------------------------------
+# Mask policy after the selection: dense fallback -> dilation -> encode buckets
+# ---------------------------------------------------------------------------
+
+def test_oracle_bucket_widths_match_reference_prewarm_tests():
+    # src/viewer.rs:1342-1376: the default densities (0.10, 0.25, 0.50) and the legacy step
+    assert oracle.sparse_mask_bucket_widths(32 * 32, 256, (0.10, 0.25, 0.50)) == [103, 256, 512, 1024]
+    assert oracle.sparse_mask_bucket_widths(64 * 64, 256, (0.10, 0.25, 0.50)) == [410, 1024, 2048, 4096]
+    # the legacy step gives 768 too; the reference's prewarm list [256, 512, 1024] drops it
+    # because 768 tokens reach the 0.75 dense fallback and finalize to the dense mask
+    assert oracle.sparse_mask_bucket_widths(32 * 32, 256, ()) == [256, 512, 768, 1024]
+    assert len(oracle.patch_diff_dense_fallback(np.arange(768), 1024, 0.75)) == 1024
+    assert oracle.sparse_mask_bucket_widths(255, 256, (0.1,)) == []
+
+
+def test_oracle_bucketed_encode_widens_context():
+    # src/viewer.rs:1322-1340: one changed token -> write mask exact, encode mask 103 tokens
+    grid = oracle.TokenGridShape(1, 32, 32)
+    changed = [15 * 32 + 16]
+    write, enc = oracle.viewer_patch_diff_masks(changed, grid, 0.75, 0)
+    assert write.tolist() == changed
+    assert len(enc) == 103 and changed[0] in enc.tolist()
+    # src/viewer.rs:1377-1389: 120 evenly spaced tokens -> the 256 bucket
+    mask = np.array([(i * 1023 + 60) // 120 for i in range(120)])
+    write, enc = oracle.viewer_patch_diff_masks(mask, grid, 0.75, 0)
+    assert write.tolist() == mask.tolist() and len(enc) == 256 and set(mask.tolist()) <= set(enc.tolist())
+
+
+def test_oracle_masks_from_scores_dense_cutoff_before_dilation():
+    # src/viewer.rs:1456-1484 through patch_diff_masks_from_scores
+    grid = oracle.TokenGridShape(1, 5, 5)
+    scores = np.zeros(25, np.float32)
+    scores[12] = 0.5
+    cfg = oracle.PatchDiffConfig.adaptive_threshold(0.10, 0, 25, 1).with_dilation(1)
+    write, enc = oracle.viewer_patch_diff_masks_from_scores(scores, grid, cfg, 0.25, bucketed=False)
+    assert len(write) == 9 and 12 in write.tolist() and enc.tolist() == write.tolist()
+
+
+def _direct_masks(seed, S, n, densities):
+    rng = np.random.default_rng(seed)
+    idx = np.zeros((S, n), np.int32)
+    cnt = np.zeros(S, np.int32)
+    for s in range(S):
+        d = densities[s % len(densities)]
+        m = int(round(n * d))
+        sel = np.sort(rng.choice(n, size=m, replace=False)) if m else np.zeros(0, np.int64)
+        idx[s, :m] = sel
+        cnt[s] = m
+    return idx, cnt
+
+
+_VIEWER_POLICIES = {
+    # name: (grid, dense_fallback_density, dilation, bucketed, bucket_tokens, densities)
+    "default": ((1, 32, 32), 0.75, 1, True, 256, (0.10, 0.25, 0.50)),
+    "exact": ((1, 32, 32), 0.75, 1, False, 256, (0.10, 0.25, 0.50)),
+    "legacy_step": ((1, 32, 48), 0.75, 2, True, 100, ()),
+    "legacy_single_width": ((1, 16, 16), 0.75, 0, True, 1, ()),
+    "no_fallback": ((1, 40, 40), 1.0, 3, True, 256, (0.05, 0.3, 0.9, 0.3)),
+    "fallback_low": ((1, 24, 24), 0.1, 1, True, 256, (0.2, 0.6)),
+    "nan_fallback": ((1, 16, 16), float("nan"), 1, True, 256, (0.1, float("nan"), -1.0, 2.0)),
+    "small_grid": ((1, 8, 8), 0.75, 1, True, 256, (0.1, 0.25, 0.5)),
+    "depth_two": ((2, 20, 20), 0.75, 2, True, 256, (0.1, 0.25, 0.5)),
+    "large_grid": ((1, 128, 256), 0.75, 1, True, 256, (0.1, 0.25, 0.5)),
+}
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", sorted(_VIEWER_POLICIES))
+def test_device_viewer_masks_match_oracle(cuda_device, name):
+    import torch
+
+    import burn_jepa_b200 as bj
+
+    g, fb, dil, bucketed, bt, dens = _VIEWER_POLICIES[name]
+    n = g[0] * g[1] * g[2]
+    dens_list = (0.0, 0.002, 0.01, 0.05, 0.09, 0.11, 0.2, 0.3, 0.6, 0.8, 1.0)
+    S = len(dens_list)
+    idx, cnt = _direct_masks(7 + n, S, n, dens_list)
+    policy = bj.ViewerMaskPolicy.new(fb, dil, bucketed, bt, dens)
+    d_idx, d_cnt = torch.from_numpy(idx).to(cuda_device), torch.from_numpy(cnt).to(cuda_device)
+    wi, wc, ei, ec = (t.cpu().numpy() for t in bj.viewer_patch_diff_masks(d_idx, d_cnt, bj.TokenGridShape(*g), policy))
+    og = oracle.TokenGridShape(*g)
+    for s in range(S):
+        w, e = oracle.viewer_patch_diff_masks(idx[s, :cnt[s]], og, fb, dil, bucketed, bt, dens)
+        assert wc[s] == len(w) and wi[s, :wc[s]].tolist() == w.tolist(), (name, s)
+        assert ec[s] == len(e) and ei[s, :ec[s]].tolist() == e.tolist(), (name, s)
+    # the direct buffers may be the write buffers
+    out = (d_idx, d_cnt, torch.empty_like(d_idx), torch.empty_like(d_cnt))
+    bj.viewer_patch_diff_masks(d_idx, d_cnt, bj.TokenGridShape(*g), policy, out=out)
+    assert np.array_equal(d_cnt.cpu().numpy(), wc) and np.array_equal(out[3].cpu().numpy(), ec)
+    for s in range(S):
+        assert d_idx[s, :wc[s]].cpu().numpy().tolist() == wi[s, :wc[s]].tolist()
+        assert out[2][s, :ec[s]].cpu().numpy().tolist() == ei[s, :ec[s]].tolist()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("threshold,dilation,fallback", [(0.10, 1, 0.25), (0.6, 2, 0.75), (0.95, 1, 0.75), (0.3, 0, 0.5)])
+def test_device_viewer_masks_from_scores_match_oracle(cuda_device, threshold, dilation, fallback):
+    import torch
+
+    import burn_jepa_b200 as bj
+
+    g = (1, 32, 32)
+    n = g[0] * g[1] * g[2]
+    S = 6
+    rng = np.random.default_rng(int(threshold * 100) + dilation)
+    scores = (rng.uniform(0, 1, size=(S, n)) ** np.linspace(1, 12, S)[:, None]).astype(np.float32)
+    cfg = bj.PatchDiffConfig.adaptive_threshold(threshold, 4, n, 1).with_dilation(dilation)
+    policy = bj.ViewerMaskPolicy.new(fallback, 0)  # the config's dilation applies
+    wi, wc, ei, ec = (t.cpu().numpy() for t in bj.viewer_patch_diff_masks_from_scores(
+        torch.from_numpy(scores).to(cuda_device), bj.TokenGridShape(*g), cfg, policy))
+    ocfg = oracle.PatchDiffConfig.adaptive_threshold(threshold, 4, n, 1).with_dilation(dilation)
+    for s in range(S):
+        w, e = oracle.viewer_patch_diff_masks_from_scores(scores[s], oracle.TokenGridShape(*g), ocfg, fallback)
+        assert wi[s, :wc[s]].tolist() == w.tolist(), s
+        assert ei[s, :ec[s]].tolist() == e.tolist(), s
+
+
+@pytest.mark.gpu
+def test_device_viewer_masks_errors(cuda_device):
+    import torch
+
+    import burn_jepa_b200 as bj
+
+    idx = torch.zeros((1, 64), dtype=torch.int32, device=cuda_device)
+    cnt = torch.zeros((1,), dtype=torch.int32, device=cuda_device)
+    bad = bj.ViewerMaskPolicy.new()
+    bad.bucket_density_count = 33
+    with pytest.raises(bj.BjfError, match="bucket densities"):
+        bj.viewer_patch_diff_masks(idx, cnt, bj.TokenGridShape(1, 8, 8), bad)
+    with pytest.raises(bj.BjfError, match="32768 tokens"):
+        big = torch.zeros((1, 2 * 128 * 256), dtype=torch.int32, device=cuda_device)
+        bj.viewer_patch_diff_masks(big, cnt, bj.TokenGridShape(2, 128, 256), bj.ViewerMaskPolicy.new())
+    neg = bj.ViewerMaskPolicy.new(dilation=-1)
+    with pytest.raises(bj.BjfError, match="non-negative"):
+        bj.viewer_patch_diff_masks(idx, cnt, bj.TokenGridShape(1, 8, 8), neg)
