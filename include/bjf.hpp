@@ -559,6 +559,128 @@ inline SparseTokenMask bucket_sparse_mask(SparseTokenMask mask, TokenGridShape g
   return mask.padded_to_multiple(std::min(bucket_tokens, std::max<size_t>(grid.len() / 4, 1)));
 }
 
+constexpr std::array<float, 3> DEFAULT_SPARSE_MASK_BUCKET_DENSITIES = {0.10f, 0.25f, 0.50f};  // :33
+
+enum class FeatureFrameSparseEncodeMode { Exact, BucketedContext };  // src/viewer.rs:128-137
+
+// sparse_mask_bucket_widths (src/viewer.rs:887-925), with density_tokens(.., Ceil, 0.0) (:739-752).
+inline std::vector<size_t> sparse_mask_bucket_widths(TokenGridShape grid, size_t bucket_tokens,
+                                                     const std::vector<float>& bucket_densities) {
+  const size_t n = grid.len();
+  if (n < 256) return {};
+  std::vector<size_t> widths;
+  if (bucket_densities.empty()) {
+    if (bucket_tokens > 1) {
+      const size_t bucket = std::min(bucket_tokens, std::max<size_t>(n / 4, 1));
+      for (size_t w = bucket; w < n; w += bucket) widths.push_back(w);
+    }
+  } else {
+    for (float d : bucket_densities)
+      if (std::isfinite(d) && d > 0.0f) {
+        const size_t t = (size_t)std::ceil((float)n * std::min(d, 1.0f));
+        widths.push_back(std::min(std::max<size_t>(t, 1), std::max<size_t>(n, 1)));
+      }
+  }
+  widths.push_back(n);
+  std::sort(widths.begin(), widths.end());
+  widths.erase(std::unique(widths.begin(), widths.end()), widths.end());
+  return widths;
+}
+
+// The mask fields of FeatureFrameViewerConfig (src/viewer.rs:566-579) with their defaults.
+struct FeatureFrameViewerMaskConfig {
+  float patch_diff_dense_fallback_density = DEFAULT_PATCH_DIFF_DENSE_FALLBACK_DENSITY;
+  size_t patch_diff_dilation_tiles = DEFAULT_PATCH_DIFF_DILATION_TILES;
+  FeatureFrameSparseEncodeMode sparse_encode_mode = FeatureFrameSparseEncodeMode::BucketedContext;
+  size_t sparse_mask_bucket_tokens = DEFAULT_SPARSE_MASK_BUCKET_TOKENS;
+  std::vector<float> sparse_mask_bucket_densities{DEFAULT_SPARSE_MASK_BUCKET_DENSITIES.begin(),
+                                                  DEFAULT_SPARSE_MASK_BUCKET_DENSITIES.end()};
+
+  std::vector<size_t> sparse_mask_bucket_widths(TokenGridShape grid) const {
+    return bjf::sparse_mask_bucket_widths(grid, sparse_mask_bucket_tokens, sparse_mask_bucket_densities);
+  }
+  bjf_viewer_mask_policy to_c() const {
+    ensure(sparse_mask_bucket_densities.size() <= 32, "viewer mask policy holds 0..32 bucket densities");
+    bjf_viewer_mask_policy p{};
+    p.dense_fallback_density = patch_diff_dense_fallback_density;
+    p.dilation = (int64_t)patch_diff_dilation_tiles;
+    p.bucketed_encode = sparse_encode_mode == FeatureFrameSparseEncodeMode::BucketedContext ? 1 : 0;
+    p.bucket_tokens = (int64_t)sparse_mask_bucket_tokens;
+    p.bucket_density_count = (int32_t)sparse_mask_bucket_densities.size();
+    for (size_t i = 0; i < sparse_mask_bucket_densities.size(); ++i) p.bucket_densities[i] = sparse_mask_bucket_densities[i];
+    return p;
+  }
+};
+
+struct FeatureFrameSparseMasks {  // src/viewer.rs:762-769
+  SparseTokenMask write_mask;
+  SparseTokenMask encode_mask;
+};
+
+// bucket_sparse_mask_with_config (src/viewer.rs:927-944)
+inline SparseTokenMask bucket_sparse_mask_with_config(SparseTokenMask mask, TokenGridShape grid,
+                                                      const FeatureFrameViewerMaskConfig& config) {
+  if (grid.len() < 256 || mask.is_dense_ordered()) return mask;
+  for (size_t w : config.sparse_mask_bucket_widths(grid))
+    if (w >= mask.len()) return mask.padded_to_len(w);
+  return mask;
+}
+
+// finalize_patch_diff_encode_masks (src/viewer.rs:946-961)
+inline FeatureFrameSparseMasks finalize_patch_diff_encode_masks(SparseTokenMask write_mask, TokenGridShape grid,
+                                                                const FeatureFrameViewerMaskConfig& config) {
+  SparseTokenMask encode = config.sparse_encode_mode == FeatureFrameSparseEncodeMode::Exact
+                               ? write_mask
+                               : bucket_sparse_mask_with_config(write_mask, grid, config);
+  return {std::move(write_mask), std::move(encode)};
+}
+
+// finalize_patch_diff_masks (src/viewer.rs:963-971)
+inline FeatureFrameSparseMasks finalize_patch_diff_masks(SparseTokenMask mask, TokenGridShape grid,
+                                                         const FeatureFrameViewerMaskConfig& config) {
+  return finalize_patch_diff_encode_masks(
+      patch_diff_dense_fallback(std::move(mask), grid, config.patch_diff_dense_fallback_density), grid, config);
+}
+
+// Device masks of S streams: row s of each [S, N] buffer holds its count of ascending indices.
+struct DeviceSparseMasks {
+  Tensor write_indices, write_counts, encode_indices, encode_counts;
+  size_t dense_len = 0;
+
+  FeatureFrameSparseMasks stream(size_t s, cudaStream_t st = nullptr) const {
+    const auto wc = write_counts.to_host<int32_t>(st), ec = encode_counts.to_host<int32_t>(st);
+    const auto wi = write_indices.to_host<int32_t>(st), ei = encode_indices.to_host<int32_t>(st);
+    ensure(s < wc.size(), "stream index outside the masks");
+    const auto row = [&](const std::vector<int32_t>& v, int32_t c) {
+      return SparseTokenMask::new_(std::vector<size_t>(v.begin() + s * dense_len, v.begin() + s * dense_len + c),
+                                   dense_len);
+    };
+    return {row(wi, wc[s]), row(ei, ec[s])};
+  }
+};
+
+// patch_diff_masks_from_scores (src/viewer.rs:831-841) on device scores [S, N] f32: the
+// selection of `sparsity` without its dilation, then dense fallback, sparsity.dilation and the
+// encode buckets, all on the device.
+inline DeviceSparseMasks patch_diff_masks_from_scores(const Tensor& scores, TokenGridShape grid,
+                                                      const SparseJepaPatchDiffSparsityConfig& sparsity,
+                                                      const FeatureFrameViewerMaskConfig& config,
+                                                      cudaStream_t st = nullptr) {
+  const int64_t n = (int64_t)grid.len();
+  ensure(scores.numel() > 0 && scores.numel() % n == 0, "patch-diff sparsity received unexpected score length");
+  const int64_t S = scores.numel() / n;
+  DeviceSparseMasks m{Tensor({S, n}, BJF_DTYPE_I32), Tensor({S}, BJF_DTYPE_I32), Tensor({S, n}, BJF_DTYPE_I32),
+                      Tensor({S}, BJF_DTYPE_I32), (size_t)n};
+  const bjf_patch_diff_config c = sparsity.to_c();
+  const bjf_viewer_mask_policy p = config.to_c();
+  const auto g = grid.dims();
+  check(bjf_viewer_patch_diff_masks_from_scores(
+      static_cast<const float*>(scores.data()), S, g.data(), &c, &p, static_cast<int32_t*>(m.write_indices.data()),
+      static_cast<int32_t*>(m.write_counts.data()), static_cast<int32_t*>(m.encode_indices.data()),
+      static_cast<int32_t*>(m.encode_counts.data()), to_bjf(st)));
+  return m;
+}
+
 // ---------------------------------------------------------------------------------------
 // plans (src/sparse_patchify.rs:236-330): coords rows (b, t, r, c), batch-major
 // ---------------------------------------------------------------------------------------

@@ -394,6 +394,38 @@ TEST(rgba_patch_diff_ignores_uniform_lighting_shift) {
   CHECK_EQ(stats[0].compensate_global_lighting, 1);
 }
 
+// patch_diff_masks_from_scores on the device against the host policy composition
+// (src/viewer.rs:819-841, 946-961), for several streams and viewer configs.
+TEST(viewer_masks_from_scores_match_host_policy) {
+  const TokenGridShape grid(1, 32, 32);
+  const size_t S = 5, N = grid.len();
+  auto u = seeded(77, S * N, 1.0f);
+  std::vector<float> scores(S * N);
+  for (size_t s = 0; s < S; ++s)
+    for (size_t i = 0; i < N; ++i) scores[s * N + i] = std::pow(std::fabs(u[s * N + i]), 1.0f + 3.0f * (float)s);
+  const Tensor dscores = Tensor::from_host(scores, {(int64_t)S, (int64_t)N}, BJF_DTYPE_F32);
+  FeatureFrameViewerMaskConfig exact;
+  exact.sparse_encode_mode = FeatureFrameSparseEncodeMode::Exact;
+  FeatureFrameViewerMaskConfig legacy;
+  legacy.sparse_mask_bucket_densities.clear();
+  legacy.sparse_mask_bucket_tokens = 100;
+  for (const auto& cfg : {FeatureFrameViewerMaskConfig{}, exact, legacy})
+    for (size_t dilation : {0, 1, 2}) {
+      const auto sparsity = SparseJepaPatchDiffSparsityConfig::adaptive_threshold(0.2f, 4, N, 1).with_dilation(dilation);
+      const auto dev = patch_diff_masks_from_scores(dscores, grid, sparsity, cfg);
+      for (size_t s = 0; s < S; ++s) {
+        const std::vector<float> row(scores.begin() + s * N, scores.begin() + (s + 1) * N);
+        const auto direct = patch_diff_context_mask_from_scores(row, grid, sparsity.with_dilation(0));
+        const auto write = dilate_sparse_patch_mask(
+            patch_diff_dense_fallback(direct, grid, cfg.patch_diff_dense_fallback_density), grid, dilation);
+        const auto host = finalize_patch_diff_encode_masks(write, grid, cfg);
+        const auto got = dev.stream(s);
+        CHECK_EQ(got.write_mask.indices(), host.write_mask.indices());
+        CHECK_EQ(got.encode_mask.indices(), host.encode_mask.indices());
+      }
+    }
+}
+
 // The fused step over S streams against the oracle's per-stream composition.  Unchanged
 // tubelets score exactly 0, so a small positive threshold selects exactly the changed ones
 // whatever the summation order.

@@ -155,6 +155,40 @@ TEST(sparse_mask_bucket_preserves_changed_tokens) {
   CHECK(!bucketed.is_dense_ordered());
 }
 
+// src/viewer.rs:1322-1340
+TEST(bucketed_masks_keep_writes_exact_and_widen_encode_context) {
+  const TokenGridShape grid(1, 32, 32);
+  const size_t changed_index = coords_to_token_index(0, 15, 16, grid);
+  const auto changed = SparseTokenMask::new_({changed_index}, grid.len());
+  const auto masks = finalize_patch_diff_masks(changed, grid, FeatureFrameViewerMaskConfig{});
+  CHECK_EQ(masks.write_mask.indices(), changed.indices());
+  CHECK_EQ(masks.encode_mask.len(), (size_t)103);
+  CHECK(std::find(masks.encode_mask.indices().begin(), masks.encode_mask.indices().end(), changed_index) !=
+        masks.encode_mask.indices().end());
+}
+
+// src/viewer.rs:1342-1376: the widths behind the prewarm lists (768 of the legacy step
+// finalizes to the dense mask under the 0.75 fallback, so the reference's prewarm list omits it)
+TEST(bucket_widths_follow_densities_or_legacy_step) {
+  const FeatureFrameViewerMaskConfig cfg;
+  CHECK_EQ(cfg.sparse_mask_bucket_widths(TokenGridShape(1, 32, 32)), (std::vector<size_t>{103, 256, 512, 1024}));
+  CHECK_EQ(cfg.sparse_mask_bucket_widths(TokenGridShape(1, 64, 64)), (std::vector<size_t>{410, 1024, 2048, 4096}));
+  FeatureFrameViewerMaskConfig legacy;
+  legacy.sparse_mask_bucket_densities.clear();
+  CHECK_EQ(legacy.sparse_mask_bucket_widths(TokenGridShape(1, 32, 32)), (std::vector<size_t>{256, 512, 768, 1024}));
+  CHECK(finalize_patch_diff_masks(SparseTokenMask::evenly_spaced(1024, 768), TokenGridShape(1, 32, 32), legacy)
+            .encode_mask.is_dense_ordered());
+}
+
+// src/viewer.rs:1377-1389
+TEST(bucket_density_list_selects_next_configured_width) {
+  const TokenGridShape grid(1, 32, 32);
+  const auto mask = SparseTokenMask::evenly_spaced(grid.len(), 120);
+  const auto masks = finalize_patch_diff_masks(mask, grid, FeatureFrameViewerMaskConfig{});
+  CHECK_EQ(masks.write_mask.indices(), mask.indices());
+  CHECK_EQ(masks.encode_mask.len(), (size_t)256);
+}
+
 // src/positional.rs:104-111
 TEST(sparse_positional_encoding_has_expected_shape) {
   const auto values = sparse_3d_sincos_pos_embed(10, TokenGridShape(2, 2, 2), {0, 7});
