@@ -332,6 +332,41 @@ def viewer_patch_diff_masks_from_scores(scores, grid, config: PatchDiffConfig, p
     return wi, wc, ei, ec
 
 
+def viewer_patch_diff_masks_from_rgba(prev, current, patch_size: int, grid, config: PatchDiffConfig,
+                                      policy: "ViewerMaskPolicy", stats: bool = False, stream=None):
+    """The Bevy RGBA mask node without refresh state (crates/bevy_jepa/src/mask.rs:126-175) on
+    the device: dense fast paths, else RGBA scores -> patch_diff_masks_from_scores.
+
+    prev / current: [S, H, W, 4] (or [H, W, 4]) uint8 CUDA tensors.  Returns (write_indices,
+    write_counts, encode_indices, encode_counts) and, with stats=True, the frame statistics."""
+    torch = _torch()
+    p = prev if prev.dim() == 4 else prev.unsqueeze(0)
+    c = current if current.dim() == 4 else current.unsqueeze(0)
+    S, H, W, _ = p.shape
+    g = tuple(int(v) for v in grid)
+    N = g[1] * g[2]
+    dims = _abi.dims(*g)
+    lib = load()
+    nbytes = lib.bjf_viewer_rgba_masks_workspace_bytes(S, dims)
+    ws = torch.empty((max(int(nbytes), 1) + 255,), dtype=torch.uint8, device=prev.device)
+    off = (-ws.data_ptr()) % 256
+    dev = prev.device
+    wi = torch.empty((S, N), dtype=torch.int32, device=dev)
+    wc = torch.empty((S,), dtype=torch.int32, device=dev)
+    ei = torch.empty((S, N), dtype=torch.int32, device=dev)
+    ec = torch.empty((S,), dtype=torch.int32, device=dev)
+    st = torch.empty((S, ctypes.sizeof(_abi.RgbaFrameStats)), dtype=torch.uint8, device=dev) if stats else None
+    check(lib.bjf_viewer_patch_diff_masks_from_rgba(
+        _ptr(p.contiguous()), _ptr(c.contiguous()), S, W, H, patch_size, dims, ctypes.byref(config),
+        ctypes.byref(policy), _ptr(wi), _ptr(wc), _ptr(ei), _ptr(ec), _ptr(st) if st is not None else None,
+        ctypes.c_void_p(ws.data_ptr() + off), int(nbytes), _stream(stream)))
+    if not stats:
+        return wi, wc, ei, ec
+    raw = st.cpu().numpy().tobytes()
+    size = ctypes.sizeof(_abi.RgbaFrameStats)
+    return (wi, wc, ei, ec), [_abi.RgbaFrameStats.from_buffer_copy(raw[i * size:(i + 1) * size]) for i in range(S)]
+
+
 # ---------------------------------------------------------------------------
 # Fused step over S independent streams
 # ---------------------------------------------------------------------------

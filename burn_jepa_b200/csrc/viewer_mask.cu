@@ -38,6 +38,11 @@ struct ViewerParams {
   int bucket_multiple;  // > 0: widths are its multiples below n, then n (no densities)
   int n_widths;         // > 0: the ascending widths below; both 0: encode mask = write mask
   int widths[kMaxBucketWidths + 1];
+  // the RGBA mask node's dense shortcuts (crates/bevy_jepa/src/mask.rs:151-168)
+  int force_dense;             // patch_diff_can_use_dense_fast_path (src/viewer.rs:1031-1036)
+  const float* sample_scores;  // non-null: patch_diff_sampled_dense_fast_path_from_rgba (:1160-1195)
+  float sample_threshold;
+  int sample_stride, sample_rows, sample_cols, sample_required;
 };
 // Exclusive scan of one int per thread in thread order; *total gets the block sum.
 __device__ __forceinline__ int viewer_scan(int v, int* sums, int* total) {
@@ -103,8 +108,22 @@ __global__ void __launch_bounds__(kViewerThreads)
   int32_t* wout = write_idx + s * n;
   int32_t* eout = enc_idx + s * n;
 
+  // 0. dense shortcuts of the RGBA mask node: every sampled patch score of the frame is the
+  // full scorer's, so the sampled decision reads the stream's scores
+  bool dense = p.force_dense != 0;
+  if (!dense && p.sample_scores) {
+    const int sampled = p.sample_rows * p.sample_cols;
+    int local = 0;
+    for (int i = threadIdx.x; i < sampled; i += blockDim.x) {
+      const int row = (i / p.sample_cols) * p.sample_stride, col = (i % p.sample_cols) * p.sample_stride;
+      local += p.sample_scores[s * n + row * p.gw + col] >= p.sample_threshold;
+    }
+    int active;
+    viewer_scan(local, sums, &active);
+    dense = sampled > 0 && active >= max(p.sample_required, 1);
+  }
   // 1. dense fallback (a dense-ordered mask stays dense through dilation and bucketing)
-  if (m == n || (p.fallback_tokens < n && m >= max(p.fallback_tokens, 1))) {
+  if (dense || m == n || (p.fallback_tokens < n && m >= max(p.fallback_tokens, 1))) {
     __syncthreads();  // all direct reads (none here) before the in-place write
     write_all(n, wout);
     write_all(n, eout);
@@ -217,6 +236,8 @@ bjf_status viewer_params(const int64_t* grid, const bjf_viewer_mask_policy* poli
   p.dilation = (int)std::min<int64_t>(policy->dilation, 1 << 20);
   p.bucket_multiple = 0;
   p.n_widths = 0;
+  p.force_dense = 0;
+  p.sample_scores = nullptr;
   // bucket_sparse_mask_with_config (src/viewer.rs:927-944) pads only grids of 256 tokens or more
   if (!policy->bucketed_encode || n < 256) return BJF_OK;
   if (policy->bucket_density_count == 0) {
@@ -241,14 +262,9 @@ bjf_status viewer_params(const int64_t* grid, const bjf_viewer_mask_policy* poli
   return BJF_OK;
 }
 
-}  // namespace
-
 bjf_status launch_viewer_masks(const int32_t* direct_idx, const int32_t* direct_cnt, int64_t streams,
-                               const int64_t* grid, const bjf_viewer_mask_policy* policy, int32_t* write_idx,
-                               int32_t* write_cnt, int32_t* enc_idx, int32_t* enc_cnt, cudaStream_t st) {
-  ViewerParams p{};
-  bjf_status rc = viewer_params(grid, policy, p);
-  if (rc) return rc;
+                               const ViewerParams& p, int32_t* write_idx, int32_t* write_cnt, int32_t* enc_idx,
+                               int32_t* enc_cnt, cudaStream_t st) {
   const size_t smem = (size_t)p.n;
   cudaError_t e = cudaSuccess;
   if (smem > 48 * 1024)
@@ -259,6 +275,7 @@ bjf_status launch_viewer_masks(const int32_t* direct_idx, const int32_t* direct_
   return check_launch("viewer mask launch");
 }
 
+}  // namespace
 }  // namespace bjf
 
 using namespace bjf;
@@ -271,8 +288,11 @@ extern "C" bjf_status bjf_viewer_patch_diff_masks(const int32_t* direct_indices,
   if (streams <= 0 || streams > (int64_t(1) << 31) - 1) return fail(BJF_ERR_INVALID_ARGUMENT, "stream count must be positive");
   if (!direct_indices || !direct_counts || !write_indices || !write_counts || !encode_indices || !encode_counts)
     return fail(BJF_ERR_INVALID_ARGUMENT, "viewer mask buffers must not be null");
-  return launch_viewer_masks(direct_indices, direct_counts, streams, grid, policy, write_indices, write_counts,
-                             encode_indices, encode_counts, as_cuda(stream));
+  ViewerParams p{};
+  const bjf_status rc = viewer_params(grid, policy, p);
+  if (rc) return rc;
+  return launch_viewer_masks(direct_indices, direct_counts, streams, p, write_indices, write_counts, encode_indices,
+                             encode_counts, as_cuda(stream));
 }
 
 extern "C" bjf_status bjf_viewer_patch_diff_masks_from_scores(const float* scores, int64_t streams,
@@ -304,6 +324,74 @@ extern "C" bjf_status bjf_viewer_patch_diff_masks_from_scores(const float* score
   cudaStream_t st = as_cuda(stream);
   rc = launch_select(scores, streams, sp, write_indices, write_counts, st);
   if (rc) return rc;
-  return launch_viewer_masks(write_indices, write_counts, streams, grid, &dilated, write_indices, write_counts,
-                             encode_indices, encode_counts, st);
+  return launch_viewer_masks(write_indices, write_counts, streams, vp, write_indices, write_counts, encode_indices,
+                             encode_counts, st);
+}
+
+namespace {
+size_t rgba_masks_scores_offset(int64_t streams) {
+  return (bjf_rgba_patch_diff_workspace_bytes(streams) + 255) & ~size_t(255);
+}
+}  // namespace
+
+extern "C" size_t bjf_viewer_rgba_masks_workspace_bytes(int64_t streams, const int64_t grid[3]) {
+  if (!grid || grid[0] != 1 || grid[1] <= 0 || grid[2] <= 0 || grid[1] * grid[2] > kMaxViewerTokens) return 0;
+  if (bjf_rgba_patch_diff_workspace_bytes(streams) == 0) return 0;
+  return rgba_masks_scores_offset(streams) + sizeof(float) * (size_t)streams * (size_t)(grid[1] * grid[2]);
+}
+
+extern "C" bjf_status bjf_viewer_patch_diff_masks_from_rgba(
+    const uint8_t* prev, const uint8_t* current, int64_t streams, int64_t width, int64_t height, int64_t patch_size,
+    const int64_t grid[3], const bjf_patch_diff_config* config, const bjf_viewer_mask_policy* policy,
+    int32_t* write_indices, int32_t* write_counts, int32_t* encode_indices, int32_t* encode_counts,
+    bjf_rgba_frame_stats* stats_out, void* workspace, size_t workspace_bytes, bjf_stream_t stream) {
+  if (!config) return fail(BJF_ERR_INVALID_ARGUMENT, "patch-diff config must not be null");
+  if (!policy) return fail(BJF_ERR_INVALID_ARGUMENT, "viewer mask policy must not be null");
+  if (!grid) return fail(BJF_ERR_INVALID_ARGUMENT, "token grid must not be null");
+  // patch_diff_mask_from_rgba (crates/bevy_jepa/src/mask.rs:126-149)
+  if (grid[0] != 1) return fail(BJF_ERR_INVALID_ARGUMENT, "RGBA patch-diff mask expects a single-frame token grid");
+  if (patch_size <= 0 || height != grid[1] * patch_size || width != grid[2] * patch_size)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "RGBA patch-diff frame size must match the V-JEPA patch grid");
+  if (!write_indices || !write_counts || !encode_indices || !encode_counts)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "viewer mask buffers must not be null");
+  const size_t need = bjf_viewer_rgba_masks_workspace_bytes(streams, grid);
+  if (need == 0) return fail(BJF_ERR_INVALID_ARGUMENT, "RGBA viewer masks support 1..65535 streams and grids up to 32768 tokens");
+  if (!workspace || workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
+    return fail(BJF_ERR_INVALID_ARGUMENT,
+                "RGBA viewer mask workspace must be 256-byte aligned and hold " + std::to_string(need) + " bytes");
+  bjf_patch_diff_config direct = *config;
+  direct.dilation = 0;
+  SelectParams sp;
+  bjf_status rc = resolve_select(&direct, grid, sp);
+  if (rc) return rc;
+  bjf_viewer_mask_policy dilated = *policy;
+  dilated.dilation = config->dilation;
+  ViewerParams vp{};
+  rc = viewer_params(grid, &dilated, vp);
+  if (rc) return rc;
+  const int64_t n = grid[1] * grid[2];
+  // patch_diff_sparsity_config's dense shortcuts (crates/bevy_jepa/src/mask.rs:151-168)
+  const bool full_context = config->allow_full_context != 0 && config->context_tokens >= n;
+  vp.force_dense = config->threshold <= 0.0f && full_context;
+  float fb = policy->dense_fallback_density;
+  fb = fb < 0.0f ? 0.0f : (fb > 1.0f ? 1.0f : fb);
+  float* scores = reinterpret_cast<float*>(static_cast<char*>(workspace) + rgba_masks_scores_offset(streams));
+  if (!(fb >= 1.0f) && config->threshold > 0.0f && full_context) {  // a NaN density takes the path
+    // stride = ceil(sqrt(len / 64)) in f32, the sampled grid its multiples (src/viewer.rs:1178-1193)
+    const int stride = std::max(1, (int)std::ceil(std::sqrt((float)n / 64.0f)));
+    vp.sample_scores = scores;
+    vp.sample_threshold = config->threshold;
+    vp.sample_stride = stride;
+    vp.sample_rows = (int)((grid[1] + stride - 1) / stride);
+    vp.sample_cols = (int)((grid[2] + stride - 1) / stride);
+    vp.sample_required = std::isnan(fb) ? 0 : (int)std::ceil((float)(vp.sample_rows * vp.sample_cols) * fb);
+  }
+  cudaStream_t st = as_cuda(stream);
+  rc = bjf_rgba_patch_diff_scores(prev, current, streams, width, height, patch_size, grid, scores, stats_out,
+                                  workspace, workspace_bytes, stream);
+  if (rc) return rc;
+  rc = launch_select(scores, streams, sp, write_indices, write_counts, st);
+  if (rc) return rc;
+  return launch_viewer_masks(write_indices, write_counts, streams, vp, write_indices, write_counts, encode_indices,
+                             encode_counts, st);
 }

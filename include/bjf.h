@@ -301,6 +301,23 @@ BJF_API bjf_status bjf_viewer_patch_diff_masks_from_scores(const float* scores, 
                                                            int32_t* encode_indices, int32_t* encode_counts,
                                                            bjf_stream_t stream);
 
+/* Bytes of device workspace bjf_viewer_patch_diff_masks_from_rgba needs (0 for a stream count
+ * outside 1..65535 or a grid that is not single-frame with at most 32768 tokens). */
+BJF_API size_t bjf_viewer_rgba_masks_workspace_bytes(int64_t streams, const int64_t grid[3]);
+
+/* Replaces the RGBA branch of the Bevy mask node, patch_diff_mask_from_rgba
+ * (crates/bevy_jepa/src/mask.rs:126-175) without its refresh state, for S camera frame pairs:
+ * the dense fast path (patch_diff_can_use_dense_fast_path, src/viewer.rs:1031-1036), the
+ * sampled dense fast path (patch_diff_sampled_dense_fast_path_from_rgba, :1160-1195), else the
+ * RGBA scores and patch_diff_masks_from_scores.  A dense shortcut gives every token in both
+ * masks.  prev / current: [S, height, width, 4] u8; height = grid[1] * P, width = grid[2] * P;
+ * outputs as bjf_viewer_patch_diff_masks_from_scores; stats_out as bjf_rgba_patch_diff_scores. */
+BJF_API bjf_status bjf_viewer_patch_diff_masks_from_rgba(
+    const uint8_t* prev, const uint8_t* current, int64_t streams, int64_t width, int64_t height, int64_t patch_size,
+    const int64_t grid[3], const bjf_patch_diff_config* config, const bjf_viewer_mask_policy* policy,
+    int32_t* write_indices, int32_t* write_counts, int32_t* encode_indices, int32_t* encode_counts,
+    bjf_rgba_frame_stats* stats_out, void* workspace, size_t workspace_bytes, bjf_stream_t stream);
+
 /* ------------------------------------------------------------------------
  * Fused step: mask -> plan -> patchify -> cache write, for S independent streams
  * ---------------------------------------------------------------------- */

@@ -681,6 +681,31 @@ inline DeviceSparseMasks patch_diff_masks_from_scores(const Tensor& scores, Toke
   return m;
 }
 
+// patch_diff_mask_from_rgba without refresh state (crates/bevy_jepa/src/mask.rs:126-175) for
+// `streams` device RGBA frame pairs [streams, height, width, 4]: the dense fast paths, else the
+// RGBA scores and patch_diff_masks_from_scores, all on the device.
+inline DeviceSparseMasks patch_diff_masks_from_rgba(const uint8_t* prev, const uint8_t* current, size_t width,
+                                                    size_t height, size_t patch_size, TokenGridShape grid,
+                                                    const SparseJepaPatchDiffSparsityConfig& sparsity,
+                                                    const FeatureFrameViewerMaskConfig& config, size_t streams = 1,
+                                                    cudaStream_t st = nullptr) {
+  const int64_t n = (int64_t)grid.len(), S = (int64_t)streams;
+  const auto g = grid.dims();
+  const size_t ws_bytes = bjf_viewer_rgba_masks_workspace_bytes(S, g.data());
+  ensure(ws_bytes > 0, "RGBA viewer masks support 1..65535 streams and grids up to 32768 tokens");
+  Tensor ws({(int64_t)((ws_bytes + 3) / 4)}, BJF_DTYPE_F32);
+  DeviceSparseMasks m{Tensor({S, n}, BJF_DTYPE_I32), Tensor({S}, BJF_DTYPE_I32), Tensor({S, n}, BJF_DTYPE_I32),
+                      Tensor({S}, BJF_DTYPE_I32), (size_t)n};
+  const bjf_patch_diff_config c = sparsity.to_c();
+  const bjf_viewer_mask_policy p = config.to_c();
+  check(bjf_viewer_patch_diff_masks_from_rgba(
+      prev, current, S, (int64_t)width, (int64_t)height, (int64_t)patch_size, g.data(), &c, &p,
+      static_cast<int32_t*>(m.write_indices.data()), static_cast<int32_t*>(m.write_counts.data()),
+      static_cast<int32_t*>(m.encode_indices.data()), static_cast<int32_t*>(m.encode_counts.data()), nullptr,
+      ws.data(), ws.nbytes(), to_bjf(st)));
+  return m;
+}
+
 // ---------------------------------------------------------------------------------------
 // plans (src/sparse_patchify.rs:236-330): coords rows (b, t, r, c), batch-major
 // ---------------------------------------------------------------------------------------

@@ -529,6 +529,48 @@ def viewer_patch_diff_masks_from_scores(scores, grid: "TokenGridShape", config: 
                                    bucket_densities)
 
 
+def patch_diff_can_use_dense_fast_path(config: "PatchDiffConfig", dense_len: int) -> bool:
+    """patch_diff_can_use_dense_fast_path (src/viewer.rs:1031-1036)."""
+    return config.threshold <= 0.0 and bool(config.allow_full_context) and config.context_tokens >= dense_len
+
+
+def patch_diff_sampled_dense_fast_path_from_rgba(prev, current, width: int, patch_size: int, grid: "TokenGridShape",
+                                                 config: "PatchDiffConfig", fallback_density: float) -> bool:
+    """patch_diff_sampled_dense_fast_path_from_rgba (src/viewer.rs:1160-1195): the lighting
+    statistics of the whole frames, then rgba_patch_diff_score on every stride-th patch row and
+    column (each the same per-patch score as patch_diff_scores_from_rgba's)."""
+    fb = np.float32(fallback_density)
+    if not np.isnan(fb):
+        fb = np.float32(min(max(fb, np.float32(0.0)), np.float32(1.0)))
+    if fb >= 1.0 or config.threshold <= 0.0 or not config.allow_full_context or config.context_tokens < len(grid):
+        return False
+    scores, _ = patch_diff_scores_from_rgba(prev, current, width, patch_size, grid)
+    stride = max(int(np.ceil(np.sqrt(np.float32(len(grid)) / np.float32(64.0)))), 1)
+    sampled = active = 0
+    for row in range(0, grid.height, stride):
+        for col in range(0, grid.width, stride):
+            sampled += 1
+            active += bool(scores[row * grid.width + col] >= np.float32(config.threshold))
+    required = 0 if np.isnan(fb) else int(np.ceil(np.float32(sampled) * fb))
+    return sampled > 0 and active >= max(required, 1)
+
+
+def viewer_patch_diff_masks_from_rgba(prev, current, width: int, patch_size: int, grid: "TokenGridShape",
+                                      config: "PatchDiffConfig", dense_fallback_density: float,
+                                      bucketed: bool = True, bucket_tokens: int = 256,
+                                      bucket_densities=(0.10, 0.25, 0.50)):
+    """patch_diff_mask_from_rgba without refresh state (crates/bevy_jepa/src/mask.rs:126-175):
+    (write mask, encode mask)."""
+    n = len(grid)
+    if patch_diff_can_use_dense_fast_path(config, n) or patch_diff_sampled_dense_fast_path_from_rgba(
+            prev, current, width, patch_size, grid, config, dense_fallback_density):
+        all_ = np.arange(n, dtype=np.int64)
+        return all_, all_.copy()
+    scores, _ = patch_diff_scores_from_rgba(prev, current, width, patch_size, grid)
+    return viewer_patch_diff_masks_from_scores(scores, grid, config, dense_fallback_density, bucketed, bucket_tokens,
+                                               bucket_densities)
+
+
 def front_end_streams(video, config: PatchifyConfig, mask_config: PatchDiffConfig, weight, bias,
                       caches, observed, age_frames, age_observed: bool) -> np.ndarray:
     """One front-end step over S independent streams (f32), in place on the caches."""

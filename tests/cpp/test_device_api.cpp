@@ -426,6 +426,40 @@ TEST(viewer_masks_from_scores_match_host_policy) {
     }
 }
 
+// src/viewer.rs:1486-1527 through the device RGBA mask node: 16 of 64 patches change, below
+// the 0.60 sampled fallback, so the masks come from the scores (direct hits dilated by one
+// tile); with 48 of 64 changed the sampled fast path gives every token.
+TEST(rgba_mask_node_sampled_dense_fast_path) {
+  const TokenGridShape grid(1, 8, 8);
+  const size_t P = 16, W = 128, H = 128;
+  const auto frames = [&](size_t rows, size_t cols) {
+    std::vector<int32_t> prev(W * H, (int32_t)0xff000000), cur(W * H, (int32_t)0xff000000);
+    for (size_t y = 0; y < rows * P; ++y)
+      for (size_t x = 0; x < cols * P; ++x) cur[y * W + x] = (int32_t)0xffffffff;
+    return std::make_pair(Tensor::from_host(prev, {(int64_t)(W * H)}, BJF_DTYPE_I32),
+                          Tensor::from_host(cur, {(int64_t)(W * H)}, BJF_DTYPE_I32));
+  };
+  const auto cfg = SparseJepaPatchDiffSparsityConfig::adaptive_threshold(0.10f, 1, grid.len(), grid.len()).with_dilation(1);
+  FeatureFrameViewerMaskConfig viewer;
+  viewer.patch_diff_dense_fallback_density = 0.60f;
+  {
+    const auto [prev, cur] = frames(4, 4);
+    const auto m = patch_diff_masks_from_rgba(static_cast<const uint8_t*>(prev.data()),
+                                              static_cast<const uint8_t*>(cur.data()), W, H, P, grid, cfg, viewer)
+                       .stream(0);
+    CHECK_EQ(m.write_mask.len(), (size_t)25);  // the 4x4 block dilated by one tile
+    CHECK(!m.write_mask.is_dense_ordered());
+  }
+  {
+    const auto [prev, cur] = frames(6, 8);
+    const auto m = patch_diff_masks_from_rgba(static_cast<const uint8_t*>(prev.data()),
+                                              static_cast<const uint8_t*>(cur.data()), W, H, P, grid, cfg, viewer)
+                       .stream(0);
+    CHECK(m.write_mask.is_dense_ordered());
+    CHECK(m.encode_mask.is_dense_ordered());
+  }
+}
+
 // The fused step over S streams against the oracle's per-stream composition.  Unchanged
 // tubelets score exactly 0, so a small positive threshold selects exactly the changed ones
 // whatever the summation order.

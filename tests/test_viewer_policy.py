@@ -256,3 +256,91 @@ def test_device_viewer_masks_errors(cuda_device):
     neg = bj.ViewerMaskPolicy.new(dilation=-1)
     with pytest.raises(bj.BjfError, match="non-negative"):
         bj.viewer_patch_diff_masks(idx, cnt, bj.TokenGridShape(1, 8, 8), neg)
+
+
+# ---------------------------------------------------------------------------
+# The RGBA mask node: dense fast paths, then scores -> masks
+# ---------------------------------------------------------------------------
+
+def _white_block_frames(grid_h, grid_w, P, rows, cols):
+    # src/viewer.rs:1579-1593 (fill_rgba_patch): black opaque frame, then white patches
+    prev = np.zeros((grid_h * P, grid_w * P, 4), np.uint8)
+    prev[..., 3] = 255
+    cur = prev.copy()
+    for r in rows:
+        for c in cols:
+            cur[r * P:(r + 1) * P, c * P:(c + 1) * P, :] = 255
+    return prev, cur
+
+
+def test_oracle_sampled_dense_fast_path_uses_direct_density():
+    # src/viewer.rs:1486-1527: 16 of 64 patches change -> below the 0.60 fallback, both dilations
+    grid = oracle.TokenGridShape(1, 8, 8)
+    prev, cur = _white_block_frames(8, 8, 16, range(4), range(4))
+    cfg = oracle.PatchDiffConfig.adaptive_threshold(0.10, 1, 64, 64).with_dilation(1)
+    assert not oracle.patch_diff_sampled_dense_fast_path_from_rgba(prev, cur, 128, 16, grid, cfg, 0.60)
+    assert not oracle.patch_diff_sampled_dense_fast_path_from_rgba(prev, cur, 128, 16, grid, cfg.with_dilation(0), 0.60)
+    # 48 of 64 change -> dense; a fallback density of 1.0 never takes the path
+    prev, cur = _white_block_frames(8, 8, 16, range(6), range(8))
+    assert oracle.patch_diff_sampled_dense_fast_path_from_rgba(prev, cur, 128, 16, grid, cfg, 0.60)
+    assert not oracle.patch_diff_sampled_dense_fast_path_from_rgba(prev, cur, 128, 16, grid, cfg, 1.0)
+    # a capped context never takes it
+    capped = oracle.PatchDiffConfig.adaptive_threshold(0.10, 1, 32, 64)
+    assert not oracle.patch_diff_sampled_dense_fast_path_from_rgba(prev, cur, 128, 16, grid, capped, 0.60)
+    w, e = oracle.viewer_patch_diff_masks_from_rgba(prev, cur, 128, 16, grid, cfg, 0.60)
+    assert w.tolist() == list(range(64)) and e.tolist() == list(range(64))
+
+
+_RGBA_NODE_CASES = {
+    # name: (changed fractions per stream, threshold, dilation, context tokens, fallback density)
+    "sparse": ((0.02, 0.05, 0.1), 0.1, 1, 256, 0.75),
+    "fast_path": ((0.7, 0.95, 0.3), 0.1, 1, 256, 0.6),
+    "capped": ((0.7, 0.2, 0.05), 0.1, 1, 64, 0.6),
+    "threshold_zero": ((0.05, 0.0), 0.0, 1, 256, 0.75),
+    "no_dilation_exact": ((0.1, 0.4), 0.1, 0, 256, 0.75),
+}
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("name", sorted(_RGBA_NODE_CASES))
+def test_device_rgba_mask_node_matches_oracle(cuda_device, name):
+    import torch
+
+    import burn_jepa_b200 as bj
+
+    fracs, thr, dil, ctx, fb = _RGBA_NODE_CASES[name]
+    S, P, gh, gw = len(fracs), 16, 16, 16
+    H, W = gh * P, gw * P
+    frames = [_frames(300 + 7 * i, 1, H, W, 0, f) for i, f in enumerate(fracs)]
+    prev = np.concatenate([f[0] for f in frames])
+    cur = np.concatenate([f[1] for f in frames])
+    bucketed = name != "no_dilation_exact"
+    cfg = bj.PatchDiffConfig.adaptive_threshold(thr, 1, ctx, 1).with_dilation(dil)
+    policy = bj.ViewerMaskPolicy.new(fb, 0, bucketed)
+    (wi, wc, ei, ec), stats = bj.viewer_patch_diff_masks_from_rgba(
+        torch.from_numpy(prev).to(cuda_device), torch.from_numpy(cur).to(cuda_device), P, (1, gh, gw), cfg, policy,
+        stats=True)
+    wi, wc, ei, ec = (t.cpu().numpy() for t in (wi, wc, ei, ec))
+    ocfg = oracle.PatchDiffConfig.adaptive_threshold(thr, 1, ctx, 1).with_dilation(dil)
+    og = oracle.TokenGridShape(1, gh, gw)
+    for s in range(S):
+        w, e = oracle.viewer_patch_diff_masks_from_rgba(prev[s], cur[s], W, P, og, ocfg, fb, bucketed)
+        assert wi[s, :wc[s]].tolist() == w.tolist(), (name, s)
+        assert ei[s, :ec[s]].tolist() == e.tolist(), (name, s)
+        _, st = oracle.patch_diff_scores_from_rgba(prev[s], cur[s], W, P, og)
+        assert stats[s].compensate_global_lighting == st.compensate_global_lighting
+
+
+@pytest.mark.gpu
+def test_device_rgba_mask_node_errors(cuda_device):
+    import torch
+
+    import burn_jepa_b200 as bj
+
+    prev = torch.zeros((64, 64, 4), dtype=torch.uint8, device=cuda_device)
+    cfg = bj.PatchDiffConfig.adaptive_threshold(0.1, 1, 16, 1)
+    pol = bj.ViewerMaskPolicy.new()
+    with pytest.raises(bj.BjfError, match="single-frame token grid"):
+        bj.viewer_patch_diff_masks_from_rgba(prev, prev, 16, (2, 4, 4), cfg, pol)
+    with pytest.raises(bj.BjfError, match="frame size must match"):
+        bj.viewer_patch_diff_masks_from_rgba(prev, prev, 16, (1, 4, 3), cfg, pol)
