@@ -650,19 +650,11 @@ __global__ void __maxnreg__(80)
   int* soff = reinterpret_cast<int*>(smem + PairSmemLayout::soff_off);
   int64_t* rowbase = reinterpret_cast<int64_t*>(smem + PairSmemLayout::rowbase_off);
 
-  pdl_wait();     // the rows and their count come from the kernels before (selection)
-  pdl_trigger();  // the next frame's patch-diff pass may start alongside this GEMM
-  int M = rows_cap;
-  if (rows_dev) M = min(M, max(0, __ldg(rows_dev)));
-  M = min(M, load_row_offsets(rs, soff));
-  const int n_tiles = (g.D + bn - 1) / bn;
-  const int num_tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * n_tiles;  // 256-row pair tiles
-  const uint32_t rank = cluster_ctarank();                           // 0: issues the MMAs
+  const uint32_t rank = cluster_ctarank();  // 0: issues the MMAs
   const int cluster = (int)(blockIdx.x >> 1);
   const int nclusters = (int)(gridDim.x >> 1);
-  if (cluster >= num_tiles) return;  // the same for both CTAs of the pair, before any allocation
+  const int n_tiles = (g.D + bn - 1) / bn;
   const int half = bn >> 1;
-  const int my_tiles = (num_tiles - cluster + nclusters - 1) / nclusters;
   // On the CTA's last tile the producer warps, idle by then, drain accumulator columns
   // [split, bn) while the epilogue warps drain [0, split): a chunk-aligned half.
   const int epi_chunk_cols = kEpiChunkBytes / ep.out_elem_bytes;
@@ -705,6 +697,26 @@ __global__ void __maxnreg__(80)
   cluster_sync();  // barriers of both CTAs initialised and TMEM allocated before any remote arrive
   tc_fence_after();
   const uint32_t tmem_base = *tmem_slot;
+
+  // Everything above depends only on the geometry, so it overlaps the kernel before (the
+  // selection); the rows and their count come from it.  The trigger comes after the wait: the
+  // next frame's patch-diff pass rewrites the scores and the selection's completion counter.
+  pdl_wait();
+  pdl_trigger();  // the next frame's patch-diff pass may start alongside this GEMM
+  int M = rows_cap;
+  if (rows_dev) M = min(M, max(0, __ldg(rows_dev)));
+  M = min(M, load_row_offsets(rs, soff));
+  const int num_tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * n_tiles;  // 256-row pair tiles
+  if (cluster >= num_tiles) {  // the same for both CTAs of the pair
+    tc_fence_before();
+    cluster_sync();
+    if (warp == kMmaWarp) {
+      tc_fence_after();
+      tmem_dealloc_pair(tmem_base, tmem_cols);
+    }
+    return;
+  }
+  const int my_tiles = (num_tiles - cluster + nclusters - 1) / nclusters;
 
   const uint32_t a_smem = smem_u32(smem + PairSmemLayout::a_off);
   const uint32_t b_smem = smem_u32(smem + PairSmemLayout::b_off);
