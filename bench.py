@@ -39,7 +39,7 @@ METRIC = "active tubelets/sec (1/2/4/8 B200) + % tensor-pipe/HBM roofline; ViT-L
 UNIT = "active tubelets/s"
 
 STREAMS_PER_GPU = 32
-KERNELS_PER_STEP = 3  # patch-diff scores, selection (+ row plan), gather-GEMM (+ cache write)
+KERNELS_PER_STEP = 3  # patch-diff scores, selection, gather-GEMM (+ row plan, + cache write)
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one scores launch per stream of
 # this workload, from one ncu --set full capture of the scores kernel at 16 streams
 # (212 447 232 bytes / 16), scaled by the stream count for the roofline's `traffic`.

@@ -374,7 +374,7 @@ class FrontEnd:
     """One frame step of the whole front end for S independent streams (``bjf_front_end_step``).
 
     Each stream is a video [C, T, H, W] (batch 1) with its own persistent token cache
-    [N, D], observed [N] and age [N].  ``step`` runs patch-diff scores -> selection (+ row plan) ->
+    [N, D], observed [N] and age [N].  ``step`` runs patch-diff scores -> selection ->
     tcgen05 gather-GEMM -> in-place cache write for every stream and returns the device
     tensor of per-stream active tubelet counts.  Owns its device workspace."""
 

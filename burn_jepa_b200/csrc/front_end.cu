@@ -3,11 +3,10 @@
 //
 //   1. patch-diff scores          [S, N] f32                  (memory-bound pass over the clips)
 //   2. selection + cache aging    indices [S, N], counts [S]  (one CTA per stream; the
-//      + row plan                 AssignLatest aging age += observed runs in the same launch,
-//                                 and the last CTA writes the first row of each stream's
-//                                 selection in the concatenated row list: the plan)
-//   3. gather-GEMM                tcgen05 tiles over the concatenated active rows, each row's
-//                                 (stream, token) read from the plan and the indices; the
+//                                 AssignLatest aging age += observed runs in the same launch)
+//   3. gather-GEMM                tcgen05 tiles over the concatenated active rows: each CTA
+//                                 scans the counts into the first row of every stream (the
+//                                 plan) and reads each row's token from the indices; the
 //                                 epilogue adds the bias and writes each row straight into
 //                                 its stream's token cache slot, setting observed = 1, age = 0
 //
@@ -35,7 +34,7 @@ namespace bjf {
 namespace {
 
 struct Workspace {
-  size_t scores, indices, counts, offsets, done, bytes;
+  size_t scores, indices, counts, bytes;
 };
 
 Workspace layout(int64_t S, int64_t N) {
@@ -48,10 +47,6 @@ Workspace layout(int64_t S, int64_t N) {
   off = up(off + sizeof(int32_t) * S * N);
   w.counts = off;
   off = up(off + sizeof(int32_t) * S);
-  w.offsets = off;
-  off = up(off + sizeof(int32_t) * (S + 1));
-  w.done = off;
-  off = up(off + sizeof(uint32_t));
   w.bytes = off;
   return w;
 }
@@ -111,20 +106,15 @@ extern "C" bjf_status bjf_front_end_step(const bjf_front_end_desc* d, const void
   float* scores = reinterpret_cast<float*>(ws + w.scores);
   int32_t* indices = reinterpret_cast<int32_t*>(ws + w.indices);
   int32_t* counts = counts_out ? counts_out : reinterpret_cast<int32_t*>(ws + w.counts);
-  int32_t* offsets = reinterpret_cast<int32_t*>(ws + w.offsets);
-  unsigned int* done = reinterpret_cast<unsigned int*>(ws + w.done);
   cudaStream_t st = as_cuda(stream);
 
   const int64_t vd[5] = {1, d->channels, d->frames, d->height, d->width};
-  // the scores pass also clears the selection's completion counter
-  rc = launch_scores(video, d->video_dtype, vd, S, d->tubelet_size, d->patch_size, scores, st, true, done);
+  rc = launch_scores(video, d->video_dtype, vd, S, d->tubelet_size, d->patch_size, scores, st, true);
   if (rc) return rc;
   if (age_observed) {
     sel.age = age_frames;
     sel.observed = observed;
   }
-  sel.offsets = offsets;
-  sel.done = done;
   rc = launch_select(scores, S, sel, indices, counts, st, true);
   if (rc) return rc;
 
@@ -152,7 +142,8 @@ extern "C" bjf_status bjf_front_end_step(const bjf_front_end_desc* d, const void
   ep.observed = observed;
   ep.age = age_frames;
   ep.bias = bias;
-  const RowSource rows{nullptr, indices, offsets, (int)N, (int)S};
+  // the GEMM scans the per-stream counts into its row offsets
+  const RowSource rows{nullptr, indices, counts, (int)N, (int)S};
   return launch_gather_gemm(*dev, video, d->video_dtype, weight, d->weight_dtype, g, rows, nullptr, S * N, ep, st,
                             true);
 }

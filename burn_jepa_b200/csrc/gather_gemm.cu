@@ -80,11 +80,31 @@ __device__ __forceinline__ int64_t row_base_offset(const GatherGeometry& g, int4
 
 // Loads the stream offsets of an index row source into shared memory (all threads of the
 // block) and returns the row count they describe; explicit coords rows return INT32_MAX.
+// Stream row offsets soff[0..streams] = exclusive prefix of the per-stream counts (warp 0
+// scans 32 streams at a time); returns the row count.  Block-wide.
 __device__ __forceinline__ int load_row_offsets(const RowSource& rs, int* soff) {
   if (rs.coords) return 0x7fffffff;
-  for (int i = threadIdx.x; i <= rs.streams; i += blockDim.x) soff[i] = __ldg(rs.offsets + i);
+  const int S = rs.streams;
+  for (int i = threadIdx.x; i < S; i += blockDim.x) soff[i + 1] = min(max(__ldg(rs.counts + i), 0), rs.index_stride);
   __syncthreads();
-  return soff[rs.streams];
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    int carry = 0;
+    for (int base = 0; base < S; base += 32) {
+      const int i = base + lane;
+      int v = i < S ? soff[i + 1] : 0;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, v, o);
+        if (lane >= o) v += y;
+      }
+      if (i < S) soff[i + 1] = carry + v;
+      carry += __shfl_sync(0xffffffffu, v, 31);
+    }
+    if (lane == 0) soff[0] = 0;
+  }
+  __syncthreads();
+  return soff[S];
 }
 
 // Coordinates (b, t, r, col) of row m; a token index outside the grid gives t = r = col = -1
@@ -700,7 +720,7 @@ __global__ void __maxnreg__(80)
 
   // Everything above depends only on the geometry, so it overlaps the kernel before (the
   // selection); the rows and their count come from it.  The trigger comes after the wait: the
-  // next frame's patch-diff pass rewrites the scores and the selection's completion counter.
+  // next frame's patch-diff pass rewrites the scores the selection reads.
   pdl_wait();
   pdl_trigger();  // the next frame's patch-diff pass may start alongside this GEMM
   int M = rows_cap;
@@ -1064,8 +1084,8 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
                               const void* weight, int32_t w_dt, const GatherGeometry& g0,
                               const RowSource& rows, const int32_t* rows_dev, int64_t rows_cap,
                               const EpilogueArgs& ep, cudaStream_t st, bool pdl) {
-  if (!rows.coords && (rows.streams <= 0 || rows.streams > kMaxRowStreams || !rows.indices || !rows.offsets))
-    return fail(BJF_ERR_INVALID_ARGUMENT, "gather-GEMM index rows need 1..4096 streams, indices and offsets");
+  if (!rows.coords && (rows.streams <= 0 || rows.streams > kMaxRowStreams || !rows.indices || !rows.counts))
+    return fail(BJF_ERR_INVALID_ARGUMENT, "gather-GEMM index rows need 1..4096 streams, indices and counts");
   if (rows_cap <= 0 || g0.D <= 0) return BJF_OK;
   GatherGeometry g = g0;
   g.num_kb = g.K / kBK;

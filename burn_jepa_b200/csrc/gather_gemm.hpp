@@ -51,7 +51,8 @@ constexpr int kMaxRowStreams = 4096;
 struct RowSource {
   const int4* coords;      // [rows] or null
   const int32_t* indices;  // [streams, index_stride] when coords is null
-  const int32_t* offsets;  // [streams + 1]; offsets[streams] = row count
+  const int32_t* counts;   // [streams] rows of each stream (clamped to 0..index_stride); the
+                           // kernel scans them into the stream row offsets
   int index_stride;
   int streams;             // <= kMaxRowStreams
 };

@@ -60,9 +60,7 @@ template <typename T>
 __global__ void __launch_bounds__(kScoreThreads, 4)
     patch_diff_scores_vec_kernel(const T* __restrict__ video, float* __restrict__ scores, int batch,
                                  int channels, int frames, int height, int width, int kt, int P,
-                                 int depth, int gh, int gw, int chunks_per_row, long long total_warps,
-                                 unsigned int* __restrict__ zero_word) {
-  if (zero_word && blockIdx.x == 0 && threadIdx.x == 0) *zero_word = 0u;
+                                 int depth, int gh, int gw, int chunks_per_row, long long total_warps) {
   constexpr int VEC = 16 / sizeof(T);
   const int LPT = P / VEC;      // lanes per token column
   const int TPW = 32 / LPT;     // token columns per warp
@@ -130,10 +128,8 @@ template <typename T>
 __global__ void __launch_bounds__(kScoreThreads)
     patch_diff_scores_scalar_kernel(const T* __restrict__ video, float* __restrict__ scores,
                                     int batch, int channels, int frames, int height, int width,
-                                    int kt, int P, int depth, int gh, int gw, long long total,
-                                    unsigned int* __restrict__ zero_word) {
+                                    int kt, int P, int depth, int gh, int gw, long long total) {
   pdl_wait();
-  if (zero_word && blockIdx.x == 0 && threadIdx.x == 0) *zero_word = 0u;
   long long i = (long long)blockIdx.x * kScoreThreads + threadIdx.x;
   if (i >= total) return;
   const long long n_tokens = (long long)depth * gh * gw;
@@ -226,35 +222,6 @@ __device__ __forceinline__ void thread_segment(int n, int& b, int& e) {
   e = min(n, b + per);
 }
 
-// Last-CTA row plan: after every stream's count is written, the last CTA to finish writes
-// the exclusive prefix of the counts (the first output row of each stream) and the total.
-// All threads of the block call it after writing counts[blockIdx.x].
-__device__ __forceinline__ void publish_row_offsets(const SelectParams& p, const int32_t* counts,
-                                                    int* warp_sums) {
-  if (!p.offsets) return;
-  __shared__ int am_last;
-  __threadfence();  // this CTA's count is visible device-wide before it is counted as done
-  __syncthreads();
-  if (threadIdx.x == 0) am_last = atomicAdd(p.done, 1u) == gridDim.x - 1;
-  __syncthreads();
-  if (!am_last) return;
-  __threadfence();
-  const int streams = (int)gridDim.x;
-  int carry = 0;
-  for (int base = 0; base < streams; base += blockDim.x) {
-    const int i = base + (int)threadIdx.x;
-    const int c = i < streams ? __ldcg(counts + i) : 0;
-    int total;
-    const int ex = block_exclusive_scan(c, warp_sums, &total);
-    if (i < streams) p.offsets[i] = carry + ex;
-    carry += total;
-  }
-  if (threadIdx.x == 0) {
-    p.offsets[streams] = carry;
-    *p.done = 0u;  // ready for the next launch
-  }
-}
-
 // Selection without dilation.  Shared memory: keys[n] (uint32).
 __global__ void __launch_bounds__(kSelectThreads)
     patch_diff_select_kernel(const float* __restrict__ scores, SelectParams p,
@@ -297,7 +264,6 @@ __global__ void __launch_bounds__(kSelectThreads)
     for (int i = seg_b; i < seg_e; ++i)
       if (pass_bits >> (i - seg_b) & 1u) out[pos++] = i;
     if (threadIdx.x == 0) counts[s] = n_sel;
-    publish_row_offsets(p, counts, warp_sums);
     return;
   }
 
@@ -359,7 +325,6 @@ __global__ void __launch_bounds__(kSelectThreads)
     }
   }
   if (threadIdx.x == 0) counts[s] = n_sel;
-  publish_row_offsets(p, counts, warp_sums);
 }
 
 __device__ __forceinline__ bool push_dilated(int index, const SelectParams& p, unsigned char* keep,
@@ -470,7 +435,6 @@ __global__ void __launch_bounds__(kSelectThreads)
   for (int i = seg_b; i < seg_e; ++i)
     if (keep[i]) out[pos++] = i;
   if (threadIdx.x == 0) counts[s] = total;
-  publish_row_offsets(p, counts, warp_sums);
 }
 
 bool grid_ok(const int64_t* g) { return g && g[0] > 0 && g[1] > 0 && g[2] > 0; }
@@ -502,8 +466,6 @@ bjf_status resolve_select(const bjf_patch_diff_config* cfg, const int64_t* grid,
   p.n = (int)len;
   p.age = nullptr;
   p.observed = nullptr;
-  p.offsets = nullptr;
-  p.done = nullptr;
   return BJF_OK;
 }
 
@@ -551,8 +513,7 @@ int sm_count() {
 }  // namespace
 
 bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* vd, int64_t streams,
-                         int64_t kt, int64_t P, float* scores, cudaStream_t st, bool pdl,
-                         unsigned int* zero_word) {
+                         int64_t kt, int64_t P, float* scores, cudaStream_t st, bool pdl) {
   const int64_t B = vd[0], C = vd[1], T = vd[2], H = vd[3], W = vd[4];
   const int64_t depth = T / kt, gh = H / P, gw = W / P;
   const int64_t n_tok = depth * gh * gw;
@@ -573,14 +534,14 @@ bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* vd, in
       cudaError_t e = launch_kernel(pdl, patch_diff_scores_vec_kernel<T_>, dim3((unsigned)blocks),
                                     dim3(kScoreThreads), 0, st, static_cast<const T_*>(video), scores, (int)B,
                                     (int)C, (int)T, (int)H, (int)W, (int)kt, (int)P, (int)depth, (int)gh,
-                                    (int)gw, chunks, warps, zero_word);
+                                    (int)gw, chunks, warps);
       rc = e == cudaSuccess ? BJF_OK : cuda_status(e, "patch-diff scores launch");
       return;
     } else {
       long long total = (long long)streams * n_tok;
       patch_diff_scores_scalar_kernel<T_><<<(unsigned)ceil_div(total, kScoreThreads), kScoreThreads, 0, st>>>(
           static_cast<const T_*>(video), scores, (int)B, (int)C, (int)T, (int)H, (int)W, (int)kt,
-          (int)P, (int)depth, (int)gh, (int)gw, total, zero_word);
+          (int)P, (int)depth, (int)gh, (int)gw, total);
     }
     rc = check_launch("patch-diff scores launch");
   });

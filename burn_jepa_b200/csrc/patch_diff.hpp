@@ -19,13 +19,6 @@ struct SelectParams {
   // src/sparse_feature_memory.rs:46-52).  Null when not requested.
   float* age;
   const float* observed;
-  // Optional row plan of the concatenated selections (the fused front end): the last CTA
-  // to finish writes offsets[s] = first row of stream s (exclusive prefix of the counts)
-  // and offsets[streams] = the total row count.  `done` counts the CTAs that finished; it
-  // must be zero when the launch starts and the last CTA sets it back to zero.  Null when
-  // not requested.
-  int32_t* offsets;
-  unsigned int* done;
 };
 
 // Resolves the reference's context budget arithmetic (src/nodes.rs:463-498, 516-520).
@@ -36,11 +29,9 @@ bjf_status launch_select(const float* scores, int64_t streams, const SelectParam
                          int32_t* counts, cudaStream_t st, bool pdl = false);
 
 // Per-tubelet mean |delta| scores for `streams` videos [B, C, T, H, W] -> [streams, N].
-// `zero_word` (device, nullable) is set to zero by the launch before any of its blocks
-// finishes (the fused step clears the selection's `done` counter with it).
 bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* video_dims, int64_t streams,
                          int64_t tubelet_size, int64_t patch_size, float* scores, cudaStream_t st,
-                         bool pdl = false, unsigned int* zero_word = nullptr);
+                         bool pdl = false);
 
 // Device plan (coords rows) from per-stream mask indices; see bjf_sparse_patchify_plan_coords.
 bjf_status launch_plan(const int32_t* indices, int64_t index_stride, const int32_t* counts, int64_t mask_rows,

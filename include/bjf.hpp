@@ -1075,7 +1075,7 @@ class InterframeJepaFeatureMemory {
 
 // ---------------------------------------------------------------------------------------
 // FrontEnd: one frame step over S independent streams, fully on the device
-// (patch-diff scores -> selection and row plan -> gather-GEMM with bias -> in-place
+// (patch-diff scores -> selection -> gather-GEMM with bias -> in-place
 // token-cache write; three kernels chained with programmatic dependent launch).
 // ---------------------------------------------------------------------------------------
 class FrontEnd {
