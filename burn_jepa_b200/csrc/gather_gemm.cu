@@ -533,9 +533,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 // the next chunk be converted while the previous one is still being read.
 constexpr int kPairStages = 4;
 constexpr int kBHalfStageBytes = (kMaxBN / 2) * kBK * 2;  // 16 KB
-constexpr int kEpiChunkBytes = 128;                       // output bytes per row per bulk copy
+constexpr int kEpiChunkBytes = 256;                       // output bytes per row per bulk copy
 constexpr int kEpiRowPitch = kEpiChunkBytes + 16;
-constexpr int kEpiBufs = 2;
+constexpr int kEpiBufs = 1;
 constexpr int kEpiWarpBytes = kEpiBufs * 32 * kEpiRowPitch;
 static_assert(kPairStages <= 32, "one relay lane per stage");
 
@@ -602,7 +602,7 @@ __device__ __forceinline__ void drain_accumulator_bulk(const GatherGeometry& g, 
       }
     }
   }
-  const int cpc = kEpiChunkBytes / ce;  // columns per chunk: 64 (16-bit) or 32 (f32)
+  const int cpc = kEpiChunkBytes / ce;  // columns per chunk: 128 (16-bit) or 64 (f32)
   for (int c0 = c_begin; c0 < bn; c0 += cpc, ++chunk) {
     const int col0 = n0 + c0;
     const int ncol = min(cpc, min(bn - c0, g.D - col0));  // the same for the whole warp
