@@ -89,11 +89,12 @@ def _oracle_front_end(xs, weight, bias, ocfg, grid, omask, ref_cache, ref_obs, r
 
 
 @pytest.mark.parametrize("name,S,T,H,W,D,mask_kind", [
-    ("dilated_cap", 3, 2, 128, 128, 256, "dilated"),      # dilated selection kernel + its row plan
+    ("dilated_cap", 3, 2, 128, 128, 256, "dilated"),      # dilated selection: a launch of its own
     ("topk_fill", 3, 2, 128, 128, 256, "topk"),           # threshold 0, fill to the budget: radix select
     ("many_streams", 70, 2, 32, 48, 128, "adaptive"),     # 70 streams, some static: binary search of offsets
     ("depth_two", 2, 4, 64, 64, 256, "adaptive"),         # two tubelets per clip
     ("one_stream", 1, 2, 256, 256, 512, "adaptive"),
+    ("fill_ties", 4, 2, 128, 128, 256, "fill"),            # fill to half the grid: ties among zero scores
 ])
 def test_front_end_mask_policies_match_oracle(cuda_device, name, S, T, H, W, D, mask_kind):
     import torch
@@ -123,6 +124,9 @@ def test_front_end_mask_policies_match_oracle(cuda_device, name, S, T, H, W, D, 
         if mask_kind == "dilated":
             args = (thr, max(2, n // 6), 1)
             mask, omask = bj.PatchDiffConfig.new(*args).with_dilation(1), oracle.PatchDiffConfig.new(*args).with_dilation(1)
+        elif mask_kind == "fill":
+            args = (thr, n // 2, n, 1)
+            mask, omask = bj.PatchDiffConfig.adaptive_threshold(*args), oracle.PatchDiffConfig.adaptive_threshold(*args)
         elif mask_kind == "topk":
             args = (0.0, max(2, n // 5), 1)
             mask, omask = bj.PatchDiffConfig.new(*args), oracle.PatchDiffConfig.new(*args)
@@ -139,3 +143,45 @@ def test_front_end_mask_policies_match_oracle(cuda_device, name, S, T, H, W, D, 
         got = caches.float().cpu().numpy()
         assert max_rel_err(got, ref_cache) <= 1e-2
         ref_cache = got.copy()
+
+
+def test_front_end_reused_workspace_matches_oracle(cuda_device):
+    """One FrontEnd (one workspace) over five steps: the per-stream completion counters of the
+    fused selection wrap back to zero every step, so every step must match the oracle."""
+    import torch
+
+    S, C, T, H, W, KT, P, D = 5, 3, 2, 96, 128, 2, 16, 128
+    grid_t = (T // KT, H // P, W // P)
+    n = grid_t[0] * grid_t[1] * grid_t[2]
+    grid = oracle.TokenGridShape(*grid_t)
+    weight = workloads.splitmix_normal(41, (D, C, KT, P, P), 0.02)
+    bias = workloads.splitmix_normal(42, (D,), 0.02)
+    wd = torch.from_numpy(weight).to(cuda_device, torch.float16)
+    bd = torch.from_numpy(bias).to(cuda_device)
+    videos = [workloads.rect_perturbation_clips(500 + k, S, C, T, H, W, area_fraction=0.1 + 0.05 * k) for k in range(5)]
+    xs_all = [torch.from_numpy(v).to(torch.float16).float().numpy() for v in videos]
+    all_scores = np.concatenate([oracle.patch_diff_token_scores(x[s:s + 1], KT, P) for x in xs_all for s in range(S)])
+    thr = workloads.choose_threshold(all_scores, 0.15)
+    args = (thr, 3, n, 1)
+    fe = bj.FrontEnd(S, C, T, H, W, KT, P, D, bj.PatchDiffConfig.adaptive_threshold(*args), torch.float16,
+                     torch.float16, cuda_device)
+    omask = oracle.PatchDiffConfig.adaptive_threshold(*args)
+    caches = torch.zeros((S, n, D), device=cuda_device, dtype=torch.float16)
+    observed = torch.zeros((S, n), device=cuda_device)
+    age = torch.zeros((S, n), device=cuda_device)
+    ref_cache = np.zeros((S, n, D), np.float32)
+    ref_obs = np.zeros((S, n), np.float32)
+    ref_age = np.zeros((S, n), np.float32)
+    ocfg = oracle.PatchifyConfig(C, D, T, H, W, KT, P, P)
+    for step in range(5):
+        vd = torch.from_numpy(videos[step]).to(cuda_device, torch.float16)
+        counts = fe.step(vd, wd, bd, caches, observed, age, age_observed=step > 0).cpu().numpy()
+        want = _oracle_front_end(xs_all[step], wd.float().cpu().numpy(), bias, ocfg, grid, omask, ref_cache, ref_obs,
+                                 ref_age, step > 0)
+        assert np.array_equal(counts, want), step
+        assert np.array_equal(observed.cpu().numpy(), ref_obs), step
+        assert np.array_equal(age.cpu().numpy(), ref_age), step
+        got = caches.float().cpu().numpy()
+        assert max_rel_err(got, ref_cache) <= 1e-2, step
+        ref_cache = got.copy()
+    assert not bj.device_error_check()
