@@ -146,8 +146,8 @@ def test_front_end_mask_policies_match_oracle(cuda_device, name, S, T, H, W, D, 
 
 
 def test_front_end_reused_workspace_matches_oracle(cuda_device):
-    """One FrontEnd (one workspace) over five steps: the per-stream completion counters of the
-    fused selection wrap back to zero every step, so every step must match the oracle."""
+    """One FrontEnd (one workspace) over five steps with changing masks: whatever the step keeps
+    in its workspace between steps, every step must match the oracle."""
     import torch
 
     S, C, T, H, W, KT, P, D = 5, 3, 2, 96, 128, 2, 16, 128
