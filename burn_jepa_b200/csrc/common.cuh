@@ -95,11 +95,15 @@ __device__ __forceinline__ void store8<__nv_bfloat16>(__nv_bfloat16* p, const fl
 }
 
 // Streaming 16-byte load that does not allocate in L1 (read-once data).
+// Streaming 16-byte load: no L1 allocation, and evict-first in L2 so a pass over hundreds of
+// MB leaves the lines other kernels reuse (the GEMM's gathered rows and weights) in place.
 __device__ __forceinline__ uint4 ld_nc_v4(const void* p) {
   uint4 r;
-  asm volatile("ld.global.nc.L1::no_allocate.v4.u32 {%0,%1,%2,%3}, [%4];"
+  uint64_t policy;
+  asm("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+  asm volatile("ld.global.nc.L1::no_allocate.L2::cache_hint.v4.u32 {%0,%1,%2,%3}, [%4], %5;"
                : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-               : "l"(p));
+               : "l"(p), "l"(policy));
   return r;
 }
 
