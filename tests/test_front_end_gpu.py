@@ -1,6 +1,6 @@
 """Fused front-end step (bjf_front_end_step) against the oracle's per-stream composition
 (patch_diff_context_mask -> plan -> sparse patchify -> AssignLatest cache write, which the
-device runs as three kernels: scores, selection with the row plan, gather-GEMM) over
+device runs as three kernels: scores, selection, gather-GEMM with the row plan) over
 several steps: masks and cache slots bit-exact, written rows within the f16 tolerance,
 untouched rows unchanged, observed/age exact."""
 import numpy as np
