@@ -6,13 +6,15 @@
 // which exposes no raw allocation to plugins, or a real-time camera loop that forbids
 // allocation after start-up because an allocation can synchronise the device and stall
 // the frame.  For them this variant keeps its scratch (patch-diff scores, mask indices,
-// counts, patchify coordinates and the row total) in a file-scope __device__ array
-// instead of a caller-provided workspace, so a call allocates nothing.
+// counts) in a file-scope __device__ array
+// instead of a caller-provided workspace, so a call allocates nothing.  The launches are those
+// of bjf_front_end_step: scores -> selection -> gather-GEMM reading its rows from the indices
+// and per-stream counts, chained with programmatic dependent launch.
 //
 // Rules a caller must know:
 //  * The array is kNoAllocScratchBytes (4 MiB) per device and lives as long as the
 //    library is loaded, on every GPU that loads it.  Steps whose scratch would not fit
-//    (streams x tokens above about 174k) are rejected with BJF_ERR_UNSUPPORTED.
+//    (streams x tokens above about 520k) are rejected with BJF_ERR_UNSUPPORTED.
 //  * Every call on a device shares the one array, and each call overwrites it: calls
 //    whose work overlaps on the GPU (different streams, or different host threads
 //    without ordering) race and corrupt each other.  Serialise them on one stream.
@@ -55,7 +57,7 @@ bjf_status scratch_address(int dev, void** out) {
 }
 
 struct Carve {
-  size_t scores, indices, counts, coords, total, bytes;
+  size_t scores, indices, counts, bytes;
 };
 
 Carve carve(int64_t S, int64_t N) {
@@ -68,10 +70,6 @@ Carve carve(int64_t S, int64_t N) {
   off = up(off + sizeof(int32_t) * S * N);
   c.counts = off;
   off = up(off + sizeof(int32_t) * S);
-  c.coords = off;
-  off = up(off + sizeof(int32_t) * 4 * S * N);
-  c.total = off;
-  off = up(off + sizeof(int32_t));
   c.bytes = off;
   return c;
 }
@@ -135,8 +133,6 @@ extern "C" bjf_status bjf_front_end_step_no_alloc(const bjf_front_end_desc* d, c
   float* scores = reinterpret_cast<float*>(ws + c.scores);
   int32_t* indices = reinterpret_cast<int32_t*>(ws + c.indices);
   int32_t* counts = counts_out ? counts_out : reinterpret_cast<int32_t*>(ws + c.counts);
-  int32_t* coords = reinterpret_cast<int32_t*>(ws + c.coords);
-  int32_t* total = reinterpret_cast<int32_t*>(ws + c.total);
   cudaStream_t st = as_cuda(stream);
 
   // The previous call's contents stay in the array; only the timeout flag must start at
@@ -145,15 +141,13 @@ extern "C" bjf_status bjf_front_end_step_no_alloc(const bjf_front_end_desc* d, c
   if (e != cudaSuccess) return cuda_status(e, "clear no-alloc scratch flag");
 
   const int64_t vd[5] = {1, d->channels, d->frames, d->height, d->width};
-  rc = launch_scores(video, d->video_dtype, vd, S, d->tubelet_size, d->patch_size, scores, st);
+  rc = launch_scores(video, d->video_dtype, vd, S, d->tubelet_size, d->patch_size, scores, st, true);
   if (rc) return rc;
   if (age_observed) {
     sel.age = age_frames;
     sel.observed = observed;
   }
-  rc = launch_select(scores, S, sel, indices, counts, st);
-  if (rc) return rc;
-  rc = bjf_sparse_patchify_plan_coords(indices, N, counts, S, S, grid, coords, S * N, total, stream);
+  rc = launch_select(scores, S, sel, indices, counts, st, true);
   if (rc) return rc;
 
   GatherGeometry g{};
@@ -180,6 +174,7 @@ extern "C" bjf_status bjf_front_end_step_no_alloc(const bjf_front_end_desc* d, c
   ep.observed = observed;
   ep.age = age_frames;
   ep.bias = bias;
-  return launch_gather_gemm(dev, video, d->video_dtype, weight, d->weight_dtype, g,
-                            coords_rows(reinterpret_cast<const int4*>(coords)), total, S * N, ep, st);
+  const RowSource rows{nullptr, indices, counts, (int)N, (int)S};  // the GEMM scans the counts
+  return launch_gather_gemm(dev, video, d->video_dtype, weight, d->weight_dtype, g, rows, nullptr, S * N, ep, st,
+                            true);
 }

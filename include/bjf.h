@@ -365,7 +365,7 @@ BJF_API bjf_status bjf_front_end_step(const bjf_front_end_desc* desc, const void
  * allocation can stall the device).  Same arguments and results as bjf_front_end_step,
  * minus the workspace: the step's scratch lives in a fixed 4 MiB __device__ array that
  * every GPU loading the library holds until exit, so streams x tokens is limited to about
- * 174k (the bench's 32 streams x 4096 tokens fit); larger steps return
+ * 520k (the bench's 32 streams x 4096 tokens fit); larger steps return
  * BJF_ERR_UNSUPPORTED.  All calls on a device share that array: calls that overlap on the
  * GPU race, so issue them in order on one stream.  The first call on each device looks up
  * the array's address; make it before any stream capture begins.  A call allocates

@@ -24,8 +24,8 @@ def _desc(S, H, W, D, thr, n):
 
 
 def test_no_alloc_rejects_steps_beyond_its_scratch():
-    # 64 streams x 4096 tokens needs more than the fixed 4 MiB: refused before any launch
-    d = _desc(64, 1024, 1024, 1024, 0.05, 4096)
+    # 160 streams x 4096 tokens needs more than the fixed 4 MiB: refused before any launch
+    d = _desc(160, 1024, 1024, 1024, 0.05, 4096)
     rc = bj.load().bjf_front_end_step_no_alloc(ctypes.byref(d), 16, 16, None, 16, 16, 16, 0, None, None)
     assert rc == _abi.BJF_ERR_UNSUPPORTED
     assert "above the fixed 4194304-byte limit" in bj.last_error()
