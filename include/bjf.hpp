@@ -33,6 +33,7 @@
 
 #include <algorithm>
 #include <array>
+#include <optional>
 #include <cmath>
 #include <cstdint>
 #include <cstring>
@@ -483,6 +484,28 @@ constexpr float DEFAULT_PATCH_DIFF_THRESHOLD = 1.0f - DEFAULT_PATCH_DIFF_QUALITY
 constexpr float DEFAULT_PATCH_DIFF_DENSE_FALLBACK_DENSITY = 0.75f;                // :27
 constexpr size_t DEFAULT_PATCH_DIFF_DILATION_TILES = 1;                           // :29
 constexpr size_t DEFAULT_SPARSE_MASK_BUCKET_TOKENS = 256;                         // :31
+constexpr float DEFAULT_CONTEXT_DENSITY = 1.0f;                                   // :17
+constexpr float DEFAULT_MIN_CONTEXT_DENSITY = 0.0f;                               // :21
+constexpr bool DEFAULT_PATCH_DIFF_REFRESH_ENABLED = false;                        // :35
+constexpr float DEFAULT_PATCH_DIFF_SUBTHRESHOLD_DECAY = 0.92f;                    // :37
+constexpr float DEFAULT_PATCH_DIFF_SUBTHRESHOLD_TRIGGER = 1.0f;                   // :39
+constexpr float DEFAULT_PATCH_DIFF_SUBTHRESHOLD_MAX_DENSITY = 0.04f;              // :41
+constexpr uint64_t DEFAULT_PATCH_DIFF_AGE_REFRESH_INTERVAL_FRAMES = 90;           // :43
+constexpr float DEFAULT_PATCH_DIFF_AGE_REFRESH_MAX_DENSITY = 0.01f;               // :45
+constexpr float DEFAULT_PATCH_DIFF_BLUE_NOISE_REFRESH_DENSITY = 0.005f;           // :47
+constexpr float DEFAULT_PATCH_DIFF_REFRESH_MAX_DENSITY = 0.05f;                   // :49
+
+// DensityRound / density_tokens (src/viewer.rs:732-752): a density of `dense_tokens` as a
+// token count in 1 ..= dense_tokens.
+enum class DensityRound { Floor, Round, Ceil };
+inline size_t density_tokens(size_t dense_tokens, float density, DensityRound round, float min_density) {
+  density = std::min(std::max(density, min_density), 1.0f);
+  const float x = (float)dense_tokens * density;
+  const float r = round == DensityRound::Floor ? std::floor(x) : (round == DensityRound::Round ? std::round(x)
+                                                                                               : std::ceil(x));
+  const size_t t = r > 0.0f ? (size_t)r : 0;  // `as usize` saturates at zero
+  return std::min(std::max<size_t>(t, 1), std::max<size_t>(dense_tokens, 1));
+}
 
 using RgbaPatchDiffFrameStats = bjf_rgba_frame_stats;
 
@@ -587,8 +610,46 @@ inline std::vector<size_t> sparse_mask_bucket_widths(TokenGridShape grid, size_t
   return widths;
 }
 
-// The mask fields of FeatureFrameViewerConfig (src/viewer.rs:566-579) with their defaults.
-struct FeatureFrameViewerMaskConfig {
+// PatchDiffRefreshConfig (src/viewer.rs:186-270): bounded extra cache writes for slow or
+// stale tokens.  Off by default.
+struct PatchDiffRefreshConfig {
+  bool enabled = DEFAULT_PATCH_DIFF_REFRESH_ENABLED;
+  bool subthreshold_enabled = false;
+  float subthreshold_decay = DEFAULT_PATCH_DIFF_SUBTHRESHOLD_DECAY;
+  float subthreshold_gain = 1.0f;
+  float subthreshold_trigger = DEFAULT_PATCH_DIFF_SUBTHRESHOLD_TRIGGER;
+  float subthreshold_max_density = DEFAULT_PATCH_DIFF_SUBTHRESHOLD_MAX_DENSITY;
+  bool age_refresh_enabled = false;
+  uint64_t age_refresh_interval_frames = DEFAULT_PATCH_DIFF_AGE_REFRESH_INTERVAL_FRAMES;
+  float age_refresh_max_density = DEFAULT_PATCH_DIFF_AGE_REFRESH_MAX_DENSITY;
+  bool blue_noise_enabled = false;
+  float blue_noise_refresh_density = DEFAULT_PATCH_DIFF_BLUE_NOISE_REFRESH_DENSITY;
+  uint64_t blue_noise_seed = 0x9e3779b97f4a7c15ull;
+  float max_extra_density = DEFAULT_PATCH_DIFF_REFRESH_MAX_DENSITY;
+
+  static PatchDiffRefreshConfig disabled() {
+    PatchDiffRefreshConfig c;
+    c.enabled = false;
+    c.subthreshold_max_density = 0.0f;
+    c.age_refresh_max_density = 0.0f;
+    c.blue_noise_refresh_density = 0.0f;
+    c.max_extra_density = 0.0f;
+    return c;
+  }
+  bool can_add_tokens() const {
+    return enabled && max_extra_density > 0.0f &&
+           ((subthreshold_enabled && subthreshold_max_density > 0.0f) ||
+            (age_refresh_enabled && age_refresh_interval_frames > 0 && age_refresh_max_density > 0.0f) ||
+            (blue_noise_enabled && blue_noise_refresh_density > 0.0f));
+  }
+};
+
+// The patch-diff fields of FeatureFrameViewerConfig (src/viewer.rs:544-602) with their defaults.
+struct FeatureFrameViewerConfig {
+  float context_density = DEFAULT_CONTEXT_DENSITY;
+  float min_context_density = DEFAULT_MIN_CONTEXT_DENSITY;
+  float patch_diff_threshold = DEFAULT_PATCH_DIFF_THRESHOLD;
+  PatchDiffRefreshConfig patch_diff_refresh;
   float patch_diff_dense_fallback_density = DEFAULT_PATCH_DIFF_DENSE_FALLBACK_DENSITY;
   size_t patch_diff_dilation_tiles = DEFAULT_PATCH_DIFF_DILATION_TILES;
   FeatureFrameSparseEncodeMode sparse_encode_mode = FeatureFrameSparseEncodeMode::BucketedContext;
@@ -598,6 +659,13 @@ struct FeatureFrameViewerMaskConfig {
 
   std::vector<size_t> sparse_mask_bucket_widths(TokenGridShape grid) const {
     return bjf::sparse_mask_bucket_widths(grid, sparse_mask_bucket_tokens, sparse_mask_bucket_densities);
+  }
+  // :649-667
+  size_t context_tokens(size_t dense_tokens) const {
+    return density_tokens(dense_tokens, context_density, DensityRound::Round, 0.01f);
+  }
+  size_t min_context_tokens(size_t dense_tokens) const {
+    return density_tokens(dense_tokens, min_context_density, DensityRound::Ceil, 0.0f);
   }
   bjf_viewer_mask_policy to_c() const {
     ensure(sparse_mask_bucket_densities.size() <= 32, "viewer mask policy holds 0..32 bucket densities");
@@ -619,7 +687,7 @@ struct FeatureFrameSparseMasks {  // src/viewer.rs:762-769
 
 // bucket_sparse_mask_with_config (src/viewer.rs:927-944)
 inline SparseTokenMask bucket_sparse_mask_with_config(SparseTokenMask mask, TokenGridShape grid,
-                                                      const FeatureFrameViewerMaskConfig& config) {
+                                                      const FeatureFrameViewerConfig& config) {
   if (grid.len() < 256 || mask.is_dense_ordered()) return mask;
   for (size_t w : config.sparse_mask_bucket_widths(grid))
     if (w >= mask.len()) return mask.padded_to_len(w);
@@ -628,7 +696,7 @@ inline SparseTokenMask bucket_sparse_mask_with_config(SparseTokenMask mask, Toke
 
 // finalize_patch_diff_encode_masks (src/viewer.rs:946-961)
 inline FeatureFrameSparseMasks finalize_patch_diff_encode_masks(SparseTokenMask write_mask, TokenGridShape grid,
-                                                                const FeatureFrameViewerMaskConfig& config) {
+                                                                const FeatureFrameViewerConfig& config) {
   SparseTokenMask encode = config.sparse_encode_mode == FeatureFrameSparseEncodeMode::Exact
                                ? write_mask
                                : bucket_sparse_mask_with_config(write_mask, grid, config);
@@ -637,10 +705,222 @@ inline FeatureFrameSparseMasks finalize_patch_diff_encode_masks(SparseTokenMask 
 
 // finalize_patch_diff_masks (src/viewer.rs:963-971)
 inline FeatureFrameSparseMasks finalize_patch_diff_masks(SparseTokenMask mask, TokenGridShape grid,
-                                                         const FeatureFrameViewerMaskConfig& config) {
+                                                         const FeatureFrameViewerConfig& config) {
   return finalize_patch_diff_encode_masks(
       patch_diff_dense_fallback(std::move(mask), grid, config.patch_diff_dense_fallback_density), grid, config);
 }
+
+// patch_diff_sparsity_config (src/viewer.rs:1012-1028): the selection a viewer config asks for.
+inline SparseJepaPatchDiffSparsityConfig patch_diff_sparsity_config(const FeatureFrameViewerConfig& config,
+                                                                    TokenGridShape grid) {
+  const size_t max_context = config.context_tokens(grid.len());
+  const size_t min_context = std::min(config.min_context_tokens(grid.len()), max_context);
+  const size_t target = std::max<size_t>(grid.len() > max_context ? grid.len() - max_context : 0, 1);
+  return SparseJepaPatchDiffSparsityConfig::adaptive_threshold(config.patch_diff_threshold, min_context,
+                                                               max_context, target)
+      .with_dilation(config.patch_diff_dilation_tiles);
+}
+
+// patch_diff_can_use_dense_fast_path (src/viewer.rs:1031-1036)
+inline bool patch_diff_can_use_dense_fast_path(const SparseJepaPatchDiffSparsityConfig& config,
+                                               TokenGridShape grid) {
+  return config.threshold <= 0.0f && config.allow_full_context && config.context_tokens >= grid.len();
+}
+
+// patch_diff_base_mask_from_scores (src/viewer.rs:819-829): selection without dilation, dense
+// fallback, then the sparsity config's dilation.
+inline SparseTokenMask patch_diff_base_mask_from_scores(const std::vector<float>& scores, TokenGridShape grid,
+                                                        const SparseJepaPatchDiffSparsityConfig& sparsity,
+                                                        const FeatureFrameViewerConfig& config,
+                                                        cudaStream_t st = nullptr) {
+  SparseTokenMask direct = patch_diff_context_mask_from_scores(scores, grid, sparsity.with_dilation(0), st);
+  direct = patch_diff_dense_fallback(std::move(direct), grid, config.patch_diff_dense_fallback_density);
+  return dilate_sparse_patch_mask(std::move(direct), grid, sparsity.dilation);
+}
+
+// patch_diff_masks_from_scores (src/viewer.rs:831-841) for one frame's host scores.
+inline FeatureFrameSparseMasks patch_diff_masks_from_scores(const std::vector<float>& scores, TokenGridShape grid,
+                                                            const SparseJepaPatchDiffSparsityConfig& sparsity,
+                                                            const FeatureFrameViewerConfig& config,
+                                                            cudaStream_t st = nullptr) {
+  return finalize_patch_diff_encode_masks(patch_diff_base_mask_from_scores(scores, grid, sparsity, config, st), grid,
+                                          config);
+}
+
+// PatchDiffRefreshState (src/viewer.rs:272-528): per-stream residuals of below-threshold
+// motion and token ages that add bounded refresh writes to the patch-diff masks.
+class PatchDiffRefreshState {
+ public:
+  void reset() {
+    dense_len_ = 0;
+    frame_index_ = 0;
+    subthreshold_residual_.clear();
+    age_frames_.clear();
+  }
+  uint64_t frame_index() const { return frame_index_; }
+  std::optional<float> subthreshold_residual(size_t index) const {
+    if (index >= subthreshold_residual_.size()) return std::nullopt;
+    return subthreshold_residual_[index];
+  }
+  std::optional<uint32_t> age_frames(size_t index) const {
+    if (index >= age_frames_.size()) return std::nullopt;
+    return age_frames_[index];
+  }
+
+  void observe_write_mask(const SparseTokenMask& mask, TokenGridShape grid) {
+    begin_frame(grid);
+    reset_selected(mask.indices());
+  }
+
+  FeatureFrameSparseMasks masks_from_scores(const std::vector<float>& scores, TokenGridShape grid,
+                                            const SparseJepaPatchDiffSparsityConfig& sparsity,
+                                            const FeatureFrameViewerConfig& config, cudaStream_t st = nullptr) {
+    ensure(scores.size() == grid.len(), "patch-diff refresh received unexpected score length");
+    SparseTokenMask base = patch_diff_base_mask_from_scores(scores, grid, sparsity, config, st);
+    begin_frame(grid);
+    if (config.patch_diff_refresh.can_add_tokens() && !base.is_dense_ordered())
+      base = augment_mask(std::move(base), scores, grid, sparsity, config.patch_diff_refresh);
+    FeatureFrameSparseMasks masks = finalize_patch_diff_encode_masks(std::move(base), grid, config);
+    reset_selected(masks.write_mask.indices());
+    return masks;
+  }
+
+ private:
+  void begin_frame(TokenGridShape grid) {
+    if (dense_len_ != grid.len()) {
+      dense_len_ = grid.len();
+      frame_index_ = 0;
+      subthreshold_residual_.assign(grid.len(), 0.0f);
+      age_frames_.assign(grid.len(), 0);
+    }
+    if (frame_index_ != UINT64_MAX) ++frame_index_;
+    for (uint32_t& a : age_frames_)
+      if (a != UINT32_MAX) ++a;
+  }
+  void reset_selected(const std::vector<size_t>& indices) {
+    for (size_t i : indices) {
+      if (i < subthreshold_residual_.size()) subthreshold_residual_[i] = 0.0f;
+      if (i < age_frames_.size()) age_frames_[i] = 0;
+    }
+  }
+  // mix64 (:530-536): the splitmix64 finaliser
+  static uint64_t mix64(uint64_t v) {
+    v ^= v >> 30;
+    v *= 0xbf58476d1ce4e5b9ull;
+    v ^= v >> 27;
+    v *= 0x94d049bb133111ebull;
+    return v ^ (v >> 31);
+  }
+  uint64_t refresh_rank(size_t index, TokenGridShape grid, uint64_t seed) const {
+    const uint64_t w = std::max<size_t>(grid.width, 1);
+    const uint64_t row = index / w, col = index % w;
+    return mix64(seed ^ (row * 0x9e3779b97f4a7c15ull) ^ (col * 0xbf58476d1ce4e5b9ull) ^
+                 (frame_index_ * 0x94d049bb133111ebull));
+  }
+  void update_subthreshold_residual(const std::vector<float>& scores, const std::vector<size_t>& chosen,
+                                    const SparseJepaPatchDiffSparsityConfig& sparsity,
+                                    const PatchDiffRefreshConfig& config) {
+    std::vector<bool> sel(scores.size(), false);
+    for (size_t i : chosen)
+      if (i < sel.size()) sel[i] = true;
+    const float decay = std::min(std::max(config.subthreshold_decay, 0.0f), 1.0f);
+    const float threshold = std::max(sparsity.threshold, 1.0e-6f);
+    for (size_t i = 0; i < subthreshold_residual_.size(); ++i) {
+      if (sel[i] || scores[i] >= sparsity.threshold) {
+        subthreshold_residual_[i] = 0.0f;
+      } else {
+        const float normalized = std::min(std::max(scores[i] / threshold, 0.0f), 1.0f);
+        subthreshold_residual_[i] = subthreshold_residual_[i] * decay + normalized * std::max(config.subthreshold_gain, 0.0f);
+      }
+    }
+  }
+  // add_ranked_candidates (:481-518): the `budget` best unselected candidates by (priority
+  // desc, rank asc, index asc), appended in that order.
+  template <typename F>
+  size_t add_ranked_candidates(std::vector<bool>& selected, std::vector<size_t>& indices, size_t budget, F rank) {
+    if (budget == 0) return 0;
+    struct Cand {
+      size_t index;
+      float priority;
+      uint64_t tie;
+    };
+    std::vector<Cand> cands;
+    for (size_t i = 0; i < selected.size(); ++i) {
+      if (selected[i]) continue;
+      float pr;
+      uint64_t tie;
+      if (rank(i, pr, tie)) cands.push_back({i, pr, tie});
+    }
+    auto before = [](const Cand& a, const Cand& b) {
+      if (a.priority > b.priority) return true;
+      if (b.priority > a.priority) return false;  // NaN priorities compare equal, as partial_cmp's fallback
+      if (a.tie != b.tie) return a.tie < b.tie;
+      return a.index < b.index;
+    };
+    std::sort(cands.begin(), cands.end(), before);
+    if (cands.size() > budget) cands.resize(budget);
+    for (const Cand& c : cands) {
+      selected[c.index] = true;
+      indices.push_back(c.index);
+    }
+    return cands.size();
+  }
+  SparseTokenMask augment_mask(SparseTokenMask base, const std::vector<float>& scores, TokenGridShape grid,
+                               const SparseJepaPatchDiffSparsityConfig& sparsity, const PatchDiffRefreshConfig& config) {
+    const size_t n = grid.len();
+    if (base.len() >= n) return base;
+    const size_t max_context = std::min(std::max<size_t>(sparsity.context_tokens, 1), n);
+    size_t remaining = max_context > base.len() ? max_context - base.len() : 0;
+    remaining = std::min(remaining, density_tokens(n, config.max_extra_density, DensityRound::Floor, 0.0f));
+    if (remaining == 0) {
+      update_subthreshold_residual(scores, base.indices(), sparsity, config);
+      return base;
+    }
+    std::vector<bool> selected(n, false);
+    std::vector<size_t> indices = base.indices();
+    for (size_t i : indices) selected[i] = true;
+    update_subthreshold_residual(scores, indices, sparsity, config);
+    const uint64_t seed = config.blue_noise_seed;
+    if (config.subthreshold_enabled && config.subthreshold_max_density > 0.0f) {
+      const size_t budget =
+          std::min(remaining, density_tokens(n, config.subthreshold_max_density, DensityRound::Floor, 0.0f));
+      const float trigger = std::max(config.subthreshold_trigger, 1.0e-6f);
+      remaining -= add_ranked_candidates(selected, indices, budget, [&](size_t i, float& pr, uint64_t& tie) {
+        if (!(subthreshold_residual_[i] >= trigger)) return false;
+        pr = subthreshold_residual_[i];
+        tie = refresh_rank(i, grid, seed);
+        return true;
+      });
+    }
+    if (remaining > 0 && config.age_refresh_enabled && config.age_refresh_interval_frames > 0 &&
+        config.age_refresh_max_density > 0.0f) {
+      const uint32_t interval = (uint32_t)std::min<uint64_t>(config.age_refresh_interval_frames, UINT32_MAX);
+      const size_t budget =
+          std::min(remaining, density_tokens(n, config.age_refresh_max_density, DensityRound::Floor, 0.0f));
+      remaining -= add_ranked_candidates(selected, indices, budget, [&](size_t i, float& pr, uint64_t& tie) {
+        if (age_frames_[i] < interval) return false;
+        pr = (float)age_frames_[i];
+        tie = refresh_rank(i, grid, seed);
+        return true;
+      });
+    }
+    if (remaining > 0 && config.blue_noise_enabled && config.blue_noise_refresh_density > 0.0f) {
+      const size_t budget =
+          std::min(remaining, density_tokens(n, config.blue_noise_refresh_density, DensityRound::Floor, 0.0f));
+      add_ranked_candidates(selected, indices, budget, [&](size_t i, float& pr, uint64_t& tie) {
+        pr = 0.0f;
+        tie = refresh_rank(i, grid, seed);
+        return true;
+      });
+    }
+    return SparseTokenMask::new_(std::move(indices), n);
+  }
+
+  size_t dense_len_ = 0;
+  uint64_t frame_index_ = 0;
+  std::vector<float> subthreshold_residual_;
+  std::vector<uint32_t> age_frames_;
+};
 
 // Device masks of S streams: row s of each [S, N] buffer holds its count of ascending indices.
 struct DeviceSparseMasks {
@@ -664,7 +944,7 @@ struct DeviceSparseMasks {
 // encode buckets, all on the device.
 inline DeviceSparseMasks patch_diff_masks_from_scores(const Tensor& scores, TokenGridShape grid,
                                                       const SparseJepaPatchDiffSparsityConfig& sparsity,
-                                                      const FeatureFrameViewerMaskConfig& config,
+                                                      const FeatureFrameViewerConfig& config,
                                                       cudaStream_t st = nullptr) {
   const int64_t n = (int64_t)grid.len();
   ensure(scores.numel() > 0 && scores.numel() % n == 0, "patch-diff sparsity received unexpected score length");
@@ -687,7 +967,7 @@ inline DeviceSparseMasks patch_diff_masks_from_scores(const Tensor& scores, Toke
 inline DeviceSparseMasks patch_diff_masks_from_rgba(const uint8_t* prev, const uint8_t* current, size_t width,
                                                     size_t height, size_t patch_size, TokenGridShape grid,
                                                     const SparseJepaPatchDiffSparsityConfig& sparsity,
-                                                    const FeatureFrameViewerMaskConfig& config, size_t streams = 1,
+                                                    const FeatureFrameViewerConfig& config, size_t streams = 1,
                                                     cudaStream_t st = nullptr) {
   const int64_t n = (int64_t)grid.len(), S = (int64_t)streams;
   const auto g = grid.dims();

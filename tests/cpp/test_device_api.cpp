@@ -404,12 +404,12 @@ TEST(viewer_masks_from_scores_match_host_policy) {
   for (size_t s = 0; s < S; ++s)
     for (size_t i = 0; i < N; ++i) scores[s * N + i] = std::pow(std::fabs(u[s * N + i]), 1.0f + 3.0f * (float)s);
   const Tensor dscores = Tensor::from_host(scores, {(int64_t)S, (int64_t)N}, BJF_DTYPE_F32);
-  FeatureFrameViewerMaskConfig exact;
+  FeatureFrameViewerConfig exact;
   exact.sparse_encode_mode = FeatureFrameSparseEncodeMode::Exact;
-  FeatureFrameViewerMaskConfig legacy;
+  FeatureFrameViewerConfig legacy;
   legacy.sparse_mask_bucket_densities.clear();
   legacy.sparse_mask_bucket_tokens = 100;
-  for (const auto& cfg : {FeatureFrameViewerMaskConfig{}, exact, legacy})
+  for (const auto& cfg : {FeatureFrameViewerConfig{}, exact, legacy})
     for (size_t dilation : {0, 1, 2}) {
       const auto sparsity = SparseJepaPatchDiffSparsityConfig::adaptive_threshold(0.2f, 4, N, 1).with_dilation(dilation);
       const auto dev = patch_diff_masks_from_scores(dscores, grid, sparsity, cfg);
@@ -440,7 +440,7 @@ TEST(rgba_mask_node_sampled_dense_fast_path) {
                           Tensor::from_host(cur, {(int64_t)(W * H)}, BJF_DTYPE_I32));
   };
   const auto cfg = SparseJepaPatchDiffSparsityConfig::adaptive_threshold(0.10f, 1, grid.len(), grid.len()).with_dilation(1);
-  FeatureFrameViewerMaskConfig viewer;
+  FeatureFrameViewerConfig viewer;
   viewer.patch_diff_dense_fallback_density = 0.60f;
   {
     const auto [prev, cur] = frames(4, 4);
@@ -458,6 +458,140 @@ TEST(rgba_mask_node_sampled_dense_fast_path) {
     CHECK(m.write_mask.is_dense_ordered());
     CHECK(m.encode_mask.is_dense_ordered());
   }
+}
+
+// src/viewer.rs:1528-1575: repeated below-threshold motion is refreshed on the third frame
+TEST(subthreshold_patch_diff_accumulates_slow_motion) {
+  const TokenGridShape grid(1, 4, 4);
+  const size_t slow_index = coords_to_token_index(0, 2, 1, grid);
+  FeatureFrameViewerConfig config;
+  config.context_density = 0.25f;
+  config.min_context_density = 0.0f;
+  config.patch_diff_threshold = 0.10f;
+  config.patch_diff_dense_fallback_density = 1.0f;
+  config.patch_diff_dilation_tiles = 0;
+  config.sparse_encode_mode = FeatureFrameSparseEncodeMode::Exact;
+  config.patch_diff_refresh.enabled = true;
+  config.patch_diff_refresh.subthreshold_enabled = true;
+  config.patch_diff_refresh.subthreshold_decay = 1.0f;
+  config.patch_diff_refresh.subthreshold_trigger = 1.0f;
+  config.patch_diff_refresh.subthreshold_max_density = 0.25f;
+  config.patch_diff_refresh.age_refresh_enabled = false;
+  config.patch_diff_refresh.blue_noise_enabled = false;
+  config.patch_diff_refresh.max_extra_density = 0.25f;
+  const auto sparsity = patch_diff_sparsity_config(config, grid);
+  PatchDiffRefreshState state;
+  std::vector<float> scores(grid.len(), 0.0f);
+  scores[0] = 0.09f;
+  scores[slow_index] = 0.04f;
+  const auto contains = [](const SparseTokenMask& m, size_t i) {
+    return std::find(m.indices().begin(), m.indices().end(), i) != m.indices().end();
+  };
+  CHECK(!contains(state.masks_from_scores(scores, grid, sparsity, config).write_mask, slow_index));
+  CHECK(!contains(state.masks_from_scores(scores, grid, sparsity, config).write_mask, slow_index));
+  CHECK(contains(state.masks_from_scores(scores, grid, sparsity, config).write_mask, slow_index));
+  CHECK(state.subthreshold_residual(slow_index) == std::optional<float>(0.0f));
+  CHECK(state.age_frames(slow_index) == std::optional<uint32_t>(0u));
+}
+
+// src/viewer.rs:1595-1632: refresh never exceeds the context budget
+TEST(subthreshold_refresh_fills_only_unused_context_budget) {
+  const TokenGridShape grid(1, 4, 4);
+  FeatureFrameViewerConfig config;
+  config.context_density = 2.0f / 16.0f;
+  config.min_context_density = 0.0f;
+  config.patch_diff_threshold = 0.10f;
+  config.patch_diff_dense_fallback_density = 1.0f;
+  config.patch_diff_dilation_tiles = 0;
+  config.sparse_encode_mode = FeatureFrameSparseEncodeMode::Exact;
+  config.patch_diff_refresh.enabled = true;
+  config.patch_diff_refresh.subthreshold_enabled = true;
+  config.patch_diff_refresh.subthreshold_decay = 1.0f;
+  config.patch_diff_refresh.subthreshold_trigger = 0.5f;
+  config.patch_diff_refresh.subthreshold_max_density = 1.0f;
+  config.patch_diff_refresh.age_refresh_enabled = false;
+  config.patch_diff_refresh.blue_noise_enabled = false;
+  config.patch_diff_refresh.max_extra_density = 1.0f;
+  const auto sparsity = patch_diff_sparsity_config(config, grid);
+  PatchDiffRefreshState state;
+  std::vector<float> scores(grid.len(), 0.06f);
+  scores[0] = 0.09f;
+  CHECK_EQ(state.masks_from_scores(scores, grid, sparsity, config).write_mask.len(), (size_t)2);
+}
+
+// src/viewer.rs:1634-1672: stale tokens are refreshed once their age reaches the interval
+TEST(age_priority_refresh_selects_stale_tokens) {
+  const TokenGridShape grid(1, 4, 4);
+  FeatureFrameViewerConfig config;
+  config.context_density = 0.50f;
+  config.min_context_density = 0.0f;
+  config.patch_diff_threshold = 0.10f;
+  config.patch_diff_dense_fallback_density = 1.0f;
+  config.patch_diff_dilation_tiles = 0;
+  config.sparse_encode_mode = FeatureFrameSparseEncodeMode::Exact;
+  config.patch_diff_refresh.subthreshold_enabled = false;
+  config.patch_diff_refresh.enabled = true;
+  config.patch_diff_refresh.age_refresh_enabled = true;
+  config.patch_diff_refresh.age_refresh_interval_frames = 2;
+  config.patch_diff_refresh.age_refresh_max_density = 0.25f;
+  config.patch_diff_refresh.blue_noise_enabled = false;
+  config.patch_diff_refresh.max_extra_density = 0.25f;
+  const auto sparsity = patch_diff_sparsity_config(config, grid);
+  PatchDiffRefreshState state;
+  std::vector<float> scores(grid.len(), 0.0f);
+  scores[0] = 0.09f;
+  const size_t first = state.masks_from_scores(scores, grid, sparsity, config).write_mask.len();
+  CHECK_EQ(first, (size_t)1);
+  CHECK(state.masks_from_scores(scores, grid, sparsity, config).write_mask.len() > first);
+}
+
+// src/viewer.rs:1674-1703: blue-noise refresh depends only on the state and the seed
+TEST(blue_noise_refresh_is_deterministic_for_same_state) {
+  const TokenGridShape grid(1, 4, 4);
+  FeatureFrameViewerConfig config;
+  config.context_density = 0.50f;
+  config.min_context_density = 0.0f;
+  config.patch_diff_threshold = 0.10f;
+  config.patch_diff_dense_fallback_density = 1.0f;
+  config.patch_diff_dilation_tiles = 0;
+  config.sparse_encode_mode = FeatureFrameSparseEncodeMode::Exact;
+  config.patch_diff_refresh.subthreshold_enabled = false;
+  config.patch_diff_refresh.age_refresh_enabled = false;
+  config.patch_diff_refresh.enabled = true;
+  config.patch_diff_refresh.blue_noise_enabled = true;
+  config.patch_diff_refresh.blue_noise_refresh_density = 0.25f;
+  config.patch_diff_refresh.max_extra_density = 0.25f;
+  config.patch_diff_refresh.blue_noise_seed = 7;
+  const auto sparsity = patch_diff_sparsity_config(config, grid);
+  PatchDiffRefreshState left, right;
+  const std::vector<float> scores(grid.len(), 0.0f);
+  const auto l = left.masks_from_scores(scores, grid, sparsity, config).write_mask;
+  const auto r = right.masks_from_scores(scores, grid, sparsity, config).write_mask;
+  CHECK_EQ(l.indices(), r.indices());
+  CHECK(l.len() > (size_t)0);
+}
+
+// src/viewer.rs:1405-1453 through the viewer config: the sparsity config dilates direct hits
+TEST(patch_diff_sparsity_config_dilates_direct_hits) {
+  const TokenGridShape grid(1, 4, 4);
+  const size_t center = coords_to_token_index(0, 2, 1, grid);
+  std::vector<float> scores(grid.len(), 0.0f);
+  scores[center] = 0.5f;
+  FeatureFrameViewerConfig config;
+  config.context_density = 1.0f;
+  config.min_context_density = 0.0f;
+  config.patch_diff_threshold = 0.10f;
+  config.patch_diff_dilation_tiles = 1;
+  config.patch_diff_refresh = PatchDiffRefreshConfig::disabled();
+  config.sparse_encode_mode = FeatureFrameSparseEncodeMode::Exact;
+  const auto dilated = patch_diff_context_mask_from_scores(scores, grid, patch_diff_sparsity_config(config, grid));
+  std::vector<size_t> want;
+  for (size_t r = 1; r <= 3; ++r)
+    for (size_t c = 0; c <= 2; ++c) want.push_back(coords_to_token_index(0, r, c, grid));
+  CHECK_EQ(dilated.indices(), want);
+  config.patch_diff_dilation_tiles = 0;
+  CHECK_EQ(patch_diff_context_mask_from_scores(scores, grid, patch_diff_sparsity_config(config, grid)).indices(),
+           (std::vector<size_t>{center}));
 }
 
 // The fused step over S streams against the oracle's per-stream composition.  Unchanged

@@ -160,7 +160,7 @@ TEST(bucketed_masks_keep_writes_exact_and_widen_encode_context) {
   const TokenGridShape grid(1, 32, 32);
   const size_t changed_index = coords_to_token_index(0, 15, 16, grid);
   const auto changed = SparseTokenMask::new_({changed_index}, grid.len());
-  const auto masks = finalize_patch_diff_masks(changed, grid, FeatureFrameViewerMaskConfig{});
+  const auto masks = finalize_patch_diff_masks(changed, grid, FeatureFrameViewerConfig{});
   CHECK_EQ(masks.write_mask.indices(), changed.indices());
   CHECK_EQ(masks.encode_mask.len(), (size_t)103);
   CHECK(std::find(masks.encode_mask.indices().begin(), masks.encode_mask.indices().end(), changed_index) !=
@@ -170,10 +170,10 @@ TEST(bucketed_masks_keep_writes_exact_and_widen_encode_context) {
 // src/viewer.rs:1342-1376: the widths behind the prewarm lists (768 of the legacy step
 // finalizes to the dense mask under the 0.75 fallback, so the reference's prewarm list omits it)
 TEST(bucket_widths_follow_densities_or_legacy_step) {
-  const FeatureFrameViewerMaskConfig cfg;
+  const FeatureFrameViewerConfig cfg;
   CHECK_EQ(cfg.sparse_mask_bucket_widths(TokenGridShape(1, 32, 32)), (std::vector<size_t>{103, 256, 512, 1024}));
   CHECK_EQ(cfg.sparse_mask_bucket_widths(TokenGridShape(1, 64, 64)), (std::vector<size_t>{410, 1024, 2048, 4096}));
-  FeatureFrameViewerMaskConfig legacy;
+  FeatureFrameViewerConfig legacy;
   legacy.sparse_mask_bucket_densities.clear();
   CHECK_EQ(legacy.sparse_mask_bucket_widths(TokenGridShape(1, 32, 32)), (std::vector<size_t>{256, 512, 768, 1024}));
   CHECK(finalize_patch_diff_masks(SparseTokenMask::evenly_spaced(1024, 768), TokenGridShape(1, 32, 32), legacy)
@@ -184,9 +184,28 @@ TEST(bucket_widths_follow_densities_or_legacy_step) {
 TEST(bucket_density_list_selects_next_configured_width) {
   const TokenGridShape grid(1, 32, 32);
   const auto mask = SparseTokenMask::evenly_spaced(grid.len(), 120);
-  const auto masks = finalize_patch_diff_masks(mask, grid, FeatureFrameViewerMaskConfig{});
+  const auto masks = finalize_patch_diff_masks(mask, grid, FeatureFrameViewerConfig{});
   CHECK_EQ(masks.write_mask.indices(), mask.indices());
   CHECK_EQ(masks.encode_mask.len(), (size_t)256);
+}
+
+// src/viewer.rs:649-667, 732-752, 1012-1028: the selection a viewer config asks for
+TEST(viewer_config_derives_the_patch_diff_selection) {
+  FeatureFrameViewerConfig config;
+  config.context_density = 0.25f;
+  const TokenGridShape grid(1, 4, 4);
+  const auto sp = patch_diff_sparsity_config(config, grid);
+  CHECK_EQ(sp.context_tokens, (size_t)4);
+  CHECK_EQ(sp.min_context_tokens, (size_t)1);  // min density 0 still keeps one token
+  CHECK_EQ(sp.target_tokens, (size_t)12);
+  CHECK_EQ(sp.dilation, DEFAULT_PATCH_DIFF_DILATION_TILES);
+  CHECK(sp.allow_full_context && !sp.fill_to_context_tokens);
+  CHECK_EQ(density_tokens(16, 0.0f, DensityRound::Round, 0.01f), (size_t)1);
+  CHECK_EQ(density_tokens(1000, 0.1234f, DensityRound::Floor, 0.0f), (size_t)123);
+  CHECK_EQ(density_tokens(1000, 0.1234f, DensityRound::Ceil, 0.0f), (size_t)124);
+  CHECK_EQ(density_tokens(10, 5.0f, DensityRound::Round, 0.0f), (size_t)10);
+  CHECK(!PatchDiffRefreshConfig{}.can_add_tokens());  // refresh is off by default
+  CHECK(!PatchDiffRefreshConfig::disabled().can_add_tokens());
 }
 
 // src/positional.rs:104-111
