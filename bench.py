@@ -42,8 +42,8 @@ STREAMS_PER_GPU = 32
 KERNELS_PER_STEP = 3  # patch-diff scores, selection, gather-GEMM (+ row plan, + cache write)
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one scores launch per stream of
 # this workload, from one ncu --set full capture of the scores kernel at 16 streams
-# (207 552 256 bytes / 16), scaled by the stream count for the roofline's `traffic`.
-SCORES_DRAM_BYTES_PER_STREAM = 12972016
+# (207 767 552 bytes / 16), scaled by the stream count for the roofline's `traffic`.
+SCORES_DRAM_BYTES_PER_STREAM = 12985472
 # The same for the CTA-pair gather-GEMM per active row (34.9 MB read + 0.65 MB written at 6 581
 # rows in the same run; cold L2, so an upper bound for a warm step).
 GEMM_DRAM_BYTES_PER_ROW = 5408
