@@ -328,6 +328,18 @@ class Tensor {
     return t;
   }
 
+  // The same storage under another shape of as many elements (burn's Tensor::reshape).
+  Tensor reshape(std::vector<int64_t> shape) && {
+    Tensor t;
+    t.shape_ = std::move(shape);
+    t.dtype_ = dtype_;
+    ensure(t.numel() == numel(), "reshape must keep the element count");
+    t.ptr_ = ptr_;
+    ptr_ = nullptr;
+    shape_.clear();
+    return t;
+  }
+
   void* data() { return ptr_; }
   const void* data() const { return ptr_; }
   bjf_dtype dtype() const { return dtype_; }
@@ -1122,6 +1134,71 @@ inline Tensor sparse_patchify3d_forward_cuda(const SparsePatchify3dConfig& confi
                                       to_bjf(st)));
   return out;
 }
+
+// The sparse patch-embed methods of VJepaEncoder on the CUDA lane (src/model.rs:1092-1328): the
+// checks of the input against the plan and the V-JEPA config, then the flex-gmm patch embed,
+// reshaped to [batch, plan tokens, embed_dim].  `weight` [D, C, tubelet, P, P] (video) or
+// [D, C, 1, P, P] (image, the tubelet-1 image embed); `bias` [D] f32 or null (zeros).
+struct VJepaSparsePatchEmbed {
+  size_t in_channels = 3, embed_dim = 0, tubelet_size = 2, patch_size = 16;
+
+  // sparse_patchify_video_cuda (:1273-1328); video [B, C, T, H, W]
+  Tensor sparse_patchify_video_cuda(const Tensor& video, const SparsePatchifyPlan& plan, const Tensor& weight,
+                                    const Tensor* bias, cudaStream_t st = nullptr) const {
+    const auto d = detail::video_dims(video);
+    ensure((size_t)d[0] == plan.batch, "video batch does not match sparse patchify plan");
+    ensure((size_t)d[1] == in_channels, "video channel count does not match V-JEPA config");
+    const size_t kt = std::max<size_t>(tubelet_size, 1), p = std::max<size_t>(patch_size, 1);
+    ensure(TokenGridShape((size_t)d[2] / kt, (size_t)d[3] / p, (size_t)d[4] / p) == plan.grid,
+           "video token grid does not match sparse patchify plan");
+    SparsePatchify3dConfig c;
+    c.in_channels = (size_t)d[1];
+    c.out_channels = embed_dim;
+    c.frames = (size_t)d[2];
+    c.height = (size_t)d[3];
+    c.width = (size_t)d[4];
+    c.tubelet_size = tubelet_size;
+    c.patch_h = patch_size;
+    c.patch_w = patch_size;
+    return sparse_patchify3d_forward_cuda(c, video, plan.coords, weight, bias, st)
+        .reshape({d[0], (int64_t)plan.token_count(), (int64_t)embed_dim});
+  }
+
+  // sparse_patchify_image_cuda (:1094-1148); image [B, C, H, W], one frame of tubelet 1
+  Tensor sparse_patchify_image_cuda(const Tensor& image, const SparsePatchifyPlan& plan, const Tensor& weight,
+                                    const Tensor* bias, cudaStream_t st = nullptr) const {
+    ensure(image.rank() == 4, "image must be a [B, C, H, W] tensor");
+    const auto& sh = image.shape();
+    ensure((size_t)sh[0] == plan.batch, "image batch does not match sparse patchify plan");
+    ensure((size_t)sh[1] == in_channels, "image channel count does not match V-JEPA config");
+    const size_t p = std::max<size_t>(patch_size, 1);
+    ensure(TokenGridShape(1, (size_t)sh[2] / p, (size_t)sh[3] / p) == plan.grid,
+           "image token grid does not match sparse patchify plan");
+    SparsePatchify3dConfig c;
+    c.in_channels = (size_t)sh[1];
+    c.out_channels = embed_dim;
+    c.frames = 1;
+    c.height = (size_t)sh[2];
+    c.width = (size_t)sh[3];
+    c.tubelet_size = 1;
+    c.patch_h = patch_size;
+    c.patch_w = patch_size;
+    // the image as a one-frame clip [B, C, 1, H, W]: the same memory, a borrowed view
+    const int64_t vd[5] = {sh[0], sh[1], 1, sh[2], sh[3]};
+    ensure(weight.rank() == 5, "sparse patchify weight must be [D, C, kt, ph, pw]");
+    std::array<int64_t, 5> wd{};
+    for (int i = 0; i < 5; ++i) wd[i] = weight.shape()[i];
+    const bjf_patchify_config cc = c.to_c();
+    const int64_t rows = plan.coords.shape()[0];
+    Tensor out({rows, (int64_t)embed_dim}, image.dtype());
+    check(bjf_sparse_patchify3d_forward(&cc, image.data(), image.dtype(), vd,
+                                        static_cast<const int32_t*>(plan.coords.data()), rows, weight.data(),
+                                        weight.dtype(), wd.data(),
+                                        bias ? static_cast<const float*>(bias->data()) : nullptr, out.data(),
+                                        image.dtype(), to_bjf(st)));
+    return std::move(out).reshape({sh[0], (int64_t)plan.token_count(), (int64_t)embed_dim});
+  }
+};
 
 // sparse_3d_sincos_pos_embed (src/positional.rs:46-87): [indices.size(), embed_dim] f32 on the
 // host, the frame / row / column sin-cos blocks of even(D/2), even(D/4), even(rest) dims.

@@ -152,6 +152,51 @@ TEST(cuda_sparse_image_patchify_matches_dense_image_encoder_on_selected_tokens) 
   CHECK(max_abs_diff(host_f32(out), want) <= kCudaParityTolerance);
 }
 
+// src/model.rs:1273-1328 and 1094-1148: the encoder methods check the input against the plan
+// and the config, then return the rows as [batch, plan tokens, D].
+TEST(encoder_sparse_patchify_methods_check_the_plan_and_reshape) {
+  const TokenGridShape grid(2, 2, 2);
+  const auto plan = SparsePatchifyPlan::new_(SparseTokenMask::new_({0, 3, 7}, grid.len()), grid, 2);
+  VJepaSparsePatchEmbed enc;
+  enc.in_channels = 3;
+  enc.embed_dim = 32;
+  enc.tubelet_size = 2;
+  enc.patch_size = 16;
+  const auto video = seeded(51, 2 * 3 * 4 * 32 * 32, 1.0f);
+  const auto weight = seeded(52, 32 * 3 * 2 * 16 * 16, 0.05f);
+  const auto bias = seeded(53, 32, 0.02f);
+  const Tensor v = Tensor::from_host(video, {2, 3, 4, 32, 32}, BJF_DTYPE_F32);
+  const Tensor w = Tensor::from_host(weight, {32, 3, 2, 16, 16}, BJF_DTYPE_F32);
+  const Tensor b = Tensor::from_host(bias, {32}, BJF_DTYPE_F32);
+  const Tensor out = enc.sparse_patchify_video_cuda(v, plan, w, &b);
+  CHECK(out.shape() == (std::vector<int64_t>{2, 3, 32}));
+  const SparsePatchify3dConfig cfg{3, 32, 4, 32, 32, 2, 16, 16};
+  CHECK(max_abs_diff(host_f32(out), dense_at_coords(oracle_cfg(cfg), 2, video, weight, bias, plan.coords_host)) <=
+        kCudaParityTolerance);
+  const auto one = SparsePatchifyPlan::new_(SparseTokenMask::new_({0, 3, 7}, grid.len()), grid, 1);
+  CHECK_THROWS_WITH(enc.sparse_patchify_video_cuda(v, one, w, &b), "video batch does not match sparse patchify plan");
+  VJepaSparsePatchEmbed four = enc;
+  four.in_channels = 4;
+  CHECK_THROWS_WITH(four.sparse_patchify_video_cuda(v, plan, w, &b), "video channel count does not match V-JEPA config");
+  const auto other = SparsePatchifyPlan::new_(SparseTokenMask::new_({0, 3}, 4), TokenGridShape(1, 2, 2), 2);
+  CHECK_THROWS_WITH(enc.sparse_patchify_video_cuda(v, other, w, &b), "video token grid does not match sparse patchify plan");
+
+  // the image twin: [B, C, H, W] as one frame of tubelet 1
+  const TokenGridShape igrid(1, 2, 2);
+  const auto iplan = SparsePatchifyPlan::new_(SparseTokenMask::new_({1, 2}, igrid.len()), igrid, 2);
+  const auto image = seeded(54, 2 * 3 * 32 * 32, 1.0f);
+  const auto iweight = seeded(55, 32 * 3 * 1 * 16 * 16, 0.05f);
+  const Tensor im = Tensor::from_host(image, {2, 3, 32, 32}, BJF_DTYPE_F32);
+  const Tensor iw = Tensor::from_host(iweight, {32, 3, 1, 16, 16}, BJF_DTYPE_F32);
+  const Tensor iout = enc.sparse_patchify_image_cuda(im, iplan, iw, nullptr);
+  CHECK(iout.shape() == (std::vector<int64_t>{2, 2, 32}));
+  const SparsePatchify3dConfig icfg{3, 32, 1, 32, 32, 1, 16, 16};
+  const std::vector<float> zeros(32, 0.0f);
+  CHECK(max_abs_diff(host_f32(iout), dense_at_coords(oracle_cfg(icfg), 2, image, iweight, zeros, iplan.coords_host)) <=
+        kCudaParityTolerance);
+  CHECK_THROWS_WITH(enc.sparse_patchify_image_cuda(im, plan, iw, nullptr), "image token grid does not match sparse patchify plan");
+}
+
 // The tensor-core path (f16 and bf16 operands, f32 accumulation) on a fixed-width batch plan,
 // against the oracle evaluated on the same rounded inputs; normwise relative error <= 1e-2.
 static void half_patchify_case(bjf_dtype dt) {
