@@ -1057,8 +1057,136 @@ class SparsePatchifyPlan {
 
 // Per-row masks of equal width (uniform or fixed-width); ragged rows are refused as in
 // SparsePatchifyBatchPlan::new (src/sparse_patchify.rs:290-330).
+// SparseMaskBatch (src/tokens.rs:180-442): per-batch-row masks, Uniform (one mask repeated),
+// FixedWidth (equal-length rows) or Ragged (rows padded with their last index).  Host rows;
+// indices_tensor() uploads the [batch, width] int32 index matrix.
+class SparseMaskBatch {
+ public:
+  enum class Kind { Uniform, FixedWidth, Ragged };
+
+  static SparseMaskBatch uniform(SparseTokenMask mask, size_t batch) {
+    ensure(batch > 0, "sparse mask batch must be non-empty");
+    SparseMaskBatch m;
+    m.kind_ = Kind::Uniform;
+    m.dense_len_ = mask.dense_len();
+    m.rows_.assign(batch, mask.indices());
+    m.lengths_.assign(batch, mask.len());
+    return m;
+  }
+  static SparseMaskBatch fixed_width(std::vector<std::vector<size_t>> rows, size_t dense_len) {
+    ensure(dense_len > 0, "dense token count must be nonzero");
+    ensure(!rows.empty(), "sparse mask batch must be non-empty");
+    const size_t width = rows[0].size();
+    ensure(width > 0, "fixed-width sparse mask rows must be non-empty");
+    ensure(std::all_of(rows.begin(), rows.end(), [&](const std::vector<size_t>& r) { return r.size() == width; }),
+           "fixed-width sparse mask rows must have equal lengths");
+    for (auto& row : rows) {
+      std::sort(row.begin(), row.end());
+      row.erase(std::unique(row.begin(), row.end()), row.end());
+      ensure(row.size() == width, "fixed-width sparse mask row contains duplicate indices");
+      ensure(std::all_of(row.begin(), row.end(), [&](size_t i) { return i < dense_len; }),
+             "sparse token index outside dense token range");
+    }
+    SparseMaskBatch m;
+    m.kind_ = Kind::FixedWidth;
+    m.dense_len_ = dense_len;
+    m.lengths_.assign(rows.size(), width);
+    m.rows_ = std::move(rows);
+    return m;
+  }
+  static SparseMaskBatch from_rows(std::vector<std::vector<size_t>> rows, size_t dense_len) {
+    ensure(!rows.empty(), "sparse mask batch must be non-empty");
+    if (std::all_of(rows.begin(), rows.end(), [&](const std::vector<size_t>& r) { return r == rows[0]; }))
+      return uniform(SparseTokenMask::new_(rows[0], dense_len), rows.size());
+    if (std::all_of(rows.begin(), rows.end(), [&](const std::vector<size_t>& r) { return r.size() == rows[0].size(); }))
+      return fixed_width(std::move(rows), dense_len);
+    return ragged(std::move(rows), dense_len);
+  }
+  static SparseMaskBatch ragged(std::vector<std::vector<size_t>> rows, size_t dense_len) {
+    ensure(dense_len > 0, "dense token count must be nonzero");
+    ensure(!rows.empty(), "ragged sparse mask batch must be non-empty");
+    SparseMaskBatch m;
+    m.kind_ = Kind::Ragged;
+    m.dense_len_ = dense_len;
+    for (auto& row : rows) {
+      std::sort(row.begin(), row.end());
+      row.erase(std::unique(row.begin(), row.end()), row.end());
+      ensure(!row.empty(), "ragged sparse mask rows must be non-empty");
+      ensure(std::all_of(row.begin(), row.end(), [&](size_t i) { return i < dense_len; }),
+             "sparse token index outside dense token range");
+      m.lengths_.push_back(row.size());
+    }
+    m.rows_ = std::move(rows);
+    return m;
+  }
+
+  size_t batch() const { return rows_.size(); }
+  size_t dense_len() const { return dense_len_; }
+  size_t len() const { return lengths_.empty() ? 0 : *std::max_element(lengths_.begin(), lengths_.end()); }
+  bool is_empty() const { return len() == 0; }
+  bool is_uniform() const { return kind_ == Kind::Uniform; }
+  bool is_ragged() const { return kind_ == Kind::Ragged; }
+  bool is_dense_ordered() const {
+    if (kind_ == Kind::Ragged) return false;
+    return std::all_of(rows_.begin(), rows_.end(), [&](const std::vector<size_t>& r) {
+      if (r.size() != dense_len_) return false;
+      for (size_t i = 0; i < r.size(); ++i)
+        if (r[i] != i) return false;
+      return true;
+    });
+  }
+  size_t valid_token_count() const {
+    size_t n = 0;
+    for (size_t l : lengths_) n += l;
+    return n;
+  }
+  std::optional<SparseTokenMask> uniform_mask() const {
+    if (kind_ != Kind::Uniform) return std::nullopt;
+    return SparseTokenMask::new_(rows_[0], dense_len_);
+  }
+  SparseTokenMask first_mask() const { return SparseTokenMask::new_(rows_[0], dense_len_); }
+  const std::vector<std::vector<size_t>>& rows() const { return rows_; }
+  // every row padded to len() with its last index (padded_rows_from_normalized, :444-454)
+  std::vector<std::vector<size_t>> padded_rows() const {
+    std::vector<std::vector<size_t>> out = rows_;
+    const size_t w = len();
+    for (auto& r : out)
+      if (!r.empty()) r.resize(w, r.back());
+    return out;
+  }
+  // 1 for a row's own tokens, 0 for its padding ([batch, len()]); ragged batches only (:405-426)
+  std::optional<std::vector<float>> valid_token_mask() const {
+    if (kind_ != Kind::Ragged) return std::nullopt;
+    const size_t w = len();
+    std::vector<float> v;
+    for (size_t l : lengths_)
+      for (size_t i = 0; i < w; ++i) v.push_back(i < l ? 1.0f : 0.0f);
+    return v;
+  }
+  Tensor indices_tensor(cudaStream_t st = nullptr) const {
+    std::vector<int32_t> flat;
+    for (const auto& r : padded_rows())
+      for (size_t i : r) flat.push_back((int32_t)i);
+    return Tensor::from_host(flat, {(int64_t)batch(), (int64_t)len()}, BJF_DTYPE_I32, st);
+  }
+
+ private:
+  Kind kind_ = Kind::Uniform;
+  size_t dense_len_ = 0;
+  std::vector<std::vector<size_t>> rows_;
+  std::vector<size_t> lengths_;
+};
+
 class SparsePatchifyBatchPlan {
  public:
+  // SparsePatchifyBatchPlan::new (src/sparse_patchify.rs:290-327)
+  static SparsePatchifyBatchPlan new_(const SparseMaskBatch& mask, TokenGridShape grid, cudaStream_t st = nullptr) {
+    ensure(mask.batch() > 0, "sparse patchify batch must be nonzero");
+    ensure(!mask.is_ragged(),
+           "sparse patchify batch plans require uniform or fixed-width masks; use ragged rollout grouping");
+    ensure(mask.dense_len() == grid.len(), "sparse patchify batch mask dense token count must match grid");
+    return from_rows(mask.rows(), grid, st);
+  }
   static SparsePatchifyBatchPlan from_rows(std::vector<std::vector<size_t>> rows, TokenGridShape grid,
                                            cudaStream_t st = nullptr) {
     ensure(!rows.empty(), "sparse patchify batch must be nonzero");

@@ -208,6 +208,41 @@ TEST(viewer_config_derives_the_patch_diff_selection) {
   CHECK(!PatchDiffRefreshConfig::disabled().can_add_tokens());
 }
 
+// src/tokens.rs:180-442 (SparseMaskBatch) and src/sparse_patchify.rs:290-300: uniform,
+// fixed-width and ragged batches, their normalisation, padding and errors
+TEST(sparse_mask_batch_kinds_padding_and_errors) {
+  const auto u = SparseMaskBatch::from_rows({{3, 0}, {3, 0}}, 8);
+  CHECK(u.is_uniform() && !u.is_ragged());
+  // rows compare before they are sorted, as in the reference: equal sets in another order
+  // make a fixed-width batch
+  CHECK(!SparseMaskBatch::from_rows({{3, 0}, {0, 3}}, 8).is_uniform());
+  CHECK_EQ(u.batch(), (size_t)2);
+  CHECK_EQ(u.len(), (size_t)2);
+  CHECK_EQ(u.valid_token_count(), (size_t)4);
+  CHECK_EQ(u.rows()[1], (std::vector<size_t>{0, 3}));
+  const auto f = SparseMaskBatch::from_rows({{5, 1}, {2, 7}}, 8);
+  CHECK(!f.is_uniform() && !f.is_ragged());
+  CHECK_EQ(f.rows()[0], (std::vector<size_t>{1, 5}));
+  CHECK(!f.valid_token_mask().has_value());
+  const auto r = SparseMaskBatch::from_rows({{4, 1, 6}, {2}}, 8);
+  CHECK(r.is_ragged());
+  CHECK_EQ(r.len(), (size_t)3);
+  CHECK_EQ(r.valid_token_count(), (size_t)4);
+  CHECK_EQ(r.padded_rows()[1], (std::vector<size_t>{2, 2, 2}));
+  CHECK_EQ(*r.valid_token_mask(), (std::vector<float>{1, 1, 1, 1, 0, 0}));
+  CHECK(!r.is_dense_ordered());
+  CHECK(SparseMaskBatch::uniform(SparseTokenMask::all(4), 3).is_dense_ordered());
+  CHECK_THROWS_WITH(SparseMaskBatch::uniform(SparseTokenMask::all(4), 0), "sparse mask batch must be non-empty");
+  CHECK_THROWS_WITH(SparseMaskBatch::fixed_width({{1, 1}}, 4), "fixed-width sparse mask row contains duplicate indices");
+  CHECK_THROWS_WITH(SparseMaskBatch::fixed_width({{1, 2}, {3}}, 4), "fixed-width sparse mask rows must have equal lengths");
+  CHECK_THROWS_WITH(SparseMaskBatch::ragged({{1}, {}}, 4), "ragged sparse mask rows must be non-empty");
+  CHECK_THROWS_WITH(SparseMaskBatch::ragged({{9}}, 4), "sparse token index outside dense token range");
+  CHECK_THROWS_WITH(SparsePatchifyBatchPlan::new_(r, TokenGridShape(2, 2, 2)),
+                    "sparse patchify batch plans require uniform or fixed-width masks; use ragged rollout grouping");
+  CHECK_THROWS_WITH(SparsePatchifyBatchPlan::new_(f, TokenGridShape(1, 2, 2)),
+                    "sparse patchify batch mask dense token count must match grid");
+}
+
 // src/positional.rs:104-111
 TEST(sparse_positional_encoding_has_expected_shape) {
   const auto values = sparse_3d_sincos_pos_embed(10, TokenGridShape(2, 2, 2), {0, 7});
