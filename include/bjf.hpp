@@ -33,6 +33,7 @@
 
 #include <algorithm>
 #include <array>
+#include <memory>
 #include <optional>
 #include <cmath>
 #include <cstdint>
@@ -1224,6 +1225,42 @@ class SparsePatchifyBatchPlan {
   size_t batch = 0, width = 0;
   Tensor coords;
   std::vector<std::array<uint32_t, 4>> coords_host;
+};
+
+// The plan caches of the stream drivers (ensure_patchify_plan, src/temporal.rs:325-345, and
+// cached_sparse_patchify_batch_plan, src/highres_pipeline.rs:2768-2793): a plan is rebuilt (and
+// its coordinates uploaded) only when the mask rows, the grid or the batch change.
+class SparsePatchifyPlanCache {
+ public:
+  // True when the cached plan already matches (nothing is rebuilt).
+  bool ensure(const SparseTokenMask& mask, TokenGridShape grid, size_t batch, cudaStream_t st = nullptr) {
+    if (plan_ && plan_->grid == grid && plan_->batch == batch && plan_->mask.dense_len() == mask.dense_len() &&
+        plan_->mask.indices() == mask.indices())
+      return true;
+    plan_ = std::make_unique<SparsePatchifyPlan>(SparsePatchifyPlan::new_(mask, grid, batch, st));
+    return false;
+  }
+  const SparsePatchifyPlan& plan() const {
+    bjf::ensure(plan_ != nullptr, "sparse patchify plan cache is empty");
+    return *plan_;
+  }
+  void reset() { plan_.reset(); }
+
+ private:
+  std::unique_ptr<SparsePatchifyPlan> plan_;
+};
+
+class SparsePatchifyBatchPlanCache {
+ public:
+  const SparsePatchifyBatchPlan& get(const SparseMaskBatch& mask, TokenGridShape grid, cudaStream_t st = nullptr) {
+    if (!(plan_ && plan_->grid == grid && plan_->rows == mask.rows()))
+      plan_ = std::make_unique<SparsePatchifyBatchPlan>(SparsePatchifyBatchPlan::new_(mask, grid, st));
+    return *plan_;
+  }
+  void reset() { plan_.reset(); }
+
+ private:
+  std::unique_ptr<SparsePatchifyBatchPlan> plan_;
 };
 
 // ---------------------------------------------------------------------------------------

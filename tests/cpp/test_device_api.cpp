@@ -197,6 +197,27 @@ TEST(encoder_sparse_patchify_methods_check_the_plan_and_reshape) {
   CHECK_THROWS_WITH(enc.sparse_patchify_image_cuda(im, plan, iw, nullptr), "image token grid does not match sparse patchify plan");
 }
 
+// src/temporal.rs:325-345, src/highres_pipeline.rs:2768-2793: plans are rebuilt only when the
+// mask rows, the grid or the batch change
+TEST(plan_caches_rebuild_only_on_change) {
+  const TokenGridShape grid(2, 3, 4);
+  SparsePatchifyPlanCache cache;
+  CHECK(!cache.ensure(SparseTokenMask::new_({0, 7, 23}, grid.len()), grid, 2));
+  CHECK(cache.ensure(SparseTokenMask::new_({23, 7, 0}, grid.len()), grid, 2));  // the same mask
+  CHECK_EQ(cache.plan().coords_host.size(), (size_t)6);
+  CHECK(!cache.ensure(SparseTokenMask::new_({0, 7}, grid.len()), grid, 2));
+  CHECK(!cache.ensure(SparseTokenMask::new_({0, 7}, grid.len()), grid, 1));
+  CHECK_EQ(cache.plan().coords.to_host<int32_t>(), (std::vector<int32_t>{0, 0, 0, 0, 0, 0, 1, 3}));
+  SparsePatchifyBatchPlanCache bcache;
+  const auto& p1 = bcache.get(SparseMaskBatch::from_rows({{0, 1}, {2, 3}}, grid.len()), grid);
+  const void* first = &p1;
+  const auto& p2 = bcache.get(SparseMaskBatch::from_rows({{1, 0}, {3, 2}}, grid.len()), grid);
+  CHECK(&p2 == first);  // same rows after normalisation: reused
+  CHECK_EQ(p2.coords_host.size(), (size_t)4);
+  cache.reset();
+  CHECK_THROWS_WITH(cache.plan(), "sparse patchify plan cache is empty");
+}
+
 // The tensor-core path (f16 and bf16 operands, f32 accumulation) on a fixed-width batch plan,
 // against the oracle evaluated on the same rounded inputs; normwise relative error <= 1e-2.
 static void half_patchify_case(bjf_dtype dt) {
