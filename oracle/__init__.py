@@ -571,6 +571,158 @@ def viewer_patch_diff_masks_from_rgba(prev, current, width: int, patch_size: int
                                                bucket_densities)
 
 
+def density_tokens(dense_tokens: int, density: float, rounding: str, min_density: float) -> int:
+    """density_tokens (src/viewer.rs:739-752) with f32 arithmetic; rounding in floor/round/ceil."""
+    d = np.float32(density)
+    d = np.float32(min(max(d, np.float32(min_density)), np.float32(1.0))) if not np.isnan(d) else d
+    x = np.float32(dense_tokens) * d
+    r = {"floor": np.floor, "ceil": np.ceil}.get(rounding)
+    v = r(x) if r else np.float32(np.sign(x) * np.floor(np.abs(x) + np.float32(0.5)))  # half away from zero
+    t = int(v) if np.isfinite(v) and v > 0 else 0
+    return min(max(t, 1), max(dense_tokens, 1))
+
+
+def patch_diff_sparsity_config(context_density: float, min_context_density: float, threshold: float,
+                               dilation: int, grid: "TokenGridShape") -> "PatchDiffConfig":
+    """patch_diff_sparsity_config (src/viewer.rs:1012-1028) for the viewer fields it reads."""
+    n = len(grid)
+    max_ctx = density_tokens(n, context_density, "round", 0.01)
+    min_ctx = min(density_tokens(n, min_context_density, "ceil", 0.0), max_ctx)
+    target = max(n - max_ctx, 1)
+    return PatchDiffConfig.adaptive_threshold(threshold, min_ctx, max_ctx, target).with_dilation(dilation)
+
+
+def _mix64(v: int) -> int:
+    """mix64 (src/viewer.rs:530-536)."""
+    m = (1 << 64) - 1
+    v ^= v >> 30
+    v = (v * 0xBF58476D1CE4E5B9) & m
+    v ^= v >> 27
+    v = (v * 0x94D049BB133111EB) & m
+    return v ^ (v >> 31)
+
+
+class PatchDiffRefreshState:
+    """PatchDiffRefreshState (src/viewer.rs:272-528) over host scores; `refresh` is a dict of the
+    PatchDiffRefreshConfig fields (src/viewer.rs:186-241)."""
+
+    DEFAULTS = dict(enabled=False, subthreshold_enabled=False, subthreshold_decay=0.92, subthreshold_gain=1.0,
+                    subthreshold_trigger=1.0, subthreshold_max_density=0.04, age_refresh_enabled=False,
+                    age_refresh_interval_frames=90, age_refresh_max_density=0.01, blue_noise_enabled=False,
+                    blue_noise_refresh_density=0.005, blue_noise_seed=0x9E3779B97F4A7C15, max_extra_density=0.05)
+
+    def __init__(self):
+        self.dense_len = 0
+        self.frame_index = 0
+        self.residual = np.zeros(0, np.float32)
+        self.age = np.zeros(0, np.uint32)
+
+    @staticmethod
+    def can_add_tokens(c) -> bool:
+        return (c["enabled"] and c["max_extra_density"] > 0.0
+                and ((c["subthreshold_enabled"] and c["subthreshold_max_density"] > 0.0)
+                     or (c["age_refresh_enabled"] and c["age_refresh_interval_frames"] > 0
+                         and c["age_refresh_max_density"] > 0.0)
+                     or (c["blue_noise_enabled"] and c["blue_noise_refresh_density"] > 0.0)))
+
+    def _begin_frame(self, n):
+        if self.dense_len != n:
+            self.dense_len, self.frame_index = n, 0
+            self.residual = np.zeros(n, np.float32)
+            self.age = np.zeros(n, np.uint32)
+        self.frame_index += 1
+        self.age = np.minimum(self.age.astype(np.uint64) + 1, 0xFFFFFFFF).astype(np.uint32)
+
+    def _reset_selected(self, idx):
+        idx = np.asarray(idx, dtype=np.int64)
+        self.residual[idx] = 0.0
+        self.age[idx] = 0
+
+    def _rank(self, index, grid, seed):
+        m = (1 << 64) - 1
+        w = max(grid.width, 1)
+        row, col = index // w, index % w
+        return _mix64(seed ^ ((row * 0x9E3779B97F4A7C15) & m) ^ ((col * 0xBF58476D1CE4E5B9) & m)
+                      ^ ((self.frame_index * 0x94D049BB133111EB) & m))
+
+    def _update_residual(self, scores, chosen, threshold, c):
+        sel = np.zeros(len(scores), bool)
+        sel[np.asarray(chosen, dtype=np.int64)] = True
+        decay = np.float32(min(max(c["subthreshold_decay"], 0.0), 1.0))
+        th = np.float32(max(np.float32(threshold), np.float32(1e-6)))
+        gain = np.float32(max(c["subthreshold_gain"], 0.0))
+        for i in range(len(scores)):
+            if sel[i] or scores[i] >= np.float32(threshold):
+                self.residual[i] = 0.0
+            else:
+                norm = np.float32(min(max(scores[i] / th, np.float32(0.0)), np.float32(1.0)))
+                self.residual[i] = np.float32(np.float32(self.residual[i] * decay) + np.float32(norm * gain))
+
+    def _add_ranked(self, selected, indices, budget, rank):
+        if budget == 0:
+            return 0
+        cands = []
+        for i in range(len(selected)):
+            if not selected[i]:
+                r = rank(i)
+                if r is not None:
+                    cands.append((i, r[0], r[1]))
+        cands.sort(key=lambda t: (-t[1], t[2], t[0]))
+        cands = cands[:budget]
+        for i, _, _ in cands:
+            selected[i] = True
+            indices.append(i)
+        return len(cands)
+
+    def _augment(self, base, scores, grid, config, c):
+        n = len(grid)
+        if len(base) >= n:
+            return base
+        remaining = max(min(max(config.context_tokens, 1), n) - len(base), 0)
+        remaining = min(remaining, density_tokens(n, c["max_extra_density"], "floor", 0.0))
+        if remaining == 0:
+            self._update_residual(scores, base, config.threshold, c)
+            return base
+        selected = np.zeros(n, bool)
+        indices = [int(i) for i in base]
+        selected[np.asarray(indices, dtype=np.int64)] = True
+        self._update_residual(scores, indices, config.threshold, c)
+        seed = c["blue_noise_seed"]
+        if c["subthreshold_enabled"] and c["subthreshold_max_density"] > 0.0:
+            budget = min(remaining, density_tokens(n, c["subthreshold_max_density"], "floor", 0.0))
+            trig = max(np.float32(c["subthreshold_trigger"]), np.float32(1e-6))
+            remaining -= self._add_ranked(selected, indices, budget, lambda i: (float(self.residual[i]),
+                                          self._rank(i, grid, seed)) if self.residual[i] >= trig else None)
+        if (remaining > 0 and c["age_refresh_enabled"] and c["age_refresh_interval_frames"] > 0
+                and c["age_refresh_max_density"] > 0.0):
+            interval = min(c["age_refresh_interval_frames"], 0xFFFFFFFF)
+            budget = min(remaining, density_tokens(n, c["age_refresh_max_density"], "floor", 0.0))
+            remaining -= self._add_ranked(selected, indices, budget, lambda i: (float(self.age[i]),
+                                          self._rank(i, grid, seed)) if self.age[i] >= interval else None)
+        if remaining > 0 and c["blue_noise_enabled"] and c["blue_noise_refresh_density"] > 0.0:
+            budget = min(remaining, density_tokens(n, c["blue_noise_refresh_density"], "floor", 0.0))
+            self._add_ranked(selected, indices, budget, lambda i: (0.0, self._rank(i, grid, seed)))
+        return sparse_token_mask_new(indices, n)
+
+    def masks_from_scores(self, scores, grid, config, dense_fallback_density, refresh, bucketed=True,
+                          bucket_tokens=256, bucket_densities=(0.10, 0.25, 0.50)):
+        """masks_from_scores (src/viewer.rs:312-347): (write mask, encode mask)."""
+        c = dict(self.DEFAULTS, **refresh)
+        scores = np.asarray(scores, dtype=np.float32)
+        n = len(grid)
+        if scores.size != n:
+            raise OracleError("patch-diff refresh received unexpected score length")
+        direct = patch_diff_context_mask_from_scores(scores, grid, config.with_dilation(0))
+        base = dilate_sparse_patch_mask(patch_diff_dense_fallback(direct, n, dense_fallback_density), grid,
+                                        config.dilation)
+        self._begin_frame(n)
+        if self.can_add_tokens(c) and not (len(base) == n):
+            base = self._augment(base, scores, grid, config, c)
+        enc = finalize_patch_diff_encode_masks(base, n, bucketed, bucket_tokens, bucket_densities)
+        self._reset_selected(base)
+        return np.asarray(base, dtype=np.int64), enc
+
+
 def front_end_streams(video, config: PatchifyConfig, mask_config: PatchDiffConfig, weight, bias,
                       caches, observed, age_frames, age_observed: bool) -> np.ndarray:
     """One front-end step over S independent streams (f32), in place on the caches."""

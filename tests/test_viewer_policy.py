@@ -344,3 +344,66 @@ def test_device_rgba_mask_node_errors(cuda_device):
         bj.viewer_patch_diff_masks_from_rgba(prev, prev, 16, (2, 4, 4), cfg, pol)
     with pytest.raises(bj.BjfError, match="frame size must match"):
         bj.viewer_patch_diff_masks_from_rgba(prev, prev, 16, (1, 4, 3), cfg, pol)
+
+
+# ---------------------------------------------------------------------------
+# Refresh state (src/viewer.rs:272-528), the oracle against the reference's own tests
+# ---------------------------------------------------------------------------
+
+def _refresh_case(context_density, refresh):
+    grid = oracle.TokenGridShape(1, 4, 4)
+    cfg = oracle.patch_diff_sparsity_config(context_density, 0.0, 0.10, 0, grid)
+    return grid, cfg, dict(refresh)
+
+
+def test_oracle_subthreshold_refresh_accumulates_slow_motion():
+    # src/viewer.rs:1528-1575
+    grid, cfg, refresh = _refresh_case(0.25, dict(enabled=True, subthreshold_enabled=True, subthreshold_decay=1.0,
+                                                  subthreshold_trigger=1.0, subthreshold_max_density=0.25,
+                                                  max_extra_density=0.25))
+    slow = 2 * 4 + 1
+    scores = np.zeros(16, np.float32)
+    scores[0] = 0.09
+    scores[slow] = 0.04
+    st = oracle.PatchDiffRefreshState()
+    assert slow not in st.masks_from_scores(scores, grid, cfg, 1.0, refresh, bucketed=False)[0].tolist()
+    assert slow not in st.masks_from_scores(scores, grid, cfg, 1.0, refresh, bucketed=False)[0].tolist()
+    assert slow in st.masks_from_scores(scores, grid, cfg, 1.0, refresh, bucketed=False)[0].tolist()
+    assert st.residual[slow] == 0.0 and st.age[slow] == 0
+
+
+def test_oracle_subthreshold_refresh_fills_only_unused_budget():
+    # src/viewer.rs:1595-1632
+    grid, cfg, refresh = _refresh_case(2.0 / 16.0, dict(enabled=True, subthreshold_enabled=True,
+                                                        subthreshold_decay=1.0, subthreshold_trigger=0.5,
+                                                        subthreshold_max_density=1.0, max_extra_density=1.0))
+    scores = np.full(16, 0.06, np.float32)
+    scores[0] = 0.09
+    w, _ = oracle.PatchDiffRefreshState().masks_from_scores(scores, grid, cfg, 1.0, refresh, bucketed=False)
+    assert len(w) == 2
+
+
+def test_oracle_age_priority_refresh_selects_stale_tokens():
+    # src/viewer.rs:1634-1672
+    grid, cfg, refresh = _refresh_case(0.5, dict(enabled=True, age_refresh_enabled=True,
+                                                 age_refresh_interval_frames=2, age_refresh_max_density=0.25,
+                                                 max_extra_density=0.25))
+    scores = np.zeros(16, np.float32)
+    scores[0] = 0.09
+    st = oracle.PatchDiffRefreshState()
+    first, _ = st.masks_from_scores(scores, grid, cfg, 1.0, refresh, bucketed=False)
+    second, _ = st.masks_from_scores(scores, grid, cfg, 1.0, refresh, bucketed=False)
+    assert len(first) == 1 and len(second) > len(first)
+
+
+def test_oracle_blue_noise_refresh_is_deterministic():
+    # src/viewer.rs:1674-1703
+    grid, cfg, refresh = _refresh_case(0.5, dict(enabled=True, blue_noise_enabled=True,
+                                                 blue_noise_refresh_density=0.25, max_extra_density=0.25,
+                                                 blue_noise_seed=7))
+    scores = np.zeros(16, np.float32)
+    a, _ = oracle.PatchDiffRefreshState().masks_from_scores(scores, grid, cfg, 1.0, refresh, bucketed=False)
+    b, _ = oracle.PatchDiffRefreshState().masks_from_scores(scores, grid, cfg, 1.0, refresh, bucketed=False)
+    assert a.tolist() == b.tolist() and len(a) > 0
+    assert oracle.density_tokens(16, 0.25, "floor", 0.0) == 4
+    assert oracle.density_tokens(1000, 0.1234, "ceil", 0.0) == 124
