@@ -7,7 +7,7 @@ active tubelets -> in-place write into the stream's persistent f16 token cache [
 (pre-filled N(0, 1)).  A "step" is one pass of that front end over every stream of the GPU.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--density D]
-                  [--sweep]
+                  [--sweep] [--no-rows]
 
 For N > 1 it is launched by torch.distributed.run, one process per GPU; streams are
 sharded with no data-path collective (streams share nothing), and timings are the max
@@ -17,6 +17,10 @@ value: active tubelets/s with the clips already resident in HBM (two input sets 
 per GPU alternate, so every step reads its clips from HBM, not L2).
 e2e:   the same metric through the public API with host buffers: every step copies its
 clips from pinned host memory, runs the step and reads the per-stream active counts back.
+rows:  (one GPU) every row of the path timed alone through its public entry point against its
+roofline: the selection, the device plan, the standalone cache updates, the RGBA viewer scorer
+and mask node, and the gather-GEMM on the ViT-g batch (32 x [3,16,512,512] bf16, 131 072 rows,
+D = 1408) plain and with the encoder-input epilogue.
 --impl reference: the reference's CPU algorithm (the C restatement in oracle/, f32 as on
 the reference's NdArray backend) on all host threads, over a bounded sample of streams.
 """
@@ -53,6 +57,10 @@ GRID = (T // KT, H // P, W // P)
 N_TOKENS = GRID[0] * GRID[1] * GRID[2]
 
 
+ROW_FLUSH_BYTES = 256 << 20  # written before every standalone row call: twice the 126 MB L2
+VITG = dict(B=32, C=3, T=16, H=512, W=512, KT=2, P=16, D=1408)  # the ViT-g batch
+
+
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -66,6 +74,8 @@ def parse_args():
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--load-seconds", type=float, default=2.0,
                     help="back-to-back steps before the timed ones, for the clock sampler (0 under a profiler)")
+    ap.add_argument("--no-rows", action="store_true",
+                    help="skip the standalone timings of each row of the path (one GPU only)")
     return ap.parse_args()
 
 
@@ -204,6 +214,144 @@ def make_inputs(torch, dev, streams, density, seed_base):
                                                          density, dev, torch.float16) for gs in streams]
         sets.append(torch.cat(clips))
     return sets
+
+
+def time_rows(torch, bj, dev, videos, weight, bias, mask_cfg, hbm_peak, tflops_peak, reps=10):
+    """Each row of the path timed alone through its public entry point, with CUDA events on the
+    launching stream.  Before every call 256 MB are written (L2 flushed) and the device sleeps
+    while the host enqueues the call, so the events bracket device work only.  Returns
+    {name: {row, workload, bound, avg_ms, achieved, unit, peak, frac, ...}}."""
+    import numpy as np
+
+    from burn_jepa_b200 import workloads
+
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(ROW_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
+    out = {}
+
+    def timed(fn):
+        for i in range(3):
+            fn(i)
+        torch.cuda.synchronize()
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
+        for i, (a, b) in enumerate(evs):
+            flush.zero_()
+            torch.cuda._sleep(100_000)
+            a.record(stream)
+            fn(i)
+            b.record(stream)
+        torch.cuda.synchronize()
+        assert not bj.device_error_check(), "a kernel reported a bounded-wait timeout"
+        return statistics.mean(a.elapsed_time(b) for a, b in evs)
+
+    def hbm(name, row, workload, ms, nbytes, **extra):
+        gbs = nbytes / (ms / 1e3) / 1e9
+        out[name] = {"row": row, "workload": workload, "bound": "hbm", "avg_ms": round(ms, 4),
+                     "algorithmic_bytes": int(nbytes), "achieved": round(gbs, 1), "unit": "GB/s", "peak": hbm_peak,
+                     "frac": round(gbs / hbm_peak, 4), **extra}
+
+    def tensor(name, row, workload, ms, flops, **extra):
+        tf = flops / (ms / 1e3) / 1e12
+        out[name] = {"row": row, "workload": workload, "bound": "tensor", "avg_ms": round(ms, 4),
+                     "algorithmic_flops": int(flops), "achieved": round(tf, 1), "unit": "TFLOP/s",
+                     "peak": tflops_peak, "frac": round(tf / tflops_peak, 4), **extra}
+
+    def latency(name, row, workload, ms, **extra):
+        out[name] = {"row": row, "workload": workload, "bound": "latency", "avg_ms": round(ms, 4), **extra}
+
+    S = videos[0].shape[0]
+    live = f"{S} streams, grid {GRID[0]}x{GRID[1]}x{GRID[2]}"
+
+    # a2: selection (+ nothing else) on one step's scores
+    sc = bj.patch_diff_token_scores(videos[0].unsqueeze(1), KT, P)
+    idx = torch.empty((S, N_TOKENS), dtype=torch.int32, device=dev)
+    cnt = torch.empty((S,), dtype=torch.int32, device=dev)
+    ms = timed(lambda i: bj.patch_diff_context_mask_from_scores(sc, GRID, mask_cfg, indices=idx, counts=cnt))
+    active = int(cnt.sum().item())
+    latency("patch_diff_select", "a2", live, ms, active_tokens=active)
+
+    # a4 / f2: device plan from the selection
+    coords = torch.empty((S * N_TOKENS, 4), dtype=torch.int32, device=dev)
+    total = torch.empty((1,), dtype=torch.int32, device=dev)
+    ms = timed(lambda i: bj.sparse_patchify_plan_coords(idx, GRID, batch=S, counts=cnt, capacity=S * N_TOKENS,
+                                                        coords=coords, total_rows=total))
+    latency("plan_coords", "a4", live, ms, rows=int(total.item()))
+
+    # a6 / f3: standalone cache updates, 410 of 4096 tokens per stream (10 %), f16 tokens and cache
+    width = 410
+    rng = np.random.default_rng(21)
+    ti = np.stack([np.sort(rng.choice(N_TOKENS, width, replace=False)) for _ in range(S)]).astype(np.int32)
+    tok_idx = torch.from_numpy(ti).to(dev)
+    tokens = torch.randn((S, width, D), device=dev).to(torch.float16)
+    feats = torch.randn((S, N_TOKENS, D), device=dev).to(torch.float16)
+    observed = torch.zeros((S, N_TOKENS), device=dev)
+    age = torch.zeros((S, N_TOKENS), device=dev)
+    m = S * width
+    aging = S * N_TOKENS * 12  # read observed and age, write age
+    wl = f"{S} streams x {width} of {N_TOKENS} tokens, D={D}, f16 tokens -> f16 cache"
+    ms = timed(lambda i: bj.feature_memory_assign_latest(feats, observed, age, tokens, tok_idx, True))
+    hbm("feature_memory_assign_latest", "a6", wl, ms, m * D * 4 + m * 4 + aging + m * 8)
+    ms = timed(lambda i: bj.feature_memory_update_ema(feats, observed, age, tokens, tok_idx, 0.5, True))
+    hbm("feature_memory_update_ema", "f3", wl, ms, m * D * 6 + m * 4 + aging + m * 8)
+    reset = torch.tensor([1, 7, 19, 30], dtype=torch.int32, device=dev)
+    ms = timed(lambda i: bj.feature_memory_reset_rows(feats, observed, age, reset))
+    hbm("feature_memory_reset_rows", "f3", f"4 of {S} stream caches [{N_TOKENS},{D}] f16 zeroed", ms,
+        4 * N_TOKENS * (D * 2 + 8))
+    del tokens, feats, observed, age
+
+    # f1: the live viewer's RGBA scorer and mask node on the same streams' frames as RGBA u8
+    def rgba(f):
+        x = (videos[0][:, :, f].float().clamp(0, 1) * 255).round().to(torch.uint8).permute(0, 2, 3, 1)
+        return torch.cat([x, torch.full_like(x[..., :1], 255)], dim=3).contiguous()
+
+    prev, cur = rgba(0), rgba(1)
+    vgrid = (1, H // P, W // P)
+    wl = f"{S} streams x {W}x{H} RGBA u8 frame pairs, {P}x{P} patches"
+    ms = timed(lambda i: bj.patch_diff_scores_from_rgba(prev, cur, P, vgrid))
+    hbm("rgba_patch_diff_scores", "f1", wl, ms, 2 * prev.numel() + 4 * S * vgrid[1] * vgrid[2])
+    vcfg = bj.PatchDiffConfig.adaptive_threshold(0.03, 0, vgrid[1] * vgrid[2], 1).with_dilation(1)
+    policy = bj.ViewerMaskPolicy.new()
+    res = {}
+    ms = timed(lambda i: res.update(m=bj.viewer_patch_diff_masks_from_rgba(prev, cur, P, vgrid, vcfg, policy)))
+    wi, wc, ei, ec = res["m"]
+    latency("viewer_patch_diff_masks_from_rgba", "f1", wl + ", threshold 0.03, dilation 1, the viewer's default "
+            "dense fallback and encode buckets", ms,
+            write_density=round(float(wc.sum().item()) / (S * vgrid[1] * vgrid[2]), 4),
+            encode_density=round(float(ec.sum().item()) / (S * vgrid[1] * vgrid[2]), 4))
+    del prev, cur
+
+    # a5 / f4: the ViT-g batch, a shared 4096-of-8192 multiblock mask, bf16
+    v = VITG
+    g = torch.Generator(device=dev).manual_seed(602)
+    clip = torch.empty((v["B"], v["C"], v["T"], v["H"], v["W"]), dtype=torch.bfloat16, device=dev)
+    for b in range(v["B"]):
+        clip[b] = ((torch.rand(clip.shape[1:], generator=g, device=dev) - 0.45) / 0.225).to(torch.bfloat16)
+    ggrid = (v["T"] // v["KT"], v["H"] // v["P"], v["W"] // v["P"])
+    gn = ggrid[0] * ggrid[1] * ggrid[2]
+    gmask = workloads.multiblock_mask(601, *ggrid, gn // 2)
+    gcoords, gtotal = bj.sparse_patchify_plan_coords(torch.from_numpy(gmask.astype(np.int32)).to(dev), ggrid,
+                                                     batch=v["B"])
+    rows = int(gtotal.item())
+    gcoords = gcoords[:rows].contiguous()
+    gk = v["C"] * v["KT"] * v["P"] * v["P"]
+    gw = torch.from_numpy(workloads.normal(603, (v["D"], v["C"], v["KT"], v["P"], v["P"]), std=0.02)).to(
+        dev, torch.bfloat16)
+    gb = torch.from_numpy(workloads.normal(604, (v["D"],), std=0.02)).to(dev)
+    gout = torch.empty((rows, v["D"]), dtype=torch.bfloat16, device=dev)
+    pcfg = bj.PatchifyConfig(v["C"], v["D"], v["T"], v["H"], v["W"], v["KT"], v["P"], v["P"])
+    wl = (f"{v['B']} clips [{v['C']},{v['T']},{v['H']},{v['W']}] bf16, {rows} rows (4096 of 8192 tokens each), "
+          f"K={gk}, D={v['D']}, bf16 out")
+    ms = timed(lambda i: bj.sparse_patchify3d_forward(pcfg, clip, gcoords, gw, gb, out=gout))
+    tensor("gather_gemm_vitg_batch", "a5", wl, ms, 2 * rows * gk * v["D"], rows=rows)
+    pos = torch.randn((gn, v["D"]), device=dev) * 0.02
+    modality = torch.randn((v["D"],), device=dev) * 0.02
+    ms = timed(lambda i: bj.sparse_patchify3d_forward_encoder_input(pcfg, clip, gcoords, gw, gb, position_table=pos,
+                                                                     modality_embed=modality, out=gout))
+    tensor("gather_gemm_vitg_encoder_input", "f4", wl + ", + position table row + modality vector", ms,
+           2 * rows * gk * v["D"], rows=rows)
+    del clip, gout, flush
+    torch.cuda.empty_cache()
+    return out
 
 
 def run_ours(args, world, rank, local):
@@ -377,6 +525,10 @@ def run_ours(args, world, rank, local):
                 "ms_per_step": round(s2m / args.steps * 1e3, 4)}
             del videos2
 
+    rows = None
+    if world == 1 and not args.no_rows:
+        rows = time_rows(torch, bj, dev, videos, weight, bias, fe.desc.mask, hbm_peak, tflops_peak)
+
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         import numpy as np
@@ -411,6 +563,8 @@ def run_ours(args, world, rank, local):
     }
     if sweep:
         result["density_sweep"] = sweep
+    if rows:
+        result["rows"] = rows
     if rank == 0:
         print(json.dumps(result), flush=True)
 

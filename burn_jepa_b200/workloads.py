@@ -9,6 +9,8 @@ frames.  These generators stand in for camera video:
 * ``normal`` -- patch-embed weights N(0, std^2).
 * ``choose_threshold`` -- a patch-diff threshold inside a wide score gap near a target density,
   so that a mask computed with a different summation order selects the same tokens.
+* ``multiblock_mask`` -- the ViT-g batch's shared mask: seeded 3-D blocks over the whole temporal
+  extent unioned to a token budget (the reference has no multiblock generator of its own).
 """
 from __future__ import annotations
 
@@ -165,3 +167,22 @@ def rect_perturbation_clips_torch(seed: int, streams: int, channels: int, frames
             frame += pert * m
             out[s, :, f] = frame.to(dtype)
     return out
+
+
+def multiblock_mask(seed: int, depth: int, height: int, width: int, keep: int) -> np.ndarray:
+    """Seeded blocks of spatial scale 0.15-0.2 of the frame and aspect 0.75-1.5, each over the
+    whole temporal extent, unioned until `keep` tokens are covered; returns the lowest `keep`
+    covered token indices (t * height * width + r * width + c), ascending."""
+    rng = np.random.default_rng(seed)
+    covered = np.zeros((height, width), bool)
+    while covered.sum() * depth < keep:
+        area = rng.uniform(0.15, 0.2) * height * width
+        aspect = rng.uniform(0.75, 1.5)
+        h = max(1, min(height, int(round(np.sqrt(area * aspect)))))
+        w = max(1, min(width, int(round(np.sqrt(area / aspect)))))
+        r0 = rng.integers(0, height - h + 1)
+        c0 = rng.integers(0, width - w + 1)
+        covered[r0:r0 + h, c0:c0 + w] = True
+    spatial = np.flatnonzero(covered.ravel())
+    idx = (np.arange(depth)[:, None] * height * width + spatial[None, :]).ravel()
+    return np.sort(idx)[:keep]

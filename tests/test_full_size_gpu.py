@@ -72,30 +72,12 @@ def test_live_streams_full_size_step(cuda_device):
         assert max_rel_err(got, ref) <= TOL_HALF, s
 
 
-def _multiblock_mask(seed, grid, keep):
-    # seeded 3-D blocks over the whole temporal extent, spatial scale 0.15-0.2 of the frame,
-    # aspect 0.75-1.5, unioned until `keep` tokens are covered (the lowest `keep` kept)
-    rng = np.random.default_rng(seed)
-    covered = np.zeros((grid.height, grid.width), bool)
-    while covered.sum() * grid.depth < keep:
-        area = rng.uniform(0.15, 0.2) * grid.height * grid.width
-        aspect = rng.uniform(0.75, 1.5)
-        h = max(1, min(grid.height, int(round(np.sqrt(area * aspect)))))
-        w = max(1, min(grid.width, int(round(np.sqrt(area / aspect)))))
-        r0 = rng.integers(0, grid.height - h + 1)
-        c0 = rng.integers(0, grid.width - w + 1)
-        covered[r0:r0 + h, c0:c0 + w] = True
-    spatial = np.flatnonzero(covered.ravel())
-    idx = (np.arange(grid.depth)[:, None] * grid.height * grid.width + spatial[None, :]).ravel()
-    return np.sort(idx)[:keep]
-
-
 def test_vitg_batch_full_size_patchify(cuda_device):
     import torch
 
     B, C, T, H, W, KT, P, D = 32, 3, 16, 512, 512, 2, 16, 1408
     grid = oracle.TokenGridShape(T // KT, H // P, W // P)
-    mask = _multiblock_mask(601, grid, len(grid) // 2)
+    mask = workloads.multiblock_mask(601, grid.depth, grid.height, grid.width, len(grid) // 2)
     assert len(mask) == 4096
     g = torch.Generator(device=cuda_device).manual_seed(602)
     video = torch.empty((B, C, T, H, W), dtype=torch.bfloat16, device=cuda_device)
