@@ -274,7 +274,7 @@ def patch_diff_scores_from_rgba(prev, current, patch_size: int, grid, stats: boo
     S, H, W, _ = prev.shape
     g = tuple(int(v) for v in (grid.depth, grid.height, grid.width)) if hasattr(grid, "depth") else tuple(grid)
     scores = torch.empty((S, g[1] * g[2]), dtype=torch.float32, device=prev.device)
-    nbytes = load().bjf_rgba_patch_diff_workspace_bytes(S)
+    nbytes = load().bjf_rgba_patch_diff_workspace_bytes(S, _abi.dims(*g))
     ws = torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=prev.device)
     st = torch.empty((S, ctypes.sizeof(RgbaFrameStats)), dtype=torch.uint8, device=prev.device) if stats else None
     check(load().bjf_rgba_patch_diff_scores(

@@ -206,12 +206,28 @@ __device__ __forceinline__ int4 next_row(const RowSource& rs, const int* soff, c
 // Encoder-input epilogue terms for 32 columns starting at col0 (ncol valid): + the row's
 // position embedding, then + the modality embedding (src/model.rs:690-703).  Rows without a
 // table row (zero rows) stay zero.  Warp-collective (the modality vector is broadcast).
+// kVec: 16-byte table loads for full aligned chunks.
+template <bool kVec>
 __device__ __forceinline__ void add_encoder_embeddings(const EpilogueArgs& ep, bool valid, const float* pos_row,
                                                        int col0, int ncol, int lane, float (&v)[32]) {
   if (pos_row) {
+    const float* p = pos_row + col0;
+    if (kVec && ncol == 32 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+      // each lane reads its own table row with 16-byte loads
+      const float4* p4 = reinterpret_cast<const float4*>(p);
 #pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j < ncol) v[j] = v[j] + __ldg(pos_row + col0 + j);
+      for (int j = 0; j < 8; ++j) {
+        const float4 q = __ldg(p4 + j);
+        v[4 * j] = v[4 * j] + q.x;
+        v[4 * j + 1] = v[4 * j + 1] + q.y;
+        v[4 * j + 2] = v[4 * j + 2] + q.z;
+        v[4 * j + 3] = v[4 * j + 3] + q.w;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j)
+        if (j < ncol) v[j] = v[j] + __ldg(p + j);
+    }
   }
   if (ep.modality_embed) {
     const float ml = lane < ncol ? __ldg(ep.modality_embed + col0 + lane) : 0.0f;
@@ -260,7 +276,7 @@ __device__ __forceinline__ void drain_accumulator(const GatherGeometry& g, const
       const float b = __shfl_sync(0xffffffffu, bl, j);
       v[j] = valid ? __uint_as_float(r[j]) + b : 0.0f;
     }
-    add_encoder_embeddings(ep, valid, pos_row, col0, ncol, lane, v);
+    add_encoder_embeddings<false>(ep, valid, pos_row, col0, ncol, lane, v);
     if (!dst_row) continue;
     char* dst = dst_row + (int64_t)col0 * ce;
     if (ep.out_dtype == BJF_DTYPE_F32)
@@ -579,6 +595,7 @@ __device__ __forceinline__ void pack_chunk32(uint8_t* dst, const float (&v)[32],
 // destination.  `stage` / `stage_smem` address this warp's staging buffers; `chunk` counts
 // this thread's staged chunks (selects the buffer).  Warp-collective.
 // Columns [c_begin, c_end) of the accumulator (c_begin a multiple of the chunk width).
+template <bool kEmbed>
 __device__ __forceinline__ void drain_accumulator_bulk(const GatherGeometry& g, const EpilogueArgs& ep, int4 c,
                                                        int M, int gm, int n0, int c_begin, int c_end, uint32_t taddr,
                                                        int lane, uint8_t* stage, uint32_t stage_smem, int& chunk) {
@@ -624,7 +641,7 @@ __device__ __forceinline__ void drain_accumulator_bulk(const GatherGeometry& g, 
         const float b = __shfl_sync(0xffffffffu, bl, j);
         v[j] = valid ? __uint_as_float(r[j]) + b : 0.0f;
       }
-      add_encoder_embeddings(ep, valid, pos_row, col0 + 32 * h, nh, lane, v);
+      add_encoder_embeddings<kEmbed>(ep, valid, pos_row, col0 + 32 * h, nh, lane, v);
       uint8_t* d = srow + 32 * h * ce;
       if (ep.out_dtype == BJF_DTYPE_F32)
         pack_chunk32<float>(d, v, nh);
@@ -655,8 +672,10 @@ __device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_addr
 
 // At most 80 registers per thread: with three of the ten warps on one SM sub-partition that
 // leaves room beside each CTA for two blocks of the next frame's patch-diff pass (which
-// programmatic dependent launch starts while this kernel runs).
-template <typename T>
+// programmatic dependent launch starts while this kernel runs).  kEmbed: the instantiation for
+// the encoder-input epilogue, whose 16-byte position-table loads would cost the other
+// epilogues registers.
+template <typename T, bool kEmbed>
 __global__ void __maxnreg__(80)
     gather_gemm_sm100_pair_kernel(const __grid_constant__ CUtensorMap wmap, const T* __restrict__ video,
                                   const RowSource rs, const int32_t* __restrict__ rows_dev,
@@ -802,7 +821,7 @@ __global__ void __maxnreg__(80)
         const int qw = warp - kEpilogueWarps;  // TMEM lane quarter of this warp (warp % 4)
         uint8_t* pstage = smem + PairSmemLayout::a_off + qw * kEpiWarpBytes;
         int pchunk = 0;
-        drain_accumulator_bulk(g, ep, last_c, M, (tile / n_tiles) * (2 * kBM) + (int)rank * kBM + 32 * qw + lane,
+        drain_accumulator_bulk<kEmbed>(g, ep, last_c, M, (tile / n_tiles) * (2 * kBM) + (int)rank * kBM + 32 * qw + lane,
                                (tile % n_tiles) * bn, split, bn,
                                tmem_base + (uint32_t)buf * acc_cols + ((uint32_t)(qw * 32) << 16), lane, pstage,
                                smem_u32(pstage), pchunk);
@@ -916,7 +935,7 @@ __global__ void __maxnreg__(80)
       const int n0 = (tile % n_tiles) * bn;
       const int gm = (tile / n_tiles) * (2 * kBM) + (int)rank * kBM + m;
       const bool last = tile + nclusters >= num_tiles;
-      drain_accumulator_bulk(g, ep, c, M, gm, n0, 0, last && split > 0 ? split : bn,
+      drain_accumulator_bulk<kEmbed>(g, ep, c, M, gm, n0, 0, last && split > 0 ? split : bn,
                              tmem_base + (uint32_t)buf * acc_cols + ((uint32_t)(warp * 32) << 16), lane, stage,
                              stage_smem, chunk);
       tc_fence_before();
@@ -1065,7 +1084,7 @@ int choose_bn(int D) {
 
 std::mutex g_attr_mu;
 bool g_attr_set[64][2] = {};
-int g_pair_clusters[64][2] = {};  // resident CTA-pair clusters per device and operand type
+int g_pair_clusters[64][4] = {};  // resident CTA-pair clusters per device, operand type and epilogue
 
 }  // namespace
 
@@ -1118,12 +1137,17 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
                   CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
       if (cr != CUDA_SUCCESS)
         return fail(BJF_ERR_CUDA, "cuTensorMapEncodeTiled(weight) failed with code " + std::to_string((int)cr));
-      const void* fn = g.is_bf16 ? (const void*)gather_gemm_sm100_pair_kernel<__nv_bfloat16>
-                                 : (const void*)gather_gemm_sm100_pair_kernel<__half>;
+      const bool embed = ep.position_table || ep.modality_embed;
+      const int pslot = slot + (embed ? 2 : 0);
+      const void* fn =
+          g.is_bf16 ? (embed ? (const void*)gather_gemm_sm100_pair_kernel<__nv_bfloat16, true>
+                             : (const void*)gather_gemm_sm100_pair_kernel<__nv_bfloat16, false>)
+                    : (embed ? (const void*)gather_gemm_sm100_pair_kernel<__half, true>
+                             : (const void*)gather_gemm_sm100_pair_kernel<__half, false>);
       int max_clusters = 0;
       {
         std::lock_guard<std::mutex> lock(g_attr_mu);
-        if (!g_pair_clusters[dev.device][slot]) {
+        if (!g_pair_clusters[dev.device][pslot]) {
           cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, PairSmemLayout::alloc);
           if (e != cudaSuccess) return cuda_status(e, "gather-GEMM pair smem attribute");
           cudaLaunchConfig_t cfg = {};
@@ -1140,9 +1164,9 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
           e = cudaOccupancyMaxActiveClusters(&max_clusters, fn, &cfg);
           if (e != cudaSuccess) return cuda_status(e, "gather-GEMM pair occupancy");
           if (max_clusters <= 0) return fail(BJF_ERR_CUDA, "gather-GEMM pair kernel cannot be resident");
-          g_pair_clusters[dev.device][slot] = max_clusters;
+          g_pair_clusters[dev.device][pslot] = max_clusters;
         }
-        max_clusters = g_pair_clusters[dev.device][slot];
+        max_clusters = g_pair_clusters[dev.device][pslot];
       }
       const int64_t pair_tiles_cap = ceil_div(g.D, bn) * ceil_div(rows_cap, 2 * kBM);
       const unsigned clusters = (unsigned)std::min<int64_t>(pair_tiles_cap, max_clusters);
@@ -1160,14 +1184,20 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
       cfg.stream = st;
       cfg.attrs = attr;
       cfg.numAttrs = pdl ? 2 : 1;
+      auto launch_pair = [&](auto kern, auto* typed_input) {
+        return cudaLaunchKernelEx(&cfg, kern, map, typed_input, rows, rows_dev, (int)rows_cap, g, bn, ep,
+                                  dev.error_flag);
+      };
       cudaError_t e;
-      if (g.is_bf16)
-        e = cudaLaunchKernelEx(&cfg, gather_gemm_sm100_pair_kernel<__nv_bfloat16>, map,
-                               static_cast<const __nv_bfloat16*>(input), rows, rows_dev, (int)rows_cap, g, bn, ep,
-                               dev.error_flag);
-      else
-        e = cudaLaunchKernelEx(&cfg, gather_gemm_sm100_pair_kernel<__half>, map, static_cast<const __half*>(input),
-                               rows, rows_dev, (int)rows_cap, g, bn, ep, dev.error_flag);
+      if (g.is_bf16) {
+        const auto* in = static_cast<const __nv_bfloat16*>(input);
+        e = embed ? launch_pair(gather_gemm_sm100_pair_kernel<__nv_bfloat16, true>, in)
+                  : launch_pair(gather_gemm_sm100_pair_kernel<__nv_bfloat16, false>, in);
+      } else {
+        const auto* in = static_cast<const __half*>(input);
+        e = embed ? launch_pair(gather_gemm_sm100_pair_kernel<__half, true>, in)
+                  : launch_pair(gather_gemm_sm100_pair_kernel<__half, false>, in);
+      }
       return e == cudaSuccess ? BJF_OK : cuda_status(e, "gather-GEMM (tcgen05 pair) launch");
     }
     {

@@ -1,19 +1,24 @@
 // rgba.cu -- the live viewer's patch-diff scorer for RGBA u8 camera frames
 // (burn_jepa src/viewer.rs:1069-1270: rgba_patch_diff_frame_stats, patch_diff_scores_from_rgba,
-// rgba_patch_diff_pixel_score), batched over S independent streams.
+// rgba_patch_diff_pixel_score), batched over S independent streams.  Two passes over the frames:
 //
-//   1. lighting means      per stream: mean RGB delta, mean luma delta, mean per-pixel |delta|
-//   2. lighting residual   mean per-pixel |delta - mean delta|; compensate the global lighting
-//                          shift when raw > 1e-4 and residual <= 0.35 raw
-//   3. scores              per patch: mean over its pixels of
-//                          max(|rgb delta| / 3, |luma delta|, relative luma / 4, chroma delta / 2)
-//                          with the global shift removed when compensating
+//   1. lighting means   (rgba_means_kernel) per stream: mean RGB delta, mean luma delta, mean
+//                       per-pixel |delta|
+//   2. patches          (rgba_patch_kernel) one warp per patch: the patch score
+//                       mean(max(|rgb delta| / 3, |luma delta|, relative luma / 4, chroma delta / 2))
+//                       both as is and with the global lighting shift removed, and the lighting
+//                       residual mean |delta - mean delta| (the shifted score's RGB term is that
+//                       residual's per-pixel term, so one pass yields both)
+//   3. finalize         (rgba_finalize_kernel, no frame reads) per stream: compensate when
+//                       raw > 1e-4 and residual <= 0.35 raw, keep that score, write the stats
 //
-// Each pass is a grid over (pixel ranges, streams); the frame-wide sums are reduced in a fixed
-// order from per-block partials (f64) kept in the caller's workspace, so results do not
-// depend on timing and no counters need resetting.  Every per-pixel operation is rounded as
-// the reference's f32 code does (no contraction); only the summation order of the means and
-// patch sums differs from the reference's sequential loops.
+// The frame-wide sums are reduced in a fixed order from per-block partials (f64) kept in the
+// caller's workspace, so results do not depend on timing and no counters need resetting.
+// Every per-pixel operation is rounded as the reference's f32 code does (no contraction):
+// u8 / 255 comes from a shared-memory table of the correctly rounded quotients, x / 3 from
+// div3_rn below, every other quotient from an IEEE division.  Only the summation order of the
+// means and patch sums differs from the reference's sequential loops.
+#include <algorithm>
 #include <string>
 
 #include "../../include/bjf.h"
@@ -25,17 +30,31 @@ namespace bjf {
 namespace {
 
 constexpr int kRgbaThreads = 256;
-constexpr int kStatBlocks = 64;     // partials per stream and pass
-constexpr int kMeanParts = 5;       // sum dR, dG, dB, d luma, per-pixel mean |delta|
+constexpr int kPatchWarps = kRgbaThreads / 32;  // patches per block of the patch pass
+constexpr int kStatBlocks = 64;                 // mean partials per stream
+constexpr int kMeanParts = 5;                   // sum dR, dG, dB, d luma, per-pixel mean |delta|
 
 struct Rgb {
   float r, g, b;
 };
 
-__device__ __forceinline__ Rgb load_rgb(const uint8_t* px) {
-  // rgba[offset + c] as f32 / 255.0 (src/viewer.rs:1246-1252)
-  const uchar4 v = *reinterpret_cast<const uchar4*>(px);
-  return Rgb{__fdiv_rn((float)v.x, 255.0f), __fdiv_rn((float)v.y, 255.0f), __fdiv_rn((float)v.z, 255.0f)};
+// Correctly rounded x / 3 for 0 <= x < 4: q = RN(x * RN(1/3)) is within one ulp of x / 3, the
+// FMA residual x - 3q is exact and RN(q + r * RN(1/3)) is the correctly rounded quotient
+// (Markstein's correction step).  Checked against IEEE division for every f32 in [0, 4).
+__device__ __forceinline__ float div3_rn(float x) {
+  constexpr float kThird = 0x1.555556p-2f;  // RN(1/3)
+  const float q = __fmul_rn(x, kThird);
+  const float r = __fmaf_rn(-q, 3.0f, x);
+  return __fmaf_rn(r, kThird, q);
+}
+
+// inv[i] = RN(i / 255), the reference's `rgba[offset + c] as f32 / 255.0` (src/viewer.rs:1246-1252).
+__device__ __forceinline__ void build_u8_table(float* inv) {
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) inv[i] = __fdiv_rn((float)i, 255.0f);
+}
+
+__device__ __forceinline__ Rgb rgb_of(uint32_t px, const float* inv) {
+  return Rgb{inv[px & 255u], inv[(px >> 8) & 255u], inv[(px >> 16) & 255u]};
 }
 
 // rgb[0] * 0.2126 + rgb[1] * 0.7152 + rgb[2] * 0.0722 (:1254-1256)
@@ -50,10 +69,10 @@ __device__ __forceinline__ float chroma_diff(Rgb p, Rgb c) {
   const float a = fabsf(__fsub_rn(__fdiv_rn(c.r, dc), __fdiv_rn(p.r, dp)));
   const float b = fabsf(__fsub_rn(__fdiv_rn(c.g, dc), __fdiv_rn(p.g, dp)));
   const float d = fabsf(__fsub_rn(__fdiv_rn(c.b, dc), __fdiv_rn(p.b, dp)));
-  return __fdiv_rn(__fadd_rn(__fadd_rn(a, b), d), 3.0f);
+  return div3_rn(__fadd_rn(__fadd_rn(a, b), d));
 }
 
-// Block-wide sum of a double (all threads get the result).
+// Block-wide sum of a double in a fixed order (all threads get the result).
 __device__ __forceinline__ double block_sum(double v, double* red) {
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -61,29 +80,52 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
   if (lane == 0) red[warp] = v;
   __syncthreads();
   double t = 0.0;
-  for (int w = 0; w < kRgbaThreads / 32; ++w) t += red[w];  // fixed order
+  for (int w = 0; w < kRgbaThreads / 32; ++w) t += red[w];
   return t;
 }
 
+// One pixel's contribution to the frame means (src/viewer.rs:1079-1100).  The deltas are
+// multiples of 2^-31 below 1 in magnitude, so their f64 sums are exact in any order.
+__device__ __forceinline__ void accumulate_means(uint32_t pp, uint32_t cp, const float* inv, double (&acc)[5]) {
+  const Rgb a = rgb_of(pp, inv), b = rgb_of(cp, inv);
+  const float dr = __fsub_rn(b.r, a.r), dg = __fsub_rn(b.g, a.g), db = __fsub_rn(b.b, a.b);
+  acc[0] += dr;
+  acc[1] += dg;
+  acc[2] += db;
+  acc[3] += __fsub_rn(luma(b), luma(a));
+  acc[4] += div3_rn(__fadd_rn(__fadd_rn(fabsf(dr), fabsf(dg)), fabsf(db)));
+}
+
 // Pass 1: per block, sums over its pixel range of the channel deltas, the luma delta and the
-// per-pixel mean |delta| (src/viewer.rs:1079-1100).
+// per-pixel mean |delta|.  vec: both frames 16-byte aligned with a multiple of 4 pixels, read
+// four pixels per load.
 __global__ void __launch_bounds__(kRgbaThreads)
-    rgba_means_kernel(const uint8_t* __restrict__ prev, const uint8_t* __restrict__ cur, long long pixels,
+    rgba_means_kernel(const uint8_t* __restrict__ prev, const uint8_t* __restrict__ cur, long long pixels, int vec,
                       double* __restrict__ partials) {
+  __shared__ float inv[256];
   __shared__ double red[kRgbaThreads / 32];
+  build_u8_table(inv);
+  __syncthreads();
   const long long s = blockIdx.y;
   const uint8_t* p0 = prev + s * pixels * 4;
   const uint8_t* c0 = cur + s * pixels * 4;
   double acc[kMeanParts] = {0, 0, 0, 0, 0};
-  for (long long i = (long long)blockIdx.x * kRgbaThreads + threadIdx.x; i < pixels;
-       i += (long long)kStatBlocks * kRgbaThreads) {
-    const Rgb a = load_rgb(p0 + i * 4), b = load_rgb(c0 + i * 4);
-    const float dr = __fsub_rn(b.r, a.r), dg = __fsub_rn(b.g, a.g), db = __fsub_rn(b.b, a.b);
-    acc[0] += dr;
-    acc[1] += dg;
-    acc[2] += db;
-    acc[3] += __fsub_rn(luma(b), luma(a));
-    acc[4] += __fdiv_rn(__fadd_rn(__fadd_rn(fabsf(dr), fabsf(dg)), fabsf(db)), 3.0f);
+  const long long first = (long long)blockIdx.x * kRgbaThreads + threadIdx.x;
+  const long long step = (long long)kStatBlocks * kRgbaThreads;
+  if (vec) {
+    const uint4* p4 = reinterpret_cast<const uint4*>(p0);
+    const uint4* c4 = reinterpret_cast<const uint4*>(c0);
+    for (long long i = first; i < pixels / 4; i += step) {
+      const uint4 a = __ldg(p4 + i), b = __ldg(c4 + i);
+      accumulate_means(a.x, b.x, inv, acc);
+      accumulate_means(a.y, b.y, inv, acc);
+      accumulate_means(a.z, b.z, inv, acc);
+      accumulate_means(a.w, b.w, inv, acc);
+    }
+  } else {
+    const uint32_t* p1 = reinterpret_cast<const uint32_t*>(p0);
+    const uint32_t* c1 = reinterpret_cast<const uint32_t*>(c0);
+    for (long long i = first; i < pixels; i += step) accumulate_means(__ldg(p1 + i), __ldg(c1 + i), inv, acc);
   }
   double* out = partials + (s * kStatBlocks + blockIdx.x) * kMeanParts;
 #pragma unroll
@@ -97,65 +139,132 @@ struct Means {
   float d[3];
   float luma;
   float raw;
-  float residual;  // pass 3 only
 };
 
-// The stream's frame means from the block partials: thread k < kMeanParts (+1 for the
-// residual) sums component k in a fixed order; the block shares them through `sh`.
-// The reference divides its f32 sums by `pixels as f32` (:1097-1100, :1114).
-__device__ __forceinline__ Means load_means(const double* mean_partials, const double* residual_partials,
-                                            long long s, long long pixels, Means* sh) {
+// The stream's frame means from the block partials: thread k < kMeanParts sums component k in
+// a fixed order; the block shares them through `sh` (the caller synchronises).  The reference
+// divides its f32 sums by `pixels as f32` (:1097-1100).
+__device__ __forceinline__ void load_means(const double* mean_partials, long long s, long long pixels, Means* sh) {
   const int k = threadIdx.x;
-  const float n = (float)pixels;
   if (k < kMeanParts) {
     const double* part = mean_partials + s * kStatBlocks * kMeanParts;
     double t = 0.0;
     for (int i = 0; i < kStatBlocks; ++i) t += part[i * kMeanParts + k];
-    const float v = __fdiv_rn((float)t, n);
+    const float v = __fdiv_rn((float)t, (float)pixels);
     if (k < 3) sh->d[k] = v; else if (k == 3) sh->luma = v; else sh->raw = v;
-  } else if (k == kMeanParts && residual_partials) {
-    double t = 0.0;
-    for (int i = 0; i < kStatBlocks; ++i) t += residual_partials[s * kStatBlocks + i];
-    sh->residual = __fdiv_rn((float)t, n);
   }
-  __syncthreads();
-  return *sh;
 }
 
-// Pass 2: per block, sum of the per-pixel mean |delta - mean delta| (:1102-1113).
+// One pixel of the patch pass: the score term without (raw) and with (comp) the global shift
+// removed (:1199-1244), and the lighting-residual term (:1102-1113), which is comp's RGB term.
+__device__ __forceinline__ void accumulate_patch(uint32_t pp, uint32_t cp, const float* inv, const Means& m,
+                                                 float& acc_raw, float& acc_comp, double& res) {
+  const Rgb a = rgb_of(pp, inv), b = rgb_of(cp, inv);
+  const float dr = __fsub_rn(b.r, a.r), dg = __fsub_rn(b.g, a.g), db = __fsub_rn(b.b, a.b);
+  const float rgb_raw = div3_rn(__fadd_rn(__fadd_rn(fabsf(dr), fabsf(dg)), fabsf(db)));
+  const float er = fabsf(__fsub_rn(dr, m.d[0])), eg = fabsf(__fsub_rn(dg, m.d[1])), eb = fabsf(__fsub_rn(db, m.d[2]));
+  const float rgb_comp = div3_rn(__fadd_rn(__fadd_rn(er, eg), eb));
+  res += rgb_comp;
+  const float pl = luma(a), cl = luma(b);
+  const float ld = __fsub_rn(cl, pl);
+  const float luma_raw = fabsf(ld), luma_comp = fabsf(__fsub_rn(ld, m.luma));
+  const float den = fmaxf(fmaxf(pl, cl), 0.10f);
+  const float rel_raw = __fmul_rn(fminf(__fdiv_rn(luma_raw, den), 1.0f), 0.25f);
+  const float rel_comp = __fmul_rn(fminf(__fdiv_rn(luma_comp, den), 1.0f), 0.25f);
+  const float chroma = __fmul_rn(chroma_diff(a, b), 0.5f);
+  acc_raw += fmaxf(fmaxf(fmaxf(rgb_raw, luma_raw), rel_raw), chroma);
+  acc_comp += fmaxf(fmaxf(fmaxf(rgb_comp, luma_comp), rel_comp), chroma);
+}
+
+// Pass 2: one warp per patch.  Writes both scores of the patch (raw into `scores`, comp into
+// `scores_comp`) and the block's partial of the lighting residual over the patch pixels
+// (:1102-1113; together the partials cover the pixel rows of the grid, `rest_rows` more rows
+// below it are added by the last block).  vec: 16-byte aligned rows and a patch width that is
+// a multiple of 4, four pixels per load.
 __global__ void __launch_bounds__(kRgbaThreads)
-    rgba_residual_kernel(const uint8_t* __restrict__ prev, const uint8_t* __restrict__ cur, long long pixels,
-                         const double* __restrict__ mean_partials, double* __restrict__ residual_partials) {
+    rgba_patch_kernel(const uint8_t* __restrict__ prev, const uint8_t* __restrict__ cur, long long pixels,
+                      int width, int patch, int gh, int gw, int vec, int rest_rows,
+                      const double* __restrict__ mean_partials, float* __restrict__ scores,
+                      float* __restrict__ scores_comp, double* __restrict__ residual_partials) {
+  __shared__ float inv[256];
+  __shared__ double red[kRgbaThreads / 32];
+  __shared__ Means sh;
+  build_u8_table(inv);
+  const long long s = blockIdx.y;
+  load_means(mean_partials, s, pixels, &sh);
+  __syncthreads();
+  const Means m = sh;
+  const int lane = threadIdx.x & 31;
+  const long long n_patches = (long long)gh * gw;
+  const long long patch_id = (long long)blockIdx.x * kPatchWarps + (threadIdx.x >> 5);
+  const uint8_t* p0 = prev + s * pixels * 4;
+  const uint8_t* c0 = cur + s * pixels * 4;
+  double res = 0.0;
+  if (patch_id < n_patches) {
+    const int row = (int)(patch_id / gw), col = (int)(patch_id % gw);
+    float acc_raw = 0.0f, acc_comp = 0.0f;
+    if (vec) {
+      const int qpr = patch >> 2;  // 4-pixel groups per patch row
+      for (int q = lane; q < patch * qpr; q += 32) {
+        const int y = row * patch + q / qpr, x = col * patch + 4 * (q % qpr);
+        const long long off = ((long long)y * width + x) * 4;
+        const uint4 a = __ldg(reinterpret_cast<const uint4*>(p0 + off));
+        const uint4 b = __ldg(reinterpret_cast<const uint4*>(c0 + off));
+        accumulate_patch(a.x, b.x, inv, m, acc_raw, acc_comp, res);
+        accumulate_patch(a.y, b.y, inv, m, acc_raw, acc_comp, res);
+        accumulate_patch(a.z, b.z, inv, m, acc_raw, acc_comp, res);
+        accumulate_patch(a.w, b.w, inv, m, acc_raw, acc_comp, res);
+      }
+    } else {
+      for (int k = lane; k < patch * patch; k += 32) {
+        const int y = row * patch + k / patch, x = col * patch + k % patch;
+        const long long off = ((long long)y * width + x) * 4;
+        accumulate_patch(__ldg(reinterpret_cast<const uint32_t*>(p0 + off)),
+                         __ldg(reinterpret_cast<const uint32_t*>(c0 + off)), inv, m, acc_raw, acc_comp, res);
+      }
+    }
+    for (int o = 16; o > 0; o >>= 1) {
+      acc_raw += __shfl_xor_sync(0xffffffffu, acc_raw, o);
+      acc_comp += __shfl_xor_sync(0xffffffffu, acc_comp, o);
+    }
+    if (lane == 0) {
+      const float area = (float)(patch * patch);
+      scores[s * n_patches + patch_id] = __fdiv_rn(acc_raw, area);
+      scores_comp[s * n_patches + patch_id] = __fdiv_rn(acc_comp, area);
+    }
+  }
+  // pixel rows below the grid (a frame taller than gh * patch) count toward the residual only
+  if (rest_rows > 0 && blockIdx.x == gridDim.x - 1) {
+    const uint32_t* p1 = reinterpret_cast<const uint32_t*>(p0) + (long long)gh * patch * width;
+    const uint32_t* c1 = reinterpret_cast<const uint32_t*>(c0) + (long long)gh * patch * width;
+    for (long long i = threadIdx.x; i < (long long)rest_rows * width; i += kRgbaThreads) {
+      const Rgb a = rgb_of(__ldg(p1 + i), inv), b = rgb_of(__ldg(c1 + i), inv);
+      const float er = fabsf(__fsub_rn(__fsub_rn(b.r, a.r), m.d[0]));
+      const float eg = fabsf(__fsub_rn(__fsub_rn(b.g, a.g), m.d[1]));
+      const float eb = fabsf(__fsub_rn(__fsub_rn(b.b, a.b), m.d[2]));
+      res += div3_rn(__fadd_rn(__fadd_rn(er, eg), eb));
+    }
+  }
+  const double t = block_sum(res, red);
+  if (threadIdx.x == 0) residual_partials[s * gridDim.x + blockIdx.x] = t;
+}
+
+// Pass 3: per stream, the lighting residual from the patch blocks' partials (fixed order), the
+// compensation decision (:1114-1123), the stats, and the compensated scores where it applies.
+__global__ void __launch_bounds__(kRgbaThreads)
+    rgba_finalize_kernel(long long pixels, long long n_patches, int patch_blocks,
+                         const double* __restrict__ mean_partials, const double* __restrict__ residual_partials,
+                         const float* __restrict__ scores_comp, float* __restrict__ scores,
+                         bjf_rgba_frame_stats* __restrict__ stats_out) {
   __shared__ double red[kRgbaThreads / 32];
   __shared__ Means sh;
   const long long s = blockIdx.y;
-  const Means m = load_means(mean_partials, nullptr, s, pixels, &sh);
-  const uint8_t* p0 = prev + s * pixels * 4;
-  const uint8_t* c0 = cur + s * pixels * 4;
-  double acc = 0.0;
-  for (long long i = (long long)blockIdx.x * kRgbaThreads + threadIdx.x; i < pixels;
-       i += (long long)kStatBlocks * kRgbaThreads) {
-    const Rgb a = load_rgb(p0 + i * 4), b = load_rgb(c0 + i * 4);
-    const float er = fabsf(__fsub_rn(__fsub_rn(b.r, a.r), m.d[0]));
-    const float eg = fabsf(__fsub_rn(__fsub_rn(b.g, a.g), m.d[1]));
-    const float eb = fabsf(__fsub_rn(__fsub_rn(b.b, a.b), m.d[2]));
-    acc += __fdiv_rn(__fadd_rn(__fadd_rn(er, eg), eb), 3.0f);
-  }
-  const double t = block_sum(acc, red);
-  if (threadIdx.x == 0) residual_partials[s * kStatBlocks + blockIdx.x] = t;
-}
-
-// Pass 3: one warp per patch (:1199-1244).  Lane l takes pixels l, l + 32, ... of the patch
-// in row-major order; the patch sum is reduced across the warp.
-__global__ void __launch_bounds__(kRgbaThreads)
-    rgba_scores_kernel(const uint8_t* __restrict__ prev, const uint8_t* __restrict__ cur, long long pixels,
-                       int width, int patch, int gh, int gw, const double* __restrict__ mean_partials,
-                       const double* __restrict__ residual_partials, float* __restrict__ scores,
-                       bjf_rgba_frame_stats* __restrict__ stats_out) {
-  __shared__ Means sh;
-  const long long s = blockIdx.y;
-  const Means m = load_means(mean_partials, residual_partials, s, pixels, &sh);
-  const float residual = m.residual;
+  load_means(mean_partials, s, pixels, &sh);
+  double part = 0.0;
+  for (int i = threadIdx.x; i < patch_blocks; i += kRgbaThreads) part += residual_partials[s * patch_blocks + i];
+  const double total = block_sum(part, red);  // synchronises, so `sh` is visible
+  const Means m = sh;
+  const float residual = __fdiv_rn((float)total, (float)pixels);
   const bool comp = m.raw > 1.0e-4f && residual <= __fmul_rn(m.raw, 0.35f);
   if (stats_out && blockIdx.x == 0 && threadIdx.x == 0) {
     bjf_rgba_frame_stats st;
@@ -168,42 +277,32 @@ __global__ void __launch_bounds__(kRgbaThreads)
     st.residual_abs = residual;
     stats_out[s] = st;
   }
-  const int lane = threadIdx.x & 31;
-  const long long patch_id = (long long)blockIdx.x * (kRgbaThreads / 32) + (threadIdx.x >> 5);
-  const long long n_patches = (long long)gh * gw;
-  if (patch_id >= n_patches) return;
-  const int row = (int)(patch_id / gw), col = (int)(patch_id % gw);
-  const uint8_t* p0 = prev + s * pixels * 4;
-  const uint8_t* c0 = cur + s * pixels * 4;
-  float acc = 0.0f;
-  const int area = patch * patch;
-  for (int k = lane; k < area; k += 32) {
-    const int y = row * patch + k / patch, x = col * patch + k % patch;
-    const long long off = ((long long)y * width + x) * 4;
-    const Rgb a = load_rgb(p0 + off), b = load_rgb(c0 + off);
-    float dr = __fsub_rn(b.r, a.r), dg = __fsub_rn(b.g, a.g), db = __fsub_rn(b.b, a.b);
-    if (comp) {
-      dr = __fsub_rn(dr, m.d[0]);
-      dg = __fsub_rn(dg, m.d[1]);
-      db = __fsub_rn(db, m.d[2]);
-    }
-    const float rgb_abs = __fdiv_rn(__fadd_rn(__fadd_rn(fabsf(dr), fabsf(dg)), fabsf(db)), 3.0f);
-    const float pl = luma(a), cl = luma(b);
-    float ld = __fsub_rn(cl, pl);
-    if (comp) ld = __fsub_rn(ld, m.luma);
-    const float luma_abs = fabsf(ld);
-    const float rel = __fmul_rn(fminf(__fdiv_rn(luma_abs, fmaxf(fmaxf(pl, cl), 0.10f)), 1.0f), 0.25f);
-    const float chroma = __fmul_rn(chroma_diff(a, b), 0.5f);
-    acc += fmaxf(fmaxf(fmaxf(rgb_abs, luma_abs), rel), chroma);
-  }
-  for (int o = 16; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
-  if (lane == 0) scores[s * n_patches + patch_id] = __fdiv_rn(acc, (float)area);
+  if (!comp) return;
+  for (long long i = (long long)blockIdx.x * kRgbaThreads + threadIdx.x; i < n_patches;
+       i += (long long)gridDim.x * kRgbaThreads)
+    scores[s * n_patches + i] = scores_comp[s * n_patches + i];
 }
 
-size_t workspace_layout(int64_t streams, size_t* residual_off) {
-  const size_t means = sizeof(double) * (size_t)streams * kStatBlocks * kMeanParts;
-  *residual_off = (means + 255) & ~size_t(255);
-  return *residual_off + sizeof(double) * (size_t)streams * kStatBlocks;
+struct Workspace {
+  size_t residual, comp, bytes;
+  int64_t patch_blocks;
+};
+
+// [S, 64, 5] f64 mean partials | [S, patch blocks] f64 residual partials | [S, patches] f32
+// compensated scores, each 256-byte aligned.
+Workspace workspace_layout(int64_t streams, int64_t n_patches) {
+  auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
+  Workspace w;
+  w.patch_blocks = ceil_div(n_patches, kPatchWarps);
+  w.residual = up(sizeof(double) * (size_t)streams * kStatBlocks * kMeanParts);
+  w.comp = up(w.residual + sizeof(double) * (size_t)streams * (size_t)w.patch_blocks);
+  w.bytes = w.comp + sizeof(float) * (size_t)streams * (size_t)n_patches;
+  return w;
+}
+
+bool grid_ok(int64_t streams, const int64_t grid[3]) {
+  return streams > 0 && streams <= 65535 && grid && grid[1] > 0 && grid[2] > 0 && grid[1] <= (1 << 20) &&
+         grid[2] <= (1 << 20) && grid[1] * grid[2] <= (int64_t(1) << 30);
 }
 
 }  // namespace
@@ -211,10 +310,9 @@ size_t workspace_layout(int64_t streams, size_t* residual_off) {
 
 using namespace bjf;
 
-extern "C" size_t bjf_rgba_patch_diff_workspace_bytes(int64_t streams) {
-  if (streams <= 0 || streams > 65535) return 0;
-  size_t r;
-  return workspace_layout(streams, &r);
+extern "C" size_t bjf_rgba_patch_diff_workspace_bytes(int64_t streams, const int64_t grid[3]) {
+  if (!grid_ok(streams, grid)) return 0;
+  return workspace_layout(streams, grid[1] * grid[2]).bytes;
 }
 
 extern "C" bjf_status bjf_rgba_patch_diff_scores(const uint8_t* prev, const uint8_t* current, int64_t streams,
@@ -237,25 +335,31 @@ extern "C" bjf_status bjf_rgba_patch_diff_scores(const uint8_t* prev, const uint
     return fail(BJF_ERR_INVALID_ARGUMENT, "RGBA patch-diff buffers must not be null");
   if ((reinterpret_cast<uintptr_t>(prev) | reinterpret_cast<uintptr_t>(current)) & 3)
     return fail(BJF_ERR_INVALID_ARGUMENT, "RGBA frames must be 4-byte aligned");
-  size_t roff;
-  const size_t need = workspace_layout(streams, &roff);
-  if (workspace_bytes < need || (reinterpret_cast<uintptr_t>(workspace) & 255))
+  const int64_t n_patches = grid[1] * grid[2];
+  if (n_patches > (int64_t(1) << 30)) return fail(BJF_ERR_UNSUPPORTED, "RGBA patch-diff grid exceeds the supported size");
+  const Workspace w = workspace_layout(streams, n_patches);
+  if (workspace_bytes < w.bytes || (reinterpret_cast<uintptr_t>(workspace) & 255))
     return fail(BJF_ERR_INVALID_ARGUMENT,
-                "RGBA patch-diff workspace must be 256-byte aligned and hold " + std::to_string(need) + " bytes");
+                "RGBA patch-diff workspace must be 256-byte aligned and hold " + std::to_string(w.bytes) + " bytes");
   const long long pixels = (long long)width * height;
-  double* means = static_cast<double*>(workspace);
-  double* resid = reinterpret_cast<double*>(static_cast<char*>(workspace) + roff);
+  char* ws = static_cast<char*>(workspace);
+  double* means = reinterpret_cast<double*>(ws);
+  double* resid = reinterpret_cast<double*>(ws + w.residual);
+  float* comp = reinterpret_cast<float*>(ws + w.comp);
+  const bool aligned = ((reinterpret_cast<uintptr_t>(prev) | reinterpret_cast<uintptr_t>(current)) & 15) == 0;
   cudaStream_t st = as_cuda(stream);
-  const dim3 sgrid(kStatBlocks, (unsigned)streams);
-  rgba_means_kernel<<<sgrid, kRgbaThreads, 0, st>>>(prev, current, pixels, means);
+  rgba_means_kernel<<<dim3(kStatBlocks, (unsigned)streams), kRgbaThreads, 0, st>>>(
+      prev, current, pixels, aligned && pixels % 4 == 0 ? 1 : 0, means);
   bjf_status rc = check_launch("RGBA lighting means launch");
   if (rc) return rc;
-  rgba_residual_kernel<<<sgrid, kRgbaThreads, 0, st>>>(prev, current, pixels, means, resid);
-  rc = check_launch("RGBA lighting residual launch");
+  const int rest_rows = (int)(height - grid[1] * patch_size);
+  rgba_patch_kernel<<<dim3((unsigned)w.patch_blocks, (unsigned)streams), kRgbaThreads, 0, st>>>(
+      prev, current, pixels, (int)width, (int)patch_size, (int)grid[1], (int)grid[2],
+      aligned && width % 4 == 0 && patch_size % 4 == 0 ? 1 : 0, rest_rows, means, scores, comp, resid);
+  rc = check_launch("RGBA patch-diff scores launch");
   if (rc) return rc;
-  const long long patches = grid[1] * grid[2];
-  const dim3 pgrid((unsigned)ceil_div(patches, kRgbaThreads / 32), (unsigned)streams);
-  rgba_scores_kernel<<<pgrid, kRgbaThreads, 0, st>>>(prev, current, pixels, (int)width, (int)patch_size,
-                                                     (int)grid[1], (int)grid[2], means, resid, scores, stats_out);
-  return check_launch("RGBA patch-diff scores launch");
+  const unsigned fin_blocks = (unsigned)std::min<int64_t>(64, ceil_div(n_patches, 4 * kRgbaThreads));
+  rgba_finalize_kernel<<<dim3(fin_blocks, (unsigned)streams), kRgbaThreads, 0, st>>>(
+      pixels, n_patches, (int)w.patch_blocks, means, resid, comp, scores, stats_out);
+  return check_launch("RGBA patch-diff finalize launch");
 }

@@ -329,15 +329,15 @@ extern "C" bjf_status bjf_viewer_patch_diff_masks_from_scores(const float* score
 }
 
 namespace {
-size_t rgba_masks_scores_offset(int64_t streams) {
-  return (bjf_rgba_patch_diff_workspace_bytes(streams) + 255) & ~size_t(255);
+size_t rgba_masks_scores_offset(int64_t streams, const int64_t grid[3]) {
+  return (bjf_rgba_patch_diff_workspace_bytes(streams, grid) + 255) & ~size_t(255);
 }
 }  // namespace
 
 extern "C" size_t bjf_viewer_rgba_masks_workspace_bytes(int64_t streams, const int64_t grid[3]) {
   if (!grid || grid[0] != 1 || grid[1] <= 0 || grid[2] <= 0 || grid[1] * grid[2] > kMaxViewerTokens) return 0;
-  if (bjf_rgba_patch_diff_workspace_bytes(streams) == 0) return 0;
-  return rgba_masks_scores_offset(streams) + sizeof(float) * (size_t)streams * (size_t)(grid[1] * grid[2]);
+  if (bjf_rgba_patch_diff_workspace_bytes(streams, grid) == 0) return 0;
+  return rgba_masks_scores_offset(streams, grid) + sizeof(float) * (size_t)streams * (size_t)(grid[1] * grid[2]);
 }
 
 extern "C" bjf_status bjf_viewer_patch_diff_masks_from_rgba(
@@ -375,7 +375,7 @@ extern "C" bjf_status bjf_viewer_patch_diff_masks_from_rgba(
   vp.force_dense = config->threshold <= 0.0f && full_context;
   float fb = policy->dense_fallback_density;
   fb = fb < 0.0f ? 0.0f : (fb > 1.0f ? 1.0f : fb);
-  float* scores = reinterpret_cast<float*>(static_cast<char*>(workspace) + rgba_masks_scores_offset(streams));
+  float* scores = reinterpret_cast<float*>(static_cast<char*>(workspace) + rgba_masks_scores_offset(streams, grid));
   if (!(fb >= 1.0f) && config->threshold > 0.0f && full_context) {  // a NaN density takes the path
     // stride = ceil(sqrt(len / 64)) in f32, the sampled grid its multiples (src/viewer.rs:1178-1193)
     const int stride = std::max(1, (int)std::ceil(std::sqrt((float)n / 64.0f)));

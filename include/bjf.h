@@ -251,9 +251,9 @@ typedef struct bjf_rgba_frame_stats {
   float residual_abs;     /* mean per-pixel |delta - channel_delta| */
 } bjf_rgba_frame_stats;
 
-/* Bytes of device workspace bjf_rgba_patch_diff_scores needs for `streams` frame pairs
- * (0 for a stream count outside 1..65535). */
-BJF_API size_t bjf_rgba_patch_diff_workspace_bytes(int64_t streams);
+/* Bytes of device workspace bjf_rgba_patch_diff_scores needs for `streams` frame pairs on
+ * `grid` (0 for a stream count outside 1..65535 or an empty grid). */
+BJF_API size_t bjf_rgba_patch_diff_workspace_bytes(int64_t streams, const int64_t grid[3]);
 
 /* Replaces `patch_diff_scores_from_rgba` (src/viewer.rs:1126-1157) with its frame statistics
  * `rgba_patch_diff_frame_stats` (:1079-1124), for S frame pairs at once.  prev / current:

@@ -529,15 +529,15 @@ inline Tensor patch_diff_scores_from_rgba(const uint8_t* prev, const uint8_t* cu
                                           size_t patch_size, TokenGridShape grid, size_t streams = 1,
                                           std::vector<RgbaPatchDiffFrameStats>* stats = nullptr,
                                           cudaStream_t st = nullptr) {
-  const size_t ws_bytes = bjf_rgba_patch_diff_workspace_bytes((int64_t)streams);
-  ensure(ws_bytes > 0, "RGBA patch-diff supports 1..65535 streams");
+  const auto gd = grid.dims();
+  // 0 for arguments the call below rejects with the reference's message
+  const size_t ws_bytes = std::max<size_t>(bjf_rgba_patch_diff_workspace_bytes((int64_t)streams, gd.data()), 256);
   Tensor ws({(int64_t)((ws_bytes + 3) / 4)}, BJF_DTYPE_F32);
   Tensor scores({(int64_t)streams, (int64_t)(grid.height * grid.width)}, BJF_DTYPE_F32);
   void* dstats = nullptr;
   if (stats) check_cuda(cudaMalloc(&dstats, sizeof(RgbaPatchDiffFrameStats) * streams), "cudaMalloc");
-  const auto g = grid.dims();
   const bjf_status rc = bjf_rgba_patch_diff_scores(prev, current, (int64_t)streams, (int64_t)width, (int64_t)height,
-                                                   (int64_t)patch_size, g.data(), static_cast<float*>(scores.data()),
+                                                   (int64_t)patch_size, gd.data(), static_cast<float*>(scores.data()),
                                                    static_cast<bjf_rgba_frame_stats*>(dstats), ws.data(), ws.nbytes(),
                                                    to_bjf(st));
   if (rc != BJF_OK) {
