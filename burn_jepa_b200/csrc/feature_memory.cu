@@ -27,8 +27,12 @@ namespace {
 
 constexpr int kThreads = 256;
 
+// The aging passes let the row scatter launched after them start at once (programmatic
+// dependent launch): the scatter copies its rows meanwhile and waits for the aging only
+// before it writes the rows' observed / age.
 __global__ void __launch_bounds__(kThreads)
     age_observed_kernel(float* __restrict__ age, const float* __restrict__ observed, long long n) {
+  pdl_trigger();
   long long i = (long long)blockIdx.x * kThreads + threadIdx.x;
   long long n4 = n >> 2;
   if (i < n4) {
@@ -43,6 +47,7 @@ __global__ void __launch_bounds__(kThreads)
 
 __global__ void __launch_bounds__(kThreads)
     age_observed_scalar_kernel(float* __restrict__ age, const float* __restrict__ observed, long long n) {
+  pdl_trigger();
   long long i = (long long)blockIdx.x * kThreads + threadIdx.x;
   if (i < n) age[i] += observed[i];
 }
@@ -57,8 +62,10 @@ __device__ __forceinline__ float ema_element(float prev, float tok, float alpha,
   return __fadd_rn(prev, __fsub_rn(next, prev));
 }
 
-// One warp per (b, s) row.  VECTOR: D % 8 == 0 and 16-byte aligned rows.  EMA: blend with
-// the cached row instead of overwriting it.
+// One warp per (b, s) row.  VECTOR: D % 8 == 0 and 16-byte aligned rows, each lane keeping up
+// to four (EMA: two, of both rows) 16-byte segments in flight.  EMA: blend with the cached row
+// instead of overwriting it.  The observed / age writes wait for the aging pass launched before
+// this kernel (the wait returns at once when there is none).
 template <typename TokT, typename CacheT, bool VECTOR, bool EMA>
 __global__ void __launch_bounds__(kThreads)
     scatter_rows_kernel(CacheT* __restrict__ features, float* __restrict__ observed,
@@ -79,16 +86,25 @@ __global__ void __launch_bounds__(kThreads)
   const float oma = __fsub_rn(1.0f, alpha);
   __syncwarp();
   if (VECTOR) {
-    for (int c = lane * 8; c < embed_dim; c += 32 * 8) {
-      float v[8];
-      load8<TokT>(src + c, v);
-      if (EMA) {
-        float pv[8];
-        load8<CacheT>(dst + c, pv);
+    constexpr int kSeg = EMA ? 2 : 4;  // 16-byte segments per lane in flight (EMA: of both rows)
+    for (int c0 = lane * 8; c0 < embed_dim; c0 += 32 * 8 * kSeg) {
+      float v[kSeg][8];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) v[j] = ema_element(pv[j], v[j], alpha, oma, obs, first);
+      for (int u = 0; u < kSeg; ++u)
+        if (c0 + u * 256 < embed_dim) load8<TokT>(src + c0 + u * 256, v[u]);
+      if (EMA) {
+        float pv[kSeg][8];
+#pragma unroll
+        for (int u = 0; u < kSeg; ++u)
+          if (c0 + u * 256 < embed_dim) load8<CacheT>(dst + c0 + u * 256, pv[u]);
+#pragma unroll
+        for (int u = 0; u < kSeg; ++u)
+#pragma unroll
+          for (int j = 0; j < 8; ++j) v[u][j] = ema_element(pv[u][j], v[u][j], alpha, oma, obs, first);
       }
-      store8<CacheT>(dst + c, v);
+#pragma unroll
+      for (int u = 0; u < kSeg; ++u)
+        if (c0 + u * 256 < embed_dim) store8<CacheT>(dst + c0 + u * 256, v[u]);
     }
   } else {
     for (int c = lane; c < embed_dim; c += 32) {
@@ -98,21 +114,25 @@ __global__ void __launch_bounds__(kThreads)
     }
   }
   if (lane == 0) {
+    pdl_wait();
     observed[b * dense_tokens + idx] = 1.0f;
     age[b * dense_tokens + idx] = 0.0f;
   }
 }
 
+// after_aging: the kernel before this one in the stream is this update's aging pass.
 template <typename TokT, typename CacheT, bool EMA>
-void launch_scatter(bool vec, void* features, float* observed, float* age, const void* tokens,
-                    const int32_t* idx, int S, int N, int D, long long rows, float alpha, cudaStream_t st) {
-  unsigned blocks = (unsigned)ceil_div(rows, kThreads / 32);
+cudaError_t launch_scatter(bool vec, bool after_aging, void* features, float* observed, float* age,
+                           const void* tokens, const int32_t* idx, int S, int N, int D, long long rows, float alpha,
+                           cudaStream_t st) {
+  const dim3 blocks((unsigned)ceil_div(rows, kThreads / 32));
   if (vec)
-    scatter_rows_kernel<TokT, CacheT, true, EMA><<<blocks, kThreads, 0, st>>>(
-        static_cast<CacheT*>(features), observed, age, static_cast<const TokT*>(tokens), idx, S, N, D, rows, alpha);
-  else
-    scatter_rows_kernel<TokT, CacheT, false, EMA><<<blocks, kThreads, 0, st>>>(
-        static_cast<CacheT*>(features), observed, age, static_cast<const TokT*>(tokens), idx, S, N, D, rows, alpha);
+    return launch_kernel(after_aging, scatter_rows_kernel<TokT, CacheT, true, EMA>, blocks, dim3(kThreads), 0, st,
+                         static_cast<CacheT*>(features), observed, age, static_cast<const TokT*>(tokens), idx, S, N,
+                         D, rows, alpha);
+  return launch_kernel(after_aging, scatter_rows_kernel<TokT, CacheT, false, EMA>, blocks, dim3(kThreads), 0, st,
+                       static_cast<CacheT*>(features), observed, age, static_cast<const TokT*>(tokens), idx, S, N, D,
+                       rows, alpha);
 }
 
 // Zeroes the features, observed and age of the listed batch rows (out-of-range rows are
@@ -172,17 +192,20 @@ bjf_status feature_memory_assign_launch(void* features, int32_t fdt, float* obse
   const bool vec = (D % 8 == 0) && reinterpret_cast<uintptr_t>(features) % 16 == 0 &&
                    reinterpret_cast<uintptr_t>(tokens) % 16 == 0 && (D * (int64_t)fe) % 16 == 0 &&
                    (D * (int64_t)te) % 16 == 0;
+  const bool after_aging = age_observed && meta > 0;
+  cudaError_t e = cudaSuccess;
   bool handled = dispatch_float(tdt, [&](auto ttag) {
     dispatch_float(fdt, [&](auto ctag) {
       if (ema)
-        launch_scatter<decltype(ttag), decltype(ctag), true>(vec, features, observed, age, tokens, idx, (int)S,
-                                                             (int)N, (int)D, rows, alpha, st);
+        e = launch_scatter<decltype(ttag), decltype(ctag), true>(vec, after_aging, features, observed, age, tokens,
+                                                                 idx, (int)S, (int)N, (int)D, rows, alpha, st);
       else
-        launch_scatter<decltype(ttag), decltype(ctag), false>(vec, features, observed, age, tokens, idx, (int)S,
-                                                              (int)N, (int)D, rows, alpha, st);
+        e = launch_scatter<decltype(ttag), decltype(ctag), false>(vec, after_aging, features, observed, age, tokens,
+                                                                  idx, (int)S, (int)N, (int)D, rows, alpha, st);
     });
   });
   if (!handled) return fail(BJF_ERR_INVALID_ARGUMENT, "token dtype must be f32, f16 or bf16");
+  if (e != cudaSuccess) return cuda_status(e, "feature memory scatter launch");
   return check_launch("feature memory scatter launch");
 }
 

@@ -673,10 +673,10 @@ __device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_addr
 // At most 80 registers per thread: with three of the ten warps on one SM sub-partition that
 // leaves room beside each CTA for two blocks of the next frame's patch-diff pass (which
 // programmatic dependent launch starts while this kernel runs).  kEmbed: the instantiation for
-// the encoder-input epilogue, whose 16-byte position-table loads would cost the other
-// epilogues registers.
+// the encoder-input epilogue, whose 16-byte position-table loads need more registers (it never
+// runs beside the patch-diff pass, so it may take them).
 template <typename T, bool kEmbed>
-__global__ void __maxnreg__(80)
+__global__ void __maxnreg__(kEmbed ? 128 : 80)
     gather_gemm_sm100_pair_kernel(const __grid_constant__ CUtensorMap wmap, const T* __restrict__ video,
                                   const RowSource rs, const int32_t* __restrict__ rows_dev,
                                   int rows_cap, GatherGeometry g, int bn, EpilogueArgs ep,

@@ -12,6 +12,9 @@
 //   3. finalize         (rgba_finalize_kernel, no frame reads) per stream: compensate when
 //                       raw > 1e-4 and residual <= 0.35 raw, keep that score, write the stats
 //
+// When the means of pass 1 already rule the compensation out and no statistics are wanted,
+// pass 2 computes the unshifted score alone and skips the pixels that did not change.
+//
 // The frame-wide sums are reduced in a fixed order from per-block partials (f64) kept in the
 // caller's workspace, so results do not depend on timing and no counters need resetting.
 // Every per-pixel operation is rounded as the reference's f32 code does (no contraction):
@@ -32,6 +35,7 @@ namespace {
 constexpr int kRgbaThreads = 256;
 constexpr int kPatchWarps = kRgbaThreads / 32;  // patches per block of the patch pass
 constexpr int kStatBlocks = 64;                 // mean partials per stream
+constexpr int kPatchBlocksTarget = 592;         // patch-pass blocks over all streams: 148 SMs x 4
 constexpr int kMeanParts = 5;                   // sum dR, dG, dB, d luma, per-pixel mean |delta|
 
 struct Rgb {
@@ -62,14 +66,47 @@ __device__ __forceinline__ float luma(Rgb c) {
   return __fadd_rn(__fadd_rn(__fmul_rn(c.r, 0.2126f), __fmul_rn(c.g, 0.7152f)), __fmul_rn(c.b, 0.0722f));
 }
 
+// The chroma denominators max(r + g + b, 0.10) of the previous and current pixel.
+struct ChromaDen {
+  float dp, dc;
+};
+
+__device__ __forceinline__ ChromaDen chroma_den(Rgb p, Rgb c) {
+  return ChromaDen{fmaxf(__fadd_rn(__fadd_rn(p.r, p.g), p.b), 0.10f),
+                   fmaxf(__fadd_rn(__fadd_rn(c.r, c.g), c.b), 0.10f)};
+}
+
 // (sum of |chroma delta|) / 3 with chroma = rgb / max(r + g + b, 0.10) (:1258-1270)
-__device__ __forceinline__ float chroma_diff(Rgb p, Rgb c) {
-  const float dp = fmaxf(__fadd_rn(__fadd_rn(p.r, p.g), p.b), 0.10f);
-  const float dc = fmaxf(__fadd_rn(__fadd_rn(c.r, c.g), c.b), 0.10f);
-  const float a = fabsf(__fsub_rn(__fdiv_rn(c.r, dc), __fdiv_rn(p.r, dp)));
-  const float b = fabsf(__fsub_rn(__fdiv_rn(c.g, dc), __fdiv_rn(p.g, dp)));
-  const float d = fabsf(__fsub_rn(__fdiv_rn(c.b, dc), __fdiv_rn(p.b, dp)));
-  return div3_rn(__fadd_rn(__fadd_rn(a, b), d));
+__device__ __forceinline__ float chroma_diff(Rgb p, Rgb c, ChromaDen d) {
+  const float a = fabsf(__fsub_rn(__fdiv_rn(c.r, d.dc), __fdiv_rn(p.r, d.dp)));
+  const float b = fabsf(__fsub_rn(__fdiv_rn(c.g, d.dc), __fdiv_rn(p.g, d.dp)));
+  const float e = fabsf(__fsub_rn(__fdiv_rn(c.b, d.dc), __fdiv_rn(p.b, d.dp)));
+  return div3_rn(__fadd_rn(__fadd_rn(a, b), e));
+}
+
+// A pixel's score is max(max(max(rgb, luma), rel), chroma) (:1238-1243).  The two tests below
+// show without a division that a term is below m = max(rgb, luma), so the maximum is the same
+// without it.  Both leave margins far above the rounding of the terms they bound (checked on
+// the host against the rounded terms for pixel pairs of several distributions).
+//
+// rel = min(RN(luma / den), 1) / 4 <= (luma / den)(1 + 2^-24) / 4: below m when
+// luma / 4 (1 + 1e-5) <= m den, up to the roundings of this test.
+__device__ __forceinline__ bool rel_below(float luma_abs, float den, float m) {
+  return __fmul_rn(__fmul_rn(luma_abs, 0.25f), 1.00001f) <= __fmul_rn(m, den);
+}
+
+// chroma / 2 with Q_i = c_i / dc - p_i / dp is at most (sum |Q_i| + 4e-7) / 6 (1 + 1e-6) after
+// its roundings (each quotient is at most 1), and sum |Q_i| = w / (dc dp) with
+// w = sum |c_i dp - p_i dc| computed here within 3e-6: below m when w + 7e-6 < 5.999 m dc dp.
+__device__ __forceinline__ bool chroma_below(Rgb p, Rgb c, ChromaDen d, float m) {
+  const float w = __fadd_rn(__fadd_rn(fabsf(__fmaf_rn(c.r, d.dp, -__fmul_rn(p.r, d.dc))),
+                                      fabsf(__fmaf_rn(c.g, d.dp, -__fmul_rn(p.g, d.dc)))),
+                            fabsf(__fmaf_rn(c.b, d.dp, -__fmul_rn(p.b, d.dc))));
+  return __fadd_rn(w, 7.0e-6f) < __fmul_rn(__fmul_rn(__fmul_rn(5.999f, m), d.dc), d.dp);
+}
+
+__device__ __forceinline__ float rel_term(float luma_abs, float den) {
+  return __fmul_rn(fminf(__fdiv_rn(luma_abs, den), 1.0f), 0.25f);
 }
 
 // Block-wide sum of a double in a fixed order (all threads get the result).
@@ -84,9 +121,14 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
   return t;
 }
 
+// True when the two pixels' RGB bytes are equal (alpha is not read).
+__device__ __forceinline__ bool same_rgb(uint32_t pp, uint32_t cp) { return ((pp ^ cp) & 0x00ffffffu) == 0; }
+
 // One pixel's contribution to the frame means (src/viewer.rs:1079-1100).  The deltas are
-// multiples of 2^-31 below 1 in magnitude, so their f64 sums are exact in any order.
+// multiples of 2^-31 below 1 in magnitude, so their f64 sums are exact in any order.  An
+// unchanged pixel adds exact zeros, so it is skipped.
 __device__ __forceinline__ void accumulate_means(uint32_t pp, uint32_t cp, const float* inv, double (&acc)[5]) {
+  if (same_rgb(pp, cp)) return;
   const Rgb a = rgb_of(pp, inv), b = rgb_of(cp, inv);
   const float dr = __fsub_rn(b.r, a.r), dg = __fsub_rn(b.g, a.g), db = __fsub_rn(b.b, a.b);
   acc[0] += dr;
@@ -139,26 +181,50 @@ struct Means {
   float d[3];
   float luma;
   float raw;
+  // an unchanged pixel's terms with the global shift removed: |0 - d| summed and / 3, |0 - luma|
+  float rgb_still;
+  float luma_still;
 };
 
-// The stream's frame means from the block partials: thread k < kMeanParts sums component k in
-// a fixed order; the block shares them through `sh` (the caller synchronises).  The reference
-// divides its f32 sums by `pixels as f32` (:1097-1100).
+// The stream's frame means from the block partials: warp 0 sums them (lane l takes partials
+// l, l + 32, ...; a fixed xor tree combines the lanes) and shares them through `sh` (the
+// caller synchronises).  The reference divides its f32 sums by `pixels as f32` (:1097-1100).
 __device__ __forceinline__ void load_means(const double* mean_partials, long long s, long long pixels, Means* sh) {
-  const int k = threadIdx.x;
-  if (k < kMeanParts) {
-    const double* part = mean_partials + s * kStatBlocks * kMeanParts;
-    double t = 0.0;
-    for (int i = 0; i < kStatBlocks; ++i) t += part[i * kMeanParts + k];
-    const float v = __fdiv_rn((float)t, (float)pixels);
-    if (k < 3) sh->d[k] = v; else if (k == 3) sh->luma = v; else sh->raw = v;
+  if (threadIdx.x >= 32) return;
+  const int lane = threadIdx.x;
+  const double* part = mean_partials + s * kStatBlocks * kMeanParts;
+  double t[kMeanParts] = {0, 0, 0, 0, 0};
+  for (int i = lane; i < kStatBlocks; i += 32)
+#pragma unroll
+    for (int k = 0; k < kMeanParts; ++k) t[k] += part[i * kMeanParts + k];
+#pragma unroll
+  for (int k = 0; k < kMeanParts; ++k)
+    for (int o = 16; o > 0; o >>= 1) t[k] += __shfl_xor_sync(0xffffffffu, t[k], o);
+  if (lane == 0) {
+    const float n = (float)pixels;
+    sh->d[0] = __fdiv_rn((float)t[0], n);
+    sh->d[1] = __fdiv_rn((float)t[1], n);
+    sh->d[2] = __fdiv_rn((float)t[2], n);
+    sh->luma = __fdiv_rn((float)t[3], n);
+    sh->raw = __fdiv_rn((float)t[4], n);
   }
 }
 
 // One pixel of the patch pass: the score term without (raw) and with (comp) the global shift
 // removed (:1199-1244), and the lighting-residual term (:1102-1113), which is comp's RGB term.
+// For an unchanged pixel every delta, the chroma difference and the raw term are exact zeros,
+// so the terms reduce to the stream's constants and one quotient (the same values the full
+// computation gives).
 __device__ __forceinline__ void accumulate_patch(uint32_t pp, uint32_t cp, const float* inv, const Means& m,
                                                  float& acc_raw, float& acc_comp, double& res) {
+  if (same_rgb(pp, cp)) {
+    const Rgb a = rgb_of(pp, inv);
+    const float den = fmaxf(luma(a), 0.10f);
+    const float still = fmaxf(m.rgb_still, m.luma_still);
+    res += m.rgb_still;
+    acc_comp += rel_below(m.luma_still, den, still) ? still : fmaxf(still, rel_term(m.luma_still, den));
+    return;
+  }
   const Rgb a = rgb_of(pp, inv), b = rgb_of(cp, inv);
   const float dr = __fsub_rn(b.r, a.r), dg = __fsub_rn(b.g, a.g), db = __fsub_rn(b.b, a.b);
   const float rgb_raw = div3_rn(__fadd_rn(__fadd_rn(fabsf(dr), fabsf(dg)), fabsf(db)));
@@ -169,21 +235,54 @@ __device__ __forceinline__ void accumulate_patch(uint32_t pp, uint32_t cp, const
   const float ld = __fsub_rn(cl, pl);
   const float luma_raw = fabsf(ld), luma_comp = fabsf(__fsub_rn(ld, m.luma));
   const float den = fmaxf(fmaxf(pl, cl), 0.10f);
-  const float rel_raw = __fmul_rn(fminf(__fdiv_rn(luma_raw, den), 1.0f), 0.25f);
-  const float rel_comp = __fmul_rn(fminf(__fdiv_rn(luma_comp, den), 1.0f), 0.25f);
-  const float chroma = __fmul_rn(chroma_diff(a, b), 0.5f);
-  acc_raw += fmaxf(fmaxf(fmaxf(rgb_raw, luma_raw), rel_raw), chroma);
-  acc_comp += fmaxf(fmaxf(fmaxf(rgb_comp, luma_comp), rel_comp), chroma);
+  const float m_raw = fmaxf(rgb_raw, luma_raw), m_comp = fmaxf(rgb_comp, luma_comp);
+  float s_raw = rel_below(luma_raw, den, m_raw) ? m_raw : fmaxf(m_raw, rel_term(luma_raw, den));
+  float s_comp = rel_below(luma_comp, den, m_comp) ? m_comp : fmaxf(m_comp, rel_term(luma_comp, den));
+  const ChromaDen cd = chroma_den(a, b);
+  if (!chroma_below(a, b, cd, fminf(m_raw, m_comp))) {
+    const float chroma = __fmul_rn(chroma_diff(a, b, cd), 0.5f);
+    s_raw = fmaxf(s_raw, chroma);
+    s_comp = fmaxf(s_comp, chroma);
+  }
+  acc_raw += s_raw;
+  acc_comp += s_comp;
 }
 
-// Pass 2: one warp per patch.  Writes both scores of the patch (raw into `scores`, comp into
-// `scores_comp`) and the block's partial of the lighting residual over the patch pixels
-// (:1102-1113; together the partials cover the pixel rows of the grid, `rest_rows` more rows
-// below it are added by the last block).  vec: 16-byte aligned rows and a patch width that is
-// a multiple of 4, four pixels per load.
+// The patch score without the shift alone (:1199-1244), for streams that cannot compensate;
+// an unchanged pixel's term is an exact zero.
+__device__ __forceinline__ void accumulate_raw(uint32_t pp, uint32_t cp, const float* inv, float& acc_raw) {
+  if (same_rgb(pp, cp)) return;
+  const Rgb a = rgb_of(pp, inv), b = rgb_of(cp, inv);
+  const float dr = __fsub_rn(b.r, a.r), dg = __fsub_rn(b.g, a.g), db = __fsub_rn(b.b, a.b);
+  const float rgb_raw = div3_rn(__fadd_rn(__fadd_rn(fabsf(dr), fabsf(dg)), fabsf(db)));
+  const float pl = luma(a), cl = luma(b);
+  const float luma_raw = fabsf(__fsub_rn(cl, pl));
+  const float den = fmaxf(fmaxf(pl, cl), 0.10f);
+  const float m_raw = fmaxf(rgb_raw, luma_raw);
+  float s_raw = rel_below(luma_raw, den, m_raw) ? m_raw : fmaxf(m_raw, rel_term(luma_raw, den));
+  const ChromaDen cd = chroma_den(a, b);
+  if (!chroma_below(a, b, cd, m_raw)) s_raw = fmaxf(s_raw, __fmul_rn(chroma_diff(a, b, cd), 0.5f));
+  acc_raw += s_raw;
+}
+
+// True when the frame means alone rule out the compensation (:1114-1123): it needs raw > 1e-4
+// and residual <= 0.35 raw, while every pixel's residual term is at least its raw term minus
+// the shift term s = (|dR| + |dG| + |dB|) / 3 of the means, so residual >= raw - s up to a few
+// ulps; s < 0.6 raw therefore leaves the residual above 0.35 raw with a wide margin.  Only used
+// when the caller does not ask for the frame statistics (which report the residual).
+__device__ __forceinline__ bool no_compensation(const Means& m, float shift) {
+  return m.raw <= 1.0e-4f || shift < __fmul_rn(0.6f, m.raw);
+}
+
+// Pass 2: one warp per patch, the blocks of a stream striding over its patches.  Writes both
+// scores of each patch (raw into `scores`, comp into `scores_comp`) and the block's partial of
+// the lighting residual over its patches' pixels (:1102-1113; together the partials cover the
+// pixel rows of the grid, `rest_rows` more rows below it are added by the last block).  vec:
+// 16-byte aligned rows and a patch width that is a multiple of 4, four pixels per load.  A
+// stream the means rule out from compensating (and no stats wanted) gets the raw scores only.
 __global__ void __launch_bounds__(kRgbaThreads)
     rgba_patch_kernel(const uint8_t* __restrict__ prev, const uint8_t* __restrict__ cur, long long pixels,
-                      int width, int patch, int gh, int gw, int vec, int rest_rows,
+                      int width, int patch, int gh, int gw, int vec, int rest_rows, int want_stats,
                       const double* __restrict__ mean_partials, float* __restrict__ scores,
                       float* __restrict__ scores_comp, double* __restrict__ residual_partials) {
   __shared__ float inv[256];
@@ -193,14 +292,17 @@ __global__ void __launch_bounds__(kRgbaThreads)
   const long long s = blockIdx.y;
   load_means(mean_partials, s, pixels, &sh);
   __syncthreads();
-  const Means m = sh;
+  Means m = sh;
+  m.rgb_still = div3_rn(__fadd_rn(__fadd_rn(fabsf(m.d[0]), fabsf(m.d[1])), fabsf(m.d[2])));
+  m.luma_still = fabsf(m.luma);
+  const bool raw_only = !want_stats && no_compensation(m, m.rgb_still);  // the same for the block
   const int lane = threadIdx.x & 31;
   const long long n_patches = (long long)gh * gw;
-  const long long patch_id = (long long)blockIdx.x * kPatchWarps + (threadIdx.x >> 5);
   const uint8_t* p0 = prev + s * pixels * 4;
   const uint8_t* c0 = cur + s * pixels * 4;
   double res = 0.0;
-  if (patch_id < n_patches) {
+  for (long long patch_id = (long long)blockIdx.x * kPatchWarps + (threadIdx.x >> 5); patch_id < n_patches;
+       patch_id += (long long)gridDim.x * kPatchWarps) {
     const int row = (int)(patch_id / gw), col = (int)(patch_id % gw);
     float acc_raw = 0.0f, acc_comp = 0.0f;
     if (vec) {
@@ -210,17 +312,28 @@ __global__ void __launch_bounds__(kRgbaThreads)
         const long long off = ((long long)y * width + x) * 4;
         const uint4 a = __ldg(reinterpret_cast<const uint4*>(p0 + off));
         const uint4 b = __ldg(reinterpret_cast<const uint4*>(c0 + off));
-        accumulate_patch(a.x, b.x, inv, m, acc_raw, acc_comp, res);
-        accumulate_patch(a.y, b.y, inv, m, acc_raw, acc_comp, res);
-        accumulate_patch(a.z, b.z, inv, m, acc_raw, acc_comp, res);
-        accumulate_patch(a.w, b.w, inv, m, acc_raw, acc_comp, res);
+        if (raw_only) {
+          accumulate_raw(a.x, b.x, inv, acc_raw);
+          accumulate_raw(a.y, b.y, inv, acc_raw);
+          accumulate_raw(a.z, b.z, inv, acc_raw);
+          accumulate_raw(a.w, b.w, inv, acc_raw);
+        } else {
+          accumulate_patch(a.x, b.x, inv, m, acc_raw, acc_comp, res);
+          accumulate_patch(a.y, b.y, inv, m, acc_raw, acc_comp, res);
+          accumulate_patch(a.z, b.z, inv, m, acc_raw, acc_comp, res);
+          accumulate_patch(a.w, b.w, inv, m, acc_raw, acc_comp, res);
+        }
       }
     } else {
       for (int k = lane; k < patch * patch; k += 32) {
         const int y = row * patch + k / patch, x = col * patch + k % patch;
         const long long off = ((long long)y * width + x) * 4;
-        accumulate_patch(__ldg(reinterpret_cast<const uint32_t*>(p0 + off)),
-                         __ldg(reinterpret_cast<const uint32_t*>(c0 + off)), inv, m, acc_raw, acc_comp, res);
+        const uint32_t a = __ldg(reinterpret_cast<const uint32_t*>(p0 + off));
+        const uint32_t b = __ldg(reinterpret_cast<const uint32_t*>(c0 + off));
+        if (raw_only)
+          accumulate_raw(a, b, inv, acc_raw);
+        else
+          accumulate_patch(a, b, inv, m, acc_raw, acc_comp, res);
       }
     }
     for (int o = 16; o > 0; o >>= 1) {
@@ -230,9 +343,10 @@ __global__ void __launch_bounds__(kRgbaThreads)
     if (lane == 0) {
       const float area = (float)(patch * patch);
       scores[s * n_patches + patch_id] = __fdiv_rn(acc_raw, area);
-      scores_comp[s * n_patches + patch_id] = __fdiv_rn(acc_comp, area);
+      if (!raw_only) scores_comp[s * n_patches + patch_id] = __fdiv_rn(acc_comp, area);
     }
   }
+  if (raw_only) return;
   // pixel rows below the grid (a frame taller than gh * patch) count toward the residual only
   if (rest_rows > 0 && blockIdx.x == gridDim.x - 1) {
     const uint32_t* p1 = reinterpret_cast<const uint32_t*>(p0) + (long long)gh * patch * width;
@@ -260,10 +374,13 @@ __global__ void __launch_bounds__(kRgbaThreads)
   __shared__ Means sh;
   const long long s = blockIdx.y;
   load_means(mean_partials, s, pixels, &sh);
+  __syncthreads();
+  const Means m = sh;
+  const float shift = div3_rn(__fadd_rn(__fadd_rn(fabsf(m.d[0]), fabsf(m.d[1])), fabsf(m.d[2])));
+  if (!stats_out && no_compensation(m, shift)) return;  // the patch pass wrote the raw scores only
   double part = 0.0;
   for (int i = threadIdx.x; i < patch_blocks; i += kRgbaThreads) part += residual_partials[s * patch_blocks + i];
-  const double total = block_sum(part, red);  // synchronises, so `sh` is visible
-  const Means m = sh;
+  const double total = block_sum(part, red);
   const float residual = __fdiv_rn((float)total, (float)pixels);
   const bool comp = m.raw > 1.0e-4f && residual <= __fmul_rn(m.raw, 0.35f);
   if (stats_out && blockIdx.x == 0 && threadIdx.x == 0) {
@@ -285,15 +402,17 @@ __global__ void __launch_bounds__(kRgbaThreads)
 
 struct Workspace {
   size_t residual, comp, bytes;
-  int64_t patch_blocks;
+  int64_t patch_blocks;  // patch-pass blocks per stream
 };
 
 // [S, 64, 5] f64 mean partials | [S, patch blocks] f64 residual partials | [S, patches] f32
-// compensated scores, each 256-byte aligned.
+// compensated scores, each 256-byte aligned.  The patch-pass grid is a function of the sizes
+// only, so the residual's summation order is too.
 Workspace workspace_layout(int64_t streams, int64_t n_patches) {
   auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
   Workspace w;
-  w.patch_blocks = ceil_div(n_patches, kPatchWarps);
+  w.patch_blocks = std::max<int64_t>(
+      1, std::min<int64_t>(ceil_div(n_patches, kPatchWarps), ceil_div(kPatchBlocksTarget, streams)));
   w.residual = up(sizeof(double) * (size_t)streams * kStatBlocks * kMeanParts);
   w.comp = up(w.residual + sizeof(double) * (size_t)streams * (size_t)w.patch_blocks);
   w.bytes = w.comp + sizeof(float) * (size_t)streams * (size_t)n_patches;
@@ -355,7 +474,8 @@ extern "C" bjf_status bjf_rgba_patch_diff_scores(const uint8_t* prev, const uint
   const int rest_rows = (int)(height - grid[1] * patch_size);
   rgba_patch_kernel<<<dim3((unsigned)w.patch_blocks, (unsigned)streams), kRgbaThreads, 0, st>>>(
       prev, current, pixels, (int)width, (int)patch_size, (int)grid[1], (int)grid[2],
-      aligned && width % 4 == 0 && patch_size % 4 == 0 ? 1 : 0, rest_rows, means, scores, comp, resid);
+      aligned && width % 4 == 0 && patch_size % 4 == 0 ? 1 : 0, rest_rows, stats_out ? 1 : 0, means, scores,
+      comp, resid);
   rc = check_launch("RGBA patch-diff scores launch");
   if (rc) return rc;
   const unsigned fin_blocks = (unsigned)std::min<int64_t>(64, ceil_div(n_patches, 4 * kRgbaThreads));

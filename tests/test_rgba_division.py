@@ -1,4 +1,7 @@
-"""The RGBA scorer divides by 3 with one correction step instead of an IEEE division:
+"""Host checks of the RGBA scorer's arithmetic shortcuts, on an emulation of the device's f32
+operations.
+
+It divides by 3 with one correction step instead of an IEEE division:
 q = RN(x * RN(1/3)), r = x - 3q (exact with an FMA), result RN(q + r * RN(1/3)) (Markstein's
 correction).  This emulates that arithmetic on the host and checks it against IEEE f32 division
 over a dense sample of [0, 4), the range of the sums of three |delta| terms it is used on (the
@@ -48,3 +51,62 @@ def test_div3_matches_ieee_division_on_every_value_near_the_binade_edges():
     x = np.unique(np.concatenate(chunks)).view(np.float32)
     x = x[(x >= 0) & (x < 4)]
     assert np.array_equal(_div3_method(x).view(np.uint32), (x / np.float32(3)).view(np.uint32))
+
+
+def _rn(x):
+    return x.astype(np.float32)
+
+
+def _luma(r, g, b):
+    f = np.float32
+    return _rn(_rn(_rn(r * f(0.2126)) + _rn(g * f(0.7152))) + _rn(b * f(0.0722)))
+
+
+def test_pixel_score_bounds_never_drop_the_maximum():
+    """The scorer skips the relative-luma and chroma quotients of a changed pixel when a
+    division-free bound shows they are below max(rgb, luma) (rel_below / chroma_below).  On
+    pixel pairs of several distributions the rounded score with and without the skips must be
+    identical."""
+    f = np.float32
+    rng = np.random.default_rng(5)
+    n = 2_000_000
+    p = rng.integers(0, 256, size=(n, 3))
+    c = p.copy()
+    kind = rng.integers(0, 4, size=n)
+    k = kind == 0
+    c[k] = rng.integers(0, 256, size=(k.sum(), 3))
+    k = kind == 1
+    c[k] = np.clip(p[k] + rng.integers(-3, 4, size=(k.sum(), 3)), 0, 255)
+    k = kind == 2  # dark pixels, where the chroma term is large
+    p[k] = rng.integers(0, 30, size=(k.sum(), 3))
+    c[k] = rng.integers(0, 30, size=(k.sum(), 3))
+    k = kind == 3
+    c[k] = np.clip(p[k] + rng.integers(-60, 61, size=(k.sum(), 3)), 0, 255)
+    keep = ~(p == c).all(axis=1)
+    inv = np.arange(256, dtype=np.float32) / f(255)
+    a, b = inv[p[keep]], inv[c[keep]]
+    d = [_rn(b[:, i] - a[:, i]) for i in range(3)]
+    rgb = _rn(_rn(_rn(np.abs(d[0]) + np.abs(d[1])) + np.abs(d[2])) / f(3))
+    pl, cl = _luma(a[:, 0], a[:, 1], a[:, 2]), _luma(b[:, 0], b[:, 1], b[:, 2])
+    lum = np.abs(_rn(cl - pl))
+    den = np.maximum(np.maximum(pl, cl), f(0.10))
+    rel = _rn(np.minimum(_rn(lum / den), f(1)) * f(0.25))
+    dp = np.maximum(_rn(_rn(a[:, 0] + a[:, 1]) + a[:, 2]), f(0.10))
+    dc = np.maximum(_rn(_rn(b[:, 0] + b[:, 1]) + b[:, 2]), f(0.10))
+    q = [np.abs(_rn(_rn(b[:, i] / dc) - _rn(a[:, i] / dp))) for i in range(3)]
+    chroma = _rn(_rn(_rn(_rn(q[0] + q[1]) + q[2]) / f(3)) * f(0.5))
+    full = np.maximum(np.maximum(np.maximum(rgb, lum), rel), chroma)
+
+    m = np.maximum(rgb, lum)
+    rel_skip = _rn(_rn(lum * f(0.25)) * f(1.00001)) <= _rn(m * den)
+
+    def fma(x, y, z):  # exact product and sum in f64, one rounding to f32
+        return _rn(x.astype(np.float64) * y.astype(np.float64) + z.astype(np.float64))
+
+    e = [np.abs(fma(b[:, i], dp, -_rn(a[:, i] * dc))) for i in range(3)]
+    w = _rn(_rn(e[0] + e[1]) + e[2])
+    chroma_skip = _rn(w + f(7e-6)) < _rn(_rn(_rn(f(5.999) * m) * dc) * dp)
+    fast = np.where(rel_skip, m, np.maximum(m, rel))
+    fast = np.where(chroma_skip, fast, np.maximum(fast, chroma))
+    assert rel_skip.mean() > 0.5 and chroma_skip.mean() > 0.5  # the skips do apply
+    assert np.array_equal(fast.view(np.uint32), full.view(np.uint32))

@@ -78,7 +78,7 @@ def _frames(seed, S, H, W, shift, changed_frac):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("shift,changed", [(0, 0.1), (25, 0.05), (-40, 0.0), (12, 0.5)])
+@pytest.mark.parametrize("shift,changed", [(0, 0.1), (25, 0.05), (-40, 0.0), (12, 0.5), (2, 0.3)])
 def test_device_rgba_scores_match_oracle(cuda_device, shift, changed):
     import torch
 
@@ -87,8 +87,12 @@ def test_device_rgba_scores_match_oracle(cuda_device, shift, changed):
     S, H, W, P = 3, 128, 192, 16
     prev, cur = _frames(1000 + shift, S, H, W, shift, changed)
     grid = bj.TokenGridShape(1, H // P, W // P)
-    got, stats = bj.patch_diff_scores_from_rgba(torch.from_numpy(prev).to(cuda_device),
-                                                torch.from_numpy(cur).to(cuda_device), P, grid, stats=True)
+    dp, dc = torch.from_numpy(prev).to(cuda_device), torch.from_numpy(cur).to(cuda_device)
+    got, stats = bj.patch_diff_scores_from_rgba(dp, dc, P, grid, stats=True)
+    # without statistics a stream the frame means rule out from compensating takes the
+    # unshifted-only pass: the same scores, bit for bit
+    plain = bj.patch_diff_scores_from_rgba(dp, dc, P, grid)
+    assert torch.equal(plain, got)
     got = got.cpu().numpy()
     for s in range(S):
         ref, st = oracle.patch_diff_scores_from_rgba(prev[s], cur[s], W, P, oracle.TokenGridShape(1, H // P, W // P))
