@@ -236,7 +236,7 @@ def time_rows(torch, bj, dev, videos, weight, bias, mask_cfg, hbm_peak, tflops_p
         evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(reps)]
         for i, (a, b) in enumerate(evs):
             flush.zero_()
-            torch.cuda._sleep(100_000)
+            torch.cuda._sleep(1_000_000)  # ~0.5 ms: longer than the host takes to enqueue the call
             a.record(stream)
             fn(i)
             b.record(stream)

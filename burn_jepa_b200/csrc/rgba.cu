@@ -155,14 +155,28 @@ __global__ void __launch_bounds__(kRgbaThreads)
   const long long first = (long long)blockIdx.x * kRgbaThreads + threadIdx.x;
   const long long step = (long long)kStatBlocks * kRgbaThreads;
   if (vec) {
+    // two iterations' loads in flight per thread, consumed in the same order as one at a time
     const uint4* p4 = reinterpret_cast<const uint4*>(p0);
     const uint4* c4 = reinterpret_cast<const uint4*>(c0);
-    for (long long i = first; i < pixels / 4; i += step) {
-      const uint4 a = __ldg(p4 + i), b = __ldg(c4 + i);
-      accumulate_means(a.x, b.x, inv, acc);
-      accumulate_means(a.y, b.y, inv, acc);
-      accumulate_means(a.z, b.z, inv, acc);
-      accumulate_means(a.w, b.w, inv, acc);
+    const long long nq = pixels / 4;
+    for (long long i = first; i < nq; i += 2 * step) {
+      const bool second = i + step < nq;
+      const uint4 a0 = __ldg(p4 + i), b0 = __ldg(c4 + i);
+      uint4 a1 = a0, b1 = b0;
+      if (second) {
+        a1 = __ldg(p4 + i + step);
+        b1 = __ldg(c4 + i + step);
+      }
+      accumulate_means(a0.x, b0.x, inv, acc);
+      accumulate_means(a0.y, b0.y, inv, acc);
+      accumulate_means(a0.z, b0.z, inv, acc);
+      accumulate_means(a0.w, b0.w, inv, acc);
+      if (second) {
+        accumulate_means(a1.x, b1.x, inv, acc);
+        accumulate_means(a1.y, b1.y, inv, acc);
+        accumulate_means(a1.z, b1.z, inv, acc);
+        accumulate_means(a1.w, b1.w, inv, acc);
+      }
     }
   } else {
     const uint32_t* p1 = reinterpret_cast<const uint32_t*>(p0);
@@ -306,22 +320,45 @@ __global__ void __launch_bounds__(kRgbaThreads)
     const int row = (int)(patch_id / gw), col = (int)(patch_id % gw);
     float acc_raw = 0.0f, acc_comp = 0.0f;
     if (vec) {
+      // quads q and q + 32 of the lane loaded together (a 16x16 patch has 64 quads), then
+      // consumed in the order q, q + 32 as one at a time would
       const int qpr = patch >> 2;  // 4-pixel groups per patch row
-      for (int q = lane; q < patch * qpr; q += 32) {
-        const int y = row * patch + q / qpr, x = col * patch + 4 * (q % qpr);
-        const long long off = ((long long)y * width + x) * 4;
-        const uint4 a = __ldg(reinterpret_cast<const uint4*>(p0 + off));
-        const uint4 b = __ldg(reinterpret_cast<const uint4*>(c0 + off));
+      const int nq = patch * qpr;
+      for (int q = lane; q < nq; q += 64) {
+        const bool second = q + 32 < nq;
+        const int y0 = row * patch + q / qpr, x0 = col * patch + 4 * (q % qpr);
+        const long long off0 = ((long long)y0 * width + x0) * 4;
+        const uint4 a0 = __ldg(reinterpret_cast<const uint4*>(p0 + off0));
+        const uint4 b0 = __ldg(reinterpret_cast<const uint4*>(c0 + off0));
+        uint4 a1 = a0, b1 = b0;
+        if (second) {
+          const int y1 = row * patch + (q + 32) / qpr, x1 = col * patch + 4 * ((q + 32) % qpr);
+          const long long off1 = ((long long)y1 * width + x1) * 4;
+          a1 = __ldg(reinterpret_cast<const uint4*>(p0 + off1));
+          b1 = __ldg(reinterpret_cast<const uint4*>(c0 + off1));
+        }
         if (raw_only) {
-          accumulate_raw(a.x, b.x, inv, acc_raw);
-          accumulate_raw(a.y, b.y, inv, acc_raw);
-          accumulate_raw(a.z, b.z, inv, acc_raw);
-          accumulate_raw(a.w, b.w, inv, acc_raw);
+          accumulate_raw(a0.x, b0.x, inv, acc_raw);
+          accumulate_raw(a0.y, b0.y, inv, acc_raw);
+          accumulate_raw(a0.z, b0.z, inv, acc_raw);
+          accumulate_raw(a0.w, b0.w, inv, acc_raw);
+          if (second) {
+            accumulate_raw(a1.x, b1.x, inv, acc_raw);
+            accumulate_raw(a1.y, b1.y, inv, acc_raw);
+            accumulate_raw(a1.z, b1.z, inv, acc_raw);
+            accumulate_raw(a1.w, b1.w, inv, acc_raw);
+          }
         } else {
-          accumulate_patch(a.x, b.x, inv, m, acc_raw, acc_comp, res);
-          accumulate_patch(a.y, b.y, inv, m, acc_raw, acc_comp, res);
-          accumulate_patch(a.z, b.z, inv, m, acc_raw, acc_comp, res);
-          accumulate_patch(a.w, b.w, inv, m, acc_raw, acc_comp, res);
+          accumulate_patch(a0.x, b0.x, inv, m, acc_raw, acc_comp, res);
+          accumulate_patch(a0.y, b0.y, inv, m, acc_raw, acc_comp, res);
+          accumulate_patch(a0.z, b0.z, inv, m, acc_raw, acc_comp, res);
+          accumulate_patch(a0.w, b0.w, inv, m, acc_raw, acc_comp, res);
+          if (second) {
+            accumulate_patch(a1.x, b1.x, inv, m, acc_raw, acc_comp, res);
+            accumulate_patch(a1.y, b1.y, inv, m, acc_raw, acc_comp, res);
+            accumulate_patch(a1.z, b1.z, inv, m, acc_raw, acc_comp, res);
+            accumulate_patch(a1.w, b1.w, inv, m, acc_raw, acc_comp, res);
+          }
         }
       }
     } else {
