@@ -35,7 +35,7 @@ namespace {
 constexpr int kRgbaThreads = 256;
 constexpr int kPatchWarps = kRgbaThreads / 32;  // patches per block of the patch pass
 constexpr int kStatBlocks = 64;                 // mean partials per stream
-constexpr int kPatchBlocksTarget = 592;         // patch-pass blocks over all streams: 148 SMs x 4
+constexpr int kPatchBlocksTarget = 592;         // patch-pass blocks over all streams: 148 SMs x 4 resident
 constexpr int kMeanParts = 5;                   // sum dR, dG, dB, d luma, per-pixel mean |delta|
 
 struct Rgb {
@@ -448,8 +448,10 @@ struct Workspace {
 Workspace workspace_layout(int64_t streams, int64_t n_patches) {
   auto up = [](size_t v) { return (v + 255) & ~size_t(255); };
   Workspace w;
+  // at most one wave of kPatchBlocksTarget blocks over all streams (rounding up left a second
+  // wave of a few blocks)
   w.patch_blocks = std::max<int64_t>(
-      1, std::min<int64_t>(ceil_div(n_patches, kPatchWarps), ceil_div(kPatchBlocksTarget, streams)));
+      1, std::min<int64_t>(ceil_div(n_patches, kPatchWarps), kPatchBlocksTarget / streams));
   w.residual = up(sizeof(double) * (size_t)streams * kStatBlocks * kMeanParts);
   w.comp = up(w.residual + sizeof(double) * (size_t)streams * (size_t)w.patch_blocks);
   w.bytes = w.comp + sizeof(float) * (size_t)streams * (size_t)n_patches;
