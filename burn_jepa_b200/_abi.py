@@ -187,8 +187,14 @@ def header_symbols() -> list[str]:
     return sorted(set(re.findall(r"BJF_API\s+[\w\s\*]+?\b(bjf_\w+)\s*\(", text)))
 
 
+def header_abi_version() -> int:
+    """BJF_ABI_VERSION as ``include/bjf.h`` defines it."""
+    return int(re.search(r"#define\s+BJF_ABI_VERSION\s+(\d+)", open(HEADER_PATH).read()).group(1))
+
+
 def load() -> ctypes.CDLL:
-    """Loads libbjf.so (raises if it has not been built)."""
+    """Loads libbjf.so (raises if it has not been built, or was built from another ABI version
+    of include/bjf.h)."""
     global _lib
     if _lib is None:
         if not os.path.exists(LIB_PATH):
@@ -199,6 +205,9 @@ def load() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
+        built, want = lib.bjf_abi_version(), header_abi_version()
+        if built != want:
+            raise RuntimeError(f"{LIB_PATH} has ABI version {built} but include/bjf.h declares {want}: rebuild it")
         _lib = lib
     return _lib
 

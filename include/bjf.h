@@ -36,7 +36,8 @@
 extern "C" {
 #endif
 
-#define BJF_ABI_VERSION 1
+/* 2: bjf_rgba_patch_diff_workspace_bytes takes the token grid. */
+#define BJF_ABI_VERSION 2
 
 #if defined(__GNUC__)
 #define BJF_API __attribute__((visibility("default")))

@@ -21,7 +21,7 @@ def test_library_exports_every_header_symbol():
 
 
 def test_abi_version():
-    assert bj.load().bjf_abi_version() == 1
+    assert bj.load().bjf_abi_version() == _abi.header_abi_version() == 2
 
 
 def _fm(features, observed, age, tokens, indices):
