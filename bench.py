@@ -293,10 +293,11 @@ def time_rows(torch, bj, dev, videos, weight, bias, mask_cfg, hbm_peak, tflops_p
     hbm("feature_memory_assign_latest", "a6", wl, ms, m * D * 4 + m * 4 + aging + m * 8)
     ms = timed(lambda i: bj.feature_memory_update_ema(feats, observed, age, tokens, tok_idx, 0.5, True))
     hbm("feature_memory_update_ema", "f3", wl, ms, m * D * 6 + m * 4 + aging + m * 8)
-    reset = torch.tensor([1, 7, 19, 30], dtype=torch.int32, device=dev)
+    reset_rows = [r for r in (1, 7, 19, 30) if r < S] or [0]
+    reset = torch.tensor(reset_rows, dtype=torch.int32, device=dev)
     ms = timed(lambda i: bj.feature_memory_reset_rows(feats, observed, age, reset))
-    hbm("feature_memory_reset_rows", "f3", f"4 of {S} stream caches [{N_TOKENS},{D}] f16 zeroed", ms,
-        4 * N_TOKENS * (D * 2 + 8))
+    hbm("feature_memory_reset_rows", "f3", f"{len(reset_rows)} of {S} stream caches [{N_TOKENS},{D}] f16 zeroed",
+        ms, len(reset_rows) * N_TOKENS * (D * 2 + 8))
     del tokens, feats, observed, age
 
     # f1: the live viewer's RGBA scorer and mask node on the same streams' frames as RGBA u8
