@@ -20,7 +20,8 @@ clips from pinned host memory, runs the step and reads the per-stream active cou
 rows:  (one GPU) every row of the path timed alone through its public entry point against its
 roofline: the selection, the device plan, the standalone cache updates, the RGBA viewer scorer
 and mask node, and the gather-GEMM on the ViT-g batch (32 x [3,16,512,512] bf16, 131 072 rows,
-D = 1408) plain and with the encoder-input epilogue.
+D = 1408) plain and with the encoder-input epilogue; beside them (cpu_ms) the oracle on a
+bounded sample of the same work, scaled to the whole row.
 --impl reference: the reference's CPU algorithm (the C restatement in oracle/, f32 as on
 the reference's NdArray backend) on all host threads, over a bounded sample of streams.
 """
@@ -203,6 +204,66 @@ def cpu_front_end_rate(video_f32_streams, weight_f32, bias_f32, thr, budget_s=15
 # ---------------------------------------------------------------------------
 # GPU leg
 # ---------------------------------------------------------------------------
+def cpu_rows(streams, budget_s=1.0):
+    """The oracle (the reference's algorithms restated in C, f32, all host threads) on a bounded
+    sample of each standalone row's workload, scaled to the whole workload of that row.  Returns
+    {row name: {"cpu_ms": ms for the row's whole workload, "cpu_sample": what was run}}."""
+    import numpy as np
+
+    import oracle
+    from burn_jepa_b200 import workloads
+
+    def per_call_s(fn):  # mean seconds of fn over at least one call and about budget_s
+        n, el = 0, 0.0
+        while n == 0 or el < budget_s:
+            t0 = time.perf_counter()
+            fn()
+            el += time.perf_counter() - t0
+            n += 1
+        return el / n
+
+    rng = np.random.default_rng(31)
+    grid = oracle.TokenGridShape(*GRID)
+    out = {}
+
+    scores = np.where(rng.uniform(size=N_TOKENS) < 0.1, rng.uniform(0.1, 1.0, N_TOKENS), 0.0).astype(np.float32)
+    cfg = oracle.PatchDiffConfig.adaptive_threshold(0.05, 1, N_TOKENS, 1)
+    s = per_call_s(lambda: oracle.patch_diff_context_mask_from_scores(scores, grid, cfg))
+    out["patch_diff_select"] = (s * streams, f"one stream's {N_TOKENS} scores, x{streams} streams")
+
+    width = 410
+    feats = rng.standard_normal((1, N_TOKENS, D)).astype(np.float32)
+    obs = np.zeros((1, N_TOKENS), np.float32)
+    age = np.zeros((1, N_TOKENS), np.float32)
+    toks = rng.standard_normal((1, width, D)).astype(np.float32)
+    idx = np.sort(rng.choice(N_TOKENS, width, replace=False)).astype(np.int32)[None]
+    s = per_call_s(lambda: oracle.feature_memory_assign_latest(feats, obs, age, toks, idx, True))
+    out["feature_memory_assign_latest"] = (s * streams, f"one stream, {width} of {N_TOKENS} rows, x{streams}")
+    s = per_call_s(lambda: oracle.feature_memory_update_ema(feats, obs, age, toks, idx, 0.5, True))
+    out["feature_memory_update_ema"] = (s * streams, f"one stream, {width} of {N_TOKENS} rows, x{streams}")
+
+    prev = rng.integers(0, 256, size=(H, W, 4), dtype=np.uint8)
+    cur = prev.copy()
+    cur[: H // 4, : W // 4, :3] = rng.integers(0, 256, size=(H // 4, W // 4, 3), dtype=np.uint8)
+    vgrid = oracle.TokenGridShape(1, H // P, W // P)
+    s = per_call_s(lambda: oracle.patch_diff_scores_from_rgba(prev, cur, W, P, vgrid))
+    out["rgba_patch_diff_scores"] = (s * streams, f"one {W}x{H} RGBA frame pair, x{streams}")
+
+    v = VITG
+    clip = rng.standard_normal((1, v["C"], v["T"], v["H"], v["W"])).astype(np.float32)
+    ggrid = oracle.TokenGridShape(v["T"] // v["KT"], v["H"] // v["P"], v["W"] // v["P"])
+    gmask = workloads.multiblock_mask(601, ggrid.depth, ggrid.height, ggrid.width, len(ggrid) // 2)
+    rows = 64
+    coords = oracle.sparse_patchify_plan_coords(gmask[:rows], ggrid, 1)
+    gw = rng.standard_normal((v["D"], v["C"], v["KT"], v["P"], v["P"])).astype(np.float32) * np.float32(0.02)
+    gb = np.zeros(v["D"], np.float32)
+    pcfg = oracle.PatchifyConfig(v["C"], v["D"], v["T"], v["H"], v["W"], v["KT"], v["P"], v["P"])
+    s = per_call_s(lambda: oracle.sparse_patchify3d_forward(pcfg, clip, coords, gw, gb))
+    total_rows = v["B"] * len(gmask)
+    out["gather_gemm_vitg_batch"] = (s * total_rows / rows, f"{rows} of the {total_rows} rows, f32")
+    return {k: {"cpu_ms": round(t * 1e3, 3), "cpu_sample": d} for k, (t, d) in out.items()}
+
+
 def make_inputs(torch, dev, streams, density, seed_base):
     """Two input sets of this rank's global streams; each stream's clip depends only on its
     global id, so a stream's content is the same at every GPU count."""
@@ -529,6 +590,13 @@ def run_ours(args, world, rank, local):
     rows = None
     if world == 1 and not args.no_rows:
         rows = time_rows(torch, bj, dev, videos, weight, bias, fe.desc.mask, hbm_peak, tflops_peak)
+        if rank == 0 and not args.no_cpu_baseline:
+            try:  # the oracle beside each row; never at the cost of the bench line
+                for name, c in cpu_rows(S).items():
+                    rows[name].update(c)
+                rows["cpu_cores"] = __import__("oracle").num_threads()
+            except Exception as e:  # noqa: BLE001
+                rows["cpu_error"] = f"{type(e).__name__}: {e}"[:300]
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:

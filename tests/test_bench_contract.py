@@ -29,3 +29,14 @@ def test_reference_arm_prints_one_json_line_with_the_contract_fields():
     e2e = r["e2e"]
     assert e2e["value"] == r["value"] and e2e["unit"] == r["unit"]
     assert e2e["h2d_bytes_per_step"] == 0 and e2e["d2h_bytes_per_step"] == 0
+
+
+def test_cpu_rows_time_the_oracle_for_each_row():
+    sys.path.insert(0, ROOT)
+    import bench
+
+    rows = bench.cpu_rows(2, budget_s=0.01)
+    assert set(rows) == {"patch_diff_select", "feature_memory_assign_latest", "feature_memory_update_ema",
+                         "rgba_patch_diff_scores", "gather_gemm_vitg_batch"}
+    for r in rows.values():
+        assert r["cpu_ms"] > 0 and r["cpu_sample"]
