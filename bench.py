@@ -70,7 +70,10 @@ def parse_args():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--density", type=float, default=0.10)
     ap.add_argument("--streams", type=int, default=STREAMS_PER_GPU)
-    ap.add_argument("--sweep", action="store_true", help="also time densities 5/10/20/40%%")
+    ap.add_argument("--no-sweep", action="store_true", help="skip the density sweep (5/10/20/40%%)")
+    ap.add_argument("--sweep-steps", type=int, default=10)
+    ap.add_argument("--strong", action="store_true",
+                    help="strong scaling: 256 streams in total, split over the GPUs (default: 32 per GPU)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--e2e-steps", type=int, default=5)
     ap.add_argument("--load-seconds", type=float, default=2.0,
@@ -382,6 +385,46 @@ def time_rows(torch, bj, dev, videos, weight, bias, mask_cfg, hbm_peak, tflops_p
             encode_density=round(float(ec.sum().item()) / (S * vgrid[1] * vgrid[2]), 4))
     del prev, cur
 
+    # C2 / C3: the other front-end configurations, each one fused step alone (inputs smaller
+    # than L2 for C2, so the flush before every call matters)
+    def front_end_row(name, row, S_, C_, T_, H_, W_, D_, density, seed):
+        vids = workloads.rect_perturbation_clips_torch(seed, S_, C_, T_, H_, W_, density, dev, torch.float16)
+        sc_ = bj.patch_diff_token_scores(vids.unsqueeze(1), KT, P).cpu().numpy().ravel()
+        thr_ = workloads.choose_threshold(sc_, density, 1e-3)
+        n_ = (T_ // KT) * (H_ // P) * (W_ // P)
+        cfg_ = bj.PatchDiffConfig.adaptive_threshold(thr_, 1, n_, 1)
+        fe_ = bj.FrontEnd(S_, C_, T_, H_, W_, KT, P, D_, cfg_, torch.float16, torch.float16, dev)
+        w_ = torch.from_numpy(workloads.normal(seed + 1, (D_, C_, KT, P, P), std=0.02)).to(dev, torch.float16)
+        b_ = torch.from_numpy(workloads.normal(seed + 2, (D_,), std=0.02)).to(dev)
+        cache_ = torch.randn((S_, n_, D_), device=dev).to(torch.float16)
+        obs_ = torch.zeros((S_, n_), device=dev)
+        age_ = torch.zeros((S_, n_), device=dev)
+        ms_ = timed(lambda i: fe_.step(vids, w_, b_, cache_, obs_, age_, age_observed=True))
+        m_ = int(fe_.counts.sum().item())
+        k_ = C_ * KT * P * P
+        nbytes = vids.numel() * 2 + S_ * n_ * 4 + m_ * D_ * 2 + S_ * n_ * 12
+        rate = m_ / (ms_ / 1e3)
+        wl_ = (f"{S_} x [{C_},{T_},{H_},{W_}] f16, grid {T_ // KT}x{H_ // P}x{W_ // P}, ViT-L/16 D={D_}, "
+               f"{m_} of {S_ * n_} tubelets active ({100.0 * m_ / (S_ * n_):.1f}%), f16 caches")
+        hbm(name, row, wl_ + "; the fused step (scores, selection, gather-GEMM + cache write)", ms_, nbytes,
+            active_tubelets=m_, active_tubelets_per_s=round(rate, 1), frames_per_s=round(S_ * (T_ // KT) /
+                                                                                      (ms_ / 1e3), 1))
+        # the gather-GEMM of the same rows alone (plain f16 output)
+        _, idx_, cnt_ = bj.patch_diff_context_mask(vids.unsqueeze(1), KT, P, (T_ // KT, H_ // P, W_ // P), cfg_)
+        co_, tot_ = bj.sparse_patchify_plan_coords(idx_, (T_ // KT, H_ // P, W_ // P), batch=S_, counts=cnt_,
+                                                   capacity=S_ * n_)
+        rows_ = int(tot_.item())
+        co_ = co_[:rows_].contiguous()
+        pc_ = bj.PatchifyConfig(C_, D_, T_, H_, W_, KT, P, P)
+        fo_ = torch.empty((rows_, D_), device=dev, dtype=torch.float16)
+        ms_ = timed(lambda i: bj.sparse_patchify3d_forward(pc_, vids, co_, w_, b_, out=fo_))
+        tensor(name + "_gather_gemm", "a5", wl_ + "; the gather-GEMM of its active rows alone", ms_,
+               2 * rows_ * k_ * D_, rows=rows_)
+        del vids, cache_, fe_
+
+    front_end_row("c2_vitl_clip_step", "a1-a6", 1, C, 16, 256, 256, D, 0.25, 711)
+    front_end_row("c3_live_8_streams_step", "a1-a6", 8, C, T, H, W, D, 0.10, 721)
+
     # a5 / f4: the ViT-g batch, a shared 4096-of-8192 multiblock mask, bf16
     v = VITG
     g = torch.Generator(device=dev).manual_seed(602)
@@ -426,8 +469,13 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     group = sharding.RankGroup(device=dev)
-    S = args.streams
-    mine = sharding.shard_streams(S * world, world, rank)  # weak scaling: S streams per GPU
+    if args.strong:  # strong scaling: 256 streams in total, split over the GPUs
+        total = 256
+        mine = sharding.shard_streams(total, world, rank)
+        S = len(mine)
+    else:  # weak scaling: S streams per GPU
+        S = args.streams
+        mine = sharding.shard_streams(S * world, world, rank)
     hbm_peak, tflops_peak, peak_kind = read_peaks()
 
     weight = torch.from_numpy(workloads.normal(11, (D, C, KT, P, P), std=0.02)).to(dev, torch.float16)
@@ -572,23 +620,23 @@ def run_ours(args, world, rank, local):
     h2d = S * C * T * H * W * 2
 
     sweep = None
-    if args.sweep:
+    if not args.no_sweep and not args.strong:
         sweep = {}
         for dens in (0.05, 0.10, 0.20, 0.40):
             del fe, caches, observed, age
             torch.cuda.empty_cache()
             videos2, thr2, fe, caches, observed, age, cps = setup(dens)
-            s2 = time_steps(fe, videos2, caches, observed, age, args.steps, args.warmup)
-            tub2 = sum(cps[i % 2] for i in range(args.steps))
+            s2 = time_steps(fe, videos2, caches, observed, age, args.sweep_steps, args.warmup)
+            tub2 = sum(cps[i % 2] for i in range(args.sweep_steps))
             s2m = group.max(s2)
             sweep[f"{int(dens * 100)}%"] = {
                 "active_fraction": round(statistics.mean(cps) / (S * N_TOKENS), 4),
                 "value": round(group.sum(float(tub2)) / s2m, 1),
-                "ms_per_step": round(s2m / args.steps * 1e3, 4)}
+                "ms_per_step": round(s2m / args.sweep_steps * 1e3, 4)}
             del videos2
 
     rows = None
-    if world == 1 and not args.no_rows:
+    if world == 1 and not args.no_rows and not args.strong:
         rows = time_rows(torch, bj, dev, videos, weight, bias, fe.desc.mask, hbm_peak, tflops_peak)
         if rank == 0 and not args.no_cpu_baseline:
             try:  # the oracle beside each row; never at the cost of the bench line
@@ -611,14 +659,18 @@ def run_ours(args, world, rank, local):
     result = {
         "metric": METRIC, "value": round(value, 1), "unit": UNIT, "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(max_secs / args.steps * 1e3, 4), "higher_is_better": True,
-        "scaling": "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
-        "config": {"workload": "live camera streams: 32 x [3,2,1024,1024] f16 per GPU, ViT-L/16 patch embed "
-                               "(D=1024, K=1536), patch-diff mask, f16 token cache [4096,1024] per stream",
+        "scaling": "strong" if args.strong else "weak", "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+        "config": {"workload": (f"live camera streams: 256 x [3,2,1024,1024] f16 split over {world} GPU(s)"
+                                if args.strong else
+                                "live camera streams: 32 x [3,2,1024,1024] f16 per GPU") +
+                               ", ViT-L/16 patch embed (D=1024, K=1536), patch-diff mask, f16 token cache "
+                               "[4096,1024] per stream",
                    "streams_per_gpu": S, "target_density": args.density,
                    "active_fraction": round(statistics.mean(counts_per_set) / (S * N_TOKENS), 4),
                    "active_tubelets_per_step_per_gpu": counts_per_set,
                    "threshold": thr,
-                   "l2": "inputs larger than L2: two 403 MB clip sets per GPU alternate between steps",
+                   "l2": f"inputs larger than L2: two {S * C * T * H * W * 2 / 1e6:.0f} MB clip sets per GPU "
+                         "alternate between steps",
                    "clocks_note": "nvidia-smi sampled every 100 ms over 2 s of back-to-back steps "
                                   "immediately before and through the timed steps",
                    "parallelism": f"stream-sharded replicas x{world}, no collective"},

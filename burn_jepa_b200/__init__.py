@@ -32,6 +32,7 @@ __all__ = [
     "PatchifyConfig",
     "TokenGridShape",
     "device_error_check",
+    "set_bounded_wait",
     "feature_memory_assign_latest",
     "load",
     "patch_diff_context_mask",
@@ -95,6 +96,12 @@ def device_error_check(stream=None) -> bool:
     flag = ctypes.c_int32(0)
     check(load().bjf_device_error_check(_stream(stream), ctypes.byref(flag)))
     return bool(flag.value)
+
+
+def set_bounded_wait(limit_ns: int = 0, stall: bool = False) -> None:
+    """bjf_set_bounded_wait: the time limit of the GEMM kernels' pipeline waits (0 = the 2 s
+    default) and the give-up test hook (see include/bjf.h)."""
+    check(load().bjf_set_bounded_wait(int(limit_ns), int(bool(stall))))
 
 
 # ---------------------------------------------------------------------------

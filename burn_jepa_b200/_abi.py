@@ -149,6 +149,7 @@ SIGNATURES = {
     "bjf_abi_version": (ctypes.c_int32, []),
     "bjf_get_last_error_string": (ctypes.c_size_t, [ctypes.c_char_p, ctypes.c_size_t]),
     "bjf_device_error_check": (_I32, [_P, ctypes.POINTER(_I32)]),
+    "bjf_set_bounded_wait": (_I32, [ctypes.c_uint64, _I32]),
     "bjf_patch_diff_token_scores": (_I32, [_P, _I32, _DIMS, _I64, _I64, _I64, _P, _P]),
     "bjf_patch_diff_context_mask_from_scores": (_I32, [_P, _I64, _DIMS, ctypes.POINTER(PatchDiffConfig), _P, _P, _P]),
     "bjf_patch_diff_context_mask": (_I32, [_P, _I32, _DIMS, _I64, _I64, _I64, _DIMS,

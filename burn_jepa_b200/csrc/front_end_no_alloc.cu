@@ -19,8 +19,13 @@
 //    whose work overlaps on the GPU (different streams, or different host threads
 //    without ordering) race and corrupt each other.  Serialise them on one stream.
 //  * The first call on each device looks up the array's device address
-//    (cudaGetSymbolAddress, with that device current); make that first call before any
-//    stream capture begins.
+//    (cudaGetSymbolAddress, with that device current) and clears the array's timeout
+//    flag; make that first call before any stream capture begins.  The address is kept
+//    for the life of the process, so a device reset (cudaDeviceReset) while the library
+//    is loaded is not supported: the array would move and the kept address go stale.
+//  * A bounded-wait timeout in the GEMM sets the array's first int, which stays set until
+//    bjf_device_error_check reads and clears it (as the workspace step's flag does); no
+//    call clears it on entry, so no evidence is lost between calls.
 #include <mutex>
 #include <string>
 
@@ -36,20 +41,24 @@ namespace {
 constexpr size_t kNoAllocScratchBytes = size_t(4) << 20;
 
 // Scratch of bjf_front_end_step_no_alloc.  Bytes [0, 256) hold the bounded-wait
-// timeout flag (cleared at the start of every call); the step's buffers follow.
+// timeout flag (cleared once, at set-up; then only by bjf_device_error_check); the step's
+// buffers follow.
 static __device__ __align__(256) unsigned char g_no_alloc_scratch[kNoAllocScratchBytes];
 
 constexpr int kMaxDevices = 64;
 std::mutex g_mu;
 void* g_scratch_addr[kMaxDevices] = {};
 
-// Device address of g_no_alloc_scratch on the current device (looked up once per device).
-bjf_status scratch_address(int dev, void** out) {
+// Device address of g_no_alloc_scratch on the current device `dev`, looked up once per
+// device; the set-up also clears the timeout flag (on `st`, ahead of the first step).
+bjf_status scratch_address(int dev, cudaStream_t st, void** out) {
   std::lock_guard<std::mutex> lock(g_mu);
   if (!g_scratch_addr[dev]) {
     void* p = nullptr;
     cudaError_t e = cudaGetSymbolAddress(&p, g_no_alloc_scratch);
     if (e != cudaSuccess) return cuda_status(e, "cudaGetSymbolAddress(no-alloc front-end scratch)");
+    e = cudaMemsetAsync(p, 0, sizeof(int), st);
+    if (e != cudaSuccess) return cuda_status(e, "clear no-alloc scratch flag");
     g_scratch_addr[dev] = p;
   }
   *out = g_scratch_addr[dev];
@@ -75,6 +84,13 @@ Carve carve(int64_t S, int64_t N) {
 }
 
 }  // namespace
+
+int* no_alloc_error_flag(int dev) {
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lock(g_mu);
+  return static_cast<int*>(g_scratch_addr[dev]);
+}
+
 }  // namespace bjf
 
 using namespace bjf;
@@ -114,8 +130,9 @@ extern "C" bjf_status bjf_front_end_step_no_alloc(const bjf_front_end_desc* d, c
   cudaError_t e = cudaGetDevice(&dev_id);
   if (e != cudaSuccess) return cuda_status(e, "cudaGetDevice");
   if (dev_id < 0 || dev_id >= kMaxDevices) return fail(BJF_ERR_UNSUPPORTED, "device ordinal out of range");
+  cudaStream_t st = as_cuda(stream);
   void* base = nullptr;
-  rc = scratch_address(dev_id, &base);
+  rc = scratch_address(dev_id, st, &base);
   if (rc) return rc;
   // Device properties by attribute queries only (nothing here allocates).
   DeviceInfo dev;
@@ -133,12 +150,10 @@ extern "C" bjf_status bjf_front_end_step_no_alloc(const bjf_front_end_desc* d, c
   float* scores = reinterpret_cast<float*>(ws + c.scores);
   int32_t* indices = reinterpret_cast<int32_t*>(ws + c.indices);
   int32_t* counts = counts_out ? counts_out : reinterpret_cast<int32_t*>(ws + c.counts);
-  cudaStream_t st = as_cuda(stream);
 
-  // The previous call's contents stay in the array; only the timeout flag must start at
-  // zero (every other buffer is fully written before it is read).
-  e = cudaMemsetAsync(dev.error_flag, 0, sizeof(int), st);
-  if (e != cudaSuccess) return cuda_status(e, "clear no-alloc scratch flag");
+  // The previous call's contents stay in the array.  Every buffer but the timeout flag is
+  // fully written before it is read; the flag is left as it is, so a timeout of an earlier
+  // call stays visible to bjf_device_error_check.
 
   const int64_t vd[5] = {1, d->channels, d->frames, d->height, d->width};
   rc = launch_scores(video, d->video_dtype, vd, S, d->tubelet_size, d->patch_size, scores, st, true);

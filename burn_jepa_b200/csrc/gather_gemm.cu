@@ -50,7 +50,9 @@ constexpr int kMmaWarp = 8;
 constexpr int kTmaWarp = 9;
 constexpr int kThreads = 32 * 10;
 constexpr int kMaxKBlocks = 128;  // K <= 8192
-constexpr uint64_t kWaitLimitNs = 2000000000ull;
+// Waits after a give-up (a role draining its own copies or MMAs) keep the default limit
+// whatever bjf_set_bounded_wait chose for the pipeline waits.
+constexpr uint64_t kDrainLimitNs = kDefaultWaitLimitNs;
 
 constexpr int kAStageBytes = kBM * kBK * 2;      // 16 KB
 constexpr int kBStageBytes = kMaxBN * kBK * 2;   // 32 KB
@@ -61,7 +63,7 @@ struct SmemLayout {
   static constexpr int bar_off = b_off + kStagesB * kBStageBytes;
   // full_a[A], empty_a[A], full_b[B], empty_b[B], acc_full[2], acc_empty[2], producers
   static constexpr int misc_off = bar_off + (2 * kStagesA + 2 * kStagesB + 5) * 8;
-  // tmem base (4 B), abort flag (4 B)
+  // tmem base (4 B), abort flag (4 B), stall barrier (8 B)
   static constexpr int koff_off = misc_off + 16;
   static constexpr int soff_off = koff_off + kMaxKBlocks * 8 * 4;  // stream row offsets
   static constexpr int rowbase_off = soff_off + ((kMaxRowStreams + 1) * 4 + 15) / 16 * 16;
@@ -135,7 +137,7 @@ __device__ __forceinline__ int64_t resolve_row(const RowSource& rs, const int* s
                                                int gm);
 __device__ __forceinline__ bool producer_rows(int64_t my_row, int p, int64_t* rowbase, int pw, int sub,
                                               int64_t (&base)[8], uint32_t& valid_mask, uint64_t* bar,
-                                              int& phase, volatile int* abort_flag);
+                                              int& phase, volatile int* abort_flag, uint64_t limit_ns);
 
 // Offset of element k of a tubelet row relative to its (b, t*kt, r*ph, col*pw) corner
 // (< C*T*H*W of one batch element, which the launch checks fits in int32).
@@ -160,13 +162,13 @@ __device__ __forceinline__ int64_t resolve_row(const RowSource& rs, const int* s
 
 __device__ __forceinline__ bool producer_rows(int64_t my_row, int p, int64_t* rowbase, int pw, int sub,
                                               int64_t (&base)[8], uint32_t& valid_mask, uint64_t* bar,
-                                              int& phase, volatile int* abort_flag) {
+                                              int& phase, volatile int* abort_flag, uint64_t limit_ns) {
   // every producer has read the previous tile's rows
   mbar_arrive(bar);
-  if (!mbar_wait_bounded(bar, (uint32_t)(phase++ & 1), abort_flag, kWaitLimitNs)) return false;
+  if (!mbar_wait_bounded(bar, (uint32_t)(phase++ & 1), abort_flag, limit_ns)) return false;
   rowbase[p] = my_row;
   mbar_arrive(bar);
-  if (!mbar_wait_bounded(bar, (uint32_t)(phase++ & 1), abort_flag, kWaitLimitNs)) return false;
+  if (!mbar_wait_bounded(bar, (uint32_t)(phase++ & 1), abort_flag, limit_ns)) return false;
   valid_mask = 0;
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -332,10 +334,12 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* prod_bar = acc_empty + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + SmemLayout::misc_off);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + SmemLayout::misc_off + 4);
+  uint64_t* stall_bar = reinterpret_cast<uint64_t*>(smem + SmemLayout::misc_off + 8);  // never completes
   int32_t* koff = reinterpret_cast<int32_t*>(smem + SmemLayout::koff_off);
 
   const int num_kb = g.num_kb;
   if (tid == 0) {
+    mbar_init(stall_bar, 1);
     for (int s = 0; s < kStagesA; ++s) {
       mbar_init(&full_a[s], kProducerWarps * 32);
       mbar_init(&empty_a[s], 1);
@@ -383,7 +387,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int64_t base[8];
       uint32_t dst_off[8];
       uint32_t valid_mask = 0;
-      if (!producer_rows(my_row, p, rowbase, pw_, sub, base, valid_mask, prod_bar, prod_phase, abort_flag)) {
+      if (!producer_rows(my_row, p, rowbase, pw_, sub, base, valid_mask, prod_bar, prod_phase, abort_flag, g.wait_ns)) {
         aborted = true;
         break;
       }
@@ -397,7 +401,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
         const int s = kbg % kStagesA;
         const uint32_t par = ((kbg / kStagesA) & 1) ^ 1;
-        if (!mbar_wait_bounded(&empty_a[s], par, abort_flag, kWaitLimitNs)) {
+        if (!mbar_wait_bounded(&empty_a[s], par, abort_flag, g.wait_ns)) {
           aborted = true;
           break;
         }
@@ -417,10 +421,13 @@ __global__ void __launch_bounds__(kThreads, 1)
       int kbg = 0, it = 0;
       int commits0 = 0;  // tcgen05.commit arrivals on acc_full[0] so far
       bool issued_any = false;
+      // Test hook of bjf_set_bounded_wait: a wait that runs out before any MMA is issued, so
+      // the give-up path (flag, drains, TMEM release) runs on a normal launch.
+      if (g.stall && !mbar_wait_bounded(stall_bar, 0, abort_flag, g.wait_ns)) aborted = true;
       for (int tile = blockIdx.x; tile < num_tiles && !aborted; tile += gridDim.x, ++it) {
         const int buf = it & 1;
         const uint32_t use_par = ((it >> 1) & 1) ^ 1;
-        if (!mbar_wait_bounded(&acc_empty[buf], use_par, abort_flag, kWaitLimitNs)) {
+        if (!mbar_wait_bounded(&acc_empty[buf], use_par, abort_flag, g.wait_ns)) {
           aborted = true;
           break;
         }
@@ -428,8 +435,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t d_tmem = tmem_base + (uint32_t)buf * acc_cols;
         for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
           const int sa = kbg % kStagesA, sb = kbg % kStagesB;
-          if (!mbar_wait_bounded(&full_a[sa], (kbg / kStagesA) & 1, abort_flag, kWaitLimitNs) ||
-              !mbar_wait_bounded(&full_b[sb], (kbg / kStagesB) & 1, abort_flag, kWaitLimitNs)) {
+          if (!mbar_wait_bounded(&full_a[sa], (kbg / kStagesA) & 1, abort_flag, g.wait_ns) ||
+              !mbar_wait_bounded(&full_b[sb], (kbg / kStagesB) & 1, abort_flag, g.wait_ns)) {
             aborted = true;
             break;
           }
@@ -455,7 +462,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // completes phase `commits0` once every earlier MMA is done (bounded, abort ignored).
         mma_commit(&acc_full[0]);
         int zero = 0;
-        mbar_wait_bounded(&acc_full[0], (uint32_t)(commits0 & 1), &zero, kWaitLimitNs);
+        mbar_wait_bounded(&acc_full[0], (uint32_t)(commits0 & 1), &zero, kDrainLimitNs);
       }
     }
   } else if (warp == kTmaWarp) {
@@ -467,7 +474,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
           const int s = kbg % kStagesB;
           const uint32_t par = ((kbg / kStagesB) & 1) ^ 1;
-          if (!mbar_wait_bounded(&empty_b[s], par, abort_flag, kWaitLimitNs)) {
+          if (!mbar_wait_bounded(&empty_b[s], par, abort_flag, g.wait_ns)) {
             aborted = true;
             break;
           }
@@ -479,7 +486,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         // Wait for the weight tiles still in flight before the CTA's smem goes away.
         int zero = 0;
         for (int k = max(0, kbg - kStagesB); k < kbg; ++k)
-          mbar_wait_bounded(&full_b[k % kStagesB], (k / kStagesB) & 1, &zero, kWaitLimitNs);
+          mbar_wait_bounded(&full_b[k % kStagesB], (k / kStagesB) & 1, &zero, kDrainLimitNs);
       }
     }
   } else {
@@ -490,7 +497,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++it) {
       const int buf = it & 1;
       const uint32_t par = (it >> 1) & 1;
-      bool ok = mbar_wait_bounded(&acc_full[buf], par, abort_flag, kWaitLimitNs);
+      bool ok = mbar_wait_bounded(&acc_full[buf], par, abort_flag, g.wait_ns);
       if (__any_sync(0xffffffffu, !ok)) {  // tcgen05.ld is warp-collective: decide per warp
         aborted = true;
         break;
@@ -777,7 +784,7 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
       int64_t base[8];
       uint32_t dst_off[8];
       uint32_t valid_mask = 0;
-      if (!producer_rows(my_row, p, rowbase, pw_, sub, base, valid_mask, prod_bar, prod_phase, abort_flag)) {
+      if (!producer_rows(my_row, p, rowbase, pw_, sub, base, valid_mask, prod_bar, prod_phase, abort_flag, g.wait_ns)) {
         aborted = true;
         break;
       }
@@ -793,7 +800,7 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
       for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
         const int s = kbg % kPairStages;
         const uint32_t par = ((kbg / kPairStages) & 1) ^ 1;
-        if (!mbar_wait_bounded(&empty[s], par, abort_flag, kWaitLimitNs)) {
+        if (!mbar_wait_bounded(&empty[s], par, abort_flag, g.wait_ns)) {
           aborted = true;
           break;
         }
@@ -813,7 +820,7 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
       const int it_last = my_tiles - 1;
       const int tile = cluster + it_last * nclusters;
       const int buf = it_last & 1;
-      bool ok = mbar_wait_bounded(&acc_full[buf], (uint32_t)((it_last >> 1) & 1), abort_flag, kWaitLimitNs);
+      bool ok = mbar_wait_bounded(&acc_full[buf], (uint32_t)((it_last >> 1) & 1), abort_flag, g.wait_ns);
       if (__any_sync(0xffffffffu, !ok)) {
         aborted = true;
       } else {
@@ -839,7 +846,7 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
       for (int tile = cluster; tile < num_tiles && !aborted; tile += nclusters, ++it) {
         const int buf = it & 1;
         const uint32_t use_par = ((it >> 1) & 1) ^ 1;
-        if (!mbar_wait_bounded_cluster(&acc_empty[buf], use_par, abort_flag, kWaitLimitNs)) {
+        if (!mbar_wait_bounded_cluster(&acc_empty[buf], use_par, abort_flag, g.wait_ns)) {
           aborted = true;
           break;
         }
@@ -848,8 +855,8 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
         for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
           const int s = kbg % kPairStages;
           const uint32_t par = (kbg / kPairStages) & 1;
-          if (!mbar_wait_bounded(&full[s], par, abort_flag, kWaitLimitNs) ||
-              !mbar_wait_bounded_cluster(&peer_full[s], par, abort_flag, kWaitLimitNs)) {
+          if (!mbar_wait_bounded(&full[s], par, abort_flag, g.wait_ns) ||
+              !mbar_wait_bounded_cluster(&peer_full[s], par, abort_flag, g.wait_ns)) {
             aborted = true;
             break;
           }
@@ -874,7 +881,7 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
         // (a commit to this CTA only; bounded, abort ignored)
         mma_commit_pair(&acc_full[0], 0x1);
         int zero = 0;
-        mbar_wait_bounded(&acc_full[0], (uint32_t)(commits0 & 1), &zero, kWaitLimitNs);
+        mbar_wait_bounded(&acc_full[0], (uint32_t)(commits0 & 1), &zero, kDrainLimitNs);
       }
     } else if (rank == 1 && lane < kPairStages) {
       // ---------------- stage relay (odd CTA): lane s relays stage s ----------------
@@ -882,7 +889,7 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
       const uint32_t remote = cluster_map(smem_u32(&peer_full[s]), 0);
       const int total_kb = my_tiles * num_kb;
       for (int kbg = s; kbg < total_kb; kbg += kPairStages) {
-        if (!mbar_wait_bounded(&full[s], (kbg / kPairStages) & 1, abort_flag, kWaitLimitNs)) {
+        if (!mbar_wait_bounded(&full[s], (kbg / kPairStages) & 1, abort_flag, g.wait_ns)) {
           aborted = true;
           break;
         }
@@ -899,7 +906,7 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
         for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
           const int s = kbg % kPairStages;
           const uint32_t par = ((kbg / kPairStages) & 1) ^ 1;
-          if (!mbar_wait_bounded(&empty[s], par, abort_flag, kWaitLimitNs)) {
+          if (!mbar_wait_bounded(&empty[s], par, abort_flag, g.wait_ns)) {
             aborted = true;
             break;
           }
@@ -910,7 +917,7 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
       // Every stage release is a multicast from the even CTA's MMA thread: wait until the
       // last one of each stage has landed here before this CTA's shared memory goes away.
       int zero = 0;
-      const uint64_t limit = aborted ? 1000000ull : kWaitLimitNs;
+      const uint64_t limit = aborted ? 1000000ull : kDrainLimitNs;
       for (int k = max(0, kbg - kPairStages); k < kbg; ++k)
         mbar_wait_bounded(&empty[k % kPairStages], (k / kPairStages) & 1, &zero, limit);
     }
@@ -926,7 +933,7 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
     for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
       const int buf = it & 1;
       const uint32_t par = (it >> 1) & 1;
-      bool ok = mbar_wait_bounded(&acc_full[buf], par, abort_flag, kWaitLimitNs);
+      bool ok = mbar_wait_bounded(&acc_full[buf], par, abort_flag, g.wait_ns);
       if (__any_sync(0xffffffffu, !ok)) {
         aborted = true;
         break;
@@ -1110,6 +1117,9 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
   GatherGeometry g = g0;
   g.num_kb = g.K / kBK;
   g.is_bf16 = in_dt == BJF_DTYPE_BF16;
+  const BoundedWait bw = bounded_wait();
+  g.wait_ns = bw.limit_ns;
+  g.stall = bw.stall;
   if (sm100_path_supported(dev, g, in_dt, w_dt, input, weight) &&
       (int64_t)g.C * g.T * g.H * g.W < (int64_t(1) << 31)) {
     EncodeTiledFn encode = nullptr;

@@ -18,6 +18,8 @@ struct GatherGeometry {
   int K, D;            // C*kt*ph*pw and output channels
   int num_kb;          // K / 64 (tensor-core path)
   int is_bf16;
+  uint64_t wait_ns;    // limit of every bounded pipeline wait (bjf_set_bounded_wait)
+  int stall;           // 1: the single-CTA kernel's MMA thread waits on a barrier nothing completes
 };
 
 enum { kEpiloguePlain = 0, kEpilogueScatter = 1 };

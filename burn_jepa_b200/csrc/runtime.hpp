@@ -20,6 +20,22 @@ struct DeviceInfo {
 // State of the current device (cudaGetDevice()), created on first use.
 bjf_status current_device(const DeviceInfo** out);
 
+// State of device `dev` if current_device() has created it, else nullptr (creates nothing).
+const DeviceInfo* peek_device(int dev);
+
+// Device address of the timeout flag of bjf_front_end_step_no_alloc on device `dev`, or
+// nullptr when that step has never been set up there (front_end_no_alloc.cu).
+int* no_alloc_error_flag(int dev);
+
+// Time limit of the bounded pipeline waits of the gather-GEMM kernels, and the stall switch
+// of bjf_set_bounded_wait (launches enqueued after a change use the new values).
+constexpr uint64_t kDefaultWaitLimitNs = 2000000000ull;
+struct BoundedWait {
+  uint64_t limit_ns;
+  int32_t stall;
+};
+BoundedWait bounded_wait();
+
 // cuTensorMapEncodeTiled from the driver (resolved once through the runtime).
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,

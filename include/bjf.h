@@ -97,8 +97,20 @@ BJF_API size_t bjf_get_last_error_string(char* buf, size_t len);
 /* Synchronises `stream` and reports whether any kernel of this library on the
  * current device gave up on a bounded wait since the last check (*flag_out = 1;
  * the flag is then cleared).  Kernels never spin forever: a pipeline wait that
- * exceeds its time limit records this flag, releases its resources and returns. */
+ * exceeds its time limit records this flag, releases its resources and returns.
+ * Covers the workspace entry points and bjf_front_end_step_no_alloc alike; the
+ * check itself allocates nothing. */
 BJF_API bjf_status bjf_device_error_check(bjf_stream_t stream, int32_t* flag_out);
+
+/* No counterpart in the reference (its failure handling is host-side): sets the time limit of
+ * every bounded pipeline wait in the gather-GEMM kernels for launches enqueued after the call
+ * (limit_ns; 0 restores the default of 2 s).  stall = 1 is a test hook for the give-up path:
+ * the MMA thread of the single-CTA tensor-core kernel (launches of at most 128 rows) first
+ * waits on a barrier that nothing completes, so that wait runs out after limit_ns, the kernel
+ * drains its copies, frees its TMEM, returns and sets the flag bjf_device_error_check reports;
+ * stall = 0 turns it off.  Process-wide; not meant to change while launches are being
+ * enqueued on other threads. */
+BJF_API bjf_status bjf_set_bounded_wait(uint64_t limit_ns, int32_t stall);
 
 /* ------------------------------------------------------------------------
  * Step 1: patch-diff mask
@@ -369,7 +381,10 @@ BJF_API bjf_status bjf_front_end_step(const bjf_front_end_desc* desc, const void
  * 520k (the bench's 32 streams x 4096 tokens fit); larger steps return
  * BJF_ERR_UNSUPPORTED.  All calls on a device share that array: calls that overlap on the
  * GPU race, so issue them in order on one stream.  The first call on each device looks up
- * the array's address; make it before any stream capture begins.  A call allocates
+ * the array's address and clears its timeout flag; make it before any stream capture
+ * begins.  The address is kept for the life of the process: resetting the device
+ * (cudaDeviceReset) while the library is loaded is not supported.  A bounded-wait timeout
+ * is reported by bjf_device_error_check, as for the workspace step.  A call allocates
  * nothing. */
 BJF_API bjf_status bjf_front_end_step_no_alloc(const bjf_front_end_desc* desc, const void* video,
                                                const void* weight, const float* bias, void* caches,
