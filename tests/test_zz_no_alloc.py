@@ -145,7 +145,7 @@ def test_no_alloc_step_matches_the_oracle(cuda_device):
     gc = got["cache"].float().cpu().numpy()
     assert np.array_equal(gc[~written], cache[~written])
     assert max_rel_err(gc[written], cache[written]) <= 1e-2
-    assert int(written.sum()) > 0 and grid.len() == n
+    assert int(written.sum()) > 0 and len(grid) == n
 
 
 @pytest.mark.gpu
