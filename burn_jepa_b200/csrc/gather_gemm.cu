@@ -160,6 +160,34 @@ __device__ __forceinline__ int64_t resolve_row(const RowSource& rs, const int* s
   return valid ? o : -1;
 }
 
+// A row in two steps, so that its load need not stall the thread that issues it: fetch_row_raw
+// issues the load (explicit coords, or the stream and token index; rows beyond M give a
+// marker), decode_row turns the loaded value into (b, t, r, col) as fetch_row does, and
+// row_offset gives its element offset (-1 for a zero row).
+__device__ __forceinline__ int4 fetch_row_raw(const RowSource& rs, const int* soff, int M, int gm) {
+  if (gm >= M) return make_int4(-1, -1, -1, -2);
+  if (rs.coords) return __ldg(rs.coords + gm);
+  int lo = 0, hi = rs.streams;  // soff[lo] <= gm < soff[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (soff[mid] <= gm) lo = mid; else hi = mid;
+  }
+  return make_int4(lo, __ldg(rs.indices + (int64_t)lo * rs.index_stride + (gm - soff[lo])), 0, 0);
+}
+__device__ __forceinline__ int4 decode_row(const RowSource& rs, const GatherGeometry& g, int4 raw) {
+  if (raw.x == -1 && raw.w == -2) return make_int4(-1, -1, -1, -1);
+  if (rs.coords) return raw;
+  const int idx = raw.y, tpf = g.gh * g.gw;
+  if (idx < 0 || idx >= g.depth * tpf) return make_int4(raw.x, -1, -1, -1);
+  const int t = idx / tpf, rem = idx - t * tpf, r = rem / g.gw;
+  return make_int4(raw.x, t, r, rem - r * g.gw);
+}
+__device__ __forceinline__ int64_t row_offset(const GatherGeometry& g, int4 c) {
+  bool valid = false;
+  const int64_t o = row_base_offset(g, c, valid);
+  return valid ? o : -1;
+}
+
 __device__ __forceinline__ bool producer_rows(int64_t my_row, int p, int64_t* rowbase, int pw, int sub,
                                               int64_t (&base)[8], uint32_t& valid_mask, uint64_t* bar,
                                               int& phase, volatile int* abort_flag, uint64_t limit_ns) {
@@ -206,11 +234,12 @@ __device__ __forceinline__ int4 next_row(const RowSource& rs, const int* soff, c
 }
 
 // Encoder-input epilogue terms for 32 columns starting at col0 (ncol valid): + the row's
-// position embedding, then + the modality embedding (src/model.rs:690-703).  Rows without a
-// table row (zero rows) stay zero.  Warp-collective (the modality vector is broadcast).
+// position embedding, then + the modality embedding (src/model.rs:690-703); `mod` holds the
+// modality values of these 32 columns, null without one.  Rows without a table row (zero
+// rows) stay zero.  Warp-collective (the modality vector is broadcast).
 // kVec: 16-byte table loads for full aligned chunks.
 template <bool kVec>
-__device__ __forceinline__ void add_encoder_embeddings(const EpilogueArgs& ep, bool valid, const float* pos_row,
+__device__ __forceinline__ void add_encoder_embeddings(bool valid, const float* pos_row, const float* mod,
                                                        int col0, int ncol, int lane, float (&v)[32]) {
   if (pos_row) {
     const float* p = pos_row + col0;
@@ -231,8 +260,8 @@ __device__ __forceinline__ void add_encoder_embeddings(const EpilogueArgs& ep, b
         if (j < ncol) v[j] = v[j] + __ldg(p + j);
     }
   }
-  if (ep.modality_embed) {
-    const float ml = lane < ncol ? __ldg(ep.modality_embed + col0 + lane) : 0.0f;
+  if (mod) {
+    const float ml = lane < ncol ? __ldg(mod + lane) : 0.0f;
 #pragma unroll
     for (int j = 0; j < 32; ++j) {
       const float m = __shfl_sync(0xffffffffu, ml, j);
@@ -278,7 +307,8 @@ __device__ __forceinline__ void drain_accumulator(const GatherGeometry& g, const
       const float b = __shfl_sync(0xffffffffu, bl, j);
       v[j] = valid ? __uint_as_float(r[j]) + b : 0.0f;
     }
-    add_encoder_embeddings<false>(ep, valid, pos_row, col0, ncol, lane, v);
+    add_encoder_embeddings<false>(valid, pos_row, ep.modality_embed ? ep.modality_embed + col0 : nullptr, col0, ncol,
+                                  lane, v);
     if (!dst_row) continue;
     char* dst = dst_row + (int64_t)col0 * ce;
     if (ep.out_dtype == BJF_DTYPE_F32)
@@ -535,11 +565,18 @@ __global__ void __launch_bounds__(kThreads, 1)
 // rows of A and loads half of the BN weight rows (B) by TMA into the same shared-memory
 // offsets, and the even CTA issues tcgen05.mma.cta_group::2 (M = 256) that reads both CTAs'
 // operands and writes 128 rows of D into each CTA's TMEM.  Per SM this halves the weight
-// traffic of the 128 x BN tile of the single-CTA kernel for the same tensor work, so the
-// shared memory goes to a deeper ring of gathered rows (the latency-bound operand).
+// traffic of the 128 x BN tile of the single-CTA kernel for the same tensor work.  BN = 256
+// whenever D > 256 (D = 1408 runs five full column tiles and a half-empty sixth): A is gathered
+// once per 256 output columns, and the gather -- bound by its request rate, each 32-byte patch
+// row of a tubelet in its own cache line -- is what limits the main loop.  Two TMEM
+// accumulators of 256 columns let a tile's epilogue overlap the next tile's MMAs.
 //
-// Stage handshake: a stage (16 KB of gathered rows + BN/2 x 64 of B per CTA) is full in a
-// CTA when its 128 producer threads' cp.async arrivals and its TMA bytes have landed.
+// (Tiles of 256 x 512 with one accumulator filling TMEM gather A half as often and ran the
+// main loop at about 1.3 PFLOP/s, but the epilogue then stalls the tensor pipe for each tile,
+// and the whole was slower than overlapped 256-column tiles.)
+//
+// Stage handshake: a stage (16 KB of gathered rows + BN/2 x 64 weight rows per CTA) is full in
+// a CTA when its 128 producer threads' cp.async arrivals and its TMA bytes have landed.
 // cp.async and TMA can only signal barriers of their own CTA, so lanes of the odd CTA's MMA
 // warp relay, one lane per stage: a lane waits for its stage's local full barrier, fences
 // the stage into the async proxy and arrives (relaxed, cluster scope) on the even CTA's
@@ -548,65 +585,96 @@ __global__ void __launch_bounds__(kThreads, 1)
 // (acc_full) to both CTAs.  Both CTAs' epilogue warps hand the accumulator back on the even
 // CTA's acc_empty barrier.
 //
-// Epilogue: each epilogue warp converts its 32 accumulator rows 256 bytes of output at a
-// time into a shared-memory staging tile (rows padded to 272 bytes, so the rows a quarter-warp
-// writes fall in distinct banks) and each lane sends its row's 256 bytes to global memory
-// with one bulk asynchronous copy.  The copies run on the TMA engine, not the load/store pipe
-// that also carries the gather; one staging buffer per warp (the next chunk waits for the
-// previous copy to have read it) measured faster than two of 128 bytes, which cost shared
-// memory that the overlapping scores pass uses.
-constexpr int kPairStages = 4;
-constexpr int kBHalfStageBytes = (kMaxBN / 2) * kBK * 2;  // 16 KB
-constexpr int kEpiChunkBytes = 256;                       // output bytes per row per bulk copy
-constexpr int kEpiRowPitch = kEpiChunkBytes + 16;
-constexpr int kEpiBufs = 1;
-constexpr int kEpiWarpBytes = kEpiBufs * 32 * kEpiRowPitch;
+// Epilogue: each epilogue warp converts its 32 accumulator rows 64 output bytes per row at a
+// time into a shared-memory staging tile and writes the staged rows back with 16-byte stores,
+// four lanes per row (drain_accumulator_rows).
+constexpr int kPairStages = 5;
+constexpr int kBHalfStageBytes = (kMaxBN / 2) * kBK * 2;  // 16 KB: 128 weight rows x 64
+constexpr int kEpiRowBytes = 64;                          // output bytes per row per staged chunk
+constexpr int kEpiRowPitch = kEpiRowBytes + 16;           // rows a quarter-warp writes fall in distinct banks
+constexpr int kEpiWarpBytes = 32 * kEpiRowPitch + 32 * 8; // one warp's staging tile + its 32 row addresses
 static_assert(kPairStages <= 32, "one relay lane per stage");
 
+template <bool kEmbed>
 struct PairSmemLayout {
+  // per tile: bias (and, kEmbed, modality) of its columns, two tiles' worth
+  static constexpr int kColBufFloats = (kEmbed ? 2 : 1) * kMaxBN;
   static constexpr int a_off = 0;
   static constexpr int b_off = a_off + kPairStages * kAStageBytes;
-  static constexpr int epi_off = b_off + kPairStages * kBHalfStageBytes;
-  static constexpr int bar_off = epi_off + kEpilogueWarps * kEpiWarpBytes;
-  // full[S], peer_full[S], empty[S], acc_full[2], acc_empty[2], producers
-  static constexpr int misc_off = bar_off + (3 * kPairStages + 5) * 8;
+  static constexpr int epi_off = b_off + kPairStages * kBHalfStageBytes;     // epilogue warps' staging
+  static constexpr int pepi_off = epi_off + kEpilogueWarps * kEpiWarpBytes;  // producer warps' staging
+  static constexpr int col_off = pepi_off + kProducerWarps * kEpiWarpBytes;
+  static constexpr int bar_off = col_off + 2 * kColBufFloats * 4;
+  // full[S], peer_full[S], empty[S], acc_full[2], acc_empty[2], producers, col_ready[2]
+  static constexpr int misc_off = bar_off + (3 * kPairStages + 7) * 8;
   // tmem base (4 B), abort flag (4 B)
-  static constexpr int koff_off = misc_off + 16;
-  static constexpr int soff_off = koff_off + kMaxKBlocks * 8 * 4;  // stream row offsets
-  static constexpr int rowbase_off = soff_off + ((kMaxRowStreams + 1) * 4 + 15) / 16 * 16;
-  static constexpr int total = rowbase_off + kBM * 8;
-  static constexpr int alloc = total + 1024;
-};
-static_assert(PairSmemLayout::alloc <= 227 * 1024, "pair kernel shared memory");
-
-// Converts 32 accumulator values + bias into `ncol` (<= 32) output elements at `dst`
-// (shared memory, 16-byte aligned; ncol * sizeof(O) bytes).
-template <typename O>
-__device__ __forceinline__ void pack_chunk32(uint8_t* dst, const float (&v)[32], int ncol) {
-  O* o = reinterpret_cast<O*>(dst);
-  if (ncol == 32) {
-#pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-      float w8[8] = {v[j], v[j + 1], v[j + 2], v[j + 3], v[j + 4], v[j + 5], v[j + 6], v[j + 7]};
-      store8<O>(o + j, w8);
-    }
-  } else {
-#pragma unroll
-    for (int j = 0; j < 32; ++j)
-      if (j < ncol) o[j] = from_f32<O>(v[j]);
+  static constexpr int rowbase_off = misc_off + 16;
+  static constexpr int koff_off = rowbase_off + kBM * 8;
+  // then the K-offset table (num_kb * 8 ints) and the stream row offsets (streams + 1 ints),
+  // sized at launch; + 1 KB to align the base to 1024 bytes
+  static constexpr size_t bytes(int num_kb, int streams) {
+    return (size_t)koff_off + (size_t)num_kb * 32 + ((size_t)streams + 1) * 4 + 1024;
   }
+  // more than half of an SM's 228 KB: one CTA per SM whatever the launch's stream count
+  static_assert(koff_off > 114 * 1024, "pair kernel residency");
+};
+static_assert(PairSmemLayout<true>::bytes(kMaxKBlocks, kMaxRowStreams) <= 227 * 1024, "pair kernel smem");
+
+// Converts 16 values to the output type and stores them at `dst` (shared memory, 16-byte
+// aligned): packed two-element conversions, 16-byte stores.
+template <typename O>
+__device__ __forceinline__ void pack16(uint8_t* dst, const float (&v)[16]);
+template <>
+__device__ __forceinline__ void pack16<float>(uint8_t* dst, const float (&v)[16]) {
+  float4* d = reinterpret_cast<float4*>(dst);
+#pragma unroll
+  for (int q = 0; q < 4; ++q) d[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+}
+template <>
+__device__ __forceinline__ void pack16<__half>(uint8_t* dst, const float (&v)[16]) {
+  uint32_t w[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const __half2 h = __floats2half2_rn(v[2 * q], v[2 * q + 1]);
+    w[q] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
+}
+template <>
+__device__ __forceinline__ void pack16<__nv_bfloat16>(uint8_t* dst, const float (&v)[16]) {
+  uint32_t w[8];
+#pragma unroll
+  for (int q = 0; q < 8; ++q) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * q], v[2 * q + 1]);
+    w[q] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  reinterpret_cast<uint4*>(dst)[0] = make_uint4(w[0], w[1], w[2], w[3]);
+  reinterpret_cast<uint4*>(dst)[1] = make_uint4(w[4], w[5], w[6], w[7]);
 }
 
-// Epilogue of one accumulator through shared-memory staging and bulk stores: this warp's
-// 32 TMEM lanes (tile rows, lane = thread) x bn columns from `taddr` -> + bias -> the row's
-// destination.  `stage` / `stage_smem` address this warp's staging buffers; `chunk` counts
-// this thread's staged chunks (selects the buffer).  Warp-collective.
-// Columns [c_begin, c_end) of the accumulator (c_begin a multiple of the chunk width).
+// Epilogue of one accumulator through a per-warp staging tile and line-wide stores: this
+// warp's 32 TMEM lanes (tile rows, lane = thread) x columns [c_begin, c_end) from `taddr` ->
+// + bias (-> + embeddings) -> converted -> each row's destination (plain [M, D], or its
+// token-cache slot, which also marks the slot observed with age 0).
+//
+// Per chunk of 64 output bytes per row (32 columns of 16-bit output, 16 of f32) each lane
+// stages its own row 16 columns at a time -- one tcgen05.ld of 16 columns, the bias (and
+// modality) as broadcast 16-byte shared-memory loads, packed conversions, 16-byte shared
+// stores -- and the warp then writes the 32 staged rows back eight at a time, four lanes x 16
+// bytes per row (the row addresses read from shared memory).  The per-row work is short,
+// independent instruction runs: the warp issues in order under an 80-register budget, and a
+// column loop of dependent shuffle -> add pairs (one shuffle per column to broadcast the bias)
+// ran at one instruction per latency.
+// bias_s / mod_s: the bias and modality values of accumulator columns [0, c_end) (shared
+// memory, 16-byte aligned, staged ahead by the epilogue warps; mod_s null without a modality
+// vector).  `stage` is this warp's staging tile: 32 rows x kEpiRowPitch bytes, then 32 row
+// addresses.  c_begin is a multiple of the chunk width.  Warp-collective.
 template <bool kEmbed>
-__device__ __forceinline__ void drain_accumulator_bulk(const GatherGeometry& g, const EpilogueArgs& ep, int4 c,
+__device__ __forceinline__ void drain_accumulator_rows(const GatherGeometry& g, const EpilogueArgs& ep, int4 c,
                                                        int M, int gm, int n0, int c_begin, int c_end, uint32_t taddr,
-                                                       int lane, uint8_t* stage, uint32_t stage_smem, int& chunk) {
-  const int bn = c_end;
+                                                       int lane, uint8_t* stage, const float* bias_s,
+                                                       const float* mod_s) {
   const int ce = ep.out_elem_bytes;
   bool valid = false;
   char* dst_row = nullptr;
@@ -627,47 +695,91 @@ __device__ __forceinline__ void drain_accumulator_bulk(const GatherGeometry& g, 
       }
     }
   }
-  const int cpc = kEpiChunkBytes / ce;  // columns per chunk: 128 (16-bit) or 64 (f32)
-  for (int c0 = c_begin; c0 < bn; c0 += cpc, ++chunk) {
+  // 16-byte stores need 16-byte aligned rows (output base and row pitch; column offsets of a
+  // chunk are multiples of 32 bytes)
+  const bool vec = ((reinterpret_cast<uintptr_t>(ep.out) | (uintptr_t)(ep.ldo * ce)) & 15) == 0;
+  const int cpc = kEpiRowBytes / ce;  // columns per chunk
+  char** rowptr = reinterpret_cast<char**>(stage + 32 * kEpiRowPitch);
+  __syncwarp();  // the previous drain's write-back has read the row addresses
+  rowptr[lane] = dst_row;
+  uint8_t* srow = stage + lane * kEpiRowPitch;
+  constexpr int kSegs = kEpiRowBytes / 16;  // 16-byte segments of a staged row
+  const int seg = lane % kSegs;             // this lane's segment of a row in the write-back
+  for (int c0 = c_begin; c0 < c_end; c0 += cpc) {
     const int col0 = n0 + c0;
-    const int ncol = min(cpc, min(bn - c0, g.D - col0));  // the same for the whole warp
+    const int ncol = min(cpc, min(c_end - c0, g.D - col0));  // the same for the whole warp
     if (ncol <= 0) break;
-    const int buf = chunk % kEpiBufs;
-    bulk_wait_read<kEpiBufs - 1>();  // this buffer's previous copy has read its source
-    __syncwarp();
-    uint8_t* srow = stage + buf * (32 * kEpiRowPitch) + lane * kEpiRowPitch;
-    for (int h = 0; h * 32 < ncol; ++h) {
-      uint32_t r[32];
-      tmem_ld_32x32b_x32(taddr + (uint32_t)(c0 + 32 * h), r);
+    __syncwarp();  // the previous chunk's staged rows have been written out
+    for (int q = 0; q * 16 < ncol; ++q) {
+      uint32_t r[16];
+      tmem_ld_32x32b_x16(taddr + (uint32_t)(c0 + 16 * q), r);
       tmem_ld_wait();
-      const int nh = min(32, ncol - 32 * h);
-      const float bl = (ep.bias && lane < nh) ? __ldg(ep.bias + col0 + 32 * h + lane) : 0.0f;
-      float v[32];
+      const float4* b4 = reinterpret_cast<const float4*>(bias_s + c0 + 16 * q);  // same address in every lane
+      float v[16];
 #pragma unroll
-      for (int j = 0; j < 32; ++j) {
-        const float b = __shfl_sync(0xffffffffu, bl, j);
-        v[j] = valid ? __uint_as_float(r[j]) + b : 0.0f;
+      for (int k = 0; k < 4; ++k) {
+        const float4 b = b4[k];
+        v[4 * k] = valid ? __uint_as_float(r[4 * k]) + b.x : 0.0f;
+        v[4 * k + 1] = valid ? __uint_as_float(r[4 * k + 1]) + b.y : 0.0f;
+        v[4 * k + 2] = valid ? __uint_as_float(r[4 * k + 2]) + b.z : 0.0f;
+        v[4 * k + 3] = valid ? __uint_as_float(r[4 * k + 3]) + b.w : 0.0f;
       }
-      add_encoder_embeddings<kEmbed>(ep, valid, pos_row, col0 + 32 * h, nh, lane, v);
-      uint8_t* d = srow + 32 * h * ce;
+      if (kEmbed) {
+        const int nq = min(16, ncol - 16 * q);
+        if (pos_row) {  // the row's position embedding (this lane's own table row)
+          const float* p = pos_row + col0 + 16 * q;
+          if (nq == 16 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+              const float4 t = __ldg(reinterpret_cast<const float4*>(p) + k);
+              v[4 * k] = v[4 * k] + t.x;
+              v[4 * k + 1] = v[4 * k + 1] + t.y;
+              v[4 * k + 2] = v[4 * k + 2] + t.z;
+              v[4 * k + 3] = v[4 * k + 3] + t.w;
+            }
+          } else {
+#pragma unroll
+            for (int k = 0; k < 16; ++k)
+              if (k < nq) v[k] = v[k] + __ldg(p + k);
+          }
+        }
+        if (mod_s && valid) {  // then the modality embedding (broadcast, like the bias)
+          const float4* m4 = reinterpret_cast<const float4*>(mod_s + c0 + 16 * q);
+#pragma unroll
+          for (int k = 0; k < 4; ++k) {
+            const float4 mm = m4[k];
+            v[4 * k] = v[4 * k] + mm.x;
+            v[4 * k + 1] = v[4 * k + 1] + mm.y;
+            v[4 * k + 2] = v[4 * k + 2] + mm.z;
+            v[4 * k + 3] = v[4 * k + 3] + mm.w;
+          }
+        }
+      }
+      uint8_t* d = srow + 16 * q * ce;
       if (ep.out_dtype == BJF_DTYPE_F32)
-        pack_chunk32<float>(d, v, nh);
+        pack16<float>(d, v);
       else if (ep.out_dtype == BJF_DTYPE_F16)
-        pack_chunk32<__half>(d, v, nh);
+        pack16<__half>(d, v);
       else
-        pack_chunk32<__nv_bfloat16>(d, v, nh);
+        pack16<__nv_bfloat16>(d, v);
     }
-    if (dst_row) {
-      char* dst = dst_row + (int64_t)col0 * ce;
-      const uint32_t nbytes = (uint32_t)(ncol * ce);
-      if (((reinterpret_cast<uintptr_t>(dst) | nbytes) & 15) == 0) {
-        fence_proxy_async_smem();  // the staged bytes feed the bulk copy (async proxy)
-        bulk_store_s2g(dst, stage_smem + (uint32_t)(buf * (32 * kEpiRowPitch) + lane * kEpiRowPitch), nbytes);
-      } else {
-        for (uint32_t b = 0; b < nbytes; ++b) dst[b] = static_cast<char>(srow[b]);  // unaligned row: bytes
+    __syncwarp();  // every row of the chunk is staged
+    const int left = ncol * ce - seg * 16;  // bytes of this lane's segment that lie inside the chunk
+    if (left > 0) {
+#pragma unroll 4
+      for (int r0 = 0; r0 < 32; r0 += 32 / kSegs) {
+        const int rr = r0 + lane / kSegs;
+        char* d = rowptr[rr];  // the same address in the lanes of a row
+        if (!d) continue;
+        d += (int64_t)col0 * ce + seg * 16;
+        const uint8_t* sp = stage + rr * kEpiRowPitch + seg * 16;
+        if (vec && left >= 16) {
+          *reinterpret_cast<uint4*>(d) = *reinterpret_cast<const uint4*>(sp);
+        } else {
+          for (int k = 0; k < min(left, 16); ++k) d[k] = static_cast<char>(sp[k]);
+        }
       }
     }
-    bulk_commit();
   }
 }
 
@@ -680,44 +792,50 @@ __device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_addr
 // At most 80 registers per thread: with three of the ten warps on one SM sub-partition that
 // leaves room beside each CTA for two blocks of the next frame's patch-diff pass (which
 // programmatic dependent launch starts while this kernel runs).  kEmbed: the instantiation for
-// the encoder-input epilogue, whose 16-byte position-table loads need more registers (it never
-// runs beside the patch-diff pass, so it may take them).
+// the encoder-input epilogue, whose position-table loads need more registers (it never runs
+// beside the patch-diff pass, so it may take them).
 template <typename T, bool kEmbed>
 __global__ void __maxnreg__(kEmbed ? 128 : 80)
     gather_gemm_sm100_pair_kernel(const __grid_constant__ CUtensorMap wmap, const T* __restrict__ video,
                                   const RowSource rs, const int32_t* __restrict__ rows_dev,
                                   int rows_cap, GatherGeometry g, int bn, EpilogueArgs ep,
                                   int* __restrict__ error_flag) {
+  using L = PairSmemLayout<kEmbed>;
   extern __shared__ uint8_t smem_dyn[];
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
   // both CTAs use the same dynamic shared memory base, so offsets agree across the pair
   uint8_t* smem = smem_dyn + ((1024 - (smem_u32(smem_dyn) & 1023)) & 1023);
-  int* soff = reinterpret_cast<int*>(smem + PairSmemLayout::soff_off);
-  int64_t* rowbase = reinterpret_cast<int64_t*>(smem + PairSmemLayout::rowbase_off);
+  int64_t* rowbase = reinterpret_cast<int64_t*>(smem + L::rowbase_off);
+  int32_t* koff = reinterpret_cast<int32_t*>(smem + L::koff_off);
+  const int num_kb = g.num_kb;
+  int* soff = koff + num_kb * 8;  // stream row offsets, after the K-offset table
 
   const uint32_t rank = cluster_ctarank();  // 0: issues the MMAs
   const int cluster = (int)(blockIdx.x >> 1);
   const int nclusters = (int)(gridDim.x >> 1);
   const int n_tiles = (g.D + bn - 1) / bn;
-  const int half = bn >> 1;
+  const int half = bn >> 1;  // weight rows per CTA
   // On the CTA's last tile the producer warps, idle by then, drain accumulator columns
-  // [split, bn) while the epilogue warps drain [0, split): a chunk-aligned half.
-  const int epi_chunk_cols = kEpiChunkBytes / ep.out_elem_bytes;
-  const int split = (bn / 2) / epi_chunk_cols * epi_chunk_cols;
+  // [split, bn) while the epilogue warps drain [0, split): a chunk-aligned half.  They wait for
+  // the accumulator's phase by parity, unambiguous only if the MMAs are at most one phase of
+  // that buffer behind, which the ring guarantees from two K stages per tile on (with one, the
+  // epilogue warps drain it all).
+  const int epi_chunk_cols = kEpiRowBytes / ep.out_elem_bytes;
+  const int split = num_kb >= 2 ? (bn / 2) / epi_chunk_cols * epi_chunk_cols : 0;
 
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + PairSmemLayout::bar_off);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bar_off);
   uint64_t* peer_full = full + kPairStages;
   uint64_t* empty = peer_full + kPairStages;
   uint64_t* acc_full = empty + kPairStages;
   uint64_t* acc_empty = acc_full + 2;
   uint64_t* prod_bar = acc_empty + 2;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + PairSmemLayout::misc_off);
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + PairSmemLayout::misc_off + 4);
-  int32_t* koff = reinterpret_cast<int32_t*>(smem + PairSmemLayout::koff_off);
+  uint64_t* col_ready = prod_bar + 1;  // [2]: a tile's column buffer is staged
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::misc_off);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::misc_off + 4);
+  float* colbuf = reinterpret_cast<float*>(smem + L::col_off);  // [2][kColBufFloats]
 
-  const int num_kb = g.num_kb;
   if (tid == 0) {
     for (int s = 0; s < kPairStages; ++s) {
       mbar_init(&full[s], kProducerWarps * 32 + 1);  // 128 cp.async arrivals + the TMA thread
@@ -729,6 +847,7 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
       mbar_init(&acc_empty[b], 2 * kEpilogueWarps);  // epilogue warps of both CTAs
     }
     mbar_init(prod_bar, kProducerWarps * 32);
+    for (int b = 0; b < 2; ++b) mbar_init(&col_ready[b], kEpilogueWarps * 32);
     *abort_flag = 0;
     fence_mbarrier_init();
   }
@@ -765,33 +884,45 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
   }
   const int my_tiles = (num_tiles - cluster + nclusters - 1) / nclusters;
 
-  const uint32_t a_smem = smem_u32(smem + PairSmemLayout::a_off);
-  const uint32_t b_smem = smem_u32(smem + PairSmemLayout::b_off);
+  const uint32_t a_smem = smem_u32(smem + L::a_off);
+  const uint32_t b_smem = smem_u32(smem + L::b_off);
   bool aborted = false;
+  auto acc_tmem = [&](int it) { return tmem_base + (uint32_t)(it & 1) * acc_cols; };
+  // The bias (and modality) values of the `it`-th tile's columns, staged in shared memory by the
+  // epilogue warps a tile ahead, buffer it & 1, published on col_ready[it & 1].  A global load
+  // issued in the drain itself would wait behind the producers' in-flight gathers on the
+  // critical path.  A buffer is rewritten for tile it + 2 only after every epilogue warp
+  // drained tile it (the MMAs of tile it + 2 need that accumulator back), so the reuse needs no
+  // further synchronisation.
+  auto col_bias = [&](int it) { return colbuf + (it & 1) * L::kColBufFloats; };
+  auto col_mod = [&](int it) { return kEmbed && ep.modality_embed ? col_bias(it) + kMaxBN : nullptr; };
 
   if (warp >= kEpilogueWarps && warp < kEpilogueWarps + kProducerWarps) {
     // ---------------- gather producers (cp.async), both CTAs ----------------
-    const int pw_ = warp - kEpilogueWarps;
+    const int pw_ = warp - kEpilogueWarps;  // = this warp's TMEM lane quarter (warp % 4)
     const int j = lane & 7;
     const int sub = lane >> 3;
     int kbg = 0;
     int prod_phase = 0;
-    int4 last_c = make_int4(-1, -1, -1, -1);  // this lane's row of the last tile (for the drain below)
-    const int p = tid - kEpilogueWarps * 32;
+    const int p = tid - kEpilogueWarps * 32;  // this thread's tile row: 32 pw_ + lane
     const int row_in_pair = (int)rank * kBM + p;
-    int64_t my_row = resolve_row(rs, soff, g, M, (cluster / n_tiles) * (2 * kBM) + row_in_pair);
+    // A tile's row is loaded (index or coords) when the tile before starts and decoded when it
+    // ends, so the load's latency never stalls the in-order issue of the copies.
+    int4 raw = fetch_row_raw(rs, soff, M, (cluster / n_tiles) * (2 * kBM) + row_in_pair);
+    int4 c_this = decode_row(rs, g, raw);
+    int64_t my_row = row_offset(g, c_this);
     for (int tile = cluster; tile < num_tiles && !aborted; tile += nclusters) {
       int64_t base[8];
       uint32_t dst_off[8];
       uint32_t valid_mask = 0;
-      if (!producer_rows(my_row, p, rowbase, pw_, sub, base, valid_mask, prod_bar, prod_phase, abort_flag, g.wait_ns)) {
+      const bool rows_ok = producer_rows(my_row, p, rowbase, pw_, sub, base, valid_mask, prod_bar, prod_phase,
+                                         abort_flag, g.wait_ns);
+      if (__any_sync(0xffffffffu, !rows_ok)) {
         aborted = true;
         break;
       }
-      const int next = tile + nclusters;  // resolved now, used at the next tile
-      my_row = next < num_tiles ? resolve_row(rs, soff, g, M, (next / n_tiles) * (2 * kBM) + row_in_pair) : -1;
-      if (next >= num_tiles) last_c = next_row(rs, soff, g, M, (tile / n_tiles) * (2 * kBM) + (int)rank * kBM +
-                                                                32 * (warp - kEpilogueWarps) + lane);
+      const int next = tile + nclusters;
+      if (next < num_tiles) raw = fetch_row_raw(rs, soff, M, (next / n_tiles) * (2 * kBM) + row_in_pair);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int m = 32 * pw_ + 4 * i + sub;
@@ -800,7 +931,8 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
       for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
         const int s = kbg % kPairStages;
         const uint32_t par = ((kbg / kPairStages) & 1) ^ 1;
-        if (!mbar_wait_bounded(&empty[s], par, abort_flag, g.wait_ns)) {
+        const bool ok = mbar_wait_bounded(&empty[s], par, abort_flag, g.wait_ns);
+        if (__any_sync(0xffffffffu, !ok)) {
           aborted = true;
           break;
         }
@@ -811,29 +943,31 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
           if (valid_mask & (1u << i)) cp_async_16(dst + dst_off[i], video + base[i] + ko);
         cp_async_arrive_noinc(&full[s]);
       }
+      if (next < num_tiles) {
+        c_this = decode_row(rs, g, raw);
+        my_row = row_offset(g, c_this);
+      }
     }
     cp_async_wait_all();
-    // warp-uniform: the drain below is warp-collective (tcgen05.ld)
-    if (__all_sync(0xffffffffu, !aborted) && split > 0 && my_tiles > 0) {
-      // Help drain the last accumulator: once it is complete every MMA has finished reading
-      // this CTA's A stages, so they serve as this warp's staging buffers.
+    // Help drain the last accumulator, columns [split, bn), through this warp's own staging
+    // area.  Warp-uniform (the drain is warp-collective).
+    if (!aborted && split > 0 && my_tiles > 0) {
       const int it_last = my_tiles - 1;
-      const int tile = cluster + it_last * nclusters;
-      const int buf = it_last & 1;
-      bool ok = mbar_wait_bounded(&acc_full[buf], (uint32_t)((it_last >> 1) & 1), abort_flag, g.wait_ns);
+      const bool ok = mbar_wait_bounded(&acc_full[it_last & 1], (uint32_t)((it_last >> 1) & 1), abort_flag,
+                                        g.wait_ns) &&
+                      mbar_wait_bounded(&col_ready[it_last & 1], (uint32_t)((it_last >> 1) & 1), abort_flag,
+                                        g.wait_ns);
       if (__any_sync(0xffffffffu, !ok)) {
         aborted = true;
       } else {
         tc_fence_after();
-        const int qw = warp - kEpilogueWarps;  // TMEM lane quarter of this warp (warp % 4)
-        uint8_t* pstage = smem + PairSmemLayout::a_off + qw * kEpiWarpBytes;
-        int pchunk = 0;
-        drain_accumulator_bulk<kEmbed>(g, ep, last_c, M, (tile / n_tiles) * (2 * kBM) + (int)rank * kBM + 32 * qw + lane,
-                               (tile % n_tiles) * bn, split, bn,
-                               tmem_base + (uint32_t)buf * acc_cols + ((uint32_t)(qw * 32) << 16), lane, pstage,
-                               smem_u32(pstage), pchunk);
+        const int tile = cluster + it_last * nclusters;
+        uint8_t* pstage = smem + L::pepi_off + pw_ * kEpiWarpBytes;
+        drain_accumulator_rows<kEmbed>(g, ep, c_this, M, (tile / n_tiles) * (2 * kBM) + row_in_pair,
+                                       (tile % n_tiles) * bn, split, bn,
+                                       acc_tmem(it_last) + ((uint32_t)(pw_ * 32) << 16), lane, pstage,
+                                       col_bias(it_last), col_mod(it_last));
         tc_fence_before();
-        bulk_wait<0>();
       }
     }
   } else if (warp == kMmaWarp) {
@@ -851,7 +985,7 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
           break;
         }
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + (uint32_t)buf * acc_cols;
+        const uint32_t d_tmem = acc_tmem(it);
         for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
           const int s = kbg % kPairStages;
           const uint32_t par = (kbg / kPairStages) & 1;
@@ -925,15 +1059,25 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
     // ---------------- epilogue (warps 0-3, both CTAs) ----------------
     const int m = tid;
     const uint32_t remote_acc_empty = cluster_map(smem_u32(&acc_empty[0]), 0);
-    uint8_t* stage = smem + PairSmemLayout::epi_off + warp * kEpiWarpBytes;
-    const uint32_t stage_smem = smem_u32(stage);
-    int chunk = 0;
+    uint8_t* stage = smem + L::epi_off + warp * kEpiWarpBytes;
+    const uint32_t lanes = (uint32_t)(warp * 32) << 16;
     int it = 0;
     int4 c = next_row(rs, soff, g, M, (cluster / n_tiles) * (2 * kBM) + (int)rank * kBM + m);
+    auto stage_columns = [&](int it_) {
+      const int n0_ = ((cluster + it_ * nclusters) % n_tiles) * bn;
+      float* dst = col_bias(it_);
+      for (int jj = tid; jj < bn; jj += kEpilogueWarps * 32) {
+        const int col = n0_ + jj;
+        dst[jj] = (ep.bias && col < g.D) ? __ldg(ep.bias + col) : 0.0f;
+        if (kEmbed) dst[kMaxBN + jj] = (ep.modality_embed && col < g.D) ? __ldg(ep.modality_embed + col) : 0.0f;
+      }
+      mbar_arrive(&col_ready[it_ & 1]);
+    };
+    stage_columns(0);
     for (int tile = cluster; tile < num_tiles; tile += nclusters, ++it) {
       const int buf = it & 1;
-      const uint32_t par = (it >> 1) & 1;
-      bool ok = mbar_wait_bounded(&acc_full[buf], par, abort_flag, g.wait_ns);
+      const bool ok = mbar_wait_bounded(&acc_full[buf], (uint32_t)((it >> 1) & 1), abort_flag, g.wait_ns) &&
+                      mbar_wait_bounded(&col_ready[buf], (uint32_t)((it >> 1) & 1), abort_flag, g.wait_ns);
       if (__any_sync(0xffffffffu, !ok)) {
         aborted = true;
         break;
@@ -942,9 +1086,8 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
       const int n0 = (tile % n_tiles) * bn;
       const int gm = (tile / n_tiles) * (2 * kBM) + (int)rank * kBM + m;
       const bool last = tile + nclusters >= num_tiles;
-      drain_accumulator_bulk<kEmbed>(g, ep, c, M, gm, n0, 0, last && split > 0 ? split : bn,
-                             tmem_base + (uint32_t)buf * acc_cols + ((uint32_t)(warp * 32) << 16), lane, stage,
-                             stage_smem, chunk);
+      drain_accumulator_rows<kEmbed>(g, ep, c, M, gm, n0, 0, last && split > 0 ? split : bn, acc_tmem(it) + lanes,
+                                     lane, stage, col_bias(it), col_mod(it));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -954,9 +1097,11 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
           mbar_arrive_remote(remote_acc_empty + (uint32_t)buf * 8);
       }
       const int next = tile + nclusters;
-      if (next < num_tiles) c = next_row(rs, soff, g, M, (next / n_tiles) * (2 * kBM) + (int)rank * kBM + m);
+      if (next < num_tiles) {
+        c = next_row(rs, soff, g, M, (next / n_tiles) * (2 * kBM) + (int)rank * kBM + m);
+        stage_columns(it + 1);
+      }
     }
-    bulk_wait<0>();  // every bulk store of this thread has written global memory
   }
 
   if (aborted) {
@@ -1082,16 +1227,20 @@ __global__ void __launch_bounds__(kSThreads)
   }
 }
 
+// Output columns per tile: all of D up to 256, else 256 (the last column tile may be partial:
+// its weight rows beyond D load as zeros and its columns beyond D are not stored).  Fewer,
+// wider tiles gather A fewer times, which pays more than the MMA work on the padding costs
+// (D = 1408: six 256-column tiles ran the ViT-g batch 1.2x faster than eight of 176).
 int choose_bn(int D) {
   if (D <= kMaxBN) return (D + 15) / 16 * 16;
-  for (int bn = kMaxBN; bn >= 128; bn -= 16)
-    if (D % bn == 0) return bn;
   return kMaxBN;
 }
 
 std::mutex g_attr_mu;
 bool g_attr_set[64][2] = {};
-int g_pair_clusters[64][4] = {};  // resident CTA-pair clusters per device, operand type and epilogue
+// resident CTA-pair clusters per device, operand type and epilogue; the pair layouts take more
+// than half an SM's shared memory, so one CTA per SM whatever the launch's stream count
+int g_pair_clusters[64][4] = {};
 
 }  // namespace
 
@@ -1103,7 +1252,9 @@ bool sm100_path_supported(const DeviceInfo& dev, const GatherGeometry& g, int32_
   if (g.K % kBK != 0 || g.K / kBK > kMaxKBlocks) return false;
   if (reinterpret_cast<uintptr_t>(input) % 16 != 0 || reinterpret_cast<uintptr_t>(weight) % 16 != 0)
     return false;
-  if (dev.max_smem_optin < (size_t)SmemLayout::alloc || dev.max_smem_optin < (size_t)PairSmemLayout::alloc) return false;
+  if (dev.max_smem_optin < (size_t)SmemLayout::alloc ||
+      dev.max_smem_optin < PairSmemLayout<true>::bytes(kMaxKBlocks, kMaxRowStreams))
+    return false;
   return true;
 }
 
@@ -1149,6 +1300,9 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
         return fail(BJF_ERR_CUDA, "cuTensorMapEncodeTiled(weight) failed with code " + std::to_string((int)cr));
       const bool embed = ep.position_table || ep.modality_embed;
       const int pslot = slot + (embed ? 2 : 0);
+      const int streams = rows.coords ? 0 : rows.streams;
+      const size_t smem_bytes = embed ? PairSmemLayout<true>::bytes(g.num_kb, streams)
+                                      : PairSmemLayout<false>::bytes(g.num_kb, streams);
       const void* fn =
           g.is_bf16 ? (embed ? (const void*)gather_gemm_sm100_pair_kernel<__nv_bfloat16, true>
                              : (const void*)gather_gemm_sm100_pair_kernel<__nv_bfloat16, false>)
@@ -1158,7 +1312,8 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
       {
         std::lock_guard<std::mutex> lock(g_attr_mu);
         if (!g_pair_clusters[dev.device][pslot]) {
-          cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, PairSmemLayout::alloc);
+          cudaError_t e = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                               (int)PairSmemLayout<true>::bytes(kMaxKBlocks, kMaxRowStreams));
           if (e != cudaSuccess) return cuda_status(e, "gather-GEMM pair smem attribute");
           cudaLaunchConfig_t cfg = {};
           cudaLaunchAttribute attr[1];
@@ -1168,7 +1323,7 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
           attr[0].val.clusterDim.z = 1;
           cfg.gridDim = dim3(2 * (unsigned)std::max(1, dev.sm_count / 2));
           cfg.blockDim = dim3(kThreads);
-          cfg.dynamicSmemBytes = PairSmemLayout::alloc;
+          cfg.dynamicSmemBytes = smem_bytes;
           cfg.attrs = attr;
           cfg.numAttrs = 1;
           e = cudaOccupancyMaxActiveClusters(&max_clusters, fn, &cfg);
@@ -1190,7 +1345,7 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
       attr[1].val.programmaticStreamSerializationAllowed = 1;
       cfg.gridDim = dim3(2 * clusters);
       cfg.blockDim = dim3(kThreads);
-      cfg.dynamicSmemBytes = PairSmemLayout::alloc;
+      cfg.dynamicSmemBytes = smem_bytes;
       cfg.stream = st;
       cfg.attrs = attr;
       cfg.numAttrs = pdl ? 2 : 1;
