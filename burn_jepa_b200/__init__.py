@@ -411,3 +411,16 @@ class FrontEnd:
             _ptr(self.counts), _stream(stream)))
         self.steps += 1
         return self.counts
+
+    def step_ring(self, ring, prev_slot: int, cur_slot: int, weight, bias, caches, observed, age_frames,
+                  age_observed=None, stream=None):
+        """``bjf_front_end_step_ring``: the step on the clip (ring[:, :, prev_slot], ring[:, :, cur_slot])
+        of a frame ring [S, C, R, H, W] (frames = tubelet = 2); results as ``step`` on that clip."""
+        if age_observed is None:
+            age_observed = self.steps > 0
+        check(load().bjf_front_end_step_ring(
+            ctypes.byref(self.desc), _ptr(ring), int(ring.shape[2]), int(prev_slot), int(cur_slot), _ptr(weight),
+            _ptr(bias), _ptr(caches), _ptr(observed), _ptr(age_frames), int(bool(age_observed)),
+            _ptr(self.workspace), self.workspace.numel(), _ptr(self.counts), _stream(stream)))
+        self.steps += 1
+        return self.counts

@@ -79,10 +79,13 @@ extern "C" size_t bjf_front_end_workspace_bytes(const bjf_front_end_desc* d) {
   return layout(d->streams, N).bytes;
 }
 
-extern "C" bjf_status bjf_front_end_step(const bjf_front_end_desc* d, const void* video, const void* weight,
-                                         const float* bias, void* caches, float* observed, float* age_frames,
-                                         int32_t age_observed, void* workspace, size_t workspace_bytes,
-                                         int32_t* counts_out, bjf_stream_t stream) {
+namespace {
+
+// One step over S streams whose clips are `video` (contiguous [S, C, T, H, W]) or, with `ring`,
+// the two slots of a frame ring [S, C, R, H, W].
+bjf_status front_end_step(const bjf_front_end_desc* d, const void* video, const FrameRing* ring, const void* weight,
+                          const float* bias, void* caches, float* observed, float* age_frames, int32_t age_observed,
+                          void* workspace, size_t workspace_bytes, int32_t* counts_out, bjf_stream_t stream) {
   int64_t N = 0;
   bjf_status rc = validate(d, N);
   if (rc) return rc;
@@ -109,7 +112,7 @@ extern "C" bjf_status bjf_front_end_step(const bjf_front_end_desc* d, const void
   cudaStream_t st = as_cuda(stream);
 
   const int64_t vd[5] = {1, d->channels, d->frames, d->height, d->width};
-  rc = launch_scores(video, d->video_dtype, vd, S, d->tubelet_size, d->patch_size, scores, st, true);
+  rc = launch_scores(video, d->video_dtype, vd, S, d->tubelet_size, d->patch_size, scores, st, true, ring);
   if (rc) return rc;
   if (age_observed) {
     sel.age = age_frames;
@@ -132,6 +135,12 @@ extern "C" bjf_status bjf_front_end_step(const bjf_front_end_desc* d, const void
   g.gw = (int)grid[2];
   g.K = (int)(d->channels * d->tubelet_size * d->patch_size * d->patch_size);
   g.D = (int)d->embed_dim;
+  if (ring) {
+    g.ring = 1;
+    g.Ts = ring->storage_frames;
+    g.slot0 = ring->slot0;
+    g.slot1 = ring->slot1;
+  }
   EpilogueArgs ep{};
   ep.mode = kEpilogueScatter;
   ep.out = caches;
@@ -146,4 +155,31 @@ extern "C" bjf_status bjf_front_end_step(const bjf_front_end_desc* d, const void
   const RowSource rows{nullptr, indices, counts, (int)N, (int)S};
   return launch_gather_gemm(*dev, video, d->video_dtype, weight, d->weight_dtype, g, rows, nullptr, S * N, ep, st,
                             true);
+}
+
+}  // namespace
+
+extern "C" bjf_status bjf_front_end_step(const bjf_front_end_desc* d, const void* video, const void* weight,
+                                         const float* bias, void* caches, float* observed, float* age_frames,
+                                         int32_t age_observed, void* workspace, size_t workspace_bytes,
+                                         int32_t* counts_out, bjf_stream_t stream) {
+  return front_end_step(d, video, nullptr, weight, bias, caches, observed, age_frames, age_observed, workspace,
+                        workspace_bytes, counts_out, stream);
+}
+
+extern "C" bjf_status bjf_front_end_step_ring(const bjf_front_end_desc* d, const void* frame_ring, int32_t ring_slots,
+                                              int32_t prev_slot, int32_t cur_slot, const void* weight,
+                                              const float* bias, void* caches, float* observed, float* age_frames,
+                                              int32_t age_observed, void* workspace, size_t workspace_bytes,
+                                              int32_t* counts_out, bjf_stream_t stream) {
+  if (!d) return fail(BJF_ERR_INVALID_ARGUMENT, "front-end descriptor must not be null");
+  if (d->frames != 2 || d->tubelet_size != 2)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "the frame-ring step needs frames = 2 and tubelet_size = 2");
+  if (ring_slots < 2 || ring_slots > 64)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "frame ring must hold 2 to 64 frames per stream");
+  if (prev_slot < 0 || prev_slot >= ring_slots || cur_slot < 0 || cur_slot >= ring_slots || prev_slot == cur_slot)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "frame ring slots must be distinct and inside the ring");
+  const FrameRing ring{ring_slots, 1, prev_slot, cur_slot};
+  return front_end_step(d, frame_ring, &ring, weight, bias, caches, observed, age_frames, age_observed, workspace,
+                        workspace_bytes, counts_out, stream);
 }

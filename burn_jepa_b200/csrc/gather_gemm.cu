@@ -76,7 +76,7 @@ __device__ __forceinline__ int64_t row_base_offset(const GatherGeometry& g, int4
   valid = c.x >= 0 && c.x < g.batch && c.y >= 0 && c.y < g.depth && c.z >= 0 && c.z < g.gh &&
           c.w >= 0 && c.w < g.gw;
   if (!valid) return 0;
-  return (((int64_t)c.x * g.C * g.T + (int64_t)c.y * g.kt) * g.H + (int64_t)c.z * g.ph) * g.W +
+  return (((int64_t)c.x * g.C * g.Ts + (int64_t)c.y * g.kt) * g.H + (int64_t)c.z * g.ph) * g.W +
          (int64_t)c.w * g.pw;
 }
 
@@ -140,7 +140,8 @@ __device__ __forceinline__ bool producer_rows(int64_t my_row, int p, int64_t* ro
                                               int& phase, volatile int* abort_flag, uint64_t limit_ns);
 
 // Offset of element k of a tubelet row relative to its (b, t*kt, r*ph, col*pw) corner
-// (< C*T*H*W of one batch element, which the launch checks fits in int32).
+// (< C*Ts*H*W of one batch element, which the launch checks fits in int32).  In a frame ring
+// the tubelet's frames dt = 0, 1 are the ring slots slot0, slot1.
 __host__ __device__ __forceinline__ int64_t k_offset(const GatherGeometry& g, int k) {
   int q = k / g.pw;
   int dx = k - q * g.pw;
@@ -148,7 +149,8 @@ __host__ __device__ __forceinline__ int64_t k_offset(const GatherGeometry& g, in
   int q2 = q / g.ph;
   int dt = q2 % g.kt;
   int ch = q2 / g.kt;
-  return (((int64_t)ch * g.T + dt) * g.H + dy) * g.W + dx;
+  const int fr = g.ring ? (dt == 0 ? g.slot0 : g.slot1) : dt;  // a ring clip has depth 1
+  return (((int64_t)ch * g.Ts + fr) * g.H + dy) * g.W + dx;
 }
 
 // Element offset of row gm in the input, or -1 for a zero row (beyond M or outside the grid).
@@ -1271,8 +1273,9 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
   const BoundedWait bw = bounded_wait();
   g.wait_ns = bw.limit_ns;
   g.stall = bw.stall;
+  if (!g.ring) g.Ts = g.T;
   if (sm100_path_supported(dev, g, in_dt, w_dt, input, weight) &&
-      (int64_t)g.C * g.T * g.H * g.W < (int64_t(1) << 31)) {
+      (int64_t)g.C * g.Ts * g.H * g.W < (int64_t(1) << 31)) {
     EncodeTiledFn encode = nullptr;
     bjf_status rc = encode_tiled_fn(&encode);
     if (rc) return rc;

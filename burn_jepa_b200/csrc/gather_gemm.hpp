@@ -20,6 +20,9 @@ struct GatherGeometry {
   int is_bf16;
   uint64_t wait_ns;    // limit of every bounded pipeline wait (bjf_set_bounded_wait)
   int stall;           // 1: the single-CTA kernel's MMA thread waits on a barrier nothing completes
+  // Frame ring (a two-frame clip of depth 1 read from slots slot0, slot1 of Ts stored frames);
+  // ring = 0: contiguous frames, Ts = T (set by launch_gather_gemm)
+  int ring, Ts, slot0, slot1;
 };
 
 enum { kEpiloguePlain = 0, kEpilogueScatter = 1 };

@@ -60,7 +60,8 @@ template <typename T>
 __global__ void __launch_bounds__(kScoreThreads, 4)
     patch_diff_scores_vec_kernel(const T* __restrict__ video, float* __restrict__ scores, int batch,
                                  int channels, int frames, int height, int width, int kt, int P,
-                                 int depth, int gh, int gw, int chunks_per_row, long long total_warps) {
+                                 int depth, int gh, int gw, int chunks_per_row, long long total_warps,
+                                 FrameRing ring) {
   constexpr int VEC = 16 / sizeof(T);
   const int LPT = P / VEC;      // lanes per token column
   const int TPW = 32 / LPT;     // token columns per warp
@@ -93,11 +94,11 @@ __global__ void __launch_bounds__(kScoreThreads, 4)
   if (valid) {
     for (int b = 0; b < batch; ++b) {
       for (int ch = 0; ch < channels; ++ch) {
-        const T* vbase = video + (((s * batch + b) * channels + ch) * frames) * plane +
+        const T* vbase = video + (((s * batch + b) * channels + ch) * ring.storage_frames) * plane +
                          (long long)(r * P) * width + x;
         for (int p = 0; p < npairs; ++p) {
-          const T* nxt = vbase + (long long)(first_next + p) * plane;
-          const T* prv = nxt - plane;
+          const T* nxt = vbase + (long long)ring.frame(first_next + p) * plane;
+          const T* prv = vbase + (long long)ring.frame(first_next + p - 1) * plane;
 #pragma unroll 8
           for (int py = 0; py < P; ++py) {
             uint4 un = ld_nc_v4(nxt + (long long)py * width);
@@ -128,7 +129,8 @@ template <typename T>
 __global__ void __launch_bounds__(kScoreThreads)
     patch_diff_scores_scalar_kernel(const T* __restrict__ video, float* __restrict__ scores,
                                     int batch, int channels, int frames, int height, int width,
-                                    int kt, int P, int depth, int gh, int gw, long long total) {
+                                    int kt, int P, int depth, int gh, int gw, long long total,
+                                    FrameRing ring) {
   pdl_wait();
   long long i = (long long)blockIdx.x * kScoreThreads + threadIdx.x;
   if (i >= total) return;
@@ -148,10 +150,10 @@ __global__ void __launch_bounds__(kScoreThreads)
   float acc = 0.0f;
   for (int b = 0; b < batch; ++b)
     for (int ch = 0; ch < channels; ++ch) {
-      const T* vbase = video + (((s * batch + b) * channels + ch) * frames) * plane;
+      const T* vbase = video + (((s * batch + b) * channels + ch) * ring.storage_frames) * plane;
       for (int p = 0; p < npairs; ++p) {
-        const T* nxt = vbase + (long long)(first_next + p) * plane;
-        const T* prv = nxt - plane;
+        const T* nxt = vbase + (long long)ring.frame(first_next + p) * plane;
+        const T* prv = vbase + (long long)ring.frame(first_next + p - 1) * plane;
         for (int py = 0; py < P; ++py)
           for (int px = 0; px < P; ++px) {
             long long off = (long long)(r * P + py) * width + c * P + px;
@@ -513,8 +515,9 @@ int sm_count() {
 }  // namespace
 
 bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* vd, int64_t streams,
-                         int64_t kt, int64_t P, float* scores, cudaStream_t st, bool pdl) {
+                         int64_t kt, int64_t P, float* scores, cudaStream_t st, bool pdl, const FrameRing* ring_in) {
   const int64_t B = vd[0], C = vd[1], T = vd[2], H = vd[3], W = vd[4];
+  const FrameRing ring = ring_in ? *ring_in : FrameRing::contiguous((int)T);
   const int64_t depth = T / kt, gh = H / P, gw = W / P;
   const int64_t n_tok = depth * gh * gw;
   if (n_tok == 0 || streams == 0) return BJF_OK;
@@ -534,14 +537,14 @@ bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* vd, in
       cudaError_t e = launch_kernel(pdl, patch_diff_scores_vec_kernel<T_>, dim3((unsigned)blocks),
                                     dim3(kScoreThreads), 0, st, static_cast<const T_*>(video), scores, (int)B,
                                     (int)C, (int)T, (int)H, (int)W, (int)kt, (int)P, (int)depth, (int)gh,
-                                    (int)gw, chunks, warps);
+                                    (int)gw, chunks, warps, ring);
       rc = e == cudaSuccess ? BJF_OK : cuda_status(e, "patch-diff scores launch");
       return;
     } else {
       long long total = (long long)streams * n_tok;
       patch_diff_scores_scalar_kernel<T_><<<(unsigned)ceil_div(total, kScoreThreads), kScoreThreads, 0, st>>>(
           static_cast<const T_*>(video), scores, (int)B, (int)C, (int)T, (int)H, (int)W, (int)kt,
-          (int)P, (int)depth, (int)gh, (int)gw, total);
+          (int)P, (int)depth, (int)gh, (int)gw, total, ring);
     }
     rc = check_launch("patch-diff scores launch");
   });

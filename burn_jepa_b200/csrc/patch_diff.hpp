@@ -28,10 +28,22 @@ bjf_status resolve_select(const bjf_patch_diff_config* cfg, const int64_t* grid,
 bjf_status launch_select(const float* scores, int64_t streams, const SelectParams& p, int32_t* indices,
                          int32_t* counts, cudaStream_t st, bool pdl = false);
 
-// Per-tubelet mean |delta| scores for `streams` videos [B, C, T, H, W] -> [streams, N].
+// Where the frames of a clip live: contiguous [.., T, H, W] (storage_frames = T, frame(f) = f), or
+// a frame ring [.., R, H, W] holding R frames per channel of which a two-frame clip uses slots
+// (slot0, slot1) in that order (storage_frames = R).
+struct FrameRing {
+  int storage_frames;
+  int ring;  // 0: contiguous
+  int slot0, slot1;
+  __host__ __device__ __forceinline__ int frame(int f) const { return ring ? (f == 0 ? slot0 : slot1) : f; }
+  static FrameRing contiguous(int frames) { return FrameRing{frames, 0, 0, 1}; }
+};
+
+// Per-tubelet mean |delta| scores for `streams` videos [B, C, T, H, W] -> [streams, N]; with a
+// ring (T = 2 only), the frames are read from its slots.
 bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* video_dims, int64_t streams,
                          int64_t tubelet_size, int64_t patch_size, float* scores, cudaStream_t st,
-                         bool pdl = false);
+                         bool pdl = false, const FrameRing* ring = nullptr);
 
 // Device plan (coords rows) from per-stream mask indices; see bjf_sparse_patchify_plan_coords.
 bjf_status launch_plan(const int32_t* indices, int64_t index_stride, const int32_t* counts, int64_t mask_rows,

@@ -36,8 +36,9 @@
 extern "C" {
 #endif
 
-/* 2: bjf_rgba_patch_diff_workspace_bytes takes the token grid. */
-#define BJF_ABI_VERSION 2
+/* 2: bjf_rgba_patch_diff_workspace_bytes takes the token grid.
+ * 3: bjf_set_bounded_wait, bjf_front_end_step_ring. */
+#define BJF_ABI_VERSION 3
 
 #if defined(__GNUC__)
 #define BJF_API __attribute__((visibility("default")))
@@ -371,6 +372,21 @@ BJF_API bjf_status bjf_front_end_step(const bjf_front_end_desc* desc, const void
                                       float* observed, float* age_frames, int32_t age_observed,
                                       void* workspace, size_t workspace_bytes, int32_t* counts_out,
                                       bjf_stream_t stream);
+
+/* bjf_front_end_step for a live stream whose previous frame is already on the device: the step
+ * that src/highres_pipeline.rs:1999-2052 runs per camera frame, which takes one new image per
+ * step.  frame_ring: [S, C, ring_slots, H, W] -- ring_slots frames per stream and channel; the
+ * step's clip is (ring[prev_slot], ring[cur_slot]), in that order, so a caller copies only each
+ * new frame into the next slot (and, with three or more slots, may copy the next frame while
+ * this step runs).  desc->frames and desc->tubelet_size must be 2; other arguments, workspace
+ * (bjf_front_end_workspace_bytes(desc)) and results as bjf_front_end_step on the clip
+ * [S, C, 2, H, W] = (prev, cur), bit for bit. */
+BJF_API bjf_status bjf_front_end_step_ring(const bjf_front_end_desc* desc, const void* frame_ring,
+                                           int32_t ring_slots, int32_t prev_slot, int32_t cur_slot,
+                                           const void* weight, const float* bias, void* caches,
+                                           float* observed, float* age_frames, int32_t age_observed,
+                                           void* workspace, size_t workspace_bytes, int32_t* counts_out,
+                                           bjf_stream_t stream);
 
 /* No counterpart in the reference: bjf_front_end_step for callers that cannot
  * allocate device memory (a host whose device memory belongs to its framework's caching

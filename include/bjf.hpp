@@ -1638,6 +1638,20 @@ class FrontEnd {
     return counts_;
   }
 
+  // The live step on a frame ring [S, C, R, H, W] (frames = tubelet = 2): the clip is
+  // (ring[prev_slot], ring[cur_slot]); results as step() on that clip.
+  const Tensor& step_ring(const Tensor& ring, int32_t prev_slot, int32_t cur_slot, const Tensor& weight,
+                          const Tensor* bias, cudaStream_t st = nullptr) {
+    if (ring.shape().size() != 5) throw Error(BJF_ERR_INVALID_ARGUMENT, "frame ring must be [S, C, R, H, W]");
+    check(bjf_front_end_step_ring(&desc_, ring.data(), (int32_t)ring.shape()[2], prev_slot, cur_slot, weight.data(),
+                                  bias ? static_cast<const float*>(bias->data()) : nullptr, caches_.data(),
+                                  static_cast<float*>(observed_.data()), static_cast<float*>(age_.data()),
+                                  steps_ > 0 ? 1 : 0, workspace_.data(), workspace_.nbytes(),
+                                  static_cast<int32_t*>(counts_.data()), to_bjf(st)));
+    ++steps_;
+    return counts_;
+  }
+
   TokenGridShape grid() const { return grid_; }
   size_t steps() const { return steps_; }
   Tensor& caches() { return caches_; }

@@ -13,7 +13,7 @@ pub type bjf_stream_t = *mut c_void;
 /// `bjf_dtype` (a C enum, int-sized).
 pub type bjf_dtype = i32;
 
-pub const BJF_ABI_VERSION: i32 = 2;
+pub const BJF_ABI_VERSION: i32 = 3;
 
 pub const BJF_OK: bjf_status = 0;
 pub const BJF_ERR_INVALID_ARGUMENT: bjf_status = -1;
@@ -287,6 +287,23 @@ unsafe extern "C" {
     pub fn bjf_front_end_step(
         desc: *const bjf_front_end_desc,
         video: *const c_void,
+        weight: *const c_void,
+        bias: *const f32,
+        caches: *mut c_void,
+        observed: *mut f32,
+        age_frames: *mut f32,
+        age_observed: i32,
+        workspace: *mut c_void,
+        workspace_bytes: usize,
+        counts_out: *mut i32,
+        stream: bjf_stream_t,
+    ) -> bjf_status;
+    pub fn bjf_front_end_step_ring(
+        desc: *const bjf_front_end_desc,
+        frame_ring: *const c_void,
+        ring_slots: i32,
+        prev_slot: i32,
+        cur_slot: i32,
         weight: *const c_void,
         bias: *const f32,
         caches: *mut c_void,

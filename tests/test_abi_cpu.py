@@ -21,7 +21,7 @@ def test_library_exports_every_header_symbol():
 
 
 def test_abi_version():
-    assert bj.load().bjf_abi_version() == _abi.header_abi_version() == 2
+    assert bj.load().bjf_abi_version() == _abi.header_abi_version() == 3
 
 
 def _fm(features, observed, age, tokens, indices):
@@ -106,3 +106,19 @@ def test_plan_errors():
     assert rc == -1 and bj.last_error() == "sparse patchify batch must be nonzero"
     rc = L.bjf_sparse_patchify_plan_coords(FAKE, 3, None, 3, 2, _abi.dims(2, 3, 4), FAKE, 6, None, None)
     assert rc == -1 and "mask rows must be 1 or equal the batch" in bj.last_error()
+
+
+def test_ring_step_rejects_bad_slots():
+    desc = bj.FrontEndDesc(2, 3, 2, 64, 64, 2, 16, 256, _abi.DTYPE_F16, _abi.DTYPE_F16, _abi.DTYPE_F16,
+                           bj.PatchDiffConfig.adaptive_threshold(0.1, 1, 16, 1))
+    lib = bj.load()
+    for slots, prev, cur in ((3, 1, 1), (3, 0, 3), (1, 0, 0), (3, -1, 0)):
+        rc = lib.bjf_front_end_step_ring(ctypes.byref(desc), 16, slots, prev, cur, 16, None, 16, 16, 16, 0, 16, 1 << 20,
+                                         None, None)
+        assert rc == _abi.BJF_ERR_INVALID_ARGUMENT
+        assert "frame ring" in bj.last_error()
+    bad = bj.FrontEndDesc(2, 3, 4, 64, 64, 2, 16, 256, _abi.DTYPE_F16, _abi.DTYPE_F16, _abi.DTYPE_F16,
+                          bj.PatchDiffConfig.adaptive_threshold(0.1, 1, 32, 1))
+    assert lib.bjf_front_end_step_ring(ctypes.byref(bad), 16, 3, 0, 1, 16, None, 16, 16, 16, 0, 16, 1 << 20, None,
+                                       None) == _abi.BJF_ERR_INVALID_ARGUMENT
+    assert "frames = 2" in bj.last_error()

@@ -185,3 +185,41 @@ def test_front_end_reused_workspace_matches_oracle(cuda_device):
         assert max_rel_err(got, ref_cache) <= 1e-2, step
         ref_cache = got.copy()
     assert not bj.device_error_check()
+
+
+@pytest.mark.parametrize("ring_slots,D,video_dt", [(3, 1024, "f16"), (2, 256, "bf16")])
+def test_ring_step_equals_the_contiguous_step(cuda_device, ring_slots, D, video_dt):
+    """bjf_front_end_step_ring on a frame ring (a live stream that copies only its new frame per
+    step) equals bjf_front_end_step on the same two frames stored as a contiguous clip, bit for
+    bit, over a sequence of frames that wraps the ring (so for some steps the newer frame sits
+    in a lower slot than the older one)."""
+    import torch
+
+    dt = {"f16": torch.float16, "bf16": torch.bfloat16}[video_dt]
+    S, C, H, W, P = 4, 3, 256, 256, 16
+    n = (H // P) * (W // P)
+    frames = [torch.from_numpy(workloads.rect_perturbation_clips(300 + f, S, C, 2, H, W, 0.25)[:, :, 0]).to(
+        cuda_device, dt) for f in range(5)]  # [S, C, H, W] each
+    wd = torch.from_numpy(workloads.splitmix_normal(31, (D, C, 2, P, P), 0.02)).to(cuda_device, dt)
+    bd = torch.from_numpy(workloads.splitmix_normal(32, (D,), 0.02)).to(cuda_device)
+    cache0 = torch.from_numpy(workloads.splitmix_normal(33, (S, n, D), 1.0)).to(cuda_device, torch.float16)
+    clip01 = torch.stack([frames[0], frames[1]], dim=2)
+    thr = workloads.choose_threshold(bj.patch_diff_token_scores(clip01.unsqueeze(1), 2, P).cpu().numpy(), 0.25)
+    mask = bj.PatchDiffConfig.adaptive_threshold(thr, 1, n, 1)
+    fe_ring = bj.FrontEnd(S, C, 2, H, W, 2, P, D, mask, dt, torch.float16, cuda_device)
+    fe_clip = bj.FrontEnd(S, C, 2, H, W, 2, P, D, mask, dt, torch.float16, cuda_device)
+    state = {k: (cache0.clone(), torch.zeros((S, n), device=cuda_device), torch.zeros((S, n), device=cuda_device))
+             for k in ("ring", "clip")}
+    ring = torch.zeros((S, C, ring_slots, H, W), dtype=dt, device=cuda_device)
+    ring[:, :, 0] = frames[0]
+    for f in range(1, 5):
+        prev_slot, cur_slot = (f - 1) % ring_slots, f % ring_slots
+        ring[:, :, cur_slot] = frames[f]  # only the new frame is written
+        c_ring = fe_ring.step_ring(ring, prev_slot, cur_slot, wd, bd, *state["ring"], age_observed=f > 1).clone()
+        clip = torch.stack([frames[f - 1], frames[f]], dim=2).contiguous()
+        c_clip = fe_clip.step(clip, wd, bd, *state["clip"], age_observed=f > 1).clone()
+        torch.cuda.synchronize()
+        assert torch.equal(c_ring, c_clip), f"frame {f}: counts"
+        assert int(c_ring.sum()) > 0
+        for a, b in zip(state["ring"], state["clip"]):
+            assert torch.equal(a, b), f"frame {f}"
