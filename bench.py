@@ -607,7 +607,7 @@ def run_ours(args, world, rank, local):
     ring_slots = 3
     ring = torch.empty((S, C, ring_slots, H, W), dtype=torch.float16, device=dev)
     e2e_steps = max(1, args.e2e_steps)
-    counts_host = torch.zeros((e2e_steps + 1, S), dtype=torch.int32).pin_memory()
+    counts_host = torch.zeros((max(e2e_steps, 3) + 1, S), dtype=torch.int32).pin_memory()  # row i: step i
     copy_stream = torch.cuda.Stream(device=dev)
     frame_bytes = H * W * 2
 
