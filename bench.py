@@ -80,6 +80,12 @@ def parse_args():
                     help="back-to-back steps before the timed ones, for the clock sampler (0 under a profiler)")
     ap.add_argument("--no-rows", action="store_true",
                     help="skip the standalone timings of each row of the path (one GPU only)")
+    ap.add_argument("--rows", default="select,plan,cache,rgba,front_end,vitg",
+                    help="row groups to time: select, plan, cache, rgba, front_end (C2, C3), vitg")
+    ap.add_argument("--rows-only", action="store_true",
+                    help="time only the row groups of --rows (front_end and/or vitg) and print them, e.g. to "
+                         "profile one row alone")
+    ap.add_argument("--vitg-clips", type=int, default=32, help="clips of the ViT-g batch row (32 = the benchmark)")
     return ap.parse_args()
 
 
@@ -280,7 +286,8 @@ def make_inputs(torch, dev, streams, density, seed_base):
     return sets
 
 
-def time_rows(torch, bj, dev, videos, weight, bias, mask_cfg, hbm_peak, tflops_peak, reps=10):
+def time_rows(torch, bj, dev, videos, weight, bias, mask_cfg, hbm_peak, tflops_peak, reps=10,
+              groups=("select", "plan", "cache", "rgba", "front_end", "vitg"), vitg_clips=32):
     """Each row of the path timed alone through its public entry point, with CUDA events on the
     launching stream.  Before every call 256 MB are written (L2 flushed) and the device sleeps
     while the host enqueues the call, so the events bracket device work only.  Returns
@@ -323,23 +330,52 @@ def time_rows(torch, bj, dev, videos, weight, bias, mask_cfg, hbm_peak, tflops_p
     def latency(name, row, workload, ms, **extra):
         out[name] = {"row": row, "workload": workload, "bound": "latency", "avg_ms": round(ms, 4), **extra}
 
-    S = videos[0].shape[0]
+    S = videos[0].shape[0] if videos is not None else 0
     live = f"{S} streams, grid {GRID[0]}x{GRID[1]}x{GRID[2]}"
+    if {"select", "plan", "cache", "rgba"} & set(groups):
+        time_live_rows(torch, bj, dev, videos, mask_cfg, groups, timed, hbm, latency, live)
+    if "front_end" in groups:
+        time_front_end_rows(torch, bj, dev, timed, hbm, tensor)
+    if "vitg" in groups:
+        time_vitg_rows(torch, bj, dev, timed, tensor, vitg_clips)
+    del flush
+    torch.cuda.empty_cache()
+    return out
 
+
+def time_live_rows(torch, bj, dev, videos, mask_cfg, groups, timed, hbm, latency, live):
+    """The selection, plan, cache and RGBA rows on the live-stream workload's frames."""
+    import numpy as np
+
+    S = videos[0].shape[0]
     # a2: selection (+ nothing else) on one step's scores
     sc = bj.patch_diff_token_scores(videos[0].unsqueeze(1), KT, P)
     idx = torch.empty((S, N_TOKENS), dtype=torch.int32, device=dev)
     cnt = torch.empty((S,), dtype=torch.int32, device=dev)
-    ms = timed(lambda i: bj.patch_diff_context_mask_from_scores(sc, GRID, mask_cfg, indices=idx, counts=cnt))
-    active = int(cnt.sum().item())
-    latency("patch_diff_select", "a2", live, ms, active_tokens=active)
+    bj.patch_diff_context_mask_from_scores(sc, GRID, mask_cfg, indices=idx, counts=cnt)
+    if "select" in groups:
+        ms = timed(lambda i: bj.patch_diff_context_mask_from_scores(sc, GRID, mask_cfg, indices=idx, counts=cnt))
+        active = int(cnt.sum().item())
+        latency("patch_diff_select", "a2", live, ms, active_tokens=active)
+    if "plan" in groups:
+        time_plan_row(torch, bj, dev, idx, cnt, S, timed, latency, live)
+    if "cache" in groups:
+        time_cache_rows(torch, bj, dev, S, timed, hbm)
+    if "rgba" in groups:
+        time_rgba_rows(torch, bj, dev, videos, S, timed, hbm, latency)
 
+
+def time_plan_row(torch, bj, dev, idx, cnt, S, timed, latency, live):
     # a4 / f2: device plan from the selection
     coords = torch.empty((S * N_TOKENS, 4), dtype=torch.int32, device=dev)
     total = torch.empty((1,), dtype=torch.int32, device=dev)
     ms = timed(lambda i: bj.sparse_patchify_plan_coords(idx, GRID, batch=S, counts=cnt, capacity=S * N_TOKENS,
                                                         coords=coords, total_rows=total))
     latency("plan_coords", "a4", live, ms, rows=int(total.item()))
+
+
+def time_cache_rows(torch, bj, dev, S, timed, hbm):
+    import numpy as np
 
     # a6 / f3: standalone cache updates, 410 of 4096 tokens per stream (10 %), f16 tokens and cache
     width = 410
@@ -364,6 +400,8 @@ def time_rows(torch, bj, dev, videos, weight, bias, mask_cfg, hbm_peak, tflops_p
         ms, len(reset_rows) * N_TOKENS * (D * 2 + 8))
     del tokens, feats, observed, age
 
+
+def time_rgba_rows(torch, bj, dev, videos, S, timed, hbm, latency):
     # f1: the live viewer's RGBA scorer and mask node on the same streams' frames as RGBA u8
     def rgba(f):
         x = (videos[0][:, :, f].float().clamp(0, 1) * 255).round().to(torch.uint8).permute(0, 2, 3, 1)
@@ -384,6 +422,10 @@ def time_rows(torch, bj, dev, videos, weight, bias, mask_cfg, hbm_peak, tflops_p
             write_density=round(float(wc.sum().item()) / (S * vgrid[1] * vgrid[2]), 4),
             encode_density=round(float(ec.sum().item()) / (S * vgrid[1] * vgrid[2]), 4))
     del prev, cur
+
+
+def time_front_end_rows(torch, bj, dev, timed, hbm, tensor):
+    from burn_jepa_b200 import workloads
 
     # C2 / C3: the other front-end configurations, each one fused step alone (inputs smaller
     # than L2 for C2, so the flush before every call matters)
@@ -425,8 +467,14 @@ def time_rows(torch, bj, dev, videos, weight, bias, mask_cfg, hbm_peak, tflops_p
     front_end_row("c2_vitl_clip_step", "a1-a6", 1, C, 16, 256, 256, D, 0.25, 711)
     front_end_row("c3_live_8_streams_step", "a1-a6", 8, C, T, H, W, D, 0.10, 721)
 
+
+def time_vitg_rows(torch, bj, dev, timed, tensor, clips):
+    import numpy as np
+
+    from burn_jepa_b200 import workloads
+
     # a5 / f4: the ViT-g batch, a shared 4096-of-8192 multiblock mask, bf16
-    v = VITG
+    v = dict(VITG, B=clips)
     g = torch.Generator(device=dev).manual_seed(602)
     clip = torch.empty((v["B"], v["C"], v["T"], v["H"], v["W"]), dtype=torch.bfloat16, device=dev)
     for b in range(v["B"]):
@@ -454,9 +502,7 @@ def time_rows(torch, bj, dev, videos, weight, bias, mask_cfg, hbm_peak, tflops_p
                                                                      modality_embed=modality, out=gout))
     tensor("gather_gemm_vitg_encoder_input", "f4", wl + ", + position table row + modality vector", ms,
            2 * rows * gk * v["D"], rows=rows)
-    del clip, gout, flush
-    torch.cuda.empty_cache()
-    return out
+    del clip, gout
 
 
 def run_ours(args, world, rank, local):
@@ -469,6 +515,16 @@ def run_ours(args, world, rank, local):
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     group = sharding.RankGroup(device=dev)
+    if args.rows_only:  # one or more rows alone, e.g. for a profiler (groups front_end and vitg)
+        groups = tuple(args.rows.split(","))
+        if not set(groups) <= {"front_end", "vitg"}:
+            raise SystemExit("--rows-only times the front_end and vitg row groups")
+        hbm_peak, tflops_peak, _ = read_peaks()
+        rows = time_rows(torch, bj, dev, None, None, None, None, hbm_peak, tflops_peak, groups=groups,
+                         vitg_clips=args.vitg_clips)
+        if rank == 0:
+            print(json.dumps({"rows": rows}), flush=True)
+        return
     if args.strong:  # strong scaling: 256 streams in total, split over the GPUs
         total = 256
         mine = sharding.shard_streams(total, world, rank)
@@ -667,7 +723,8 @@ def run_ours(args, world, rank, local):
 
     rows = None
     if world == 1 and not args.no_rows and not args.strong:
-        rows = time_rows(torch, bj, dev, videos, weight, bias, fe.desc.mask, hbm_peak, tflops_peak)
+        rows = time_rows(torch, bj, dev, videos, weight, bias, fe.desc.mask, hbm_peak, tflops_peak,
+                         groups=tuple(args.rows.split(",")), vitg_clips=args.vitg_clips)
         if rank == 0 and not args.no_cpu_baseline:
             try:  # the oracle beside each row; never at the cost of the bench line
                 for name, c in cpu_rows(S).items():
