@@ -49,9 +49,9 @@ KERNELS_PER_STEP = 3  # patch-diff scores, selection, gather-GEMM (+ row plan, +
 # this workload, from one ncu --set full capture of the scores kernel at 16 streams
 # (207 767 552 bytes / 16), scaled by the stream count for the roofline's `traffic`.
 SCORES_DRAM_BYTES_PER_STREAM = 12985472
-# The same for the CTA-pair gather-GEMM per active row (34.9 MB read + 0.65 MB written at 6 581
-# rows in the same run; cold L2, so an upper bound for a warm step).
-GEMM_DRAM_BYTES_PER_ROW = 5408
+# The same for the CTA-pair gather-GEMM per active row (34.7 MB read + 0.90 MB written at 6 581
+# rows, profiles/gather_gemm_sm100_pair_live_streams_16.md; cold L2, so an upper bound for a warm step).
+GEMM_DRAM_BYTES_PER_ROW = 5267
 C, T, H, W, KT, P, D = 3, 2, 1024, 1024, 2, 16, 1024
 K = C * KT * P * P
 GRID = (T // KT, H // P, W // P)
