@@ -15,12 +15,16 @@
 // When the means of pass 1 already rule the compensation out and no statistics are wanted,
 // pass 2 computes the unshifted score alone and skips the pixels that did not change.
 //
-// The frame-wide sums are reduced in a fixed order from per-block partials (f64) kept in the
-// caller's workspace, so results do not depend on timing and no counters need resetting.
-// Every per-pixel operation is rounded as the reference's f32 code does (no contraction):
-// u8 / 255 comes from a shared-memory table of the correctly rounded quotients, x / 3 from
-// div3_rn below, every other quotient from an IEEE division.  Only the summation order of the
-// means and patch sums differs from the reference's sequential loops.
+// The frame-wide sums are accumulated in f64 and reduced in a fixed order from per-block
+// partials kept in the caller's workspace, so results do not depend on timing and no counters
+// need resetting.  Every per-pixel operation is rounded as the reference's f32 code does (no
+// contraction): u8 / 255 comes from a shared-memory table of the correctly rounded quotients,
+// x / 3 from div3_rn below, every other quotient from an IEEE division.  The sums differ from
+// the reference's sequential f32 loops in order and in precision: the channel-delta means are
+// exact here (see accumulate_means), the luma and mean-|delta| sums nearly so, while the
+// reference's f32 running sums round at every pixel.  The frame statistics therefore agree to
+// within the reference's own f32 summation error, and a frame whose lighting residual sits
+// within that error of 0.35 x the raw mean can take the other compensation decision.
 #include <algorithm>
 #include <string>
 
@@ -124,9 +128,11 @@ __device__ __forceinline__ double block_sum(double v, double* red) {
 // True when the two pixels' RGB bytes are equal (alpha is not read).
 __device__ __forceinline__ bool same_rgb(uint32_t pp, uint32_t cp) { return ((pp ^ cp) & 0x00ffffffu) == 0; }
 
-// One pixel's contribution to the frame means (src/viewer.rs:1079-1100).  The deltas are
-// multiples of 2^-31 below 1 in magnitude, so their f64 sums are exact in any order.  An
-// unchanged pixel adds exact zeros, so it is skipped.
+// One pixel's contribution to the frame means (src/viewer.rs:1079-1100).  The channel deltas are
+// multiples of 2^-31 below 1 in magnitude, so their f64 sums are exact in any order; the luma
+// delta and the mean |delta| have finer steps, so their f64 sums round (far below the f32
+// rounding of the reference's running sums).  An unchanged pixel adds exact zeros, so it is
+// skipped.
 __device__ __forceinline__ void accumulate_means(uint32_t pp, uint32_t cp, const float* inv, double (&acc)[5]) {
   if (same_rgb(pp, cp)) return;
   const Rgb a = rgb_of(pp, inv), b = rgb_of(cp, inv);
