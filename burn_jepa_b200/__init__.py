@@ -29,6 +29,8 @@ __all__ = [
     "BjfError",
     "FrontEnd",
     "PatchDiffConfig",
+    "PatchDiffRefreshConfig",
+    "PatchDiffRefreshState",
     "PatchifyConfig",
     "TokenGridShape",
     "device_error_check",
@@ -372,6 +374,102 @@ def viewer_patch_diff_masks_from_rgba(prev, current, patch_size: int, grid, conf
     raw = st.cpu().numpy().tobytes()
     size = ctypes.sizeof(_abi.RgbaFrameStats)
     return (wi, wc, ei, ec), [_abi.RgbaFrameStats.from_buffer_copy(raw[i * size:(i + 1) * size]) for i in range(S)]
+
+
+PatchDiffRefreshConfig = _abi.PatchDiffRefreshConfig
+
+
+class PatchDiffRefreshState:
+    """PatchDiffRefreshState (src/viewer.rs:275-528) of S streams, held on the device.
+
+    Per stream and token: the decayed residual of below-threshold motion (f32) and the frames
+    since the token was last written (u32, stored in an int32 tensor); per stream the frame
+    index (u64, stored in an int64 tensor).  Each call advances every stream one frame in the
+    viewer mask launch itself; nothing is read back.  Like the reference, the state starts over
+    (zeros, frame 0) when the grid's token count changes, and on `reset()`."""
+
+    def __init__(self, streams: int = 1, device=None):
+        self.streams = int(streams)
+        self.device = device
+        self.dense_len = 0
+        self.residual = self.age = self.frame = None
+
+    def reset(self):
+        self.dense_len = 0
+
+    def _begin(self, n: int, device):
+        torch = _torch()
+        if self.dense_len != n or self.residual is None or self.residual.device != device:
+            S = self.streams
+            self.residual = torch.zeros((S, n), dtype=torch.float32, device=device)
+            self.age = torch.zeros((S, n), dtype=torch.int32, device=device)
+            self.frame = torch.zeros((S,), dtype=torch.int64, device=device)
+            self.dense_len = n
+        st = _abi.PatchDiffRefreshState(self.residual.data_ptr(), self.age.data_ptr(), self.frame.data_ptr())
+        return st
+
+    def frame_index(self):
+        """Per-stream frame index (numpy uint64)."""
+        return None if self.frame is None else self.frame.cpu().numpy().view("uint64")
+
+    def subthreshold_residual(self):
+        return None if self.residual is None else self.residual.cpu().numpy()
+
+    def age_frames(self):
+        """[S, N] numpy uint32."""
+        return None if self.age is None else self.age.cpu().numpy().view("uint32")
+
+    def _outputs(self, S, N, dev):
+        torch = _torch()
+        return (torch.empty((S, N), dtype=torch.int32, device=dev), torch.empty((S,), dtype=torch.int32, device=dev),
+                torch.empty((S, N), dtype=torch.int32, device=dev), torch.empty((S,), dtype=torch.int32, device=dev))
+
+    def masks_from_scores(self, scores, grid, config: PatchDiffConfig, policy: "ViewerMaskPolicy",
+                          refresh: "PatchDiffRefreshConfig", stream=None):
+        """PatchDiffRefreshState::masks_from_scores (src/viewer.rs:312-356): scores [S, N] f32 ->
+        (write_indices, write_counts, encode_indices, encode_counts), as
+        viewer_patch_diff_masks_from_scores with the refresh tokens in the write mask."""
+        sc = scores if scores.dim() == 2 else scores.unsqueeze(0)
+        S, N = sc.shape
+        if S != self.streams:
+            raise ValueError(f"refresh state holds {self.streams} streams, scores have {S}")
+        st = self._begin(N, sc.device)
+        wi, wc, ei, ec = self._outputs(S, N, sc.device)
+        check(load().bjf_viewer_patch_diff_refresh_masks_from_scores(
+            _ptr(sc.contiguous()), S, _abi.dims(*grid), ctypes.byref(config), ctypes.byref(policy),
+            ctypes.byref(refresh), ctypes.byref(st), _ptr(wi), _ptr(wc), _ptr(ei), _ptr(ec), _stream(stream)))
+        return wi, wc, ei, ec
+
+    def masks_from_rgba(self, prev, current, patch_size: int, grid, config: PatchDiffConfig,
+                        policy: "ViewerMaskPolicy", refresh: "PatchDiffRefreshConfig", stream=None):
+        """The RGBA mask node with this refresh state (crates/bevy_jepa/src/mask.rs:126-185)."""
+        torch = _torch()
+        p = prev if prev.dim() == 4 else prev.unsqueeze(0)
+        c = current if current.dim() == 4 else current.unsqueeze(0)
+        S, H, W, _ = p.shape
+        if S != self.streams:
+            raise ValueError(f"refresh state holds {self.streams} streams, frames have {S}")
+        g = tuple(int(v) for v in grid)
+        N = g[1] * g[2]
+        dims = _abi.dims(*g)
+        lib = load()
+        nbytes = lib.bjf_viewer_rgba_masks_workspace_bytes(S, dims)
+        ws = torch.empty((max(int(nbytes), 1) + 255,), dtype=torch.uint8, device=prev.device)
+        off = (-ws.data_ptr()) % 256
+        st = self._begin(N, prev.device)
+        wi, wc, ei, ec = self._outputs(S, N, prev.device)
+        check(lib.bjf_viewer_patch_diff_refresh_masks_from_rgba(
+            _ptr(p.contiguous()), _ptr(c.contiguous()), S, W, H, patch_size, dims, ctypes.byref(config),
+            ctypes.byref(policy), ctypes.byref(refresh), ctypes.byref(st), _ptr(wi), _ptr(wc), _ptr(ei), _ptr(ec),
+            None, ctypes.c_void_p(ws.data_ptr() + off), int(nbytes), _stream(stream)))
+        return wi, wc, ei, ec
+
+    def observe_write_mask(self, write_indices, write_counts, grid, stream=None):
+        """observe_write_mask (src/viewer.rs:309-313): write_indices [S, N] / write_counts [S]."""
+        S, N = write_indices.shape
+        st = self._begin(N, write_indices.device)
+        check(load().bjf_viewer_patch_diff_refresh_observe(_ptr(write_indices), _ptr(write_counts), S,
+                                                            _abi.dims(*grid), ctypes.byref(st), _stream(stream)))
 
 
 # ---------------------------------------------------------------------------

@@ -139,6 +139,50 @@ class ViewerMaskPolicy(ctypes.Structure):
         return p
 
 
+class PatchDiffRefreshConfig(ctypes.Structure):
+    """bjf_patch_diff_refresh_config: PatchDiffRefreshConfig (src/viewer.rs:186-270)."""
+
+    _fields_ = [
+        ("enabled", ctypes.c_int32),
+        ("subthreshold_enabled", ctypes.c_int32),
+        ("subthreshold_decay", ctypes.c_float),
+        ("subthreshold_gain", ctypes.c_float),
+        ("subthreshold_trigger", ctypes.c_float),
+        ("subthreshold_max_density", ctypes.c_float),
+        ("age_refresh_enabled", ctypes.c_int32),
+        ("age_refresh_interval_frames", ctypes.c_uint64),
+        ("age_refresh_max_density", ctypes.c_float),
+        ("blue_noise_enabled", ctypes.c_int32),
+        ("blue_noise_refresh_density", ctypes.c_float),
+        ("blue_noise_seed", ctypes.c_uint64),
+        ("max_extra_density", ctypes.c_float),
+    ]
+
+    # the reference's defaults (src/viewer.rs:35-49, 243-256)
+    DEFAULTS = dict(enabled=False, subthreshold_enabled=False, subthreshold_decay=0.92, subthreshold_gain=1.0,
+                    subthreshold_trigger=1.0, subthreshold_max_density=0.04, age_refresh_enabled=False,
+                    age_refresh_interval_frames=90, age_refresh_max_density=0.01, blue_noise_enabled=False,
+                    blue_noise_refresh_density=0.005, blue_noise_seed=0x9E3779B97F4A7C15, max_extra_density=0.05)
+
+    @classmethod
+    def from_fields(cls, **fields) -> "PatchDiffRefreshConfig":
+        unknown = set(fields) - set(cls.DEFAULTS)
+        if unknown:
+            raise TypeError(f"unknown refresh config fields: {sorted(unknown)}")
+        c = dict(cls.DEFAULTS, **fields)
+        return cls(**{k: (int(bool(v)) if k.endswith("enabled") else v) for k, v in c.items()})
+
+
+class PatchDiffRefreshState(ctypes.Structure):
+    """bjf_patch_diff_refresh_state: device pointers to a PatchDiffRefreshState of S streams."""
+
+    _fields_ = [
+        ("subthreshold_residual", ctypes.c_void_p),
+        ("age_frames", ctypes.c_void_p),
+        ("frame_index", ctypes.c_void_p),
+    ]
+
+
 _P = ctypes.c_void_p
 _I64 = ctypes.c_int64
 _I32 = ctypes.c_int32
@@ -171,6 +215,19 @@ SIGNATURES = {
     "bjf_viewer_patch_diff_masks": (_I32, [_P, _P, _I64, _DIMS, ctypes.POINTER(ViewerMaskPolicy), _P, _P, _P, _P, _P]),
     "bjf_viewer_patch_diff_masks_from_scores": (_I32, [_P, _I64, _DIMS, ctypes.POINTER(PatchDiffConfig),
                                                         ctypes.POINTER(ViewerMaskPolicy), _P, _P, _P, _P, _P]),
+    "bjf_viewer_patch_diff_refresh_masks_from_scores": (_I32, [_P, _I64, _DIMS, ctypes.POINTER(PatchDiffConfig),
+                                                                ctypes.POINTER(ViewerMaskPolicy),
+                                                                ctypes.POINTER(PatchDiffRefreshConfig),
+                                                                ctypes.POINTER(PatchDiffRefreshState),
+                                                                _P, _P, _P, _P, _P]),
+    "bjf_viewer_patch_diff_refresh_masks_from_rgba": (_I32, [_P, _P, _I64, _I64, _I64, _I64, _DIMS,
+                                                              ctypes.POINTER(PatchDiffConfig),
+                                                              ctypes.POINTER(ViewerMaskPolicy),
+                                                              ctypes.POINTER(PatchDiffRefreshConfig),
+                                                              ctypes.POINTER(PatchDiffRefreshState),
+                                                              _P, _P, _P, _P, _P, _P, ctypes.c_size_t, _P]),
+    "bjf_viewer_patch_diff_refresh_observe": (_I32, [_P, _P, _I64, _DIMS, ctypes.POINTER(PatchDiffRefreshState),
+                                                      _P]),
     "bjf_sparse_patchify3d_forward_encoder_input": (_I32, [ctypes.POINTER(PatchifyConfig), _P, _I32, _DIMS, _P, _I64,
                                                            _P, _I32, _DIMS, _P, _P, _P, _P, _I32, _P]),
     "bjf_rgba_patch_diff_scores": (_I32, [_P, _P, _I64, _I64, _I64, _I64, _DIMS, _P, _P, _P, ctypes.c_size_t, _P]),

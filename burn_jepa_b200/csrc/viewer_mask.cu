@@ -44,6 +44,24 @@ struct ViewerParams {
   float sample_threshold;
   int sample_stride, sample_rows, sample_cols, sample_required;
 };
+// PatchDiffRefreshState (src/viewer.rs:275-528) of the launch's streams, in device memory, and
+// the PatchDiffRefreshConfig (:186-270) values the kernel reads, resolved on the host.
+struct RefreshParams {
+  float* residual;                  // [S, n] subthreshold residuals; null: no refresh state
+  uint32_t* age;                    // [S, n] frames since the token was last written
+  unsigned long long* frame_index;  // [S]
+  const float* scores;              // [S, n] the frame's patch-diff scores
+  int augment;                      // can_add_tokens (:258-269)
+  float threshold;                  // the sparsity threshold, compared as given (:515)
+  float norm_threshold;             // threshold.max(1e-6) (:512)
+  float decay, gain, trigger;       // decay.clamp(0, 1), gain.max(0), trigger.max(1e-6)
+  int max_context;                  // context_tokens.max(1).min(n) (:388)
+  int max_extra;                    // density_tokens(n, max_extra_density, Floor, 0)
+  int stage_tokens[3];              // subthreshold / age / blue-noise budgets before `remaining`; 0: off
+  uint32_t interval;                // age_refresh_interval_frames.min(u32::MAX)
+  unsigned long long seed;          // blue_noise_seed
+};
+
 // Exclusive scan of one int per thread in thread order; *total gets the block sum.
 __device__ __forceinline__ int viewer_scan(int v, int* sums, int* total) {
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
@@ -92,14 +110,206 @@ __device__ __forceinline__ void write_all(int n, int32_t* out) {
   for (int i = threadIdx.x; i < n; i += blockDim.x) out[i] = i;
 }
 
+// ---- refresh stage (PatchDiffRefreshState::augment_mask and its bookkeeping) ----------------
+
+__device__ __forceinline__ uint32_t sat_inc32(uint32_t v) { return v == 0xffffffffu ? v : v + 1; }
+
+// mix64 (src/viewer.rs:530-536): the splitmix64 output function.
+__device__ __forceinline__ unsigned long long refresh_mix64(unsigned long long v) {
+  v ^= v >> 30;
+  v *= 0xbf58476d1ce4e5b9ull;
+  v ^= v >> 27;
+  v *= 0x94d049bb133111ebull;
+  return v ^ (v >> 31);
+}
+
+// A candidate's place in add_ranked_candidates' order (:505-511) as one 128-bit unsigned key,
+// smaller first: priority descending, then the refresh rank, then the token index.  Every key is
+// distinct because the index is in it.  -0.0 and 0.0 compare equal under partial_cmp, so both
+// map to 0.0's key; no priority here is NaN (residual >= trigger, age as f32, or 0.0).
+struct RefreshKey {
+  unsigned long long hi, lo;
+};
+__device__ __forceinline__ RefreshKey refresh_key(float priority, unsigned long long rank, int index) {
+  uint32_t b = __float_as_uint(priority == 0.0f ? 0.0f : priority);
+  b = (b & 0x80000000u) ? ~b : (b | 0x80000000u);  // unsigned order = float order
+  return {((unsigned long long)~b << 32) | (rank >> 32), (rank << 32) | (uint32_t)index};
+}
+__device__ __forceinline__ int key_digit(const RefreshKey& k, int d) {  // byte d, most significant first
+  return d < 8 ? (int)((k.hi >> (56 - 8 * d)) & 0xff) : (int)((k.lo >> (56 - 8 * (d - 8))) & 0xff);
+}
+__device__ __forceinline__ bool key_prefix_is(const RefreshKey& k, int d, unsigned long long ph,
+                                              unsigned long long pl) {  // top 8 d bits equal
+  const unsigned long long mh = d == 0 ? 0ull : (d >= 8 ? ~0ull : ~0ull << (64 - 8 * d));
+  const unsigned long long ml = d <= 8 ? 0ull : ~0ull << (64 - 8 * (d - 8));
+  return (k.hi & mh) == ph && (k.lo & ml) == pl;
+}
+
+// Whether unselected token i is a candidate of `stage` (0 subthreshold, 1 age, 2 blue noise,
+// the closures of :409-459) and its key.  Ages are read before this frame's increment.
+__device__ __forceinline__ bool refresh_candidate(const RefreshParams& r, int stage, const float* res,
+                                                  const uint32_t* age, int gw, unsigned long long frame, int i,
+                                                  RefreshKey& key) {
+  float priority = 0.0f;
+  if (stage == 0) {
+    priority = res[i];
+    if (!(priority >= r.trigger)) return false;
+  } else if (stage == 1) {
+    const uint32_t a = sat_inc32(age[i]);
+    if (a < r.interval) return false;
+    priority = __uint2float_rn(a);  // `age as f32`
+  }
+  // refresh_rank (:520-528): the row and column of the flat index over the grid's width
+  const unsigned long long row = (unsigned)i / (unsigned)gw, col = (unsigned)i % (unsigned)gw;
+  const unsigned long long rank = refresh_mix64(r.seed ^ (row * 0x9e3779b97f4a7c15ull) ^
+                                                (col * 0xbf58476d1ce4e5b9ull) ^ (frame * 0x94d049bb133111ebull));
+  key = refresh_key(priority, rank, i);
+  return true;
+}
+
+// add_ranked_candidates (:481-518): marks in keep (as 1) the `budget` smallest keys among the
+// stage's candidates that keep does not hold, and returns how many it marked.  With more
+// candidates than budget, a most-significant-byte-first radix select over the 128-bit key
+// finds them: each pass takes every candidate below the byte holding the budget-th key, and
+// stops when that byte's candidates are exactly the ones still needed.  Each token is owned by
+// one thread (i = threadIdx.x + k blockDim.x) in every loop.
+__device__ int refresh_add_ranked(const RefreshParams& r, int stage, int budget, int n, int gw, long long s,
+                                  unsigned long long frame, unsigned char* keep, int* sums, int* hist, int* pick) {
+  const float* res = r.residual + s * n;
+  const uint32_t* age = r.age + s * n;
+  RefreshKey k;
+  int local = 0;
+  for (int i = threadIdx.x; i < n; i += blockDim.x)
+    local += keep[i] == 0 && refresh_candidate(r, stage, res, age, gw, frame, i, k);
+  int total;
+  viewer_scan(local, sums, &total);
+  if (total <= budget) {
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+      if (keep[i] == 0 && refresh_candidate(r, stage, res, age, gw, frame, i, k)) keep[i] = 1;
+    __syncthreads();
+    return total;
+  }
+  int need = budget;
+  unsigned long long ph = 0, pl = 0;
+  for (int d = 0; d < 16; ++d) {
+    for (int b = threadIdx.x; b < 256; b += blockDim.x) hist[b] = 0;
+    __syncthreads();
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+      if (keep[i] == 0 && refresh_candidate(r, stage, res, age, gw, frame, i, k) && key_prefix_is(k, d, ph, pl))
+        atomicAdd(&hist[key_digit(k, d)], 1);
+    __syncthreads();
+    if (threadIdx.x < 32) {  // the byte b with (candidates below b) < need <= (candidates up to b)
+      const int lane = threadIdx.x;
+      int c = 0;
+      for (int j = 0; j < 8; ++j) c += hist[lane * 8 + j];
+      int inc = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int y = __shfl_up_sync(0xffffffffu, inc, o);
+        if (lane >= o) inc += y;
+      }
+      int before = inc - c;
+      if (before < need && need <= inc) {
+        for (int j = 0; j < 8; ++j) {
+          const int h = hist[lane * 8 + j];
+          if (before + h >= need) {
+            pick[0] = lane * 8 + j;
+            pick[1] = before;
+            pick[2] = h;
+            break;
+          }
+          before += h;
+        }
+      }
+    }
+    __syncthreads();
+    const int b = pick[0];
+    need -= pick[1];
+    const bool whole = pick[2] == need;  // the byte's candidates are all still needed
+    for (int i = threadIdx.x; i < n; i += blockDim.x)
+      if (keep[i] == 0 && refresh_candidate(r, stage, res, age, gw, frame, i, k) && key_prefix_is(k, d, ph, pl)) {
+        const int dg = key_digit(k, d);
+        if (dg < b || (whole && dg == b)) keep[i] = 1;
+      }
+    __syncthreads();
+    if (whole) break;  // reached by d = 15 at the latest: keys are distinct
+    if (d < 8)
+      ph |= (unsigned long long)b << (56 - 8 * d);
+    else
+      pl |= (unsigned long long)b << (56 - 8 * (d - 8));
+  }
+  return budget;
+}
+
+// One frame of the stream's refresh state around its write mask, held in keep as nonzero flags
+// (count of n set): augment_mask (:377-458) when the config can add tokens and the mask is not
+// every token, then begin_frame's increments and reset_selected over the final write mask
+// (:352-375).  Residuals are updated before any ranking reads them; ages are read before the
+// increment and written once at the end.
+__device__ void refresh_stream(const RefreshParams& r, int n, int gw, long long s, int count, unsigned char* keep,
+                               int* sums, int* hist, int* pick) {
+  const unsigned long long f0 = r.frame_index[s];
+  const unsigned long long frame = f0 == ~0ull ? f0 : f0 + 1;
+  float* res = r.residual + s * n;
+  uint32_t* age = r.age + s * n;
+  if (r.augment && count < n) {
+    int remaining = max(r.max_context - count, 0);
+    remaining = min(remaining, r.max_extra);
+    // update_subthreshold_residual (:461-479) against the base mask; Rust evaluates r * decay
+    // and normalized * gain as separate f32 products and adds them, hence no contraction
+    const float* scores = r.scores + s * n;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) {
+      const float sc = scores[i];
+      float v = 0.0f;
+      if (keep[i] == 0 && !(sc >= r.threshold)) {
+        float norm = __fdiv_rn(sc, r.norm_threshold);
+        norm = norm < 0.0f ? 0.0f : (norm > 1.0f ? 1.0f : norm);  // f32::clamp keeps a NaN
+        v = __fadd_rn(__fmul_rn(res[i], r.decay), __fmul_rn(norm, r.gain));
+      }
+      res[i] = v;
+    }
+    __syncthreads();
+    for (int stage = 0; stage < 3 && remaining > 0; ++stage) {
+      if (r.stage_tokens[stage] == 0) continue;
+      const int budget = min(remaining, r.stage_tokens[stage]);
+      remaining -= refresh_add_ranked(r, stage, budget, n, gw, s, frame, keep, sums, hist, pick);
+    }
+  }
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    if (keep[i]) {
+      res[i] = 0.0f;
+      age[i] = 0;
+    } else {
+      age[i] = sat_inc32(age[i]);
+    }
+  }
+  __syncthreads();  // every thread has read the old frame index
+  if (threadIdx.x == 0) r.frame_index[s] = frame;
+}
+
+// observe_write_mask (:309-313) of a write mask that is every token.
+__device__ __forceinline__ void refresh_all_written(const RefreshParams& r, int n, long long s) {
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    r.residual[s * n + i] = 0.0f;
+    r.age[s * n + i] = 0;
+  }
+  if (threadIdx.x == 0) {
+    const unsigned long long f0 = r.frame_index[s];
+    r.frame_index[s] = f0 == ~0ull ? f0 : f0 + 1;
+  }
+}
+
 // direct_idx / direct_cnt may alias write_idx / write_cnt: every direct index and count is
 // read before the write mask is stored.
 __global__ void __launch_bounds__(kViewerThreads)
-    viewer_mask_kernel(const int32_t* direct_idx, const int32_t* direct_cnt, ViewerParams p, int32_t* write_idx,
-                       int32_t* write_cnt, int32_t* __restrict__ enc_idx, int32_t* __restrict__ enc_cnt) {
+    viewer_mask_kernel(const int32_t* direct_idx, const int32_t* direct_cnt, ViewerParams p, RefreshParams r,
+                       int32_t* write_idx, int32_t* write_cnt, int32_t* __restrict__ enc_idx,
+                       int32_t* __restrict__ enc_cnt) {
   extern __shared__ unsigned char keep[];
   __shared__ int sums[33];
   __shared__ int taken_sh;
+  __shared__ int hist[256];
+  __shared__ int pick[3];
   pdl_wait();
   const int n = p.n;
   const long long s = blockIdx.x;
@@ -131,6 +341,7 @@ __global__ void __launch_bounds__(kViewerThreads)
       write_cnt[s] = n;
       enc_cnt[s] = n;
     }
+    if (r.residual) refresh_all_written(r, n, s);
     return;
   }
 
@@ -148,6 +359,13 @@ __global__ void __launch_bounds__(kViewerThreads)
       for (int c = c0; c <= c1; ++c) keep[t * tpf + r * p.gw + c] = 1;
   }
   __syncthreads();
+  if (r.residual) {
+    // the refresh tokens join the write mask before the encode buckets (src/viewer.rs:343-346)
+    int base = 0;
+    for (int i = threadIdx.x; i < n; i += blockDim.x) base += keep[i] != 0;
+    viewer_scan(base, sums, &base);
+    refresh_stream(r, n, p.gw, s, base, keep, sums, hist, pick);
+  }
   const int count = compact_flags(keep, n, wout, sums);
   if (threadIdx.x == 0) write_cnt[s] = count;
 
@@ -264,15 +482,82 @@ bjf_status viewer_params(const int64_t* grid, const bjf_viewer_mask_policy* poli
 
 bjf_status launch_viewer_masks(const int32_t* direct_idx, const int32_t* direct_cnt, int64_t streams,
                                const ViewerParams& p, int32_t* write_idx, int32_t* write_cnt, int32_t* enc_idx,
-                               int32_t* enc_cnt, cudaStream_t st) {
+                               int32_t* enc_cnt, cudaStream_t st, const RefreshParams* refresh = nullptr) {
   const size_t smem = (size_t)p.n;
   cudaError_t e = cudaSuccess;
-  if (smem > 48 * 1024)
+  if (smem > 48 * 1024 - 2048)  // the static arrays take the rest of the default 48 KB
     e = cudaFuncSetAttribute(viewer_mask_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return cuda_status(e, "viewer mask attribute");
-  viewer_mask_kernel<<<(unsigned)streams, kViewerThreads, smem, st>>>(direct_idx, direct_cnt, p, write_idx, write_cnt,
-                                                                      enc_idx, enc_cnt);
+  RefreshParams r{};
+  if (refresh) r = *refresh;
+  viewer_mask_kernel<<<(unsigned)streams, kViewerThreads, smem, st>>>(direct_idx, direct_cnt, p, r, write_idx,
+                                                                      write_cnt, enc_idx, enc_cnt);
   return check_launch("viewer mask launch");
+}
+
+// f32::clamp(lo, hi): a NaN stays NaN.
+float rust_clamp(float v, float lo, float hi) { return v < lo ? lo : (v > hi ? hi : v); }
+
+// density_tokens(n, density, Floor, 0.0) (src/viewer.rs:739-752): f32 product, floor, a
+// saturating `as usize`, then clamp(1, n).
+int density_tokens_floor(int64_t n, float density) {
+  const float x = std::floor((float)n * rust_clamp(density, 0.0f, 1.0f));
+  const int64_t t = x > 0.0f ? (x >= (float)n ? n : (int64_t)x) : 0;  // NaN casts to 0
+  return (int)std::min<int64_t>(std::max<int64_t>(t, 1), std::max<int64_t>(n, 1));
+}
+
+// The refresh state and config as the kernel reads them.  context_tokens is the sparsity
+// config's (src/viewer.rs:388).
+bjf_status refresh_params(const bjf_patch_diff_refresh_config* c, const bjf_patch_diff_refresh_state* state,
+                          const float* scores, int64_t n, const bjf_patch_diff_config* sparsity, RefreshParams& r) {
+  if (!c) return fail(BJF_ERR_INVALID_ARGUMENT, "patch-diff refresh config must not be null");
+  if (!state || !state->subthreshold_residual || !state->age_frames || !state->frame_index)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "patch-diff refresh state buffers must not be null");
+  r = RefreshParams{};
+  r.residual = state->subthreshold_residual;
+  r.age = state->age_frames;
+  r.frame_index = reinterpret_cast<unsigned long long*>(state->frame_index);
+  r.scores = scores;
+  const bool sub = c->subthreshold_enabled && c->subthreshold_max_density > 0.0f;
+  const bool aged = c->age_refresh_enabled && c->age_refresh_interval_frames > 0 && c->age_refresh_max_density > 0.0f;
+  const bool blue = c->blue_noise_enabled && c->blue_noise_refresh_density > 0.0f;
+  // PatchDiffRefreshConfig::can_add_tokens (:258-269); without scores (the dense shortcuts of
+  // the RGBA node) nothing is ranked
+  r.augment = scores && c->enabled && c->max_extra_density > 0.0f && (sub || aged || blue);
+  r.threshold = sparsity ? sparsity->threshold : 0.0f;
+  r.norm_threshold = std::fmax(r.threshold, 1.0e-6f);  // f32::max returns the number for a NaN
+  r.decay = rust_clamp(c->subthreshold_decay, 0.0f, 1.0f);
+  r.gain = std::fmax(c->subthreshold_gain, 0.0f);
+  r.trigger = std::fmax(c->subthreshold_trigger, 1.0e-6f);
+  const int64_t ctx = sparsity ? sparsity->context_tokens : 1;
+  r.max_context = (int)std::min<int64_t>(std::max<int64_t>(ctx, 1), n);
+  r.max_extra = density_tokens_floor(n, c->max_extra_density);
+  r.stage_tokens[0] = sub ? density_tokens_floor(n, c->subthreshold_max_density) : 0;
+  r.stage_tokens[1] = aged ? density_tokens_floor(n, c->age_refresh_max_density) : 0;
+  r.stage_tokens[2] = blue ? density_tokens_floor(n, c->blue_noise_refresh_density) : 0;
+  r.interval = (uint32_t)std::min<uint64_t>(c->age_refresh_interval_frames, 0xffffffffull);
+  r.seed = c->blue_noise_seed;
+  return BJF_OK;
+}
+
+// observe_write_mask (src/viewer.rs:309-313) for one stream per CTA: every age advances, then
+// the written tokens' residuals and ages return to zero.
+__global__ void __launch_bounds__(kViewerThreads)
+    refresh_observe_kernel(const int32_t* __restrict__ idx, const int32_t* __restrict__ cnt, int n, RefreshParams r) {
+  const long long s = blockIdx.x;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) r.age[s * n + i] = sat_inc32(r.age[s * n + i]);
+  __syncthreads();  // the block's global writes are visible to it after the barrier
+  const int m = min(max(cnt[s], 0), n);
+  for (int j = threadIdx.x; j < m; j += blockDim.x) {
+    const int i = idx[s * n + j];
+    if (i < 0 || i >= n) continue;  // SparseTokenMask holds in-range indices; `get_mut` skips others
+    r.residual[s * n + i] = 0.0f;
+    r.age[s * n + i] = 0;
+  }
+  if (threadIdx.x == 0) {
+    const unsigned long long f0 = r.frame_index[s];
+    r.frame_index[s] = f0 == ~0ull ? f0 : f0 + 1;
+  }
 }
 
 }  // namespace
@@ -295,13 +580,13 @@ extern "C" bjf_status bjf_viewer_patch_diff_masks(const int32_t* direct_indices,
                              encode_counts, as_cuda(stream));
 }
 
-extern "C" bjf_status bjf_viewer_patch_diff_masks_from_scores(const float* scores, int64_t streams,
-                                                              const int64_t grid[3],
-                                                              const bjf_patch_diff_config* config,
-                                                              const bjf_viewer_mask_policy* policy,
-                                                              int32_t* write_indices, int32_t* write_counts,
-                                                              int32_t* encode_indices, int32_t* encode_counts,
-                                                              bjf_stream_t stream) {
+namespace {
+bjf_status masks_from_scores(const float* scores, int64_t streams, const int64_t grid[3],
+                             const bjf_patch_diff_config* config, const bjf_viewer_mask_policy* policy,
+                             int32_t* write_indices, int32_t* write_counts, int32_t* encode_indices,
+                             int32_t* encode_counts, bjf_stream_t stream,
+                             const bjf_patch_diff_refresh_config* refresh,
+                             const bjf_patch_diff_refresh_state* state) {
   if (!config) return fail(BJF_ERR_INVALID_ARGUMENT, "patch-diff config must not be null");
   if (!grid || grid[0] <= 0 || grid[1] <= 0 || grid[2] <= 0)
     return fail(BJF_ERR_INVALID_ARGUMENT, "token grid must be non-empty");
@@ -321,11 +606,58 @@ extern "C" bjf_status bjf_viewer_patch_diff_masks_from_scores(const float* score
   ViewerParams vp{};
   rc = viewer_params(grid, &dilated, vp);
   if (rc) return rc;
+  RefreshParams rp{};
+  if (state) {
+    rc = refresh_params(refresh, state, scores, vp.n, config, rp);
+    if (rc) return rc;
+  }
   cudaStream_t st = as_cuda(stream);
   rc = launch_select(scores, streams, sp, write_indices, write_counts, st);
   if (rc) return rc;
   return launch_viewer_masks(write_indices, write_counts, streams, vp, write_indices, write_counts, encode_indices,
-                             encode_counts, st);
+                             encode_counts, st, state ? &rp : nullptr);
+}
+}  // namespace
+
+extern "C" bjf_status bjf_viewer_patch_diff_masks_from_scores(const float* scores, int64_t streams,
+                                                              const int64_t grid[3],
+                                                              const bjf_patch_diff_config* config,
+                                                              const bjf_viewer_mask_policy* policy,
+                                                              int32_t* write_indices, int32_t* write_counts,
+                                                              int32_t* encode_indices, int32_t* encode_counts,
+                                                              bjf_stream_t stream) {
+  return masks_from_scores(scores, streams, grid, config, policy, write_indices, write_counts, encode_indices,
+                           encode_counts, stream, nullptr, nullptr);
+}
+
+extern "C" bjf_status bjf_viewer_patch_diff_refresh_masks_from_scores(
+    const float* scores, int64_t streams, const int64_t grid[3], const bjf_patch_diff_config* config,
+    const bjf_viewer_mask_policy* policy, const bjf_patch_diff_refresh_config* refresh,
+    const bjf_patch_diff_refresh_state* state, int32_t* write_indices, int32_t* write_counts,
+    int32_t* encode_indices, int32_t* encode_counts, bjf_stream_t stream) {
+  if (!state) return fail(BJF_ERR_INVALID_ARGUMENT, "patch-diff refresh state buffers must not be null");
+  return masks_from_scores(scores, streams, grid, config, policy, write_indices, write_counts, encode_indices,
+                           encode_counts, stream, refresh, state);
+}
+
+extern "C" bjf_status bjf_viewer_patch_diff_refresh_observe(const int32_t* write_indices,
+                                                            const int32_t* write_counts, int64_t streams,
+                                                            const int64_t grid[3],
+                                                            const bjf_patch_diff_refresh_state* state,
+                                                            bjf_stream_t stream) {
+  if (!grid || grid[0] <= 0 || grid[1] <= 0 || grid[2] <= 0)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "token grid must be non-empty");
+  if (streams <= 0 || streams > (int64_t(1) << 31) - 1) return fail(BJF_ERR_INVALID_ARGUMENT, "stream count must be positive");
+  const int64_t n = grid[0] * grid[1] * grid[2];
+  if (n > kMaxViewerTokens) return fail(BJF_ERR_UNSUPPORTED, "viewer masks support grids up to 32768 tokens");
+  if (!write_indices || !write_counts) return fail(BJF_ERR_INVALID_ARGUMENT, "viewer mask buffers must not be null");
+  const bjf_patch_diff_refresh_config off{};
+  RefreshParams r{};
+  const bjf_status rc = refresh_params(&off, state, nullptr, n, nullptr, r);
+  if (rc) return rc;
+  refresh_observe_kernel<<<(unsigned)streams, kViewerThreads, 0, as_cuda(stream)>>>(write_indices, write_counts,
+                                                                                    (int)n, r);
+  return check_launch("refresh observe launch");
 }
 
 namespace {
@@ -340,11 +672,14 @@ extern "C" size_t bjf_viewer_rgba_masks_workspace_bytes(int64_t streams, const i
   return rgba_masks_scores_offset(streams, grid) + sizeof(float) * (size_t)streams * (size_t)(grid[1] * grid[2]);
 }
 
-extern "C" bjf_status bjf_viewer_patch_diff_masks_from_rgba(
-    const uint8_t* prev, const uint8_t* current, int64_t streams, int64_t width, int64_t height, int64_t patch_size,
-    const int64_t grid[3], const bjf_patch_diff_config* config, const bjf_viewer_mask_policy* policy,
-    int32_t* write_indices, int32_t* write_counts, int32_t* encode_indices, int32_t* encode_counts,
-    bjf_rgba_frame_stats* stats_out, void* workspace, size_t workspace_bytes, bjf_stream_t stream) {
+namespace {
+bjf_status masks_from_rgba(const uint8_t* prev, const uint8_t* current, int64_t streams, int64_t width,
+                           int64_t height, int64_t patch_size, const int64_t grid[3],
+                           const bjf_patch_diff_config* config, const bjf_viewer_mask_policy* policy,
+                           const bjf_patch_diff_refresh_config* refresh, const bjf_patch_diff_refresh_state* state,
+                           int32_t* write_indices, int32_t* write_counts, int32_t* encode_indices,
+                           int32_t* encode_counts, bjf_rgba_frame_stats* stats_out, void* workspace,
+                           size_t workspace_bytes, bjf_stream_t stream) {
   if (!config) return fail(BJF_ERR_INVALID_ARGUMENT, "patch-diff config must not be null");
   if (!policy) return fail(BJF_ERR_INVALID_ARGUMENT, "viewer mask policy must not be null");
   if (!grid) return fail(BJF_ERR_INVALID_ARGUMENT, "token grid must not be null");
@@ -386,6 +721,13 @@ extern "C" bjf_status bjf_viewer_patch_diff_masks_from_rgba(
     vp.sample_cols = (int)((grid[2] + stride - 1) / stride);
     vp.sample_required = std::isnan(fb) ? 0 : (int)std::ceil((float)(vp.sample_rows * vp.sample_cols) * fb);
   }
+  RefreshParams rp{};
+  if (state) {
+    // PatchDiffRefreshState::masks_from_scores after the scores; a dense shortcut is
+    // observe_write_mask of every token (crates/bevy_jepa/src/mask.rs:151-175)
+    rc = refresh_params(refresh, state, scores, n, config, rp);
+    if (rc) return rc;
+  }
   cudaStream_t st = as_cuda(stream);
   rc = bjf_rgba_patch_diff_scores(prev, current, streams, width, height, patch_size, grid, scores, stats_out,
                                   workspace, workspace_bytes, stream);
@@ -393,5 +735,28 @@ extern "C" bjf_status bjf_viewer_patch_diff_masks_from_rgba(
   rc = launch_select(scores, streams, sp, write_indices, write_counts, st);
   if (rc) return rc;
   return launch_viewer_masks(write_indices, write_counts, streams, vp, write_indices, write_counts, encode_indices,
-                             encode_counts, st);
+                             encode_counts, st, state ? &rp : nullptr);
+}
+}  // namespace
+
+extern "C" bjf_status bjf_viewer_patch_diff_masks_from_rgba(
+    const uint8_t* prev, const uint8_t* current, int64_t streams, int64_t width, int64_t height, int64_t patch_size,
+    const int64_t grid[3], const bjf_patch_diff_config* config, const bjf_viewer_mask_policy* policy,
+    int32_t* write_indices, int32_t* write_counts, int32_t* encode_indices, int32_t* encode_counts,
+    bjf_rgba_frame_stats* stats_out, void* workspace, size_t workspace_bytes, bjf_stream_t stream) {
+  return masks_from_rgba(prev, current, streams, width, height, patch_size, grid, config, policy, nullptr, nullptr,
+                         write_indices, write_counts, encode_indices, encode_counts, stats_out, workspace,
+                         workspace_bytes, stream);
+}
+
+extern "C" bjf_status bjf_viewer_patch_diff_refresh_masks_from_rgba(
+    const uint8_t* prev, const uint8_t* current, int64_t streams, int64_t width, int64_t height, int64_t patch_size,
+    const int64_t grid[3], const bjf_patch_diff_config* config, const bjf_viewer_mask_policy* policy,
+    const bjf_patch_diff_refresh_config* refresh, const bjf_patch_diff_refresh_state* state,
+    int32_t* write_indices, int32_t* write_counts, int32_t* encode_indices, int32_t* encode_counts,
+    bjf_rgba_frame_stats* stats_out, void* workspace, size_t workspace_bytes, bjf_stream_t stream) {
+  if (!state) return fail(BJF_ERR_INVALID_ARGUMENT, "patch-diff refresh state buffers must not be null");
+  return masks_from_rgba(prev, current, streams, width, height, patch_size, grid, config, policy, refresh, state,
+                         write_indices, write_counts, encode_indices, encode_counts, stats_out, workspace,
+                         workspace_bytes, stream);
 }

@@ -37,8 +37,9 @@ extern "C" {
 #endif
 
 /* 2: bjf_rgba_patch_diff_workspace_bytes takes the token grid.
- * 3: bjf_set_bounded_wait, bjf_front_end_step_ring. */
-#define BJF_ABI_VERSION 3
+ * 3: bjf_set_bounded_wait, bjf_front_end_step_ring.
+ * 4: the patch-diff refresh state on the device (bjf_viewer_patch_diff_refresh_*). */
+#define BJF_ABI_VERSION 4
 
 #if defined(__GNUC__)
 #define BJF_API __attribute__((visibility("default")))
@@ -331,6 +332,67 @@ BJF_API bjf_status bjf_viewer_patch_diff_masks_from_rgba(
     const int64_t grid[3], const bjf_patch_diff_config* config, const bjf_viewer_mask_policy* policy,
     int32_t* write_indices, int32_t* write_counts, int32_t* encode_indices, int32_t* encode_counts,
     bjf_rgba_frame_stats* stats_out, void* workspace, size_t workspace_bytes, bjf_stream_t stream);
+
+/* PatchDiffRefreshConfig (src/viewer.rs:186-270): bounded extra cache writes for tokens whose
+ * motion stays below the threshold (subthreshold), tokens unwritten for a number of frames
+ * (age) and a seeded scatter (blue noise).  Flags are 0 or 1; the reference's defaults are
+ * enabled 0, decay 0.92, gain 1, trigger 1, subthreshold 0.04, interval 90, age 0.01, blue
+ * noise 0.005 with seed 0x9e3779b97f4a7c15, max extra 0.05 (src/viewer.rs:35-49). */
+typedef struct bjf_patch_diff_refresh_config {
+  int32_t enabled;
+  int32_t subthreshold_enabled;
+  float subthreshold_decay;
+  float subthreshold_gain;
+  float subthreshold_trigger;
+  float subthreshold_max_density;
+  int32_t age_refresh_enabled;
+  uint64_t age_refresh_interval_frames;
+  float age_refresh_max_density;
+  int32_t blue_noise_enabled;
+  float blue_noise_refresh_density;
+  uint64_t blue_noise_seed;
+  float max_extra_density;
+} bjf_patch_diff_refresh_config;
+
+/* PatchDiffRefreshState (src/viewer.rs:275-283) of S streams, in device memory the caller owns:
+ * per stream and token the decayed below-threshold residual and the frames since the token was
+ * last written, per stream the frame index.  All zeros is the state before a stream's first
+ * frame.  The reference starts a state over when the grid's token count changes; a caller that
+ * changes grids zeroes the buffers (sized for the new grid) itself. */
+typedef struct bjf_patch_diff_refresh_state {
+  float* subthreshold_residual; /* [S, N] f32 */
+  uint32_t* age_frames;         /* [S, N] */
+  uint64_t* frame_index;        /* [S] */
+} bjf_patch_diff_refresh_state;
+
+/* PatchDiffRefreshState::masks_from_scores (src/viewer.rs:312-356) for S streams, each with
+ * its own state: bjf_viewer_patch_diff_masks_from_scores with the refresh tokens of
+ * augment_mask (:377-458) added to the write mask before the encode buckets, and every stream's
+ * state advanced one frame, inside the same launch after the selection.  Inputs and outputs as
+ * bjf_viewer_patch_diff_masks_from_scores.  Errors: those, and a null config or state buffer. */
+BJF_API bjf_status bjf_viewer_patch_diff_refresh_masks_from_scores(
+    const float* scores, int64_t streams, const int64_t grid[3], const bjf_patch_diff_config* config,
+    const bjf_viewer_mask_policy* policy, const bjf_patch_diff_refresh_config* refresh,
+    const bjf_patch_diff_refresh_state* state, int32_t* write_indices, int32_t* write_counts,
+    int32_t* encode_indices, int32_t* encode_counts, bjf_stream_t stream);
+
+/* The RGBA mask node with its refresh state (crates/bevy_jepa/src/mask.rs:126-185):
+ * bjf_viewer_patch_diff_masks_from_rgba, where a dense shortcut is observe_write_mask of every
+ * token and the scored path is PatchDiffRefreshState::masks_from_scores. */
+BJF_API bjf_status bjf_viewer_patch_diff_refresh_masks_from_rgba(
+    const uint8_t* prev, const uint8_t* current, int64_t streams, int64_t width, int64_t height, int64_t patch_size,
+    const int64_t grid[3], const bjf_patch_diff_config* config, const bjf_viewer_mask_policy* policy,
+    const bjf_patch_diff_refresh_config* refresh, const bjf_patch_diff_refresh_state* state,
+    int32_t* write_indices, int32_t* write_counts, int32_t* encode_indices, int32_t* encode_counts,
+    bjf_rgba_frame_stats* stats_out, void* workspace, size_t workspace_bytes, bjf_stream_t stream);
+
+/* PatchDiffRefreshState::observe_write_mask (src/viewer.rs:309-313) for S streams: each stream
+ * advances one frame with write_indices [S, N] / write_counts [S] (ascending, as the mask
+ * entries write them) as its written tokens; indices outside the grid are skipped. */
+BJF_API bjf_status bjf_viewer_patch_diff_refresh_observe(const int32_t* write_indices, const int32_t* write_counts,
+                                                         int64_t streams, const int64_t grid[3],
+                                                         const bjf_patch_diff_refresh_state* state,
+                                                         bjf_stream_t stream);
 
 /* ------------------------------------------------------------------------
  * Fused step: mask -> plan -> patchify -> cache write, for S independent streams

@@ -649,6 +649,23 @@ struct PatchDiffRefreshConfig {
     c.max_extra_density = 0.0f;
     return c;
   }
+  bjf_patch_diff_refresh_config to_c() const {
+    bjf_patch_diff_refresh_config c{};
+    c.enabled = enabled;
+    c.subthreshold_enabled = subthreshold_enabled;
+    c.subthreshold_decay = subthreshold_decay;
+    c.subthreshold_gain = subthreshold_gain;
+    c.subthreshold_trigger = subthreshold_trigger;
+    c.subthreshold_max_density = subthreshold_max_density;
+    c.age_refresh_enabled = age_refresh_enabled;
+    c.age_refresh_interval_frames = age_refresh_interval_frames;
+    c.age_refresh_max_density = age_refresh_max_density;
+    c.blue_noise_enabled = blue_noise_enabled;
+    c.blue_noise_refresh_density = blue_noise_refresh_density;
+    c.blue_noise_seed = blue_noise_seed;
+    c.max_extra_density = max_extra_density;
+    return c;
+  }
   bool can_add_tokens() const {
     return enabled && max_extra_density > 0.0f &&
            ((subthreshold_enabled && subthreshold_max_density > 0.0f) ||
@@ -760,181 +777,6 @@ inline FeatureFrameSparseMasks patch_diff_masks_from_scores(const std::vector<fl
                                           config);
 }
 
-// PatchDiffRefreshState (src/viewer.rs:272-528): per-stream residuals of below-threshold
-// motion and token ages that add bounded refresh writes to the patch-diff masks.
-class PatchDiffRefreshState {
- public:
-  void reset() {
-    dense_len_ = 0;
-    frame_index_ = 0;
-    subthreshold_residual_.clear();
-    age_frames_.clear();
-  }
-  uint64_t frame_index() const { return frame_index_; }
-  std::optional<float> subthreshold_residual(size_t index) const {
-    if (index >= subthreshold_residual_.size()) return std::nullopt;
-    return subthreshold_residual_[index];
-  }
-  std::optional<uint32_t> age_frames(size_t index) const {
-    if (index >= age_frames_.size()) return std::nullopt;
-    return age_frames_[index];
-  }
-
-  void observe_write_mask(const SparseTokenMask& mask, TokenGridShape grid) {
-    begin_frame(grid);
-    reset_selected(mask.indices());
-  }
-
-  FeatureFrameSparseMasks masks_from_scores(const std::vector<float>& scores, TokenGridShape grid,
-                                            const SparseJepaPatchDiffSparsityConfig& sparsity,
-                                            const FeatureFrameViewerConfig& config, cudaStream_t st = nullptr) {
-    ensure(scores.size() == grid.len(), "patch-diff refresh received unexpected score length");
-    SparseTokenMask base = patch_diff_base_mask_from_scores(scores, grid, sparsity, config, st);
-    begin_frame(grid);
-    if (config.patch_diff_refresh.can_add_tokens() && !base.is_dense_ordered())
-      base = augment_mask(std::move(base), scores, grid, sparsity, config.patch_diff_refresh);
-    FeatureFrameSparseMasks masks = finalize_patch_diff_encode_masks(std::move(base), grid, config);
-    reset_selected(masks.write_mask.indices());
-    return masks;
-  }
-
- private:
-  void begin_frame(TokenGridShape grid) {
-    if (dense_len_ != grid.len()) {
-      dense_len_ = grid.len();
-      frame_index_ = 0;
-      subthreshold_residual_.assign(grid.len(), 0.0f);
-      age_frames_.assign(grid.len(), 0);
-    }
-    if (frame_index_ != UINT64_MAX) ++frame_index_;
-    for (uint32_t& a : age_frames_)
-      if (a != UINT32_MAX) ++a;
-  }
-  void reset_selected(const std::vector<size_t>& indices) {
-    for (size_t i : indices) {
-      if (i < subthreshold_residual_.size()) subthreshold_residual_[i] = 0.0f;
-      if (i < age_frames_.size()) age_frames_[i] = 0;
-    }
-  }
-  // mix64 (:530-536): the splitmix64 finaliser
-  static uint64_t mix64(uint64_t v) {
-    v ^= v >> 30;
-    v *= 0xbf58476d1ce4e5b9ull;
-    v ^= v >> 27;
-    v *= 0x94d049bb133111ebull;
-    return v ^ (v >> 31);
-  }
-  uint64_t refresh_rank(size_t index, TokenGridShape grid, uint64_t seed) const {
-    const uint64_t w = std::max<size_t>(grid.width, 1);
-    const uint64_t row = index / w, col = index % w;
-    return mix64(seed ^ (row * 0x9e3779b97f4a7c15ull) ^ (col * 0xbf58476d1ce4e5b9ull) ^
-                 (frame_index_ * 0x94d049bb133111ebull));
-  }
-  void update_subthreshold_residual(const std::vector<float>& scores, const std::vector<size_t>& chosen,
-                                    const SparseJepaPatchDiffSparsityConfig& sparsity,
-                                    const PatchDiffRefreshConfig& config) {
-    std::vector<bool> sel(scores.size(), false);
-    for (size_t i : chosen)
-      if (i < sel.size()) sel[i] = true;
-    const float decay = std::min(std::max(config.subthreshold_decay, 0.0f), 1.0f);
-    const float threshold = std::max(sparsity.threshold, 1.0e-6f);
-    for (size_t i = 0; i < subthreshold_residual_.size(); ++i) {
-      if (sel[i] || scores[i] >= sparsity.threshold) {
-        subthreshold_residual_[i] = 0.0f;
-      } else {
-        const float normalized = std::min(std::max(scores[i] / threshold, 0.0f), 1.0f);
-        subthreshold_residual_[i] = subthreshold_residual_[i] * decay + normalized * std::max(config.subthreshold_gain, 0.0f);
-      }
-    }
-  }
-  // add_ranked_candidates (:481-518): the `budget` best unselected candidates by (priority
-  // desc, rank asc, index asc), appended in that order.
-  template <typename F>
-  size_t add_ranked_candidates(std::vector<bool>& selected, std::vector<size_t>& indices, size_t budget, F rank) {
-    if (budget == 0) return 0;
-    struct Cand {
-      size_t index;
-      float priority;
-      uint64_t tie;
-    };
-    std::vector<Cand> cands;
-    for (size_t i = 0; i < selected.size(); ++i) {
-      if (selected[i]) continue;
-      float pr;
-      uint64_t tie;
-      if (rank(i, pr, tie)) cands.push_back({i, pr, tie});
-    }
-    auto before = [](const Cand& a, const Cand& b) {
-      if (a.priority > b.priority) return true;
-      if (b.priority > a.priority) return false;  // NaN priorities compare equal, as partial_cmp's fallback
-      if (a.tie != b.tie) return a.tie < b.tie;
-      return a.index < b.index;
-    };
-    std::sort(cands.begin(), cands.end(), before);
-    if (cands.size() > budget) cands.resize(budget);
-    for (const Cand& c : cands) {
-      selected[c.index] = true;
-      indices.push_back(c.index);
-    }
-    return cands.size();
-  }
-  SparseTokenMask augment_mask(SparseTokenMask base, const std::vector<float>& scores, TokenGridShape grid,
-                               const SparseJepaPatchDiffSparsityConfig& sparsity, const PatchDiffRefreshConfig& config) {
-    const size_t n = grid.len();
-    if (base.len() >= n) return base;
-    const size_t max_context = std::min(std::max<size_t>(sparsity.context_tokens, 1), n);
-    size_t remaining = max_context > base.len() ? max_context - base.len() : 0;
-    remaining = std::min(remaining, density_tokens(n, config.max_extra_density, DensityRound::Floor, 0.0f));
-    if (remaining == 0) {
-      update_subthreshold_residual(scores, base.indices(), sparsity, config);
-      return base;
-    }
-    std::vector<bool> selected(n, false);
-    std::vector<size_t> indices = base.indices();
-    for (size_t i : indices) selected[i] = true;
-    update_subthreshold_residual(scores, indices, sparsity, config);
-    const uint64_t seed = config.blue_noise_seed;
-    if (config.subthreshold_enabled && config.subthreshold_max_density > 0.0f) {
-      const size_t budget =
-          std::min(remaining, density_tokens(n, config.subthreshold_max_density, DensityRound::Floor, 0.0f));
-      const float trigger = std::max(config.subthreshold_trigger, 1.0e-6f);
-      remaining -= add_ranked_candidates(selected, indices, budget, [&](size_t i, float& pr, uint64_t& tie) {
-        if (!(subthreshold_residual_[i] >= trigger)) return false;
-        pr = subthreshold_residual_[i];
-        tie = refresh_rank(i, grid, seed);
-        return true;
-      });
-    }
-    if (remaining > 0 && config.age_refresh_enabled && config.age_refresh_interval_frames > 0 &&
-        config.age_refresh_max_density > 0.0f) {
-      const uint32_t interval = (uint32_t)std::min<uint64_t>(config.age_refresh_interval_frames, UINT32_MAX);
-      const size_t budget =
-          std::min(remaining, density_tokens(n, config.age_refresh_max_density, DensityRound::Floor, 0.0f));
-      remaining -= add_ranked_candidates(selected, indices, budget, [&](size_t i, float& pr, uint64_t& tie) {
-        if (age_frames_[i] < interval) return false;
-        pr = (float)age_frames_[i];
-        tie = refresh_rank(i, grid, seed);
-        return true;
-      });
-    }
-    if (remaining > 0 && config.blue_noise_enabled && config.blue_noise_refresh_density > 0.0f) {
-      const size_t budget =
-          std::min(remaining, density_tokens(n, config.blue_noise_refresh_density, DensityRound::Floor, 0.0f));
-      add_ranked_candidates(selected, indices, budget, [&](size_t i, float& pr, uint64_t& tie) {
-        pr = 0.0f;
-        tie = refresh_rank(i, grid, seed);
-        return true;
-      });
-    }
-    return SparseTokenMask::new_(std::move(indices), n);
-  }
-
-  size_t dense_len_ = 0;
-  uint64_t frame_index_ = 0;
-  std::vector<float> subthreshold_residual_;
-  std::vector<uint32_t> age_frames_;
-};
-
 // Device masks of S streams: row s of each [S, N] buffer holds its count of ascending indices.
 struct DeviceSparseMasks {
   Tensor write_indices, write_counts, encode_indices, encode_counts;
@@ -998,6 +840,127 @@ inline DeviceSparseMasks patch_diff_masks_from_rgba(const uint8_t* prev, const u
       ws.data(), ws.nbytes(), to_bjf(st)));
   return m;
 }
+
+// PatchDiffRefreshState (src/viewer.rs:275-528): per-stream residuals of below-threshold
+// motion and token ages that add bounded refresh writes to the patch-diff masks.  The state of
+// `streams` streams lives in device memory; each call advances every stream one frame inside
+// the viewer mask launch (the selection, dense fallback, dilation, refresh ranking and encode
+// buckets all run there), so a frame loop reads nothing back.  The host accessors copy one
+// value back for inspection.
+class PatchDiffRefreshState {
+ public:
+  explicit PatchDiffRefreshState(size_t streams = 1) : streams_(std::max<size_t>(streams, 1)) {}
+
+  // The reference clears the buffers; the next frame starts over on zeros.
+  void reset() { dense_len_ = 0; }
+  size_t streams() const { return streams_; }
+  uint64_t frame_index(size_t stream = 0) const {
+    if (dense_len_ == 0) return 0;
+    ensure(stream < streams_, "stream index outside the refresh state");
+    const auto v = frame_.to_host<int32_t>();
+    return (uint64_t)(uint32_t)v[2 * stream] | ((uint64_t)(uint32_t)v[2 * stream + 1] << 32);
+  }
+  std::optional<float> subthreshold_residual(size_t index, size_t stream = 0) const {
+    if (index >= dense_len_ || stream >= streams_) return std::nullopt;
+    return residual_.to_host<float>()[stream * dense_len_ + index];
+  }
+  std::optional<uint32_t> age_frames(size_t index, size_t stream = 0) const {
+    if (index >= dense_len_ || stream >= streams_) return std::nullopt;
+    return (uint32_t)age_.to_host<int32_t>()[stream * dense_len_ + index];
+  }
+
+  // observe_write_mask (:309-313) of one stream's host mask (a single-stream state).
+  void observe_write_mask(const SparseTokenMask& mask, TokenGridShape grid, cudaStream_t st = nullptr) {
+    ensure(streams_ == 1, "a host write mask belongs to a single-stream refresh state");
+    std::vector<int32_t> idx(grid.len(), 0);
+    for (size_t k = 0; k < mask.len(); ++k) idx[k] = (int32_t)mask.indices()[k];
+    const Tensor wi = Tensor::from_host(idx, {1, (int64_t)grid.len()}, BJF_DTYPE_I32, st);
+    const Tensor wc = Tensor::from_host(std::vector<int32_t>{(int32_t)mask.len()}, {1}, BJF_DTYPE_I32, st);
+    observe_write_masks(wi, wc, grid, st);
+  }
+  // observe_write_mask of every stream: write_indices [S, N], write_counts [S] on the device.
+  void observe_write_masks(const Tensor& write_indices, const Tensor& write_counts, TokenGridShape grid,
+                           cudaStream_t st = nullptr) {
+    bjf_patch_diff_refresh_state s = begin(grid, st);
+    const auto g = grid.dims();
+    check(bjf_viewer_patch_diff_refresh_observe(static_cast<const int32_t*>(write_indices.data()),
+                                                static_cast<const int32_t*>(write_counts.data()), (int64_t)streams_,
+                                                g.data(), &s, to_bjf(st)));
+  }
+
+  // masks_from_scores (:312-356) on device scores [S, N] f32.
+  DeviceSparseMasks masks_from_scores(const Tensor& scores, TokenGridShape grid,
+                                      const SparseJepaPatchDiffSparsityConfig& sparsity,
+                                      const FeatureFrameViewerConfig& config, cudaStream_t st = nullptr) {
+    const int64_t n = (int64_t)grid.len(), S = (int64_t)streams_;
+    ensure(scores.numel() == (size_t)(S * n), "patch-diff refresh received unexpected score length");
+    DeviceSparseMasks m{Tensor({S, n}, BJF_DTYPE_I32), Tensor({S}, BJF_DTYPE_I32), Tensor({S, n}, BJF_DTYPE_I32),
+                        Tensor({S}, BJF_DTYPE_I32), (size_t)n};
+    bjf_patch_diff_refresh_state s = begin(grid, st);
+    const bjf_patch_diff_config c = sparsity.to_c();
+    const bjf_viewer_mask_policy p = config.to_c();
+    const bjf_patch_diff_refresh_config r = config.patch_diff_refresh.to_c();
+    const auto g = grid.dims();
+    check(bjf_viewer_patch_diff_refresh_masks_from_scores(
+        static_cast<const float*>(scores.data()), S, g.data(), &c, &p, &r, &s,
+        static_cast<int32_t*>(m.write_indices.data()), static_cast<int32_t*>(m.write_counts.data()),
+        static_cast<int32_t*>(m.encode_indices.data()), static_cast<int32_t*>(m.encode_counts.data()), to_bjf(st)));
+    return m;
+  }
+
+  // masks_from_scores of one stream's host scores (the reference's Vec<f32>).
+  FeatureFrameSparseMasks masks_from_scores(const std::vector<float>& scores, TokenGridShape grid,
+                                            const SparseJepaPatchDiffSparsityConfig& sparsity,
+                                            const FeatureFrameViewerConfig& config, cudaStream_t st = nullptr) {
+    ensure(streams_ == 1, "host scores belong to a single-stream refresh state");
+    ensure(scores.size() == grid.len(), "patch-diff refresh received unexpected score length");
+    const Tensor d = Tensor::from_host(scores, {1, (int64_t)grid.len()}, BJF_DTYPE_F32, st);
+    return masks_from_scores(d, grid, sparsity, config, st).stream(0, st);
+  }
+
+  // The RGBA mask node with this state (crates/bevy_jepa/src/mask.rs:126-185) for device frame
+  // pairs [S, height, width, 4].
+  DeviceSparseMasks masks_from_rgba(const uint8_t* prev, const uint8_t* current, size_t width, size_t height,
+                                    size_t patch_size, TokenGridShape grid,
+                                    const SparseJepaPatchDiffSparsityConfig& sparsity,
+                                    const FeatureFrameViewerConfig& config, cudaStream_t st = nullptr) {
+    const int64_t n = (int64_t)grid.len(), S = (int64_t)streams_;
+    const auto g = grid.dims();
+    const size_t ws_bytes = bjf_viewer_rgba_masks_workspace_bytes(S, g.data());
+    ensure(ws_bytes > 0, "RGBA viewer masks support 1..65535 streams and grids up to 32768 tokens");
+    Tensor ws({(int64_t)((ws_bytes + 3) / 4)}, BJF_DTYPE_F32);
+    DeviceSparseMasks m{Tensor({S, n}, BJF_DTYPE_I32), Tensor({S}, BJF_DTYPE_I32), Tensor({S, n}, BJF_DTYPE_I32),
+                        Tensor({S}, BJF_DTYPE_I32), (size_t)n};
+    bjf_patch_diff_refresh_state s = begin(grid, st);
+    const bjf_patch_diff_config c = sparsity.to_c();
+    const bjf_viewer_mask_policy p = config.to_c();
+    const bjf_patch_diff_refresh_config r = config.patch_diff_refresh.to_c();
+    check(bjf_viewer_patch_diff_refresh_masks_from_rgba(
+        prev, current, S, (int64_t)width, (int64_t)height, (int64_t)patch_size, g.data(), &c, &p, &r, &s,
+        static_cast<int32_t*>(m.write_indices.data()), static_cast<int32_t*>(m.write_counts.data()),
+        static_cast<int32_t*>(m.encode_indices.data()), static_cast<int32_t*>(m.encode_counts.data()), nullptr,
+        ws.data(), ws.nbytes(), to_bjf(st)));
+    return m;
+  }
+
+ private:
+  // begin_frame's start-over (:352-359): new zeroed buffers when the token count changes.
+  bjf_patch_diff_refresh_state begin(TokenGridShape grid, cudaStream_t st) {
+    const int64_t n = (int64_t)grid.len(), S = (int64_t)streams_;
+    if (dense_len_ != grid.len()) {
+      residual_ = Tensor::zeros({S, n}, BJF_DTYPE_F32, st);
+      age_ = Tensor::zeros({S, n}, BJF_DTYPE_I32, st);
+      frame_ = Tensor::zeros({2 * S}, BJF_DTYPE_I32, st);
+      dense_len_ = grid.len();
+    }
+    return {static_cast<float*>(residual_.data()), static_cast<uint32_t*>(age_.data()),
+            static_cast<uint64_t*>(frame_.data())};
+  }
+
+  size_t streams_ = 1;
+  size_t dense_len_ = 0;
+  Tensor residual_, age_, frame_;  // [S, N] f32, [S, N] u32 (as i32), [S] u64 (as 2 i32)
+};
 
 // ---------------------------------------------------------------------------------------
 // plans (src/sparse_patchify.rs:236-330): coords rows (b, t, r, c), batch-major

@@ -630,7 +630,7 @@ class PatchDiffRefreshState:
             self.dense_len, self.frame_index = n, 0
             self.residual = np.zeros(n, np.float32)
             self.age = np.zeros(n, np.uint32)
-        self.frame_index += 1
+        self.frame_index = min(self.frame_index + 1, (1 << 64) - 1)  # saturating_add
         self.age = np.minimum(self.age.astype(np.uint64) + 1, 0xFFFFFFFF).astype(np.uint32)
 
     def _reset_selected(self, idx):
@@ -697,12 +697,18 @@ class PatchDiffRefreshState:
                 and c["age_refresh_max_density"] > 0.0):
             interval = min(c["age_refresh_interval_frames"], 0xFFFFFFFF)
             budget = min(remaining, density_tokens(n, c["age_refresh_max_density"], "floor", 0.0))
-            remaining -= self._add_ranked(selected, indices, budget, lambda i: (float(self.age[i]),
+            # the priority is `age as f32` (src/viewer.rs:436): ages round to the nearest f32
+            remaining -= self._add_ranked(selected, indices, budget, lambda i: (float(np.float32(self.age[i])),
                                           self._rank(i, grid, seed)) if self.age[i] >= interval else None)
         if remaining > 0 and c["blue_noise_enabled"] and c["blue_noise_refresh_density"] > 0.0:
             budget = min(remaining, density_tokens(n, c["blue_noise_refresh_density"], "floor", 0.0))
             self._add_ranked(selected, indices, budget, lambda i: (0.0, self._rank(i, grid, seed)))
         return sparse_token_mask_new(indices, n)
+
+    def observe_write_mask(self, mask, n: int):
+        """observe_write_mask (src/viewer.rs:309-313)."""
+        self._begin_frame(n)
+        self._reset_selected(np.asarray(mask, dtype=np.int64))
 
     def masks_from_scores(self, scores, grid, config, dense_fallback_density, refresh, bucketed=True,
                           bucket_tokens=256, bucket_densities=(0.10, 0.25, 0.50)):
@@ -721,6 +727,23 @@ class PatchDiffRefreshState:
         enc = finalize_patch_diff_encode_masks(base, n, bucketed, bucket_tokens, bucket_densities)
         self._reset_selected(base)
         return np.asarray(base, dtype=np.int64), enc
+
+
+def viewer_patch_diff_refresh_masks_from_rgba(state: "PatchDiffRefreshState", prev, current, width: int,
+                                              patch_size: int, grid: "TokenGridShape", config: "PatchDiffConfig",
+                                              dense_fallback_density: float, refresh, bucketed: bool = True,
+                                              bucket_tokens: int = 256, bucket_densities=(0.10, 0.25, 0.50)):
+    """patch_diff_mask_from_rgba with a refresh state (crates/bevy_jepa/src/mask.rs:126-185):
+    a dense shortcut is observe_write_mask of every token, else masks_from_scores."""
+    n = len(grid)
+    if patch_diff_can_use_dense_fast_path(config, n) or patch_diff_sampled_dense_fast_path_from_rgba(
+            prev, current, width, patch_size, grid, config, dense_fallback_density):
+        all_ = np.arange(n, dtype=np.int64)
+        state.observe_write_mask(all_, n)
+        return all_, all_.copy()
+    scores, _ = patch_diff_scores_from_rgba(prev, current, width, patch_size, grid)
+    return state.masks_from_scores(scores, grid, config, dense_fallback_density, refresh, bucketed, bucket_tokens,
+                                   bucket_densities)
 
 
 def front_end_streams(video, config: PatchifyConfig, mask_config: PatchDiffConfig, weight, bias,

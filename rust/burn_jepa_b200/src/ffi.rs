@@ -13,7 +13,7 @@ pub type bjf_stream_t = *mut c_void;
 /// `bjf_dtype` (a C enum, int-sized).
 pub type bjf_dtype = i32;
 
-pub const BJF_ABI_VERSION: i32 = 3;
+pub const BJF_ABI_VERSION: i32 = 4;
 
 pub const BJF_OK: bjf_status = 0;
 pub const BJF_ERR_INVALID_ARGUMENT: bjf_status = -1;
@@ -73,6 +73,35 @@ pub struct bjf_viewer_mask_policy {
     pub bucket_tokens: i64,
     pub bucket_density_count: i32,
     pub bucket_densities: [f32; 32],
+}
+
+/// `PatchDiffRefreshConfig` (src/viewer.rs:186-270); flags are 0 or 1.
+#[repr(C)]
+#[derive(Clone, Copy, Debug, Default)]
+pub struct bjf_patch_diff_refresh_config {
+    pub enabled: i32,
+    pub subthreshold_enabled: i32,
+    pub subthreshold_decay: f32,
+    pub subthreshold_gain: f32,
+    pub subthreshold_trigger: f32,
+    pub subthreshold_max_density: f32,
+    pub age_refresh_enabled: i32,
+    pub age_refresh_interval_frames: u64,
+    pub age_refresh_max_density: f32,
+    pub blue_noise_enabled: i32,
+    pub blue_noise_refresh_density: f32,
+    pub blue_noise_seed: u64,
+    pub max_extra_density: f32,
+}
+
+/// `PatchDiffRefreshState` (src/viewer.rs:275-283) of S streams in device memory: residuals
+/// [S, N] f32, ages [S, N] u32, frame indices [S] u64; all zeros before the first frame.
+#[repr(C)]
+#[derive(Clone, Copy, Debug)]
+pub struct bjf_patch_diff_refresh_state {
+    pub subthreshold_residual: *mut f32,
+    pub age_frames: *mut u32,
+    pub frame_index: *mut u64,
 }
 
 /// One video stream per index s: video [S, C, T, H, W], caches [S, N, D], observed / age [S, N].
@@ -280,6 +309,50 @@ unsafe extern "C" {
         stats_out: *mut bjf_rgba_frame_stats,
         workspace: *mut c_void,
         workspace_bytes: usize,
+        stream: bjf_stream_t,
+    ) -> bjf_status;
+
+    pub fn bjf_viewer_patch_diff_refresh_masks_from_scores(
+        scores: *const f32,
+        streams: i64,
+        grid: *const i64,
+        config: *const bjf_patch_diff_config,
+        policy: *const bjf_viewer_mask_policy,
+        refresh: *const bjf_patch_diff_refresh_config,
+        state: *const bjf_patch_diff_refresh_state,
+        write_indices: *mut i32,
+        write_counts: *mut i32,
+        encode_indices: *mut i32,
+        encode_counts: *mut i32,
+        stream: bjf_stream_t,
+    ) -> bjf_status;
+    pub fn bjf_viewer_patch_diff_refresh_masks_from_rgba(
+        prev: *const u8,
+        current: *const u8,
+        streams: i64,
+        width: i64,
+        height: i64,
+        patch_size: i64,
+        grid: *const i64,
+        config: *const bjf_patch_diff_config,
+        policy: *const bjf_viewer_mask_policy,
+        refresh: *const bjf_patch_diff_refresh_config,
+        state: *const bjf_patch_diff_refresh_state,
+        write_indices: *mut i32,
+        write_counts: *mut i32,
+        encode_indices: *mut i32,
+        encode_counts: *mut i32,
+        stats_out: *mut bjf_rgba_frame_stats,
+        workspace: *mut c_void,
+        workspace_bytes: usize,
+        stream: bjf_stream_t,
+    ) -> bjf_status;
+    pub fn bjf_viewer_patch_diff_refresh_observe(
+        write_indices: *const i32,
+        write_counts: *const i32,
+        streams: i64,
+        grid: *const i64,
+        state: *const bjf_patch_diff_refresh_state,
         stream: bjf_stream_t,
     ) -> bjf_status;
 

@@ -21,7 +21,7 @@ def test_library_exports_every_header_symbol():
 
 
 def test_abi_version():
-    assert bj.load().bjf_abi_version() == _abi.header_abi_version() == 3
+    assert bj.load().bjf_abi_version() == _abi.header_abi_version() == 4
 
 
 def _fm(features, observed, age, tokens, indices):
@@ -122,3 +122,31 @@ def test_ring_step_rejects_bad_slots():
     assert lib.bjf_front_end_step_ring(ctypes.byref(bad), 16, 3, 0, 1, 16, None, 16, 16, 16, 0, 16, 1 << 20, None,
                                        None) == _abi.BJF_ERR_INVALID_ARGUMENT
     assert "frames = 2" in bj.last_error()
+
+
+def test_ctypes_structs_have_the_c_layout(tmp_path):
+    """Every ctypes mirror has the size and field offsets gcc gives the struct in bjf.h."""
+    import os
+    import subprocess
+
+    structs = {"bjf_patchify_config": _abi.PatchifyConfig, "bjf_patch_diff_config": _abi.PatchDiffConfig,
+               "bjf_front_end_desc": _abi.FrontEndDesc, "bjf_rgba_frame_stats": _abi.RgbaFrameStats,
+               "bjf_viewer_mask_policy": _abi.ViewerMaskPolicy,
+               "bjf_patch_diff_refresh_config": _abi.PatchDiffRefreshConfig,
+               "bjf_patch_diff_refresh_state": _abi.PatchDiffRefreshState}
+    lines = ['#include <stdio.h>', '#include <stddef.h>', '#include "bjf.h"', "int main(void) {"]
+    want = []
+    for cname, py in structs.items():
+        lines.append(f'printf("%zu\\n", sizeof({cname}));')
+        want.append(ctypes.sizeof(py))
+        for field, *_ in py._fields_:
+            lines.append(f'printf("%zu\\n", offsetof({cname}, {field}));')
+            want.append(getattr(py, field).offset)
+    lines.append("return 0; }")
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    inc = os.path.dirname(_abi.HEADER_PATH)
+    subprocess.run(["gcc", "-std=c11", "-I", inc, str(src), "-o", str(exe)], check=True)
+    got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    assert got == want

@@ -13,9 +13,9 @@ from burn_jepa_b200 import _abi
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 FFI = os.path.join(ROOT, "rust", "burn_jepa_b200", "src", "ffi.rs")
 
-C_SCALARS = {"int32_t": "i32", "bjf_status": "i32", "bjf_dtype": "i32", "int64_t": "i64", "uint64_t": "u64",
+C_SCALARS = {"int32_t": "i32", "uint32_t": "u32", "bjf_status": "i32", "bjf_dtype": "i32", "int64_t": "i64", "uint64_t": "u64",
              "size_t": "usize", "float": "f32", "void": "void"}
-RUST_SCALARS = {"i32": "i32", "bjf_status": "i32", "bjf_dtype": "i32", "i64": "i64", "u64": "u64", "usize": "usize",
+RUST_SCALARS = {"i32": "i32", "u32": "u32", "bjf_status": "i32", "bjf_dtype": "i32", "i64": "i64", "u64": "u64", "usize": "usize",
                 "f32": "f32"}
 
 
@@ -77,6 +77,9 @@ def _c_struct_fields(name):
         line = line.strip()
         if not line:
             continue
+        if "*" in line:  # a device pointer
+            fields.append((line.split("*")[-1].strip(), "ptr", 1))
+            continue
         m = re.match(r"([\w\s]+?)\s+(\w+)(\[(\d+)\])?$", line)
         ty, field, _, n = m.groups()
         ty = ty.strip()
@@ -92,7 +95,9 @@ def _rust_struct_fields(name):
         field, ty = m.groups()
         ty = ty.strip()
         arr = re.match(r"\[(\w+);\s*(\d+)\]", ty)
-        if arr:
+        if ty.startswith("*"):
+            fields.append((field, "ptr", 1))
+        elif arr:
             fields.append((field, RUST_SCALARS[arr.group(1)], int(arr.group(2))))
         elif ty.startswith("bjf_") and ty != "bjf_dtype":
             fields.append((field, "struct", 1))
@@ -103,7 +108,7 @@ def _rust_struct_fields(name):
 
 def test_ffi_structs_match_the_header():
     for name in ("bjf_patchify_config", "bjf_patch_diff_config", "bjf_rgba_frame_stats", "bjf_viewer_mask_policy",
-                 "bjf_front_end_desc"):
+                 "bjf_patch_diff_refresh_config", "bjf_patch_diff_refresh_state", "bjf_front_end_desc"):
         assert _rust_struct_fields(name) == _c_struct_fields(name), name
 
 
