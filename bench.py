@@ -80,11 +80,12 @@ def parse_args():
                     help="back-to-back steps before the timed ones, for the clock sampler (0 under a profiler)")
     ap.add_argument("--no-rows", action="store_true",
                     help="skip the standalone timings of each row of the path (one GPU only)")
-    ap.add_argument("--rows", default="select,plan,cache,rgba,front_end,vitg",
-                    help="row groups to time: select, plan, cache, rgba, front_end (C2, C3), vitg")
+    ap.add_argument("--rows", default="select,plan,cache,rgba,front_end,vitg,f32",
+                    help="row groups to time: select, plan, cache, rgba, front_end (C2, C3), vitg, f32 (the "
+                         "gather-GEMM on f32 operands, the reference's dtype)")
     ap.add_argument("--rows-only", action="store_true",
-                    help="time only the row groups of --rows (front_end and/or vitg) and print them, e.g. to "
-                         "profile one row alone")
+                    help="time only the row groups of --rows (front_end, vitg and/or f32) and print them, e.g. "
+                         "to profile one row alone")
     ap.add_argument("--vitg-clips", type=int, default=32, help="clips of the ViT-g batch row (32 = the benchmark)")
     return ap.parse_args()
 
@@ -338,6 +339,8 @@ def time_rows(torch, bj, dev, videos, weight, bias, mask_cfg, hbm_peak, tflops_p
         time_front_end_rows(torch, bj, dev, timed, hbm, tensor)
     if "vitg" in groups:
         time_vitg_rows(torch, bj, dev, timed, tensor, vitg_clips)
+    if "f32" in groups:
+        time_f32_rows(torch, bj, dev, timed, tensor)
     del flush
     torch.cuda.empty_cache()
     return out
@@ -468,6 +471,38 @@ def time_front_end_rows(torch, bj, dev, timed, hbm, tensor):
     front_end_row("c3_live_8_streams_step", "a1-a6", 8, C, T, H, W, D, 0.10, 721)
 
 
+def time_f32_rows(torch, bj, dev, timed, tensor):
+    from burn_jepa_b200 import workloads
+
+    # a5 on f32 operands (the reference's CUDA dtype): the tensor cores through the bf16 split,
+    # which executes three bf16 products per useful one (K' = 3K); the row reports the useful
+    # FLOPs 2 M K D and the executed ones beside them
+    def f32_row(name, S_, T_, H_, W_, density, seed):
+        vids = workloads.rect_perturbation_clips_torch(seed, S_, C, T_, H_, W_, density, dev, torch.float32)
+        grid_ = (T_ // KT, H_ // P, W_ // P)
+        n_ = grid_[0] * grid_[1] * grid_[2]
+        sc_ = bj.patch_diff_token_scores(vids.unsqueeze(1), KT, P).cpu().numpy().ravel()
+        cfg_ = bj.PatchDiffConfig.adaptive_threshold(workloads.choose_threshold(sc_, density, 1e-3), 1, n_, 1)
+        _, idx_, cnt_ = bj.patch_diff_context_mask(vids.unsqueeze(1), KT, P, grid_, cfg_)
+        co_, tot_ = bj.sparse_patchify_plan_coords(idx_, grid_, batch=S_, counts=cnt_, capacity=S_ * n_)
+        rows_ = int(tot_.item())
+        co_ = co_[:rows_].contiguous()
+        w_ = torch.from_numpy(workloads.normal(seed + 1, (D, C, KT, P, P), std=0.02)).to(dev)
+        b_ = torch.from_numpy(workloads.normal(seed + 2, (D,), std=0.02)).to(dev)
+        pc_ = bj.PatchifyConfig(C, D, T_, H_, W_, KT, P, P)
+        fo_ = torch.empty((rows_, D), device=dev, dtype=torch.float32)
+        ms_ = timed(lambda i: bj.sparse_patchify3d_forward(pc_, vids, co_, w_, b_, out=fo_))
+        k_ = C * KT * P * P
+        wl_ = (f"{S_} x [{C},{T_},{H_},{W_}] f32, grid {grid_[0]}x{grid_[1]}x{grid_[2]}, ViT-L/16 D={D}, {rows_} "
+               f"active rows ({100.0 * rows_ / (S_ * n_):.1f}%), f32 weight and output; bf16 hi/lo split of both "
+               f"operands (split kernels included), three bf16 products per term")
+        tensor(name, "a5", wl_, ms_, 2 * rows_ * k_ * D, rows=rows_, executed_flops=6 * rows_ * k_ * D)
+        del vids, fo_
+
+    f32_row("gather_gemm_f32_c2_vitl_clip", 1, 16, 256, 256, 0.25, 731)
+    f32_row("gather_gemm_f32_c3_live_8_streams", 8, T, H, W, 0.10, 741)
+
+
 def time_vitg_rows(torch, bj, dev, timed, tensor, clips):
     import numpy as np
 
@@ -517,8 +552,8 @@ def run_ours(args, world, rank, local):
     group = sharding.RankGroup(device=dev)
     if args.rows_only:  # one or more rows alone, e.g. for a profiler (groups front_end and vitg)
         groups = tuple(args.rows.split(","))
-        if not set(groups) <= {"front_end", "vitg"}:
-            raise SystemExit("--rows-only times the front_end and vitg row groups")
+        if not set(groups) <= {"front_end", "vitg", "f32"}:
+            raise SystemExit("--rows-only times the front_end, vitg and f32 row groups")
         hbm_peak, tflops_peak, _ = read_peaks()
         rows = time_rows(torch, bj, dev, None, None, None, None, hbm_peak, tflops_peak, groups=groups,
                          vitg_clips=args.vitg_clips)

@@ -190,6 +190,7 @@ extern "C" bjf_status bjf_front_end_step_no_alloc(const bjf_front_end_desc* d, c
   ep.age = age_frames;
   ep.bias = bias;
   const RowSource rows{nullptr, indices, counts, (int)N, (int)S};  // the GEMM scans the counts
+  // f32 operands stay on the SIMT kernel here: their tensor-core split needs scratch memory
   return launch_gather_gemm(dev, video, d->video_dtype, weight, d->weight_dtype, g, rows, nullptr, S * N, ep, st,
-                            true);
+                            true, /*may_allocate=*/false);
 }

@@ -1260,13 +1260,140 @@ bool sm100_path_supported(const DeviceInfo& dev, const GatherGeometry& g, int32_
   return true;
 }
 
+// ---- f32 operands on the tensor cores: an error-compensated bf16 split ----------------------
+//
+// x = hi + lo with hi = bf16(x) and lo = bf16(x - hi) (x - hi is exact in f32), so hi + lo
+// carries 16 significant bits and |x - hi - lo| <= 2^-17 |x|.  Per product
+// a w = a_hi w_hi + a_hi w_lo + a_lo w_hi + O(2^-16 |a w|): three bf16 products, each exact in
+// the f32 accumulator.  The three run as one bf16 GEMM over K' = 3K by tripling the channel
+// axis: the gathered rows as [a_hi | a_hi | a_lo] and the weight as [w_hi | w_lo | w_hi], channel
+// groups in K order (the channel is K's slowest axis).  split_rows_kernel writes the split rows
+// into a bf16 copy of the input with 3C channels at the same (b, t, r, col) positions, so the
+// GEMM reads it with the caller's own rows and epilogue (plain, encoder input or cache scatter).
+// Only the selected tubelets of that copy are written, and only they are read.
+
+__device__ __forceinline__ uint32_t bf162_bits(__nv_bfloat162 v) {
+  return (uint32_t)__bfloat16_as_ushort(v.x) | ((uint32_t)__bfloat16_as_ushort(v.y) << 16);
+}
+__device__ __forceinline__ void split_bf16x2(float a, float b, uint32_t& hi, uint32_t& lo) {
+  const __nv_bfloat162 h = __floats2bfloat162_rn(a, b);  // .x = a's, the low half
+  const float2 hf = __bfloat1622float2(h);
+  hi = bf162_bits(h);
+  lo = bf162_bits(__floats2bfloat162_rn(a - hf.x, b - hf.y));
+}
+__device__ __forceinline__ void split_bf16x4(float4 x, uint2& hi, uint2& lo) {
+  split_bf16x2(x.x, x.y, hi.x, lo.x);
+  split_bf16x2(x.z, x.w, hi.y, lo.y);
+}
+
+// weight [D, K] f32 -> [D, 3K] bf16 as [hi | lo | hi] per row; K % 4 == 0.
+__global__ void __launch_bounds__(256) split_weight_kernel(const float* __restrict__ w, int D, int K,
+                                                           __nv_bfloat16* __restrict__ w3) {
+  const int64_t n4 = (int64_t)D * (K / 4);
+  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t d = i / (K / 4), k = (i - d * (K / 4)) * 4;
+    uint2 hi, lo;
+    split_bf16x4(__ldg(reinterpret_cast<const float4*>(w + d * K + k)), hi, lo);
+    uint2* row = reinterpret_cast<uint2*>(w3 + d * 3 * K + k);
+    row[0] = hi;
+    row[K / 4] = lo;
+    row[K / 2] = hi;
+  }
+}
+
+// The rows of `rs` (as the GEMM resolves them) from the f32 input into a bf16 input of 3C
+// channels, one warp per row, four consecutive k (inside one pw run, pw % 4 == 0) per lane.
+// Rows outside the grid are skipped, as the GEMM reads them as zeros.
+__global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ video, const RowSource rs,
+                                                         const int32_t* __restrict__ rows_dev, int rows_cap,
+                                                         GatherGeometry g, __nv_bfloat16* __restrict__ pv) {
+  __shared__ int soff[kMaxRowStreams + 1];
+  pdl_wait();  // the rows come from the kernels before
+  int M = rows_cap;
+  if (rows_dev) M = min(M, max(0, __ldg(rows_dev)));
+  M = min(M, load_row_offsets(rs, soff));
+  const int lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
+  const int64_t plane = (int64_t)g.Ts * g.H * g.W;  // one channel of one batch element
+  for (int m = blockIdx.x * wpb + (threadIdx.x >> 5); m < M; m += gridDim.x * wpb) {
+    bool valid = false;
+    const int4 c = fetch_row(rs, soff, g, m);
+    const int64_t base = row_base_offset(g, c, valid);
+    if (!valid) continue;
+    const int64_t pbase = base + (int64_t)c.x * 2 * g.C * plane;  // batch stride 3C planes
+    for (int k = lane * 4; k < g.K; k += 128) {
+      const int64_t ko = k_offset(g, k);
+      uint2 hi, lo;
+      split_bf16x4(__ldg(reinterpret_cast<const float4*>(video + base + ko)), hi, lo);
+      *reinterpret_cast<uint2*>(pv + pbase + ko) = hi;
+      *reinterpret_cast<uint2*>(pv + pbase + ko + g.C * plane) = hi;
+      *reinterpret_cast<uint2*>(pv + pbase + ko + 2 * g.C * plane) = lo;
+    }
+  }
+}
+
+// Whether f32 operands take the split: the bf16 path must take the tripled geometry, and the
+// vector accesses need 16-byte aligned inputs with pw and W multiples of 8.
+bool split_f32_supported(const DeviceInfo& dev, const GatherGeometry& g, const void* input, const void* weight) {
+  if (dev.cc_major != 10 || g.pw % 8 != 0 || g.W % 8 != 0) return false;
+  if (reinterpret_cast<uintptr_t>(input) % 16 != 0 || reinterpret_cast<uintptr_t>(weight) % 16 != 0) return false;
+  const int64_t K3 = 3 * (int64_t)g.K;
+  if (K3 % kBK != 0 || K3 / kBK > kMaxKBlocks) return false;
+  const int64_t Ts = g.ring ? g.Ts : g.T;
+  if (3 * (int64_t)g.C * Ts * g.H * g.W >= (int64_t(1) << 31)) return false;
+  return dev.max_smem_optin >= (size_t)SmemLayout::alloc &&
+         dev.max_smem_optin >= PairSmemLayout<true>::bytes(kMaxKBlocks, kMaxRowStreams);
+}
+
+bjf_status launch_split_f32(const DeviceInfo& dev, const float* input, const float* weight, const GatherGeometry& g0,
+                            const RowSource& rows, const int32_t* rows_dev, int64_t rows_cap,
+                            const EpilogueArgs& ep, cudaStream_t st, bool pdl) {
+  GatherGeometry g = g0;
+  if (!g.ring) g.Ts = g.T;
+  const int64_t plane = (int64_t)g.Ts * g.H * g.W;
+  const size_t pv_bytes = (size_t)g.batch * 3 * g.C * plane * sizeof(__nv_bfloat16);
+  const size_t w_bytes = (size_t)g.D * 3 * g.K * sizeof(__nv_bfloat16);
+  void* pv = nullptr;
+  void* w3 = nullptr;
+  bjf_status rc = stream_alloc(dev.device, pv_bytes, st, &pv);
+  if (rc) return rc;
+  rc = stream_alloc(dev.device, w_bytes, st, &w3);
+  if (rc) {
+    stream_free(pv, st);
+    return rc;
+  }
+  const int sms = dev.sm_count > 0 ? dev.sm_count : 148;
+  const int64_t w4 = (int64_t)g.D * (g.K / 4);
+  split_weight_kernel<<<(unsigned)std::min<int64_t>(ceil_div(w4, 256), 4 * sms), 256, 0, st>>>(
+      weight, g.D, g.K, static_cast<__nv_bfloat16*>(w3));
+  rc = check_launch("f32 weight split launch");
+  if (!rc) {
+    const unsigned grid = (unsigned)std::min<int64_t>(ceil_div(rows_cap, 8), 8 * sms);
+    cudaError_t e = launch_kernel(pdl, split_rows_kernel, dim3(grid), dim3(256), 0, st, input, rows, rows_dev,
+                                  (int)rows_cap, g, static_cast<__nv_bfloat16*>(pv));
+    rc = e == cudaSuccess ? BJF_OK : cuda_status(e, "f32 row split launch");
+  }
+  if (!rc) {
+    GatherGeometry g3 = g;
+    g3.C = 3 * g.C;
+    g3.K = 3 * g.K;
+    rc = launch_gather_gemm(dev, pv, BJF_DTYPE_BF16, w3, BJF_DTYPE_BF16, g3, rows, rows_dev, rows_cap, ep, st,
+                            /*pdl=*/true, /*may_allocate=*/false);
+  }
+  // stream-ordered: the memory returns to the pool once the GEMM has finished with it
+  const bjf_status f1 = stream_free(w3, st), f2 = stream_free(pv, st);
+  return rc ? rc : (f1 ? f1 : f2);
+}
+
 bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t in_dt,
                               const void* weight, int32_t w_dt, const GatherGeometry& g0,
                               const RowSource& rows, const int32_t* rows_dev, int64_t rows_cap,
-                              const EpilogueArgs& ep, cudaStream_t st, bool pdl) {
+                              const EpilogueArgs& ep, cudaStream_t st, bool pdl, bool may_allocate) {
   if (!rows.coords && (rows.streams <= 0 || rows.streams > kMaxRowStreams || !rows.indices || !rows.counts))
     return fail(BJF_ERR_INVALID_ARGUMENT, "gather-GEMM index rows need 1..4096 streams, indices and counts");
   if (rows_cap <= 0 || g0.D <= 0) return BJF_OK;
+  if (in_dt == BJF_DTYPE_F32 && w_dt == BJF_DTYPE_F32 && may_allocate && split_f32_supported(dev, g0, input, weight))
+    return launch_split_f32(dev, static_cast<const float*>(input), static_cast<const float*>(weight), g0, rows,
+                            rows_dev, rows_cap, ep, st, pdl);
   GatherGeometry g = g0;
   g.num_kb = g.K / kBK;
   g.is_bf16 = in_dt == BJF_DTYPE_BF16;

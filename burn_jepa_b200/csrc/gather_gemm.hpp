@@ -69,7 +69,8 @@ inline RowSource coords_rows(const int4* coords) { return RowSource{coords, null
 bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t in_dt,
                               const void* weight, int32_t w_dt, const GatherGeometry& g,
                               const RowSource& rows, const int32_t* rows_dev, int64_t rows_cap,
-                              const EpilogueArgs& ep, cudaStream_t st, bool pdl = false);
+                              const EpilogueArgs& ep, cudaStream_t st, bool pdl = false,
+                              bool may_allocate = true);
 
 bool sm100_path_supported(const DeviceInfo& dev, const GatherGeometry& g, int32_t in_dt,
                           int32_t w_dt, const void* input, const void* weight);

@@ -15,7 +15,39 @@ DeviceInfo g_devices[kMaxDevices];
 EncodeTiledFn g_encode = nullptr;
 std::atomic<uint64_t> g_wait_limit_ns{kDefaultWaitLimitNs};
 std::atomic<int32_t> g_wait_stall{0};
+cudaMemPool_t g_pools[kMaxDevices] = {};
 }  // namespace
+
+bjf_status stream_alloc(int dev, size_t bytes, cudaStream_t st, void** out) {
+  if (dev < 0 || dev >= kMaxDevices) return fail(BJF_ERR_UNSUPPORTED, "device ordinal out of range");
+  cudaMemPool_t pool;
+  {
+    std::lock_guard<std::mutex> lock(g_mu);
+    if (!g_pools[dev]) {
+      cudaMemPoolProps props = {};
+      props.allocType = cudaMemAllocationTypePinned;
+      props.location.type = cudaMemLocationTypeDevice;
+      props.location.id = dev;
+      cudaError_t e = cudaMemPoolCreate(&g_pools[dev], &props);
+      if (e != cudaSuccess) {
+        g_pools[dev] = nullptr;
+        return cuda_status(e, "cudaMemPoolCreate");
+      }
+      uint64_t keep = UINT64_MAX;
+      e = cudaMemPoolSetAttribute(g_pools[dev], cudaMemPoolAttrReleaseThreshold, &keep);
+      if (e != cudaSuccess) return cuda_status(e, "cudaMemPoolSetAttribute");
+    }
+    pool = g_pools[dev];
+  }
+  const cudaError_t e = cudaMallocFromPoolAsync(out, bytes, pool, st);
+  return e == cudaSuccess ? BJF_OK : cuda_status(e, "cudaMallocFromPoolAsync");
+}
+
+bjf_status stream_free(void* p, cudaStream_t st) {
+  if (!p) return BJF_OK;
+  const cudaError_t e = cudaFreeAsync(p, st);
+  return e == cudaSuccess ? BJF_OK : cuda_status(e, "cudaFreeAsync");
+}
 
 const DeviceInfo* peek_device(int dev) {
   if (dev < 0 || dev >= kMaxDevices) return nullptr;

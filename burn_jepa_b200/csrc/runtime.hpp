@@ -36,6 +36,12 @@ struct BoundedWait {
 };
 BoundedWait bounded_wait();
 
+// Stream-ordered device memory from the library's own pool on device `dev` (a pool per
+// device, created on first use, that keeps freed memory for the next call instead of
+// returning it to the driver).  Capturable in a CUDA graph.
+bjf_status stream_alloc(int dev, size_t bytes, cudaStream_t st, void** out);
+bjf_status stream_free(void* p, cudaStream_t st);
+
 // cuTensorMapEncodeTiled from the driver (resolved once through the runtime).
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
                                    const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,

@@ -180,8 +180,13 @@ BJF_API bjf_status bjf_sparse_patchify_plan_coords(const int32_t* indices, int64
  * input: [B, C, T, H, W] (dims in input_dims); weight: [D, C, kt, ph, pw];
  * bias: [D] f32 or NULL (zeros, as the reference substitutes at src/model.rs:1307-1318);
  * out: [rows, D].  f16/bf16 input and weight (same dtype) run on the tcgen05 tensor
- * cores with f32 accumulation; f32 runs in f32.  Rows whose coords lie outside
- * the input are written as zeros. */
+ * cores with f32 accumulation.  f32 input and weight run there too, each operand split into
+ * bf16 high and low parts and three bf16 products per term (a_hi w_hi + a_hi w_lo + a_lo w_hi,
+ * dropped terms below 3 * 2^-16 |a w|), when pw and W are multiples of 8, K <= 2730 and both
+ * buffers are 16-byte aligned; else on a SIMT f32 kernel.  The split's bf16 copies (1.5x the
+ * input's f32 bytes and 1.5x the weight's) come from the library's stream-ordered memory pool
+ * and return to it when the call's kernels finish.  Rows whose coords lie outside the input
+ * are written as zeros. */
 BJF_API bjf_status bjf_sparse_patchify3d_forward(const bjf_patchify_config* config, const void* input,
                                          bjf_dtype input_dtype, const int64_t input_dims[5],
                                          const int32_t* coords, int64_t rows, const void* weight,
@@ -409,7 +414,7 @@ typedef struct bjf_front_end_desc {
   int64_t tubelet_size;
   int64_t patch_size;
   int64_t embed_dim;
-  bjf_dtype video_dtype;  /* f16 / bf16 run the tcgen05 path; f32 runs SIMT */
+  bjf_dtype video_dtype;  /* f16 / bf16 / f32 (f32 as bjf_sparse_patchify3d_forward runs it) */
   bjf_dtype weight_dtype; /* same as video_dtype for the tensor-core path */
   bjf_dtype cache_dtype;  /* f32 / f16 / bf16 */
   bjf_patch_diff_config mask;
@@ -463,7 +468,7 @@ BJF_API bjf_status bjf_front_end_step_ring(const bjf_front_end_desc* desc, const
  * begins.  The address is kept for the life of the process: resetting the device
  * (cudaDeviceReset) while the library is loaded is not supported.  A bounded-wait timeout
  * is reported by bjf_device_error_check, as for the workspace step.  A call allocates
- * nothing. */
+ * nothing, so f32 operands run on the SIMT kernel here. */
 BJF_API bjf_status bjf_front_end_step_no_alloc(const bjf_front_end_desc* desc, const void* video,
                                                const void* weight, const float* bias, void* caches,
                                                float* observed, float* age_frames,
