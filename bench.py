@@ -699,17 +699,22 @@ def run_ours(args, world, rank, local):
     ring = torch.empty((S, C, ring_slots, H, W), dtype=torch.float16, device=dev)
     e2e_steps = max(1, args.e2e_steps)
     counts_host = torch.zeros((max(e2e_steps, 3) + 1, S), dtype=torch.int32).pin_memory()  # row i: step i
-    copy_stream = torch.cuda.Stream(device=dev)
+    # two copy streams, each uploading half of the streams' planes with bjf_frame_ring_upload
+    # (one 2-D copy each), so two copy engines share the host link
+    copy_streams = [torch.cuda.Stream(device=dev) for _ in range(2)]
+    halves = [(0, S // 2), (S // 2, S)] if S > 1 else [(0, S)]
     frame_bytes = H * W * 2
 
-    def upload(i, after=None):  # frame i into slot i % 3 on the copy stream
-        with torch.cuda.stream(copy_stream):
+    def upload(i, after=None):  # frame i into slot i % 3 on the copy streams
+        evs = []
+        for cs, half in zip(copy_streams, halves):
             if after is not None:
-                copy_stream.wait_event(after)
-            ring[:, :, i % ring_slots].copy_(host_frames[i % 4], non_blocking=True)
+                cs.wait_event(after)
+            fe.upload_frame(host_frames[i % 4], ring, i % ring_slots, streams=half, stream=cs)
             ev = torch.cuda.Event()
-            ev.record(copy_stream)
-        return ev
+            ev.record(cs)
+            evs.append(ev)
+        return evs
 
     def e2e_run(n_steps, start_event=None):
         copied, done = {}, {}
@@ -718,7 +723,8 @@ def run_ours(args, world, rank, local):
         for i in range(1, n_steps + 1):
             # slot i % 3 last held frame i - 3, read by steps i - 3 and i - 2
             copied[i] = upload(i, done.get(i - 2, start_event))
-            stream.wait_event(copied[i])
+            for ev in copied[i]:
+                stream.wait_event(ev)
             fe.step_ring(ring, (i - 1) % ring_slots, i % ring_slots, weight, bias, caches, observed, age)
             counts_host[i].copy_(fe.counts, non_blocking=True)
             done[i] = torch.cuda.Event()
@@ -801,9 +807,10 @@ def run_ours(args, world, rank, local):
         "cpu_baseline": cpu,
         "e2e": {"value": round(e2e_value, 1), "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": S * 4,
                 "steps": e2e_steps, "active_fraction": round(e2e_density, 4),
-                "how": "bjf_front_end_step_ring on a 3-slot frame ring per stream: each step copies its one new "
-                       "[3,1024,1024] f16 frame per stream from pinned host memory (on a copy stream, overlapping "
-                       "the step before) and reads the per-stream active counts back; timed with CUDA events"},
+                "how": "bjf_front_end_step_ring on a 3-slot frame ring per stream: each step uploads its one new "
+                       "[3,1024,1024] f16 frame per stream from pinned host memory with bjf_frame_ring_upload (two "
+                       "2-D copies on two copy streams, overlapping the step before) and reads the per-stream "
+                       "active counts back; timed with CUDA events"},
         "gpu_launches": KERNELS_PER_STEP * args.steps,
         "clocks": clocks.summary(),
     }

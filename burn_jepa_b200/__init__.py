@@ -522,3 +522,12 @@ class FrontEnd:
             _ptr(self.workspace), self.workspace.numel(), _ptr(self.counts), _stream(stream)))
         self.steps += 1
         return self.counts
+
+    def upload_frame(self, host_frame, ring, slot: int, streams=None, stream=None):
+        """``bjf_frame_ring_upload``: host_frame [S, C, H, W] (pinned, contiguous) into slot `slot`
+        of ring [S, C, R, H, W]; `streams` = (begin, end) uploads part of the streams."""
+        if not host_frame.is_contiguous() or host_frame.device.type != "cpu":
+            raise ValueError("host_frame must be a contiguous host tensor")
+        b, e = (0, int(self.desc.streams)) if streams is None else streams
+        check(load().bjf_frame_ring_upload(ctypes.byref(self.desc), ctypes.c_void_p(host_frame.data_ptr()), _ptr(ring),
+                                           int(ring.shape[2]), int(slot), int(b), int(e), _stream(stream)))

@@ -207,6 +207,7 @@ SIGNATURES = {
     "bjf_front_end_step_no_alloc": (_I32, [ctypes.POINTER(FrontEndDesc), _P, _P, _P, _P, _P, _P, _I32, _P, _P]),
     "bjf_front_end_step_ring": (_I32, [ctypes.POINTER(FrontEndDesc), _P, _I32, _I32, _I32, _P, _P, _P, _P, _P, _I32,
                                        _P, ctypes.c_size_t, _P, _P]),
+    "bjf_frame_ring_upload": (_I32, [ctypes.POINTER(FrontEndDesc), _P, _P, _I32, _I32, _I64, _I64, _P]),
     "bjf_rgba_patch_diff_workspace_bytes": (ctypes.c_size_t, [_I64, _DIMS]),
     "bjf_viewer_rgba_masks_workspace_bytes": (ctypes.c_size_t, [_I64, _DIMS]),
     "bjf_viewer_patch_diff_masks_from_rgba": (_I32, [_P, _P, _I64, _I64, _I64, _I64, _DIMS,

@@ -183,3 +183,29 @@ extern "C" bjf_status bjf_front_end_step_ring(const bjf_front_end_desc* d, const
   return front_end_step(d, frame_ring, &ring, weight, bias, caches, observed, age_frames, age_observed, workspace,
                         workspace_bytes, counts_out, stream);
 }
+
+extern "C" bjf_status bjf_frame_ring_upload(const bjf_front_end_desc* d, const void* host_frame, void* frame_ring,
+                                            int32_t ring_slots, int32_t slot, int64_t stream_begin,
+                                            int64_t stream_end, bjf_stream_t stream) {
+  if (!d) return fail(BJF_ERR_INVALID_ARGUMENT, "front-end descriptor must not be null");
+  if (ring_slots < 2 || ring_slots > 64)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "frame ring must hold 2 to 64 frames per stream");
+  if (slot < 0 || slot >= ring_slots) return fail(BJF_ERR_INVALID_ARGUMENT, "frame ring slot outside the ring");
+  if (stream_begin < 0 || stream_end > d->streams || stream_begin > stream_end)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "frame ring upload streams outside the descriptor's");
+  const size_t esz = dtype_size(d->video_dtype);
+  if (esz == 0 || d->video_dtype == BJF_DTYPE_I32) return fail(BJF_ERR_INVALID_ARGUMENT, "video dtype must be f32, f16 or bf16");
+  if (d->channels <= 0 || d->height <= 0 || d->width <= 0)
+    return fail(BJF_ERR_INVALID_ARGUMENT, "front-end descriptor dims must be positive");
+  if (!host_frame || !frame_ring) return fail(BJF_ERR_INVALID_ARGUMENT, "buffers must not be null");
+  if (stream_begin == stream_end) return BJF_OK;
+  // one [H, W] plane per (stream, channel): a 2-D copy of S C rows, one plane each, from a
+  // dense source to the ring's slot (row pitch ring_slots planes)
+  const size_t plane = (size_t)d->height * (size_t)d->width * esz;
+  const size_t rows = (size_t)(stream_end - stream_begin) * (size_t)d->channels;
+  const char* src = static_cast<const char*>(host_frame) + (size_t)stream_begin * d->channels * plane;
+  char* dst = static_cast<char*>(frame_ring) + ((size_t)stream_begin * d->channels * ring_slots + slot) * plane;
+  const cudaError_t e = cudaMemcpy2DAsync(dst, plane * ring_slots, src, plane, plane, rows, cudaMemcpyHostToDevice,
+                                          as_cuda(stream));
+  return e == cudaSuccess ? BJF_OK : cuda_status(e, "frame ring upload");
+}

@@ -38,7 +38,8 @@ extern "C" {
 
 /* 2: bjf_rgba_patch_diff_workspace_bytes takes the token grid.
  * 3: bjf_set_bounded_wait, bjf_front_end_step_ring.
- * 4: the patch-diff refresh state on the device (bjf_viewer_patch_diff_refresh_*). */
+ * 4: the patch-diff refresh state on the device (bjf_viewer_patch_diff_refresh_*),
+ *    bjf_frame_ring_upload. */
 #define BJF_ABI_VERSION 4
 
 #if defined(__GNUC__)
@@ -454,6 +455,16 @@ BJF_API bjf_status bjf_front_end_step_ring(const bjf_front_end_desc* desc, const
                                            float* observed, float* age_frames, int32_t age_observed,
                                            void* workspace, size_t workspace_bytes, int32_t* counts_out,
                                            bjf_stream_t stream);
+
+/* The upload half of a live stream's step (src/highres_pipeline.rs:1999-2052 receives one new
+ * image per step): copies streams [stream_begin, stream_end) of one new frame, host_frame
+ * [S, C, H, W] (pinned host memory for an asynchronous copy), into slot `slot` of the frame
+ * ring [S, C, ring_slots, H, W] that bjf_front_end_step_ring reads, as one 2-D copy (one
+ * H x W plane per stream and channel).  Dims and dtype are desc's.  The copy is ordered on
+ * `stream`; issue it on a copy stream to overlap the step that reads the other slots. */
+BJF_API bjf_status bjf_frame_ring_upload(const bjf_front_end_desc* desc, const void* host_frame, void* frame_ring,
+                                         int32_t ring_slots, int32_t slot, int64_t stream_begin, int64_t stream_end,
+                                         bjf_stream_t stream);
 
 /* No counterpart in the reference: bjf_front_end_step for callers that cannot
  * allocate device memory (a host whose device memory belongs to its framework's caching

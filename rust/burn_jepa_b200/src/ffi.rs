@@ -356,6 +356,17 @@ unsafe extern "C" {
         stream: bjf_stream_t,
     ) -> bjf_status;
 
+    pub fn bjf_frame_ring_upload(
+        desc: *const bjf_front_end_desc,
+        host_frame: *const c_void,
+        frame_ring: *mut c_void,
+        ring_slots: i32,
+        slot: i32,
+        stream_begin: i64,
+        stream_end: i64,
+        stream: bjf_stream_t,
+    ) -> bjf_status;
+
     pub fn bjf_front_end_workspace_bytes(desc: *const bjf_front_end_desc) -> usize;
     pub fn bjf_front_end_step(
         desc: *const bjf_front_end_desc,

@@ -150,3 +150,16 @@ def test_ctypes_structs_have_the_c_layout(tmp_path):
     subprocess.run(["gcc", "-std=c11", "-I", inc, str(src), "-o", str(exe)], check=True)
     got = [int(v) for v in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
     assert got == want
+
+
+def test_frame_ring_upload_rejects_bad_arguments():
+    mask = bj.PatchDiffConfig.adaptive_threshold(0.1, 1, 16, 1)
+    d = bj.FrontEndDesc(4, 3, 2, 64, 64, 2, 16, 64, _abi.DTYPE_F16, _abi.DTYPE_F16, _abi.DTYPE_F16, mask)
+    up = bj.load().bjf_frame_ring_upload
+    assert up(ctypes.byref(d), FAKE, FAKE, 3, 3, 0, 4, None) == _abi.BJF_ERR_INVALID_ARGUMENT
+    assert "slot outside the ring" in bj.last_error()
+    assert up(ctypes.byref(d), FAKE, FAKE, 1, 0, 0, 4, None) == _abi.BJF_ERR_INVALID_ARGUMENT
+    assert up(ctypes.byref(d), FAKE, FAKE, 3, 0, 2, 5, None) == _abi.BJF_ERR_INVALID_ARGUMENT
+    assert "streams outside" in bj.last_error()
+    assert up(ctypes.byref(d), None, FAKE, 3, 0, 0, 4, None) == _abi.BJF_ERR_INVALID_ARGUMENT
+    assert up(ctypes.byref(d), FAKE, FAKE, 3, 0, 2, 2, None) == 0  # nothing to copy

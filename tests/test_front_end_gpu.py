@@ -223,3 +223,28 @@ def test_ring_step_equals_the_contiguous_step(cuda_device, ring_slots, D, video_
         assert int(c_ring.sum()) > 0
         for a, b in zip(state["ring"], state["clip"]):
             assert torch.equal(a, b), f"frame {f}"
+
+
+@pytest.mark.gpu
+def test_frame_ring_upload_writes_only_its_slot_and_streams(cuda_device):
+    """bjf_frame_ring_upload copies streams [b, e) of a host frame into one ring slot; every
+    other slot and stream of the ring is left as it was."""
+    import torch
+
+    import burn_jepa_b200 as bj
+
+    S, C, H, W, R = 5, 3, 64, 48, 3
+    mask = bj.PatchDiffConfig.adaptive_threshold(0.1, 1, (H // 16) * (W // 16), 1)
+    fe = bj.FrontEnd(S, C, 2, H, W, 2, 16, 64, mask, torch.float16, torch.float16, cuda_device)
+    ring = torch.randn((S, C, R, H, W), device=cuda_device).to(torch.float16)
+    before = ring.clone()
+    frame = torch.randn((S, C, H, W)).to(torch.float16).pin_memory()
+    fe.upload_frame(frame, ring, 1, streams=(1, 4))
+    torch.cuda.synchronize()
+    want = before.clone()
+    want[1:4, :, 1] = frame[1:4].to(cuda_device)
+    assert torch.equal(ring, want)
+    fe.upload_frame(frame, ring, 2)
+    torch.cuda.synchronize()
+    want[:, :, 2] = frame.to(cuda_device)
+    assert torch.equal(ring, want)
