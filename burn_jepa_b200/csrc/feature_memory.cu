@@ -20,6 +20,7 @@
 #include <string>
 
 #include "common.cuh"
+#include "runtime.hpp"
 #include "status.hpp"
 
 namespace bjf {
@@ -72,12 +73,13 @@ __global__ void __launch_bounds__(kThreads)
                         float* __restrict__ age, const TokT* __restrict__ tokens,
                         const int32_t* __restrict__ token_indices, int sparse_len, int dense_tokens,
                         int embed_dim, long long rows, float alpha) {
-  long long row = (long long)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5);
-  if (row >= rows) return;
   const int lane = threadIdx.x & 31;
+  // a grid of resident blocks whose warps stride over the rows: no tail wave
+  for (long long row = (long long)blockIdx.x * (kThreads / 32) + (threadIdx.x >> 5); row < rows;
+       row += (long long)gridDim.x * (kThreads / 32)) {
   const long long b = row / sparse_len;
   const int32_t idx = token_indices[row];
-  if (idx < 0 || idx >= dense_tokens) return;
+  if (idx < 0 || idx >= dense_tokens) continue;
   const TokT* src = tokens + row * embed_dim;
   CacheT* dst = features + (b * dense_tokens + idx) * (long long)embed_dim;
   // the slot's observed value before this update (read by every lane before lane 0 sets it)
@@ -118,6 +120,14 @@ __global__ void __launch_bounds__(kThreads)
     observed[b * dense_tokens + idx] = 1.0f;
     age[b * dense_tokens + idx] = 0.0f;
   }
+  }
+}
+
+// Blocks of kThreads for `work_blocks` blocks of work: at most the resident 8 per SM.
+unsigned resident_blocks(long long work_blocks) {
+  const DeviceInfo* dev = nullptr;
+  const int sms = current_device(&dev) == BJF_OK && dev->sm_count > 0 ? dev->sm_count : 148;
+  return (unsigned)std::max<long long>(1, std::min<long long>(work_blocks, 8LL * sms));
 }
 
 // after_aging: the kernel before this one in the stream is this update's aging pass.
@@ -125,7 +135,7 @@ template <typename TokT, typename CacheT, bool EMA>
 cudaError_t launch_scatter(bool vec, bool after_aging, void* features, float* observed, float* age,
                            const void* tokens, const int32_t* idx, int S, int N, int D, long long rows, float alpha,
                            cudaStream_t st) {
-  const dim3 blocks((unsigned)ceil_div(rows, kThreads / 32));
+  const dim3 blocks(resident_blocks(ceil_div(rows, kThreads / 32)));
   if (vec)
     return launch_kernel(after_aging, scatter_rows_kernel<TokT, CacheT, true, EMA>, blocks, dim3(kThreads), 0, st,
                          static_cast<CacheT*>(features), observed, age, static_cast<const TokT*>(tokens), idx, S, N,
