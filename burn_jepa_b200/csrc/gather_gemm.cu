@@ -676,7 +676,7 @@ template <bool kEmbed>
 __device__ __forceinline__ void drain_accumulator_rows(const GatherGeometry& g, const EpilogueArgs& ep, int4 c,
                                                        int M, int gm, int n0, int c_begin, int c_end, uint32_t taddr,
                                                        int lane, uint8_t* stage, const float* bias_s,
-                                                       const float* mod_s) {
+                                                       const float* mod_s, char* out_base) {
   const int ce = ep.out_elem_bytes;
   bool valid = false;
   char* dst_row = nullptr;
@@ -686,11 +686,11 @@ __device__ __forceinline__ void drain_accumulator_rows(const GatherGeometry& g, 
     if (valid && ep.position_table)
       pos_row = ep.position_table + (((int64_t)c.y * g.gh + c.z) * g.gw + c.w) * ep.pos_ld;
     if (ep.mode == kEpiloguePlain) {
-      dst_row = static_cast<char*>(ep.out) + (int64_t)gm * ep.ldo * ce;
+      dst_row = out_base + (int64_t)gm * ep.ldo * ce;
     } else if (valid) {
       const int64_t idx = ((int64_t)c.y * g.gh + c.z) * g.gw + c.w;
       const int64_t slot = (int64_t)c.x * ep.dense_tokens + idx;
-      dst_row = static_cast<char*>(ep.out) + slot * ep.ldo * ce;
+      dst_row = out_base + slot * ep.ldo * ce;
       if (n0 == 0) {
         if (ep.observed) ep.observed[slot] = 1.0f;
         if (ep.age) ep.age[slot] = 0.0f;
@@ -699,7 +699,7 @@ __device__ __forceinline__ void drain_accumulator_rows(const GatherGeometry& g, 
   }
   // 16-byte stores need 16-byte aligned rows (output base and row pitch; column offsets of a
   // chunk are multiples of 32 bytes)
-  const bool vec = ((reinterpret_cast<uintptr_t>(ep.out) | (uintptr_t)(ep.ldo * ce)) & 15) == 0;
+  const bool vec = ((reinterpret_cast<uintptr_t>(out_base) | (uintptr_t)(ep.ldo * ce)) & 15) == 0;
   const int cpc = kEpiRowBytes / ce;  // columns per chunk
   char** rowptr = reinterpret_cast<char**>(stage + 32 * kEpiRowPitch);
   __syncwarp();  // the previous drain's write-back has read the row addresses
@@ -818,6 +818,13 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
   const int cluster = (int)(blockIdx.x >> 1);
   const int nclusters = (int)(gridDim.x >> 1);
   const int n_tiles = (g.D + bn - 1) / bn;
+  // a work unit is a 256 x bn tile, or with split K one of its ks K ranges of kbs blocks
+  const int ks = max(g.ksplit, 1), kbs = (num_kb + ks - 1) / ks;
+  auto unit_row = [&](int u) { return (u / ks) / n_tiles; };
+  auto unit_col = [&](int u) { return (u / ks) % n_tiles; };
+  auto unit_kb0 = [&](int u) { return (u % ks) * kbs; };
+  auto unit_kb1 = [&](int u) { return min(num_kb, (u % ks + 1) * kbs); };
+  auto unit_out = [&](int u) { return static_cast<char*>(ep.out) + (int64_t)(u % ks) * ep.split_stride; };
   const int half = bn >> 1;  // weight rows per CTA
   // On the CTA's last tile the producer warps, idle by then, drain accumulator columns
   // [split, bn) while the epilogue warps drain [0, split): a chunk-aligned half.  They wait for
@@ -825,7 +832,7 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
   // that buffer behind, which the ring guarantees from two K stages per tile on (with one, the
   // epilogue warps drain it all).
   const int epi_chunk_cols = kEpiRowBytes / ep.out_elem_bytes;
-  const int split = num_kb >= 2 ? (bn / 2) / epi_chunk_cols * epi_chunk_cols : 0;
+  const int split = num_kb - (ks - 1) * kbs >= 2 ? (bn / 2) / epi_chunk_cols * epi_chunk_cols : 0;
 
   uint64_t* full = reinterpret_cast<uint64_t*>(smem + L::bar_off);
   uint64_t* peer_full = full + kPairStages;
@@ -874,7 +881,7 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
   int M = rows_cap;
   if (rows_dev) M = min(M, max(0, __ldg(rows_dev)));
   M = min(M, load_row_offsets(rs, soff));
-  const int num_tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * n_tiles;  // 256-row pair tiles
+  const int num_tiles = ((M + 2 * kBM - 1) / (2 * kBM)) * n_tiles * ks;  // units of 256-row pair tiles
   if (cluster >= num_tiles) {  // the same for both CTAs of the pair
     tc_fence_before();
     cluster_sync();
@@ -910,7 +917,7 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
     const int row_in_pair = (int)rank * kBM + p;
     // A tile's row is loaded (index or coords) when the tile before starts and decoded when it
     // ends, so the load's latency never stalls the in-order issue of the copies.
-    int4 raw = fetch_row_raw(rs, soff, M, (cluster / n_tiles) * (2 * kBM) + row_in_pair);
+    int4 raw = fetch_row_raw(rs, soff, M, unit_row(cluster) * (2 * kBM) + row_in_pair);
     int4 c_this = decode_row(rs, g, raw);
     int64_t my_row = row_offset(g, c_this);
     for (int tile = cluster; tile < num_tiles && !aborted; tile += nclusters) {
@@ -924,13 +931,13 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
         break;
       }
       const int next = tile + nclusters;
-      if (next < num_tiles) raw = fetch_row_raw(rs, soff, M, (next / n_tiles) * (2 * kBM) + row_in_pair);
+      if (next < num_tiles) raw = fetch_row_raw(rs, soff, M, unit_row(next) * (2 * kBM) + row_in_pair);
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         const int m = 32 * pw_ + 4 * i + sub;
         dst_off[i] = (uint32_t)((m >> 3) * 1024 + (m & 7) * 128 + ((j ^ (m & 7)) << 4));
       }
-      for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
+      for (int kb = unit_kb0(tile); kb < unit_kb1(tile); ++kb, ++kbg) {
         const int s = kbg % kPairStages;
         const uint32_t par = ((kbg / kPairStages) & 1) ^ 1;
         const bool ok = mbar_wait_bounded(&empty[s], par, abort_flag, g.wait_ns);
@@ -965,10 +972,10 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
         tc_fence_after();
         const int tile = cluster + it_last * nclusters;
         uint8_t* pstage = smem + L::pepi_off + pw_ * kEpiWarpBytes;
-        drain_accumulator_rows<kEmbed>(g, ep, c_this, M, (tile / n_tiles) * (2 * kBM) + row_in_pair,
-                                       (tile % n_tiles) * bn, split, bn,
+        drain_accumulator_rows<kEmbed>(g, ep, c_this, M, unit_row(tile) * (2 * kBM) + row_in_pair,
+                                       unit_col(tile) * bn, split, bn,
                                        acc_tmem(it_last) + ((uint32_t)(pw_ * 32) << 16), lane, pstage,
-                                       col_bias(it_last), col_mod(it_last));
+                                       col_bias(it_last), col_mod(it_last), unit_out(tile));
         tc_fence_before();
       }
     }
@@ -988,7 +995,8 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
         }
         tc_fence_after();
         const uint32_t d_tmem = acc_tmem(it);
-        for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
+        const int kb0 = unit_kb0(tile);
+        for (int kb = kb0; kb < unit_kb1(tile); ++kb, ++kbg) {
           const int s = kbg % kPairStages;
           const uint32_t par = (kbg / kPairStages) & 1;
           if (!mbar_wait_bounded(&full[s], par, abort_flag, g.wait_ns) ||
@@ -1003,7 +1011,7 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
 #pragma unroll
           for (int kk = 0; kk < kBK / 16; ++kk) {
             mma_f16_ss_pair(d_tmem, smem_desc_sw128_kmajor(a_base + kk * 32),
-                            smem_desc_sw128_kmajor(b_base + kk * 32), idesc, (kb | kk) != 0);
+                            smem_desc_sw128_kmajor(b_base + kk * 32), idesc, kb != kb0 || kk != 0);
           }
           issued_any = true;
           mma_commit_pair(&empty[s], 0x3);
@@ -1023,7 +1031,8 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
       // ---------------- stage relay (odd CTA): lane s relays stage s ----------------
       const int s = lane;
       const uint32_t remote = cluster_map(smem_u32(&peer_full[s]), 0);
-      const int total_kb = my_tiles * num_kb;
+      int total_kb = 0;  // K blocks of this cluster's units
+      for (int u = cluster; u < num_tiles; u += nclusters) total_kb += unit_kb1(u) - unit_kb0(u);
       for (int kbg = s; kbg < total_kb; kbg += kPairStages) {
         if (!mbar_wait_bounded(&full[s], (kbg / kPairStages) & 1, abort_flag, g.wait_ns)) {
           aborted = true;
@@ -1038,8 +1047,8 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
     if (lane == 0) {
       int kbg = 0;
       for (int tile = cluster; tile < num_tiles && !aborted; tile += nclusters) {
-        const int n0 = (tile % n_tiles) * bn + (int)rank * half;
-        for (int kb = 0; kb < num_kb; ++kb, ++kbg) {
+        const int n0 = unit_col(tile) * bn + (int)rank * half;
+        for (int kb = unit_kb0(tile); kb < unit_kb1(tile); ++kb, ++kbg) {
           const int s = kbg % kPairStages;
           const uint32_t par = ((kbg / kPairStages) & 1) ^ 1;
           if (!mbar_wait_bounded(&empty[s], par, abort_flag, g.wait_ns)) {
@@ -1064,9 +1073,9 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
     uint8_t* stage = smem + L::epi_off + warp * kEpiWarpBytes;
     const uint32_t lanes = (uint32_t)(warp * 32) << 16;
     int it = 0;
-    int4 c = next_row(rs, soff, g, M, (cluster / n_tiles) * (2 * kBM) + (int)rank * kBM + m);
+    int4 c = next_row(rs, soff, g, M, unit_row(cluster) * (2 * kBM) + (int)rank * kBM + m);
     auto stage_columns = [&](int it_) {
-      const int n0_ = ((cluster + it_ * nclusters) % n_tiles) * bn;
+      const int n0_ = unit_col(cluster + it_ * nclusters) * bn;
       float* dst = col_bias(it_);
       for (int jj = tid; jj < bn; jj += kEpilogueWarps * 32) {
         const int col = n0_ + jj;
@@ -1085,11 +1094,11 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
         break;
       }
       tc_fence_after();
-      const int n0 = (tile % n_tiles) * bn;
-      const int gm = (tile / n_tiles) * (2 * kBM) + (int)rank * kBM + m;
+      const int n0 = unit_col(tile) * bn;
+      const int gm = unit_row(tile) * (2 * kBM) + (int)rank * kBM + m;
       const bool last = tile + nclusters >= num_tiles;
       drain_accumulator_rows<kEmbed>(g, ep, c, M, gm, n0, 0, last && split > 0 ? split : bn, acc_tmem(it) + lanes,
-                                     lane, stage, col_bias(it), col_mod(it));
+                                     lane, stage, col_bias(it), col_mod(it), unit_out(tile));
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
@@ -1100,7 +1109,7 @@ __global__ void __maxnreg__(kEmbed ? 128 : 80)
       }
       const int next = tile + nclusters;
       if (next < num_tiles) {
-        c = next_row(rs, soff, g, M, (next / n_tiles) * (2 * kBM) + (int)rank * kBM + m);
+        c = next_row(rs, soff, g, M, unit_row(next) * (2 * kBM) + (int)rank * kBM + m);
         stage_columns(it + 1);
       }
     }
@@ -1260,6 +1269,63 @@ bool sm100_path_supported(const DeviceInfo& dev, const GatherGeometry& g, int32_
   return true;
 }
 
+// ---- split K for small row counts ----------------------------------------------------------
+//
+// A plain GEMM with fewer 256 x bn tiles than half the CTA pairs leaves most SMs idle while each
+// tile walks the whole K loop.  Then each tile becomes ks units over K ranges of num_kb / ks
+// blocks (ks a divisor of num_kb, at least four blocks a unit); every unit writes its f32 partial
+// sums to its own slice of a scratch buffer, and splitk_reduce_kernel adds the slices in a fixed
+// order, then the bias, and writes the output (zeros for rows outside the grid, as the epilogue
+// does), so results do not depend on timing.
+int choose_ksplit(int64_t pair_tiles, int max_clusters, int num_kb) {
+  if (pair_tiles <= 0 || pair_tiles * 2 > max_clusters) return 1;
+  const int64_t want = max_clusters / pair_tiles;
+  int best = 1;
+  for (int k = 2; k <= want && k <= num_kb; ++k)
+    if (num_kb % k == 0 && num_kb / k >= 4) best = k;
+  return best;
+}
+
+// out[m, 4q .. 4q + 3] from the ks partial slices; one thread per four columns (D % 4 == 0).
+template <typename O>
+__global__ void __launch_bounds__(256)
+    splitk_reduce_kernel(const float* __restrict__ part, int ks, int64_t slice, const RowSource rs,
+                         const int32_t* __restrict__ rows_dev, int rows_cap, GatherGeometry g, EpilogueArgs ep) {
+  pdl_wait();
+  int M = rows_cap;
+  if (rows_dev) M = min(M, max(0, __ldg(rows_dev)));
+  const int d4 = g.D / 4;
+  const int64_t total = (int64_t)M * d4;
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < total; i += (int64_t)gridDim.x * blockDim.x) {
+    const int m = (int)(i / d4), d = (int)(i - (int64_t)m * d4) * 4;
+    bool valid = false;
+    row_base_offset(g, __ldg(rs.coords + m), valid);
+    float4 v = make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (valid) {
+      v = __ldg(reinterpret_cast<const float4*>(part + (int64_t)m * g.D + d));
+      for (int k = 1; k < ks; ++k) {
+        const float4 p = __ldg(reinterpret_cast<const float4*>(part + k * slice + (int64_t)m * g.D + d));
+        v.x = v.x + p.x;
+        v.y = v.y + p.y;
+        v.z = v.z + p.z;
+        v.w = v.w + p.w;
+      }
+      if (ep.bias) {
+        const float4 b = __ldg(reinterpret_cast<const float4*>(ep.bias + d));
+        v.x = v.x + b.x;
+        v.y = v.y + b.y;
+        v.z = v.z + b.z;
+        v.w = v.w + b.w;
+      }
+    }
+    O* o = reinterpret_cast<O*>(static_cast<char*>(ep.out) + ((int64_t)m * ep.ldo + d) * (int64_t)sizeof(O));
+    o[0] = from_f32<O>(v.x);
+    o[1] = from_f32<O>(v.y);
+    o[2] = from_f32<O>(v.z);
+    o[3] = from_f32<O>(v.w);
+  }
+}
+
 // ---- f32 operands on the tensor cores: an error-compensated bf16 split ----------------------
 //
 // x = hi + lo with hi = bf16(x) and lo = bf16(x - hi) (x - hi is exact in f32), so hi + lo
@@ -1320,13 +1386,25 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
     const int64_t base = row_base_offset(g, c, valid);
     if (!valid) continue;
     const int64_t pbase = base + (int64_t)c.x * 2 * g.C * plane;  // batch stride 3C planes
-    for (int k = lane * 4; k < g.K; k += 128) {
-      const int64_t ko = k_offset(g, k);
-      uint2 hi, lo;
-      split_bf16x4(__ldg(reinterpret_cast<const float4*>(video + base + ko)), hi, lo);
-      *reinterpret_cast<uint2*>(pv + pbase + ko) = hi;
-      *reinterpret_cast<uint2*>(pv + pbase + ko + g.C * plane) = hi;
-      *reinterpret_cast<uint2*>(pv + pbase + ko + 2 * g.C * plane) = lo;
+    // four loads in flight per lane before their splits and stores
+    for (int k0 = lane * 4; k0 < g.K; k0 += 4 * 128) {
+      float4 x[4];
+      int64_t ko[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int k = k0 + u * 128;
+        ko[u] = k < g.K ? k_offset(g, k) : -1;
+        if (ko[u] >= 0) x[u] = __ldg(reinterpret_cast<const float4*>(video + base + ko[u]));
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (ko[u] < 0) continue;
+        uint2 hi, lo;
+        split_bf16x4(x[u], hi, lo);
+        *reinterpret_cast<uint2*>(pv + pbase + ko[u]) = hi;
+        *reinterpret_cast<uint2*>(pv + pbase + ko[u] + g.C * plane) = hi;
+        *reinterpret_cast<uint2*>(pv + pbase + ko[u] + 2 * g.C * plane) = lo;
+      }
     }
   }
 }
@@ -1377,7 +1455,7 @@ bjf_status launch_split_f32(const DeviceInfo& dev, const float* input, const flo
     g3.C = 3 * g.C;
     g3.K = 3 * g.K;
     rc = launch_gather_gemm(dev, pv, BJF_DTYPE_BF16, w3, BJF_DTYPE_BF16, g3, rows, rows_dev, rows_cap, ep, st,
-                            /*pdl=*/true, /*may_allocate=*/false);
+                            /*pdl=*/true);
   }
   // stream-ordered: the memory returns to the pool once the GEMM has finished with it
   const bjf_status f1 = stream_free(w3, st), f2 = stream_free(pv, st);
@@ -1464,7 +1542,27 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
         max_clusters = g_pair_clusters[dev.device][pslot];
       }
       const int64_t pair_tiles_cap = ceil_div(g.D, bn) * ceil_div(rows_cap, 2 * kBM);
-      const unsigned clusters = (unsigned)std::min<int64_t>(pair_tiles_cap, max_clusters);
+      EpilogueArgs epk = ep;
+      void* scratch = nullptr;
+      int ks = 1;
+      if (rows.coords && ep.mode == kEpiloguePlain && !embed && may_allocate && g.D % 4 == 0 &&
+          (reinterpret_cast<uintptr_t>(ep.bias) & 15) == 0)
+        ks = choose_ksplit(pair_tiles_cap, max_clusters, g.num_kb);
+      const int64_t slice = rows_cap * (int64_t)g.D;  // f32 elements of one split's partials
+      if (ks > 1) {
+        bjf_status arc = stream_alloc(dev.device, (size_t)ks * slice * sizeof(float), st, &scratch);
+        if (arc) return arc;
+        g.ksplit = ks;
+        epk.out = scratch;
+        epk.out_dtype = BJF_DTYPE_F32;
+        epk.out_elem_bytes = 4;
+        epk.ldo = g.D;
+        epk.bias = nullptr;
+        epk.split_stride = slice * (int64_t)sizeof(float);
+      } else {
+        g.ksplit = 1;
+      }
+      const unsigned clusters = (unsigned)std::min<int64_t>(pair_tiles_cap * ks, max_clusters);
       cudaLaunchConfig_t cfg = {};
       cudaLaunchAttribute attr[2];
       attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -1480,7 +1578,7 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
       cfg.attrs = attr;
       cfg.numAttrs = pdl ? 2 : 1;
       auto launch_pair = [&](auto kern, auto* typed_input) {
-        return cudaLaunchKernelEx(&cfg, kern, map, typed_input, rows, rows_dev, (int)rows_cap, g, bn, ep,
+        return cudaLaunchKernelEx(&cfg, kern, map, typed_input, rows, rows_dev, (int)rows_cap, g, bn, epk,
                                   dev.error_flag);
       };
       cudaError_t e;
@@ -1493,7 +1591,27 @@ bjf_status launch_gather_gemm(const DeviceInfo& dev, const void* input, int32_t 
         e = embed ? launch_pair(gather_gemm_sm100_pair_kernel<__half, true>, in)
                   : launch_pair(gather_gemm_sm100_pair_kernel<__half, false>, in);
       }
-      return e == cudaSuccess ? BJF_OK : cuda_status(e, "gather-GEMM (tcgen05 pair) launch");
+      bjf_status rc2 = e == cudaSuccess ? BJF_OK : cuda_status(e, "gather-GEMM (tcgen05 pair) launch");
+      if (ks > 1) {
+        if (!rc2) {
+          const int64_t work = rows_cap * (g.D / 4);
+          const unsigned rgrid = (unsigned)std::min<int64_t>(ceil_div(work, 256), 8LL * std::max(1, dev.sm_count));
+          const float* part = static_cast<const float*>(scratch);
+          if (ep.out_dtype == BJF_DTYPE_F32)
+            e = launch_kernel(true, splitk_reduce_kernel<float>, dim3(rgrid), dim3(256), 0, st, part, ks, slice,
+                              rows, rows_dev, (int)rows_cap, g, ep);
+          else if (ep.out_dtype == BJF_DTYPE_F16)
+            e = launch_kernel(true, splitk_reduce_kernel<__half>, dim3(rgrid), dim3(256), 0, st, part, ks, slice,
+                              rows, rows_dev, (int)rows_cap, g, ep);
+          else
+            e = launch_kernel(true, splitk_reduce_kernel<__nv_bfloat16>, dim3(rgrid), dim3(256), 0, st, part, ks,
+                              slice, rows, rows_dev, (int)rows_cap, g, ep);
+          rc2 = e == cudaSuccess ? BJF_OK : cuda_status(e, "split-K reduce launch");
+        }
+        const bjf_status frc = stream_free(scratch, st);  // after the reduce, in stream order
+        if (!rc2) rc2 = frc;
+      }
+      return rc2;
     }
     {
       std::lock_guard<std::mutex> lock(g_attr_mu);

@@ -23,6 +23,10 @@ struct GatherGeometry {
   // Frame ring (a two-frame clip of depth 1 read from slots slot0, slot1 of Ts stored frames);
   // ring = 0: contiguous frames, Ts = T (set by launch_gather_gemm)
   int ring, Ts, slot0, slot1;
+  // Split K (pair kernel, plain epilogue): each 256 x bn tile is ksplit units of num_kb / ksplit
+  // K blocks whose f32 partial sums go to ep.out + unit's split x ep.split_stride bytes, summed
+  // by a reduce launch.  0 or 1: none.
+  int ksplit;
 };
 
 enum { kEpiloguePlain = 0, kEpilogueScatter = 1 };
@@ -46,6 +50,7 @@ struct EpilogueArgs {
   const float* position_table;
   int64_t pos_ld;
   const float* modality_embed;
+  int64_t split_stride;  // bytes between the split-K partial outputs (GatherGeometry::ksplit)
 };
 
 // Where the gathered rows come from: either explicit coords rows (b, t, r, col), or the
