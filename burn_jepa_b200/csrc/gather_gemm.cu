@@ -707,12 +707,40 @@ __device__ __forceinline__ void drain_accumulator_rows(const GatherGeometry& g, 
   uint8_t* srow = stage + lane * kEpiRowPitch;
   constexpr int kSegs = kEpiRowBytes / 16;  // 16-byte segments of a staged row
   const int seg = lane % kSegs;             // this lane's segment of a row in the write-back
+  // Encoder input: the row's position values of the next 16 columns are loaded one subchunk
+  // ahead, so their L2 latency overlaps this subchunk's TMEM load, conversion and write-back.
+  const int pos_lim = min(c_end, g.D - n0);  // columns of this drain inside the row
+  float pnext[16];
+  auto load_pos = [&](int col) {  // the 16 values from column col (zeros past the row's end)
+    if (!kEmbed || !pos_row || col >= pos_lim) return;
+    const float* p = pos_row + n0 + col;
+    if (col + 16 <= pos_lim && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const float4 t = __ldg(reinterpret_cast<const float4*>(p) + k);
+        pnext[4 * k] = t.x;
+        pnext[4 * k + 1] = t.y;
+        pnext[4 * k + 2] = t.z;
+        pnext[4 * k + 3] = t.w;
+      }
+    } else {
+#pragma unroll
+      for (int k = 0; k < 16; ++k) pnext[k] = col + k < pos_lim ? __ldg(p + k) : 0.0f;
+    }
+  };
+  if (kEmbed) load_pos(c_begin);
   for (int c0 = c_begin; c0 < c_end; c0 += cpc) {
     const int col0 = n0 + c0;
     const int ncol = min(cpc, min(c_end - c0, g.D - col0));  // the same for the whole warp
     if (ncol <= 0) break;
     __syncwarp();  // the previous chunk's staged rows have been written out
     for (int q = 0; q * 16 < ncol; ++q) {
+      float pcur[16];
+      if (kEmbed) {
+#pragma unroll
+        for (int k = 0; k < 16; ++k) pcur[k] = pnext[k];
+        load_pos(c0 + 16 * q + 16);
+      }
       uint32_t r[16];
       tmem_ld_32x32b_x16(taddr + (uint32_t)(c0 + 16 * q), r);
       tmem_ld_wait();
@@ -727,23 +755,9 @@ __device__ __forceinline__ void drain_accumulator_rows(const GatherGeometry& g, 
         v[4 * k + 3] = valid ? __uint_as_float(r[4 * k + 3]) + b.w : 0.0f;
       }
       if (kEmbed) {
-        const int nq = min(16, ncol - 16 * q);
         if (pos_row) {  // the row's position embedding (this lane's own table row)
-          const float* p = pos_row + col0 + 16 * q;
-          if (nq == 16 && (reinterpret_cast<uintptr_t>(p) & 15) == 0) {
 #pragma unroll
-            for (int k = 0; k < 4; ++k) {
-              const float4 t = __ldg(reinterpret_cast<const float4*>(p) + k);
-              v[4 * k] = v[4 * k] + t.x;
-              v[4 * k + 1] = v[4 * k + 1] + t.y;
-              v[4 * k + 2] = v[4 * k + 2] + t.z;
-              v[4 * k + 3] = v[4 * k + 3] + t.w;
-            }
-          } else {
-#pragma unroll
-            for (int k = 0; k < 16; ++k)
-              if (k < nq) v[k] = v[k] + __ldg(p + k);
-          }
+          for (int k = 0; k < 16; ++k) v[k] = v[k] + pcur[k];
         }
         if (mod_s && valid) {  // then the modality embedding (broadcast, like the bias)
           const float4* m4 = reinterpret_cast<const float4*>(mod_s + c0 + 16 * q);
