@@ -19,7 +19,8 @@
 // partials kept in the caller's workspace, so results do not depend on timing and no counters
 // need resetting.  Every per-pixel operation is rounded as the reference's f32 code does (no
 // contraction): u8 / 255 comes from a shared-memory table of the correctly rounded quotients,
-// x / 3 from div3_rn below, every other quotient from an IEEE division.  The sums differ from
+// x / 3 from div3_rn below, the chroma quotients from a reciprocal and a correction step
+// (div_by_rcp), every other quotient from an IEEE division.  The sums differ from
 // the reference's sequential f32 loops in order and in precision: the channel-delta means are
 // exact here (see accumulate_means), the luma and mean-|delta| sums nearly so, while the
 // reference's f32 running sums round at every pixel.  The frame statistics therefore agree to
@@ -80,11 +81,22 @@ __device__ __forceinline__ ChromaDen chroma_den(Rgb p, Rgb c) {
                    fmaxf(__fadd_rn(__fadd_rn(c.r, c.g), c.b), 0.10f)};
 }
 
-// (sum of |chroma delta|) / 3 with chroma = rgb / max(r + g + b, 0.10) (:1258-1270)
+// a / b correctly rounded from y = RN(1 / b): q = RN(a y), then Markstein's correction step
+// RN(q + (a - b q) y) (the residual is exact with an FMA).  Used where a is a channel value
+// i / 255 and b a chroma denominator max(r + g + b, 0.10) of such values: checked on the host
+// against IEEE division for every one of those (a, b) pairs.
+__device__ __forceinline__ float div_by_rcp(float a, float b, float y) {
+  const float q = __fmul_rn(a, y);
+  return __fmaf_rn(__fmaf_rn(-q, b, a), y, q);
+}
+
+// (sum of |chroma delta|) / 3 with chroma = rgb / max(r + g + b, 0.10) (:1258-1270): one
+// reciprocal per pixel and denominator instead of six divisions
 __device__ __forceinline__ float chroma_diff(Rgb p, Rgb c, ChromaDen d) {
-  const float a = fabsf(__fsub_rn(__fdiv_rn(c.r, d.dc), __fdiv_rn(p.r, d.dp)));
-  const float b = fabsf(__fsub_rn(__fdiv_rn(c.g, d.dc), __fdiv_rn(p.g, d.dp)));
-  const float e = fabsf(__fsub_rn(__fdiv_rn(c.b, d.dc), __fdiv_rn(p.b, d.dp)));
+  const float yc = __frcp_rn(d.dc), yp = __frcp_rn(d.dp);
+  const float a = fabsf(__fsub_rn(div_by_rcp(c.r, d.dc, yc), div_by_rcp(p.r, d.dp, yp)));
+  const float b = fabsf(__fsub_rn(div_by_rcp(c.g, d.dc, yc), div_by_rcp(p.g, d.dp, yp)));
+  const float e = fabsf(__fsub_rn(div_by_rcp(c.b, d.dc, yc), div_by_rcp(p.b, d.dp, yp)));
   return div3_rn(__fadd_rn(__fadd_rn(a, b), e));
 }
 

@@ -110,3 +110,34 @@ def test_pixel_score_bounds_never_drop_the_maximum():
     fast = np.where(chroma_skip, fast, np.maximum(fast, chroma))
     assert rel_skip.mean() > 0.5 and chroma_skip.mean() > 0.5  # the skips do apply
     assert np.array_equal(fast.view(np.uint32), full.view(np.uint32))
+
+
+def _div_by_rcp_method(a: np.ndarray, b: np.ndarray) -> np.ndarray:
+    """The device's chroma quotient: y = RN(1/b), q = RN(a y), result RN(q + (a - b q) y), with
+    the FMA residual and the final FMA rounded once each (exact rationals at midpoints)."""
+    y = (np.float32(1) / b).astype(np.float32)
+    q = (a * y).astype(np.float32)
+    r64 = a.astype(np.float64) - b.astype(np.float64) * q.astype(np.float64)  # exact in f64
+    r = r64.astype(np.float32)  # the FMA's one rounding of the exact residual
+    s64 = q.astype(np.float64) + r.astype(np.float64) * y.astype(np.float64)
+    got = s64.astype(np.float32)
+    ulp = np.spacing(got).astype(np.float64)
+    exact_check = np.abs(s64 - got.astype(np.float64)) * 2 >= ulp * 0.999  # near a midpoint: redo exactly
+    for i in np.flatnonzero(exact_check):
+        e = Fraction(float(q[i])) + Fraction(float(r[i])) * Fraction(float(y[i]))
+        g = np.float32(float(e))
+        cands = [np.nextafter(g, np.float32(-np.inf)), g, np.nextafter(g, np.float32(np.inf))]
+        got[i] = min(cands, key=lambda c: (abs(Fraction(float(c)) - e), int(c.view(np.uint32)) & 1))
+    return got
+
+
+def test_chroma_quotient_matches_ieee_division_on_every_operand_pair():
+    """Every channel value i / 255 over every chroma denominator max(r + g + b, 0.10) the u8
+    pixels produce (1325 values): the reciprocal-and-correction quotient equals a / b."""
+    v = (np.arange(256, dtype=np.float32) / np.float32(255)).astype(np.float32)
+    sums = ((v[:, None, None] + v[None, :, None]).astype(np.float32) + v[None, None, :]).astype(np.float32)
+    dens = np.unique(np.maximum(sums, np.float32(0.10)))
+    assert len(dens) == 1325
+    a = np.repeat(v, len(dens))
+    b = np.tile(dens, len(v))
+    assert np.array_equal(_div_by_rcp_method(a, b).view(np.uint32), (a / b).view(np.uint32))
