@@ -163,3 +163,37 @@ def test_frame_ring_upload_rejects_bad_arguments():
     assert "streams outside" in bj.last_error()
     assert up(ctypes.byref(d), None, FAKE, 3, 0, 0, 4, None) == _abi.BJF_ERR_INVALID_ARGUMENT
     assert up(ctypes.byref(d), FAKE, FAKE, 3, 0, 2, 2, None) == 0  # nothing to copy
+
+
+def test_refresh_entries_reject_bad_arguments_before_any_launch():
+    lib = bj.load()
+    cfg = bj.PatchDiffConfig.adaptive_threshold(0.1, 1, 16, 1)
+    pol = bj._abi.ViewerMaskPolicy.new()
+    refresh = bj.PatchDiffRefreshConfig.from_fields(enabled=True, blue_noise_enabled=True)
+    dims = _abi.dims(1, 4, 4)
+    state = _abi.PatchDiffRefreshState(FAKE.value, FAKE.value, FAKE.value)
+    missing = _abi.PatchDiffRefreshState(None, None, None)
+    out = [FAKE] * 4
+    args = lambda r, st: (FAKE, 1, dims, ctypes.byref(cfg), ctypes.byref(pol), r, st, *out, None)  # noqa: E731
+    assert lib.bjf_viewer_patch_diff_refresh_masks_from_scores(*args(ctypes.byref(refresh), None)) == -1
+    assert "refresh state buffers" in bj.last_error()
+    assert lib.bjf_viewer_patch_diff_refresh_masks_from_scores(*args(ctypes.byref(refresh),
+                                                                     ctypes.byref(missing))) == -1
+    assert "refresh state buffers" in bj.last_error()
+    assert lib.bjf_viewer_patch_diff_refresh_masks_from_scores(*args(None, ctypes.byref(state))) == -1
+    assert "refresh config" in bj.last_error()
+    big = _abi.dims(2, 128, 256)  # 65 536 tokens: above the viewer kernels' 32 768
+    assert lib.bjf_viewer_patch_diff_refresh_observe(FAKE, FAKE, 1, big, ctypes.byref(state), None) == -2
+    assert "32768 tokens" in bj.last_error()
+    assert lib.bjf_viewer_patch_diff_refresh_observe(None, FAKE, 1, dims, ctypes.byref(state), None) == -1
+    assert lib.bjf_viewer_patch_diff_refresh_observe(FAKE, FAKE, 1, dims, ctypes.byref(missing), None) == -1
+    assert lib.bjf_viewer_patch_diff_refresh_observe(FAKE, FAKE, 0, dims, ctypes.byref(state), None) == -1
+
+
+def test_refresh_config_fields_and_defaults():
+    c = bj.PatchDiffRefreshConfig.from_fields()
+    assert (c.enabled, c.subthreshold_enabled, c.age_refresh_enabled, c.blue_noise_enabled) == (0, 0, 0, 0)
+    assert c.age_refresh_interval_frames == 90 and c.blue_noise_seed == 0x9E3779B97F4A7C15
+    assert abs(c.subthreshold_decay - 0.92) < 1e-7 and abs(c.max_extra_density - 0.05) < 1e-9
+    with pytest.raises(TypeError, match="unknown refresh config fields"):
+        bj.PatchDiffRefreshConfig.from_fields(nonsense=1)
