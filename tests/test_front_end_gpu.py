@@ -187,7 +187,7 @@ def test_front_end_reused_workspace_matches_oracle(cuda_device):
     assert not bj.device_error_check()
 
 
-@pytest.mark.parametrize("ring_slots,D,video_dt", [(3, 1024, "f16"), (2, 256, "bf16")])
+@pytest.mark.parametrize("ring_slots,D,video_dt", [(3, 1024, "f16"), (2, 256, "bf16"), (3, 512, "f32")])
 def test_ring_step_equals_the_contiguous_step(cuda_device, ring_slots, D, video_dt):
     """bjf_front_end_step_ring on a frame ring (a live stream that copies only its new frame per
     step) equals bjf_front_end_step on the same two frames stored as a contiguous clip, bit for
@@ -195,7 +195,7 @@ def test_ring_step_equals_the_contiguous_step(cuda_device, ring_slots, D, video_
     in a lower slot than the older one)."""
     import torch
 
-    dt = {"f16": torch.float16, "bf16": torch.bfloat16}[video_dt]
+    dt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}[video_dt]
     S, C, H, W, P = 4, 3, 256, 256, 16
     n = (H // P) * (W // P)
     frames = [torch.from_numpy(workloads.rect_perturbation_clips(300 + f, S, C, 2, H, W, 0.25)[:, :, 0]).to(

@@ -14,8 +14,9 @@ from helpers import max_rel_err
 pytestmark = pytest.mark.gpu
 
 
-@pytest.mark.parametrize("dtype,out", [("f16", "f16"), ("bf16", "f32"), ("f32", "f32")])
-def test_split_k_matches_oracle_and_repeats_bit_for_bit(cuda_device, dtype, out):
+@pytest.mark.parametrize("dtype,out,with_bias", [("f16", "f16", True), ("bf16", "f32", True), ("f32", "f32", True),
+                                               ("f16", "f32", False)])
+def test_split_k_matches_oracle_and_repeats_bit_for_bit(cuda_device, dtype, out, with_bias):
     import torch
 
     dt = {"f16": torch.float16, "bf16": torch.bfloat16, "f32": torch.float32}
@@ -27,11 +28,11 @@ def test_split_k_matches_oracle_and_repeats_bit_for_bit(cuda_device, dtype, out)
     coords[::50, 3] = grid.width + 1  # outside the grid: a zero row
     x = workloads.splitmix_normal(78, (1, C, T, H, W), 1.0)
     w = workloads.splitmix_normal(79, (D, C, kt, P, P), 0.02)
-    b = workloads.splitmix_normal(80, (D,), 0.5)
+    b = workloads.splitmix_normal(80, (D,), 0.5) if with_bias else np.zeros(D, np.float32)
     xd = torch.from_numpy(x).to(cuda_device, dt[dtype])
     wd = torch.from_numpy(w).to(cuda_device, dt[dtype])
     cd = torch.from_numpy(coords).to(cuda_device)
-    bd = torch.from_numpy(b).to(cuda_device)
+    bd = torch.from_numpy(b).to(cuda_device) if with_bias else None
     cfg = bj.PatchifyConfig(C, D, T, H, W, kt, P, P)
     first = bj.sparse_patchify3d_forward(cfg, xd, cd, wd, bd, out_dtype=dt[out])
     again = bj.sparse_patchify3d_forward(cfg, xd, cd, wd, bd, out_dtype=dt[out])
