@@ -112,9 +112,13 @@ bjf_status front_end_step(const bjf_front_end_desc* d, const void* video, const 
   cudaStream_t st = as_cuda(stream);
 
   const int64_t vd[5] = {1, d->channels, d->frames, d->height, d->width};
-  rc = launch_scores(video, d->video_dtype, vd, S, d->tubelet_size, d->patch_size, scores, st, true, ring);
+  // the cache aging rides at the end of the scores pass when it can, else in the selection
+  const ScoresAging aging{age_frames, observed, (long long)(S * N)};
+  bool aged = false;
+  rc = launch_scores(video, d->video_dtype, vd, S, d->tubelet_size, d->patch_size, scores, st, true, ring,
+                     age_observed ? &aging : nullptr, &aged);
   if (rc) return rc;
-  if (age_observed) {
+  if (age_observed && !aged) {
     sel.age = age_frames;
     sel.observed = observed;
   }

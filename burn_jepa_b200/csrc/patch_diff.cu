@@ -61,7 +61,7 @@ __global__ void __launch_bounds__(kScoreThreads, 4)
     patch_diff_scores_vec_kernel(const T* __restrict__ video, float* __restrict__ scores, int batch,
                                  int channels, int frames, int height, int width, int kt, int P,
                                  int depth, int gh, int gw, int chunks_per_row, long long total_warps,
-                                 FrameRing ring) {
+                                 FrameRing ring, ScoresAging aging) {
   constexpr int VEC = 16 / sizeof(T);
   const int LPT = P / VEC;      // lanes per token column
   const int TPW = 32 / LPT;     // token columns per warp
@@ -122,6 +122,24 @@ __global__ void __launch_bounds__(kScoreThreads, 4)
   // previous frame's gather-GEMM, which none of its inputs depend on); it still does not
   // complete before that kernel, so everything after it in the stream sees both finished.
   pdl_wait();
+  // The cache aging, now that the previous frame's GEMM (which writes observed / age) is done;
+  // blocks that finish their units early do it while others still stream.
+  if (aging.age) {
+    const long long n4 = aging.len >> 2;
+    const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x, step = (long long)gridDim.x * blockDim.x;
+    float4* a4 = reinterpret_cast<float4*>(aging.age);
+    const float4* o4 = reinterpret_cast<const float4*>(aging.observed);
+    for (long long i = tid; i < n4; i += step) {
+      float4 a = a4[i];
+      const float4 o = o4[i];
+      a.x += o.x;
+      a.y += o.y;
+      a.z += o.z;
+      a.w += o.w;
+      a4[i] = a;
+    }
+    for (long long i = n4 * 4 + tid; i < aging.len; i += step) aging.age[i] += aging.observed[i];
+  }
 }
 
 // Generic scores (any patch size / alignment): one thread per token.
@@ -515,7 +533,9 @@ int sm_count() {
 }  // namespace
 
 bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* vd, int64_t streams,
-                         int64_t kt, int64_t P, float* scores, cudaStream_t st, bool pdl, const FrameRing* ring_in) {
+                         int64_t kt, int64_t P, float* scores, cudaStream_t st, bool pdl, const FrameRing* ring_in,
+                         const ScoresAging* aging_in, bool* aged) {
+  if (aged) *aged = false;
   const int64_t B = vd[0], C = vd[1], T = vd[2], H = vd[3], W = vd[4];
   const FrameRing ring = ring_in ? *ring_in : FrameRing::contiguous((int)T);
   const int64_t depth = T / kt, gh = H / P, gw = W / P;
@@ -534,11 +554,17 @@ bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* vd, in
       long long warps = (long long)streams * depth * gh * chunks;
       // persistent: a few resident blocks per SM stride over the work units
       long long blocks = std::min<long long>(ceil_div(warps, kScoreThreads / 32), (long long)sm_count() * 4);
+      // 16-byte aligned metadata for the float4 aging loop
+      ScoresAging aging{};
+      if (aging_in && aging_in->age &&
+          ((reinterpret_cast<uintptr_t>(aging_in->age) | reinterpret_cast<uintptr_t>(aging_in->observed)) & 15) == 0)
+        aging = *aging_in;
       cudaError_t e = launch_kernel(pdl, patch_diff_scores_vec_kernel<T_>, dim3((unsigned)blocks),
                                     dim3(kScoreThreads), 0, st, static_cast<const T_*>(video), scores, (int)B,
                                     (int)C, (int)T, (int)H, (int)W, (int)kt, (int)P, (int)depth, (int)gh,
-                                    (int)gw, chunks, warps, ring);
+                                    (int)gw, chunks, warps, ring, aging);
       rc = e == cudaSuccess ? BJF_OK : cuda_status(e, "patch-diff scores launch");
+      if (!rc && aged) *aged = aging.age != nullptr;
       return;
     } else {
       long long total = (long long)streams * n_tok;

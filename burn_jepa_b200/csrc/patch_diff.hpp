@@ -41,9 +41,19 @@ struct FrameRing {
 
 // Per-tubelet mean |delta| scores for `streams` videos [B, C, T, H, W] -> [streams, N]; with a
 // ring (T = 2 only), the frames are read from its slots.
+// With `aging` (age[i] += observed[i] over `aging_len` floats, the first half of the AssignLatest
+// update), the vector pass does the aging after its closing wait for the kernel before it (the
+// previous frame's GEMM, which writes those arrays) and sets *aged; otherwise *aged = false and
+// the caller ages elsewhere.
+struct ScoresAging {
+  float* age;
+  const float* observed;
+  long long len;
+};
 bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* video_dims, int64_t streams,
                          int64_t tubelet_size, int64_t patch_size, float* scores, cudaStream_t st,
-                         bool pdl = false, const FrameRing* ring = nullptr);
+                         bool pdl = false, const FrameRing* ring = nullptr, const ScoresAging* aging = nullptr,
+                         bool* aged = nullptr);
 
 // Device plan (coords rows) from per-stream mask indices; see bjf_sparse_patchify_plan_coords.
 bjf_status launch_plan(const int32_t* indices, int64_t index_stride, const int32_t* counts, int64_t mask_rows,
