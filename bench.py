@@ -287,7 +287,7 @@ def make_inputs(torch, dev, streams, density, seed_base):
     return sets
 
 
-def time_rows(torch, bj, dev, videos, weight, bias, mask_cfg, hbm_peak, tflops_peak, reps=10,
+def time_rows(torch, bj, dev, videos, weight, bias, mask_cfg, hbm_peak, tflops_peak, reps=20,
               groups=("select", "plan", "cache", "rgba", "front_end", "vitg", "f32"), vitg_clips=32):
     """Each row of the path timed alone through its public entry point, with CUDA events on the
     launching stream.  Before every call 256 MB are written (L2 flushed), another 256 MB are
@@ -305,6 +305,7 @@ def time_rows(torch, bj, dev, videos, weight, bias, mask_cfg, hbm_peak, tflops_p
     flush_clean = torch.ones(ROW_FLUSH_BYTES // 4, dtype=torch.int32, device=dev)
     flush_sum = torch.zeros((), dtype=torch.int64, device=dev)
     out = {}
+    spread = {}  # median and 95th percentile of the last timed() call
 
     def timed(fn):
         for i in range(3):
@@ -320,22 +321,25 @@ def time_rows(torch, bj, dev, videos, weight, bias, mask_cfg, hbm_peak, tflops_p
             b.record(stream)
         torch.cuda.synchronize()
         assert not bj.device_error_check(), "a kernel reported a bounded-wait timeout"
-        return statistics.mean(a.elapsed_time(b) for a, b in evs)
+        times = sorted(a.elapsed_time(b) for a, b in evs)
+        spread["p50_ms"] = round(statistics.median(times), 4)
+        spread["p95_ms"] = round(times[min(len(times) - 1, int(0.95 * len(times)))], 4)
+        return statistics.mean(times)
 
     def hbm(name, row, workload, ms, nbytes, **extra):
         gbs = nbytes / (ms / 1e3) / 1e9
-        out[name] = {"row": row, "workload": workload, "bound": "hbm", "avg_ms": round(ms, 4),
+        out[name] = {"row": row, "workload": workload, "bound": "hbm", "avg_ms": round(ms, 4), **spread,
                      "algorithmic_bytes": int(nbytes), "achieved": round(gbs, 1), "unit": "GB/s", "peak": hbm_peak,
                      "frac": round(gbs / hbm_peak, 4), **extra}
 
     def tensor(name, row, workload, ms, flops, **extra):
         tf = flops / (ms / 1e3) / 1e12
-        out[name] = {"row": row, "workload": workload, "bound": "tensor", "avg_ms": round(ms, 4),
+        out[name] = {"row": row, "workload": workload, "bound": "tensor", "avg_ms": round(ms, 4), **spread,
                      "algorithmic_flops": int(flops), "achieved": round(tf, 1), "unit": "TFLOP/s",
                      "peak": tflops_peak, "frac": round(tf / tflops_peak, 4), **extra}
 
     def latency(name, row, workload, ms, **extra):
-        out[name] = {"row": row, "workload": workload, "bound": "latency", "avg_ms": round(ms, 4), **extra}
+        out[name] = {"row": row, "workload": workload, "bound": "latency", "avg_ms": round(ms, 4), **spread, **extra}
 
     S = videos[0].shape[0] if videos is not None else 0
     live = f"{S} streams, grid {GRID[0]}x{GRID[1]}x{GRID[2]}"
