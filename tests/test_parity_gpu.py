@@ -262,7 +262,9 @@ def cfg_o(c: bj.PatchifyConfig) -> oracle.PatchifyConfig:
 PATCHIFY_SHAPES = [
     # (batch, C, T, H, W, kt, P, D, rows)
     (1, 3, 16, 64, 64, 2, 16, 1024, 300),    # ViT-L/16 width, rows not a multiple of 128
-    (2, 3, 2, 128, 96, 2, 16, 1408, 131),    # ViT-g/16 width (BN = 176)
+    (2, 3, 2, 128, 96, 2, 16, 1408, 131),    # ViT-g/16 width (six 240-column tiles)
+    (2, 3, 2, 64, 128, 2, 16, 257, 300),     # two 144-column tiles, odd D (unaligned output rows)
+    (1, 3, 4, 64, 64, 2, 16, 1100, 400),     # five 224-column tiles (split K applies)
     (4, 3, 2, 64, 64, 2, 16, 768, 512),      # ViT-B width, several full M tiles
     (1, 3, 4, 32, 32, 2, 16, 32, 4),         # tiny config
     (3, 3, 2, 32, 64, 2, 16, 96, 1),         # a single row
