@@ -51,8 +51,8 @@ __device__ __forceinline__ void tubelet_pairs(int t, int kt, int frames, int& fi
 }
 
 // Vectorised scores: a work unit is one (stream, tubelet, token row, chunk of token
-// columns); warps stride over the units (a grid of 5 blocks of 8 warps per SM, 4 resident at
-// <= 64 registers; the row loop unrolled eight deep so each lane keeps up to 16 loads in
+// columns); warps stride over the units (a grid of 4 or 5 blocks of 8 warps per SM, 4 resident
+// at <= 64 registers; the row loop unrolled eight deep so each lane keeps up to 16 loads in
 // flight).  Consecutive warps of a block take adjacent column chunks of the same rows.
 // Lane l covers VEC elements of token column (chunk*TPW + l/LPT).
 template <typename T>
@@ -551,11 +551,15 @@ bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* vd, in
       const int TPW = 32 / LPT;
       const int chunks = (int)ceil_div(gw, TPW);
       long long warps = (long long)streams * depth * gh * chunks;
-      // persistent: five blocks per SM (one more than are resident at once) stride over the
-      // work units.  In the fused step the pass starts beside the previous frame's GEMM, where
-      // only two blocks an SM fit; measured on the live step (32 streams), five blocks per SM
-      // gave 0.111 ms a step against 0.118 with four and 0.113 with six, the pass alone the same.
-      long long blocks = std::min<long long>(ceil_div(warps, kScoreThreads / 32), (long long)sm_count() * 5);
+      // A grid-stride grid of one resident wave (4 blocks per SM), or of 5 blocks per SM for a
+      // pass of at most 1.5 units a warp at that size.  In the fused step the pass starts beside
+      // the previous frame's GEMM, where only two blocks an SM fit; measured on the live step
+      // (32 streams, 8192 units) five blocks per SM gave 0.111 ms a step against 0.118 with four,
+      // while at 64 streams (16 384 units) four were best, and five left the pass alone a tail
+      // (0.90 vs 0.98 of HBM).
+      const long long sms = sm_count();
+      const long long per_sm = warps * 2 <= sms * 5 * (kScoreThreads / 32) * 3 ? 5 : 4;
+      long long blocks = std::min<long long>(ceil_div(warps, kScoreThreads / 32), sms * per_sm);
       // 16-byte aligned metadata for the float4 aging loop
       ScoresAging aging{};
       if (aging_in && aging_in->age &&
