@@ -411,7 +411,18 @@ def time_cache_rows(torch, bj, dev, S, timed, hbm):
     ms = timed(lambda i: bj.feature_memory_reset_rows(feats, observed, age, reset))
     hbm("feature_memory_reset_rows", "f3", f"{len(reset_rows)} of {S} stream caches [{N_TOKENS},{D}] f16 zeroed",
         ms, len(reset_rows) * N_TOKENS * (D * 2 + 8))
-    del tokens, feats, observed, age
+    # a6 again at 40 % (the density sweep's top point): four times the rows, where a call's fixed
+    # cost (launch, first-load latency, tail) no longer dominates
+    width4 = 4 * width
+    ti4 = np.stack([np.sort(rng.choice(N_TOKENS, width4, replace=False)) for _ in range(S)]).astype(np.int32)
+    tok_idx4 = torch.from_numpy(ti4).to(dev)
+    del tokens
+    tokens4 = torch.randn((S, width4, D), device=dev).to(torch.float16)
+    m4 = S * width4
+    ms = timed(lambda i: bj.feature_memory_assign_latest(feats, observed, age, tokens4, tok_idx4, True))
+    hbm("feature_memory_assign_latest_40pct", "a6", f"{S} streams x {width4} of {N_TOKENS} tokens, D={D}, "
+        "f16 tokens -> f16 cache", ms, m4 * D * 4 + m4 * 4 + aging + m4 * 8)
+    del tokens4, feats, observed, age
 
 
 def time_rgba_rows(torch, bj, dev, videos, S, timed, hbm, latency):
