@@ -1349,7 +1349,7 @@ __global__ void __launch_bounds__(256)
 // a w = a_hi w_hi + a_hi w_lo + a_lo w_hi + O(2^-16 |a w|): three bf16 products, each exact in
 // the f32 accumulator.  The three run as one bf16 GEMM over K' = 3K by tripling the channel
 // axis: the gathered rows as [a_hi | a_hi | a_lo] and the weight as [w_hi | w_lo | w_hi], channel
-// groups in K order (the channel is K's slowest axis).  split_rows_kernel writes the split rows
+// groups in K order (the channel is K's slowest axis).  split_rows_part writes the split rows
 // into a bf16 copy of the input with 3C channels at the same (b, t, r, col) positions, so the
 // GEMM reads it with the caller's own rows and epilogue (plain, encoder input or cache scatter).
 // Only the selected tubelets of that copy are written, and only they are read.
@@ -1369,10 +1369,11 @@ __device__ __forceinline__ void split_bf16x4(float4 x, uint2& hi, uint2& lo) {
 }
 
 // weight [D, K] f32 -> [D, 3K] bf16 as [hi | lo | hi] per row; K % 4 == 0.
-__global__ void __launch_bounds__(256) split_weight_kernel(const float* __restrict__ w, int D, int K,
-                                                           __nv_bfloat16* __restrict__ w3) {
+// The weight split by blocks [0, nblocks) of a launch (this is block `bid`).
+__device__ __forceinline__ void split_weight_part(const float* __restrict__ w, int D, int K,
+                                                  __nv_bfloat16* __restrict__ w3, int bid, int nblocks) {
   const int64_t n4 = (int64_t)D * (K / 4);
-  for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)gridDim.x * blockDim.x) {
+  for (int64_t i = bid * (int64_t)blockDim.x + threadIdx.x; i < n4; i += (int64_t)nblocks * blockDim.x) {
     const int64_t d = i / (K / 4), k = (i - d * (K / 4)) * 4;
     uint2 hi, lo;
     split_bf16x4(__ldg(reinterpret_cast<const float4*>(w + d * K + k)), hi, lo);
@@ -1386,17 +1387,19 @@ __global__ void __launch_bounds__(256) split_weight_kernel(const float* __restri
 // The rows of `rs` (as the GEMM resolves them) from the f32 input into a bf16 input of 3C
 // channels, one warp per row, four consecutive k (inside one pw run, pw % 4 == 0) per lane.
 // Rows outside the grid are skipped, as the GEMM reads them as zeros.
-__global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict__ video, const RowSource rs,
-                                                         const int32_t* __restrict__ rows_dev, int rows_cap,
-                                                         GatherGeometry g, __nv_bfloat16* __restrict__ pv) {
-  __shared__ int soff[kMaxRowStreams + 1];
+// By blocks [0, nblocks) of a launch (this is block `bid`); block-wide (`soff`: kMaxRowStreams + 1
+// ints of shared memory).
+__device__ __forceinline__ void split_rows_part(const float* __restrict__ video, const RowSource& rs,
+                                                const int32_t* __restrict__ rows_dev, int rows_cap,
+                                                const GatherGeometry& g, __nv_bfloat16* __restrict__ pv, int* soff,
+                                                int bid, int nblocks) {
   pdl_wait();  // the rows come from the kernels before
   int M = rows_cap;
   if (rows_dev) M = min(M, max(0, __ldg(rows_dev)));
   M = min(M, load_row_offsets(rs, soff));
   const int lane = threadIdx.x & 31, wpb = blockDim.x >> 5;
   const int64_t plane = (int64_t)g.Ts * g.H * g.W;  // one channel of one batch element
-  for (int m = blockIdx.x * wpb + (threadIdx.x >> 5); m < M; m += gridDim.x * wpb) {
+  for (int m = bid * wpb + (threadIdx.x >> 5); m < M; m += nblocks * wpb) {
     bool valid = false;
     const int4 c = fetch_row(rs, soff, g, m);
     const int64_t base = row_base_offset(g, c, valid);
@@ -1423,6 +1426,22 @@ __global__ void __launch_bounds__(256) split_rows_kernel(const float* __restrict
       }
     }
   }
+}
+
+// Both splits in one launch: blocks [0, wblocks) split the weight, the rest the rows, so the two
+// memory-bound passes share the device instead of running one after the other.  The weight
+// blocks need nothing from the kernels before; the row blocks wait for them.
+__global__ void __launch_bounds__(256) split_operands_kernel(const float* __restrict__ weight, int wblocks,
+                                                             __nv_bfloat16* __restrict__ w3,
+                                                             const float* __restrict__ video, const RowSource rs,
+                                                             const int32_t* __restrict__ rows_dev, int rows_cap,
+                                                             GatherGeometry g, __nv_bfloat16* __restrict__ pv) {
+  __shared__ int soff[kMaxRowStreams + 1];
+  if ((int)blockIdx.x < wblocks) {
+    split_weight_part(weight, g.D, g.K, w3, (int)blockIdx.x, wblocks);
+    return;
+  }
+  split_rows_part(video, rs, rows_dev, rows_cap, g, pv, soff, (int)blockIdx.x - wblocks, (int)gridDim.x - wblocks);
 }
 
 // Whether f32 operands take the split: the bf16 path must take the tripled geometry, and the
@@ -1457,14 +1476,13 @@ bjf_status launch_split_f32(const DeviceInfo& dev, const float* input, const flo
   }
   const int sms = dev.sm_count > 0 ? dev.sm_count : 148;
   const int64_t w4 = (int64_t)g.D * (g.K / 4);
-  split_weight_kernel<<<(unsigned)std::min<int64_t>(ceil_div(w4, 256), 4 * sms), 256, 0, st>>>(
-      weight, g.D, g.K, static_cast<__nv_bfloat16*>(w3));
-  rc = check_launch("f32 weight split launch");
-  if (!rc) {
-    const unsigned grid = (unsigned)std::min<int64_t>(ceil_div(rows_cap, 8), 8 * sms);
-    cudaError_t e = launch_kernel(pdl, split_rows_kernel, dim3(grid), dim3(256), 0, st, input, rows, rows_dev,
-                                  (int)rows_cap, g, static_cast<__nv_bfloat16*>(pv));
-    rc = e == cudaSuccess ? BJF_OK : cuda_status(e, "f32 row split launch");
+  const int wblocks = (int)std::min<int64_t>(ceil_div(w4, 256), sms);  // one block an SM for the weight
+  const int rblocks = (int)std::min<int64_t>(ceil_div(rows_cap, 8), 8 * sms);
+  {
+    const cudaError_t e = launch_kernel(pdl, split_operands_kernel, dim3((unsigned)(wblocks + rblocks)), dim3(256),
+                                        0, st, weight, wblocks, static_cast<__nv_bfloat16*>(w3), input, rows,
+                                        rows_dev, (int)rows_cap, g, static_cast<__nv_bfloat16*>(pv));
+    rc = e == cudaSuccess ? BJF_OK : cuda_status(e, "f32 operand split launch");
   }
   if (!rc) {
     GatherGeometry g3 = g;
