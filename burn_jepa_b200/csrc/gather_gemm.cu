@@ -1393,7 +1393,7 @@ __device__ __forceinline__ void split_rows_part(const float* __restrict__ video,
                                                 const int32_t* __restrict__ rows_dev, int rows_cap,
                                                 const GatherGeometry& g, __nv_bfloat16* __restrict__ pv, int* soff,
                                                 int bid, int nblocks) {
-  pdl_wait();  // the rows come from the kernels before
+  pdl_wait();  // the rows come from the kernels before, and `pv` may be memory they read
   int M = rows_cap;
   if (rows_dev) M = min(M, max(0, __ldg(rows_dev)));
   M = min(M, load_row_offsets(rs, soff));
@@ -1429,8 +1429,10 @@ __device__ __forceinline__ void split_rows_part(const float* __restrict__ video,
 }
 
 // Both splits in one launch: blocks [0, wblocks) split the weight, the rest the rows, so the two
-// memory-bound passes share the device instead of running one after the other.  The weight
-// blocks need nothing from the kernels before; the row blocks wait for them.
+// memory-bound passes share the device instead of running one after the other.  Every block
+// waits for the kernels before it (as a programmatic dependent): the row blocks read their rows,
+// and the split buffers come from the stream-ordered pool, whose memory an earlier GEMM of the
+// stream may have been reading.
 __global__ void __launch_bounds__(256) split_operands_kernel(const float* __restrict__ weight, int wblocks,
                                                              __nv_bfloat16* __restrict__ w3,
                                                              const float* __restrict__ video, const RowSource rs,
@@ -1438,6 +1440,7 @@ __global__ void __launch_bounds__(256) split_operands_kernel(const float* __rest
                                                              GatherGeometry g, __nv_bfloat16* __restrict__ pv) {
   __shared__ int soff[kMaxRowStreams + 1];
   if ((int)blockIdx.x < wblocks) {
+    pdl_wait();
     split_weight_part(weight, g.D, g.K, w3, (int)blockIdx.x, wblocks);
     return;
   }
