@@ -50,6 +50,31 @@ __device__ __forceinline__ void tubelet_pairs(int t, int kt, int frames, int& fi
   }
 }
 
+// The end of a scores pass.  Launched as a programmatic dependent, the pass may overlap the kernel
+// before it (the previous frame's gather-GEMM, which none of its inputs depend on); it still does
+// not complete before that kernel, so everything after it in the stream sees both finished.  Then
+// the cache aging, now that the previous frame's GEMM (which writes observed / age) is done;
+// blocks that finish their units early do it while others still stream.
+__device__ __forceinline__ void finish_scores_pass(const ScoresAging& aging) {
+  pdl_wait();
+  if (aging.age) {
+    const long long n4 = aging.len >> 2;
+    const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x, step = (long long)gridDim.x * blockDim.x;
+    float4* a4 = reinterpret_cast<float4*>(aging.age);
+    const float4* o4 = reinterpret_cast<const float4*>(aging.observed);
+    for (long long i = tid; i < n4; i += step) {
+      float4 a = a4[i];
+      const float4 o = o4[i];
+      a.x += o.x;
+      a.y += o.y;
+      a.z += o.z;
+      a.w += o.w;
+      a4[i] = a;
+    }
+    for (long long i = n4 * 4 + tid; i < aging.len; i += step) aging.age[i] += aging.observed[i];
+  }
+}
+
 // Vectorised scores: a work unit is one (stream, tubelet, token row, chunk of token
 // columns); warps stride over the units (a grid of 4 or 5 blocks of 8 warps per SM, 4 resident
 // at <= 64 registers; the row loop unrolled eight deep so each lane keeps up to 16 loads in
@@ -117,28 +142,79 @@ __global__ void __launch_bounds__(kScoreThreads, 4)
     out[col] = acc * (float)(1.0 / denom);
   }
   }
-  // Launched as a programmatic dependent, this pass may overlap the kernel before it (the
-  // previous frame's gather-GEMM, which none of its inputs depend on); it still does not
-  // complete before that kernel, so everything after it in the stream sees both finished.
-  pdl_wait();
-  // The cache aging, now that the previous frame's GEMM (which writes observed / age) is done;
-  // blocks that finish their units early do it while others still stream.
-  if (aging.age) {
-    const long long n4 = aging.len >> 2;
-    const long long tid = (long long)blockIdx.x * blockDim.x + threadIdx.x, step = (long long)gridDim.x * blockDim.x;
-    float4* a4 = reinterpret_cast<float4*>(aging.age);
-    const float4* o4 = reinterpret_cast<const float4*>(aging.observed);
-    for (long long i = tid; i < n4; i += step) {
-      float4 a = a4[i];
-      const float4 o = o4[i];
-      a.x += o.x;
-      a.y += o.y;
-      a.z += o.z;
-      a.w += o.w;
-      a4[i] = a;
+  finish_scores_pass(aging);
+}
+
+// Scores of a small pass (a single clip, a few streams): one block per work unit (the 16 or so
+// token columns one warp covers in the pass above), its warps splitting the unit's
+// (batch, channel, frame pair, pixel row) iterations round-robin, so the pass spreads over the
+// SMs instead of one warp per unit on a few of them.  Each warp's per-token partial sum (lanes of
+// a token combined by shuffles) meets the others in shared memory, where warp 0 adds them in
+// warp order: the same result whatever the timing.
+template <typename T>
+__global__ void __launch_bounds__(kScoreThreads)
+    patch_diff_scores_split_kernel(const T* __restrict__ video, float* __restrict__ scores, int batch,
+                                   int channels, int frames, int height, int width, int kt, int P, int depth,
+                                   int gh, int gw, int chunks_per_row, long long units, FrameRing ring,
+                                   ScoresAging aging) {
+  constexpr int VEC = 16 / sizeof(T);
+  constexpr int kWarps = kScoreThreads / 32;
+  __shared__ float part[kWarps][32];
+  const int LPT = P / VEC;   // lanes per token column
+  const int TPW = 32 / LPT;  // token columns per unit
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (long long u = blockIdx.x; u < units; u += gridDim.x) {
+    const int chunk = (int)(u % chunks_per_row);
+    long long rest = u / chunks_per_row;
+    const int r = (int)(rest % gh);
+    rest /= gh;
+    const int t = (int)(rest % depth);
+    const long long s = rest / depth;
+    const int col = chunk * TPW + lane / LPT;
+    const int sub = lane % LPT;
+    const bool valid = col < gw;
+    const int x = col * P + sub * VEC;
+    int first_next, npairs;
+    tubelet_pairs(t, kt, frames, first_next, npairs);
+    const long long plane = (long long)height * width;
+    float acc = 0.0f;
+    if (valid && npairs > 0) {
+      const int iters = batch * channels * npairs * P;  // (b, ch, p, py), py fastest
+#pragma unroll 4
+      for (int it = warp; it < iters; it += kWarps) {
+        const int py = it % P;
+        int q = it / P;
+        const int p = q % npairs;
+        q /= npairs;
+        const int ch = q % channels, b = q / channels;
+        const T* vbase = video + (((s * batch + b) * channels + ch) * ring.storage_frames) * plane +
+                         (long long)(r * P + py) * width + x;
+        const uint4 un = ld_nc_v4(vbase + (long long)ring.frame(first_next + p) * plane);
+        const uint4 up = ld_nc_v4(vbase + (long long)ring.frame(first_next + p - 1) * plane);
+        const T* a = reinterpret_cast<const T*>(&un);
+        const T* c = reinterpret_cast<const T*>(&up);
+#pragma unroll
+        for (int v = 0; v < VEC; ++v) acc += fabsf(to_f32<T>(a[v]) - to_f32<T>(c[v]));
+      }
     }
-    for (long long i = n4 * 4 + tid; i < aging.len; i += step) aging.age[i] += aging.observed[i];
+    for (int o = LPT >> 1; o > 0; o >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, o);
+    part[warp][lane] = acc;
+    __syncthreads();
+    if (warp == 0 && valid && sub == 0) {
+      float* out = scores + s * ((long long)depth * gh * gw) + ((long long)t * gh + r) * gw;
+      if (npairs == 0) {
+        out[col] = 0.0f;
+      } else {
+        float sum = 0.0f;
+#pragma unroll
+        for (int w = 0; w < kWarps; ++w) sum += part[w][lane];
+        const double denom = (double)npairs * batch * channels * P * P;
+        out[col] = sum * (float)(1.0 / denom);
+      }
+    }
+    __syncthreads();  // the partials are read before the next unit writes them
   }
+  finish_scores_pass(aging);
 }
 
 // Generic scores (any patch size / alignment): one thread per token.
@@ -565,10 +641,22 @@ bjf_status launch_scores(const void* video, int32_t dtype, const int64_t* vd, in
       if (aging_in && aging_in->age &&
           ((reinterpret_cast<uintptr_t>(aging_in->age) | reinterpret_cast<uintptr_t>(aging_in->observed)) & 15) == 0)
         aging = *aging_in;
-      cudaError_t e = launch_kernel(pdl, patch_diff_scores_vec_kernel<T_>, dim3((unsigned)blocks),
-                                    dim3(kScoreThreads), 0, st, static_cast<const T_*>(video), scores, (int)B,
-                                    (int)C, (int)T, (int)H, (int)W, (int)kt, (int)P, (int)depth, (int)gh,
-                                    (int)gw, chunks, warps, ring, aging);
+      cudaError_t e;
+      if (warps < sms * (kScoreThreads / 32)) {
+        // too few units for a block of them on every SM (a single clip): a block per unit, its
+        // warps splitting the unit's loop.  Measured: one ViT-L clip [3, 16, 256, 256] (128 units),
+        // fused step 0.034 vs 0.046 ms; 8 live streams (2048 units) stay faster one warp a unit
+        // (0.050 vs 0.057 ms split).
+        e = launch_kernel(pdl, patch_diff_scores_split_kernel<T_>,
+                          dim3((unsigned)std::min<long long>(warps, sms * (kScoreThreads / 32))),
+                          dim3(kScoreThreads), 0, st, static_cast<const T_*>(video), scores, (int)B, (int)C, (int)T,
+                          (int)H, (int)W, (int)kt, (int)P, (int)depth, (int)gh, (int)gw, chunks, warps, ring,
+                          aging);
+      } else {
+        e = launch_kernel(pdl, patch_diff_scores_vec_kernel<T_>, dim3((unsigned)blocks), dim3(kScoreThreads), 0,
+                          st, static_cast<const T_*>(video), scores, (int)B, (int)C, (int)T, (int)H, (int)W,
+                          (int)kt, (int)P, (int)depth, (int)gh, (int)gw, chunks, warps, ring, aging);
+      }
       rc = e == cudaSuccess ? BJF_OK : cuda_status(e, "patch-diff scores launch");
       if (!rc && aged) *aged = aging.age != nullptr;
       return;
